@@ -1,0 +1,264 @@
+"""ctypes bindings for the CPU oracle (liboracle.so) and, when built, the
+reference's own op code (_ref/libtpref.so).
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, __graft_entry__.smoke() and
+bench.py's CPU-baseline / reference legs, as the checker. The product
+(libtpmd.so and its Python binding) never imports this module.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE_SO = os.path.join(HERE, "liboracle.so")
+REF_SO = os.path.join(HERE, "_ref", "libtpref.so")
+
+ST_IC = (512, 512, 512, 512, 256, 128, 64)
+ST_OC = (512, 512, 512, 256, 128, 64, 32)
+
+_f32p = C.POINTER(C.c_float)
+_i64p = C.POINTER(C.c_int64)
+
+
+def _p(a: np.ndarray):
+    return a.ctypes.data_as(C.c_void_p)
+
+
+def build() -> None:
+    """Compile liboracle.so (and oracle/_ref when the reference is present)."""
+    import subprocess
+    import sys
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+    subprocess.run([sys.executable, os.path.join(HERE, "ref_build.py")], check=True)
+
+
+_lib = None
+_ref = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(ORACLE_SO):
+            build()
+        L = C.CDLL(ORACLE_SO)
+        v = C.c_void_p
+        L.orc_bilinear_gather.argtypes = [v, C.c_int, C.c_int, C.c_int, C.c_int, v, C.c_int64,
+                                          C.c_int, C.c_int, v]
+        L.orc_im2col_cf.argtypes = [v] + [C.c_int] * 12 + [v, C.c_int]
+        L.orc_bias_lrelu.argtypes = [v, v, v, C.c_int, C.c_float, v]
+        L.orc_subpix_lrelu.argtypes = [v, v, v, C.c_int, C.c_int, C.c_int, C.c_float, v]
+        L.orc_subpix_lrelu_cl.argtypes = [v, v, C.c_int, C.c_int64, C.c_int64, C.c_int,
+                                          C.c_float, v]
+        L.orc_upfirdn2x.argtypes = [v, v, C.c_int, C.c_int, C.c_int64, v]
+        L.orc_clsp_mul.argtypes = [v, v, C.c_int, C.c_int64, v]
+        L.orc_clsp_lerp.argtypes = [v, v, v, C.c_int, C.c_int64, v]
+        L.orc_flow_grid.argtypes = [v, v, C.c_int64, v]
+        L.orc_scale_for.argtypes = [C.c_char_p, v]
+        L.orc_scale_for.restype = C.c_double
+        L.orc_saug.argtypes = [v, C.c_int, C.c_int, v]
+        L.orc_tsubcf.argtypes = [v, v, C.c_int, C.c_int, v]
+        L.orc_dec_create.restype = v
+        L.orc_dec_destroy.argtypes = [v]
+        L.orc_dec_set.argtypes = [v, C.c_char_p, v, C.c_int64]
+        L.orc_dec_set_feat.argtypes = [v, C.c_int, v, C.c_int64]
+        L.orc_dec_prepare.argtypes = [v]
+        L.orc_dec_decode.argtypes = [v, v, C.c_int, C.c_int, v]
+        L.orc_dec_tap.argtypes = [v, C.c_char_p, v, C.c_int64]
+        L.orc_dec_tap.restype = C.c_int64
+        L.orc_dec_error.argtypes = [v]
+        L.orc_dec_error.restype = C.c_char_p
+        L.orc_set_threads.argtypes = [C.c_int]
+        L.orc_get_threads.restype = C.c_int
+        _lib = L
+    return _lib
+
+
+def ref_lib():
+    """The reference's op code built by ref_build.py, or None if absent."""
+    global _ref
+    if _ref is None and os.path.exists(REF_SO):
+        L = C.CDLL(REF_SO)
+        v = C.c_void_p
+        for pre in ("ref_cpu_", "ref_cu_"):
+            getattr(L, pre + "bilinear_gather").argtypes = [v, C.c_int, C.c_int, C.c_int, C.c_int,
+                                                           v, C.c_int64, C.c_int, C.c_int, v]
+            getattr(L, pre + "bias_lrelu").argtypes = [v, v, v, C.c_int, C.c_float, v]
+            getattr(L, pre + "subpix_lrelu").argtypes = [v, v, v, C.c_int, C.c_int, C.c_int,
+                                                        C.c_float, v]
+            getattr(L, pre + "subpix_lrelu_cl").argtypes = [v, v, C.c_int, C.c_int64, C.c_int64,
+                                                           C.c_int, C.c_float, v]
+            getattr(L, pre + "upfirdn2x").argtypes = [v, v, C.c_int, C.c_int, C.c_int64, v]
+            getattr(L, pre + "flow_grid").argtypes = [v, v, C.c_int64, v]
+        L.ref_cpu_clsp_mul.argtypes = [v, v, C.c_int, C.c_int64, v]
+        L.ref_cpu_clsp_lerp.argtypes = [v, v, v, C.c_int, C.c_int64, v]
+        L.ref_cu_clsp.argtypes = [v, v, v, C.c_int, C.c_int64, C.c_int, v]
+        L.ref_cu_im2col_cf.argtypes = [v] + [C.c_int] * 12 + [v, C.c_int]
+        _ref = L
+    return _ref
+
+
+# ---------------------------------------------------------------------------
+# op wrappers. `impl` selects: "oracle" (this restatement), "ref_cpu" or
+# "ref_cu" (the reference's own CPU function / CUDA kernel run on the host).
+# ---------------------------------------------------------------------------
+def _L(impl):
+    if impl == "oracle":
+        return lib(), "orc_"
+    r = ref_lib()
+    if r is None:
+        raise RuntimeError("oracle/_ref/libtpref.so not built (reference absent)")
+    return r, impl + "_"
+
+
+def bilinear_gather(feat, W, H, grid, planar=False, sp=False, impl="oracle"):
+    feat = np.ascontiguousarray(feat)
+    grid = np.ascontiguousarray(grid, dtype=np.float32)
+    Cc = feat.shape[-1]
+    N = grid.size // 2
+    out = np.empty((Cc, N) if sp else (N, Cc), np.float32)
+    L, pre = _L(impl)
+    getattr(L, pre + "bilinear_gather")(_p(feat), int(feat.dtype == np.float16), Cc, W, H,
+                                        _p(grid), N, int(planar), int(sp), _p(out))
+    return out
+
+
+def im2col_cf(src, IC, IW, IH, N, KW=3, KH=3, s0=1, s1=1, p0=1, p1=1, d0=1, d1=1,
+              dst_f16=False, impl="oracle"):
+    src = np.ascontiguousarray(src, dtype=np.float32)
+    OW = (IW + 2 * p0 - d0 * (KW - 1) - 1) // s0 + 1
+    OH = (IH + 2 * p1 - d1 * (KH - 1) - 1) // s1 + 1
+    out = np.empty((N, OH, OW, IC * KW * KH), np.float16 if dst_f16 else np.float32)
+    if impl == "oracle":
+        lib().orc_im2col_cf(_p(src), IC, IW, IH, N, KW, KH, s0, s1, p0, p1, d0, d1, _p(out),
+                            int(dst_f16))
+    else:
+        if impl != "ref_cu":
+            raise ValueError("im2col_cf reference: only the CUDA kernel is self-contained")
+        _L(impl)[0].ref_cu_im2col_cf(_p(src), IC, IW, IH, N, KW, KH, s0, s1, p0, p1, d0, d1,
+                                     _p(out), int(dst_f16))
+    return out
+
+
+def bias_lrelu(x, bias, axis, slope=0.2, impl="oracle"):
+    """x given in ggml ne order as a flat array plus ne (4-tuple)."""
+    arr, ne = x
+    arr = np.ascontiguousarray(arr, np.float32)
+    ne = np.asarray(list(ne) + [1] * (4 - len(ne)), np.int64)
+    bias = np.ascontiguousarray(bias, np.float32)
+    out = np.empty_like(arr)
+    L, pre = _L(impl)
+    getattr(L, pre + "bias_lrelu")(_p(arr), _p(bias), _p(ne), axis, slope, _p(out))
+    return out
+
+
+def subpix_lrelu(g0, g1, bias, W, H, OC, slope=0.2, impl="oracle"):
+    out = np.empty(4 * W * H * OC, np.float32)
+    L, pre = _L(impl)
+    getattr(L, pre + "subpix_lrelu")(_p(g0), _p(g1), _p(bias), W, H, OC, slope, _p(out))
+    return out
+
+
+def subpix_lrelu_cl(y4, bias, OC, N, B, W, slope=0.2, impl="oracle"):
+    out = np.empty(4 * OC * N * B, np.float32)
+    L, pre = _L(impl)
+    getattr(L, pre + "subpix_lrelu_cl")(_p(y4), _p(bias), OC, N, B, W, slope, _p(out))
+    return out
+
+
+def upfirdn2x(x, k4, W, H, CB, impl="oracle"):
+    out = np.empty(4 * W * H * CB, np.float32)
+    L, pre = _L(impl)
+    getattr(L, pre + "upfirdn2x")(_p(x), _p(k4), W, H, CB, _p(out))
+    return out
+
+
+def clsp(cl, m, Cc, N, o=None, impl="oracle"):
+    out = np.empty(Cc * N, np.float32)
+    L, pre = _L(impl)
+    if impl == "ref_cu":
+        L.ref_cu_clsp(_p(cl), _p(m), _p(o) if o is not None else None, Cc, N,
+                      int(o is not None), _p(out))
+    elif o is None:
+        getattr(L, pre + "clsp_mul")(_p(cl), _p(m), Cc, N, _p(out))
+    else:
+        getattr(L, pre + "clsp_lerp")(_p(cl), _p(m), _p(o), Cc, N, _p(out))
+    return out
+
+
+def flow_grid(fl, xs, N, impl="oracle"):
+    out = np.empty(3 * N, np.float32)
+    L, pre = _L(impl)
+    getattr(L, pre + "flow_grid")(_p(fl), _p(xs), N, _p(out))
+    return out
+
+
+def scale_for(name: str, ne) -> float:
+    ne = np.asarray(list(ne) + [1] * (4 - len(ne)), np.int64)
+    return lib().orc_scale_for(name.encode(), _p(ne))
+
+
+def saug(W, IC, OC):
+    out = np.empty((OC, IC + 1), np.float32)
+    lib().orc_saug(_p(np.ascontiguousarray(W, np.float32)), IC, OC, _p(out))
+    return out
+
+
+def tsubcf(W, K, IC, OC):
+    out = np.empty((4 * OC, 9 * IC), np.float32)
+    lib().orc_tsubcf(_p(np.ascontiguousarray(W, np.float32)),
+                     _p(np.ascontiguousarray(K, np.float32)), IC, OC, _p(out))
+    return out
+
+
+class Decoder:
+    """The oracle decoder: folded tensors in, CHW f32 frames out."""
+
+    def __init__(self, tensors: dict, feats: list):
+        L = lib()
+        self._L = L
+        self._h = L.orc_dec_create()
+        for name, arr in tensors.items():
+            a = np.ascontiguousarray(arr, np.float32)
+            if L.orc_dec_set(self._h, name.encode(), _p(a), a.size) != 0:
+                raise ValueError(self.error())
+        for j, f in enumerate(feats):
+            a = np.ascontiguousarray(f, np.float32)
+            if L.orc_dec_set_feat(self._h, j, _p(a), a.size) != 0:
+                raise ValueError(self.error())
+        if L.orc_dec_prepare(self._h) != 0:
+            raise ValueError(self.error())
+
+    def error(self) -> str:
+        return self._L.orc_dec_error(self._h).decode()
+
+    def decode(self, style, mode=0, keep_taps=False):
+        style = np.ascontiguousarray(style, np.float32)
+        img = np.empty((3, 512, 512), np.float32)
+        if self._L.orc_dec_decode(self._h, _p(style), mode, int(keep_taps), _p(img)) != 0:
+            raise RuntimeError(self.error())
+        return img
+
+    def tap(self, name: str) -> np.ndarray:
+        n = self._L.orc_dec_tap(self._h, name.encode(), None, 0)
+        if n < 0:
+            raise KeyError(name)
+        out = np.empty(n, np.float32)
+        self._L.orc_dec_tap(self._h, name.encode(), _p(out), n)
+        return out
+
+    def __del__(self):
+        if getattr(self, "_h", None):
+            self._L.orc_dec_destroy(self._h)
+            self._h = None
+
+
+def set_threads(n: int) -> None:
+    lib().orc_set_threads(n)
+
+
+def threads() -> int:
+    return lib().orc_get_threads()

@@ -1,0 +1,748 @@
+// CPU oracle for the motion decoder — TEST INFRASTRUCTURE ONLY (see
+// tp_oracle.h). Each function names the reference lines it restates; paths are
+// relative to the reference project root (patch:N = patches/ggml-tp-ops.patch
+// line N).
+#include "tp_oracle.h"
+
+#include <omp.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <string>
+#include <vector>
+
+namespace {
+
+const int ST_IC[7] = {512, 512, 512, 512, 256, 128, 64};  // motion_dec.cpp:12
+const int ST_OC[7] = {512, 512, 512, 256, 128, 64, 32};   // motion_dec.cpp:13
+
+inline float h2f(uint16_t h) {
+    _Float16 v;
+    memcpy(&v, &h, 2);
+    return (float) v;
+}
+inline uint16_t f2h(float f) {
+    _Float16 v = (_Float16) f;  // round-to-nearest-even
+    uint16_t h;
+    memcpy(&h, &v, 2);
+    return h;
+}
+inline float lrelu(float v, float s) { return v > 0.0f ? v : s * v; }
+
+// One output row of a stride-1 2-D correlation for a block of `nb` output
+// channels: acc[o][ox] += sum_{ic,ky,kx} w[o][ic][ky][kx] * x[ic][iy][ox+kx-pl]
+// (iy = oy + ky - pt, zero outside the input). Cloned for AVX-512 / AVX2 so the
+// oracle runs near the host's vector width wherever the library travels.
+__attribute__((target_clones("arch=x86-64-v4", "default")))
+void conv_row(const float *x, int IC, int IH, int IW, const float *w, int KH,
+              int KW, int pt, int pl, int oy, int OW, int nb, float *acc,
+              int accs) {
+    for (int ic = 0; ic < IC; ic++) {
+        for (int ky = 0; ky < KH; ky++) {
+            const int iy = oy + ky - pt;
+            if (iy < 0 || iy >= IH) continue;
+            const float *row = x + ((size_t) ic * IH + iy) * IW;
+            for (int kx = 0; kx < KW; kx++) {
+                const int sh = kx - pl;
+                const int lo = std::max(0, -sh), hi = std::min(OW, IW - sh);
+                for (int o = 0; o < nb; o++) {
+                    const float wv = w[(((size_t) o * IC + ic) * KH + ky) * KW + kx];
+                    float *a = acc + (size_t) o * accs;
+                    for (int ox = lo; ox < hi; ox++) a[ox] += wv * row[ox + sh];
+                }
+            }
+        }
+    }
+}
+
+// y[OC][OH][OW] = corr2d(x[IC][IH][IW], w[OC][IC][KH][KW]), stride 1, top/left
+// padding pt/pl (zeros), output size given (the bottom/right padding follows).
+// Stands in for ggml_conv_2d_direct as used by src/motion_dec.cpp:597-632.
+void conv2d(const float *x, int IC, int IH, int IW, const float *w, int OC, int KH,
+            int KW, int pt, int pl, int OH, int OW, float *y) {
+    const int OB = 8;
+    const int nob = (OC + OB - 1) / OB;
+#pragma omp parallel
+    {
+        std::vector<float> acc((size_t) OB * OW);
+#pragma omp for collapse(2) schedule(dynamic, 4)
+        for (int ob = 0; ob < nob; ob++) {
+            for (int oy = 0; oy < OH; oy++) {
+                const int o0 = ob * OB, nb = std::min(OB, OC - o0);
+                std::fill(acc.begin(), acc.end(), 0.0f);
+                conv_row(x, IC, IH, IW, w + (size_t) o0 * IC * KH * KW, KH, KW, pt, pl,
+                         oy, OW, nb, acc.data(), OW);
+                for (int o = 0; o < nb; o++)
+                    memcpy(y + ((size_t) (o0 + o) * OH + oy) * OW,
+                           acc.data() + (size_t) o * OW, (size_t) OW * 4);
+            }
+        }
+    }
+}
+
+std::map<std::string, int64_t> expected_tensors() {
+    std::map<std::string, int64_t> m;
+    char nm[64];
+    m["dec.input.input"] = 512 * 16;
+    m["dec.conv1.conv.weight"] = (int64_t) 512 * 512 * 9;
+    m["dec.conv1.conv.modulation.weight"] = 512 * 512;
+    m["dec.conv1.conv.modulation.bias"] = 512;
+    m["dec.conv1.activate.bias"] = 512;
+    for (int i = 0; i < 14; i++) {
+        const int j = i / 2;
+        const bool up = (i % 2) == 0;
+        const int IC = up ? ST_IC[j] : ST_OC[j], OC = ST_OC[j];
+        snprintf(nm, sizeof nm, "dec.convs.%d.conv.weight", i);
+        m[nm] = (int64_t) OC * IC * 9;
+        snprintf(nm, sizeof nm, "dec.convs.%d.conv.modulation.weight", i);
+        m[nm] = (int64_t) IC * 512;
+        snprintf(nm, sizeof nm, "dec.convs.%d.conv.modulation.bias", i);
+        m[nm] = IC;
+        snprintf(nm, sizeof nm, "dec.convs.%d.activate.bias", i);
+        m[nm] = OC;
+        if (up) {
+            snprintf(nm, sizeof nm, "dec.convs.%d.conv.blur.kernel", i);
+            m[nm] = 16;
+        }
+    }
+    for (int j = 0; j < 7; j++) {
+        const int OC = ST_OC[j];
+        snprintf(nm, sizeof nm, "dec.to_flows.%d.conv.weight", j);
+        m[nm] = 3 * OC;
+        snprintf(nm, sizeof nm, "dec.to_flows.%d.conv.modulation.weight", j);
+        m[nm] = (int64_t) OC * 512;
+        snprintf(nm, sizeof nm, "dec.to_flows.%d.conv.modulation.bias", j);
+        m[nm] = OC;
+        snprintf(nm, sizeof nm, "dec.to_flows.%d.bias", j);
+        m[nm] = 3;
+        snprintf(nm, sizeof nm, "dec.to_flows.%d.upsample.kernel", j);
+        m[nm] = 16;
+        snprintf(nm, sizeof nm, "dec.to_rgbs.%d.conv.0.weight", j);
+        m[nm] = 3 * OC;
+        snprintf(nm, sizeof nm, "dec.to_rgbs.%d.conv.1.bias", j);
+        m[nm] = 3;
+        snprintf(nm, sizeof nm, "dec.to_rgbs.%d.bias", j);
+        m[nm] = 3;
+        snprintf(nm, sizeof nm, "dec.to_rgbs.%d.upsample.kernel", j);
+        m[nm] = 16;
+    }
+    return m;
+}
+
+}  // namespace
+
+extern "C" {
+
+// ---------------------------------------------------------------------------
+// patched ops
+// ---------------------------------------------------------------------------
+
+// torch grid_sample (bilinear, zeros, align_corners=false) over a channel-last
+// map; patch:319-369 (CPU) / patch:688-718 (CUDA). fx = (gx+1)/2*W - 1/2 with
+// the final multiply-add fused, taps k = 0..3 at (x0 + (k&1), y0 + (k>>1)),
+// out-of-range taps skipped, accumulation in tap order with fused multiply-add.
+void orc_bilinear_gather(const void *feat, int feat_f16, int C, int W, int H,
+                         const float *grid, int64_t N, int planar, int sp,
+                         float *dst) {
+#pragma omp parallel for schedule(static)
+    for (int64_t n = 0; n < N; n++) {
+        const float gx = planar ? grid[n] : grid[2 * n + 0];
+        const float gy = planar ? grid[N + n] : grid[2 * n + 1];
+        const float fx = fmaf((gx + 1.0f) * 0.5f, (float) W, -0.5f);
+        const float fy = fmaf((gy + 1.0f) * 0.5f, (float) H, -0.5f);
+        const int64_t x0 = (int64_t) floorf(fx), y0 = (int64_t) floorf(fy);
+        const float wx = fx - (float) x0, wy = fy - (float) y0;
+        float *d = dst + (sp ? n : (int64_t) C * n);
+        const int64_t ds = sp ? N : 1;
+        for (int c = 0; c < C; c++) d[c * ds] = 0.0f;
+        for (int k = 0; k < 4; k++) {
+            const int64_t cx = x0 + (k & 1), cy = y0 + (k >> 1);
+            if (cx < 0 || cx >= W || cy < 0 || cy >= H) continue;
+            const float wgt = ((k & 1) ? wx : 1.0f - wx) * ((k >> 1) ? wy : 1.0f - wy);
+            const int64_t row = cy * W + cx;
+            if (feat_f16) {
+                const uint16_t *f = (const uint16_t *) feat + (int64_t) C * row;
+                for (int c = 0; c < C; c++) d[c * ds] = fmaf(wgt, h2f(f[c]), d[c * ds]);
+            } else {
+                const float *f = (const float *) feat + (int64_t) C * row;
+                for (int c = 0; c < C; c++) d[c * ds] = fmaf(wgt, f[c], d[c * ds]);
+            }
+        }
+    }
+}
+
+// channels-first im2col, patch:201-307 (CPU) / patch:830-861 (CUDA): source
+// [IC, IW, IH, N] (ic fastest), dst [IC*KW*KH, OW, OH, N] with row
+// r = ic + IC*(kw + KW*kh), zero outside the source.
+void orc_im2col_cf(const float *src, int IC, int IW, int IH, int N, int KW, int KH,
+                   int s0, int s1, int p0, int p1, int d0, int d1, void *dst,
+                   int dst_f16) {
+    const int64_t OW = (IW + 2 * p0 - d0 * (KW - 1) - 1) / s0 + 1;
+    const int64_t OH = (IH + 2 * p1 - d1 * (KH - 1) - 1) / s1 + 1;
+    const int64_t R = (int64_t) IC * KW * KH;
+#pragma omp parallel for collapse(2) schedule(static)
+    for (int64_t in = 0; in < N; in++) {
+        for (int64_t oh = 0; oh < OH; oh++) {
+            for (int64_t ow = 0; ow < OW; ow++) {
+                const int64_t base = ((in * OH + oh) * OW + ow) * R;
+                const float *sb = src + in * (int64_t) IC * IW * IH;
+                for (int kh = 0; kh < KH; kh++) {
+                    for (int kw = 0; kw < KW; kw++) {
+                        const int64_t iw = ow * s0 + kw * d0 - p0;
+                        const int64_t ih = oh * s1 + kh * d1 - p1;
+                        const bool in_b = iw >= 0 && iw < IW && ih >= 0 && ih < IH;
+                        for (int ic = 0; ic < IC; ic++) {
+                            const int64_t r = ic + (int64_t) IC * (kw + KW * kh);
+                            const float v = in_b ? sb[ic + (int64_t) IC * (iw + IW * ih)] : 0.0f;
+                            if (dst_f16)
+                                ((uint16_t *) dst)[base + r] = f2h(v);
+                            else
+                                ((float *) dst)[base + r] = v;
+                        }
+                    }
+                }
+            }
+        }
+    }
+}
+
+// y = leaky_relu(x + bias, slope), bias along ggml dim `axis` (0 or 2);
+// patch:376-430.
+void orc_bias_lrelu(const float *x, const float *bias, const int64_t *ne, int axis,
+                    float slope, float *y) {
+    const int64_t n = ne[0] * ne[1] * ne[2] * ne[3];
+    const int64_t C = ne[axis], d01 = ne[0] * ne[1];
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < n; i++) {
+        const int64_t c = axis == 0 ? i % C : (i / d01) % C;
+        y[i] = lrelu(x[i] + bias[c], slope);
+    }
+}
+
+// spatial sub-pixel interleave + bias + lrelu, patch:435-482:
+// dst[2n+bx, 2m+by, o] = lrelu(g{by}[n, m, o + OC*bx] + bias[o]).
+void orc_subpix_lrelu(const float *g0, const float *g1, const float *bias, int W,
+                      int H, int OC, float slope, float *y) {
+#pragma omp parallel for collapse(2) schedule(static)
+    for (int o = 0; o < OC; o++) {
+        for (int Y = 0; Y < 2 * H; Y++) {
+            const float *g = (Y & 1) ? g1 : g0;
+            const int m = Y >> 1;
+            for (int X = 0; X < 2 * W; X++) {
+                const int nn = X >> 1, bx = X & 1;
+                const float v = g[nn + (int64_t) W * (m + (int64_t) H * (o + OC * bx))] + bias[o];
+                y[X + 2 * (int64_t) W * (Y + 2 * (int64_t) H * o)] = lrelu(v, slope);
+            }
+        }
+    }
+}
+
+// channel-last sub-pixel interleave, patch:488-530:
+// dst[o, (2n+bx) + 2W(2m+by), b] = lrelu(y4[o + OC*(2by+bx), n + W*m, b] + bias[o]).
+void orc_subpix_lrelu_cl(const float *y4, const float *bias, int OC, int64_t N,
+                         int64_t B, int W, float slope, float *y) {
+    const int64_t W2 = 2 * (int64_t) W;
+    const int64_t npix = 4 * N * B;
+#pragma omp parallel for schedule(static)
+    for (int64_t p = 0; p < npix; p++) {
+        const int64_t nn = p % (4 * N), bb = p / (4 * N);
+        const int64_t X = nn % W2, Y = nn / W2;
+        const int64_t k = (Y & 1) * 2 + (X & 1);
+        const float *s = y4 + OC * k + 4 * (int64_t) OC * ((X >> 1) + W * (Y >> 1) + N * bb);
+        for (int o = 0; o < OC; o++) y[(int64_t) OC * p + o] = lrelu(s[o] + bias[o], slope);
+    }
+}
+
+// upfirdn2d(up=2, pad=(2,1)) with a 4x4 FIR, patch:535-572:
+// y[X,Y] = sum_{j,i} zstuff(x)[X+i-2, Y+j-2] * k4[i + 4j].
+void orc_upfirdn2x(const float *x, const float *k4, int W, int H, int64_t CB,
+                   float *y) {
+    const int64_t n_tot = 4 * (int64_t) W * H * CB;
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < n_tot; i++) {
+        const int64_t X = i % (2 * W), Y = (i / (2 * W)) % (2 * H);
+        const int64_t cb = i / (4 * (int64_t) W * H);
+        const float *xp = x + (int64_t) W * H * cb;
+        float acc = 0.0f;
+        for (int j = 0; j < 4; j++) {
+            const int64_t vy = Y + j - 2;
+            if (vy < 0 || vy >= 2 * H || (vy & 1)) continue;
+            for (int ii = 0; ii < 4; ii++) {
+                const int64_t vx = X + ii - 2;
+                if (vx < 0 || vx >= 2 * W || (vx & 1)) continue;
+                acc = fmaf(xp[(vx >> 1) + W * (vy >> 1)], k4[ii + 4 * j], acc);
+            }
+        }
+        y[i] = acc;
+    }
+}
+
+// channel-last -> spatial transpose times the mask, patch:578-601.
+void orc_clsp_mul(const float *cl, const float *m, int C, int64_t N, float *y) {
+#pragma omp parallel for collapse(2) schedule(static)
+    for (int c = 0; c < C; c++)
+        for (int64_t n = 0; n < N; n++) y[n + N * c] = cl[c + (int64_t) C * n] * m[n];
+}
+
+// transpose + blend, patch:603-626: y = cl^T*m + out*(1-m).
+void orc_clsp_lerp(const float *cl, const float *m, const float *o, int C, int64_t N,
+                   float *y) {
+#pragma omp parallel for collapse(2) schedule(static)
+    for (int c = 0; c < C; c++)
+        for (int64_t n = 0; n < N; n++) {
+            const int64_t i = n + N * c;
+            const float a = cl[c + (int64_t) C * n] * m[n];
+            const float b = o[i] * (1.0f - m[n]);
+            y[i] = a + b;
+        }
+}
+
+// flow head, patch:632-657: planar (tanh(f0)+xs0, tanh(f1)+xs1, sigmoid(f2)).
+void orc_flow_grid(const float *fl, const float *xs, int64_t N, float *y) {
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < 3 * N; i++) {
+        const int64_t pln = i / N, n = i % N;
+        y[i] = pln == 2 ? 1.0f / (1.0f + expf(-fl[2 * N + n]))
+                        : tanhf(fl[pln * N + n]) + xs[pln * N + n];
+    }
+}
+
+// ---------------------------------------------------------------------------
+// load-time scale folding: src/motion_enc.cpp:14-45
+// ---------------------------------------------------------------------------
+double orc_scale_for(const char *cname, const int64_t *ne) {
+    const std::string name = cname;
+    const double SQRT2 = 1.4142135623730951;
+    auto ends = [&](const char *s) {
+        const size_t n = strlen(s);
+        return name.size() >= n && name.compare(name.size() - n, n, s) == 0;
+    };
+    auto starts = [&](const char *s) { return name.rfind(s, 0) == 0; };
+    if (name == "enc.net_app.convs.0.1.bias" || ends(".conv1.1.bias") ||
+        ends(".activate.bias") || (starts("dec.to_rgbs.") && ends(".conv.1.bias")))
+        return SQRT2;
+    if (!ends(".weight")) return 1.0;
+    if (starts("dec.direction")) return 1.0;
+    if (ends("noise.weight")) return 1.0;
+    if (ends("modulation.weight")) return 1.0 / sqrt((double) ne[0]);
+    if (starts("enc.fc.")) return 1.0 / sqrt((double) ne[0]);
+    const double conv = 1.0 / sqrt((double) (ne[0] * ne[1] * ne[2]));
+    if (name == "enc.net_app.convs.0.0.weight" || ends(".conv1.0.weight")) return conv * SQRT2;
+    if (ends(".conv2.1.weight")) return conv;
+    if (ends(".skip.1.weight")) return conv / SQRT2;
+    if (name == "enc.net_app.convs.8.weight") return conv;
+    if (starts("dec.to_rgbs.") && ends(".conv.0.weight")) return conv * SQRT2;
+    if (ends(".conv.weight")) return conv;
+    return 1.0;
+}
+
+// ---------------------------------------------------------------------------
+// derived weights: src/motion_dec.cpp:108-120 (S_aug), :144-191 (tsubcf)
+// ---------------------------------------------------------------------------
+void orc_saug(const float *W, int IC, int OC, float *saug) {
+    for (int o = 0; o < OC; o++) {
+        for (int i = 0; i < IC; i++) {
+            double s = 0;
+            const float *pw = W + ((size_t) o * IC + i) * 9;
+            for (int k = 0; k < 9; k++) s += (double) pw[k] * pw[k];
+            saug[(size_t) o * (IC + 1) + i] = (float) (s * 0.5);
+        }
+        saug[(size_t) o * (IC + 1) + IC] = 0.5e-8f;
+    }
+}
+
+// conv_transpose(3x3, stride 2) followed by the 4x4 blur (pad 1,1) equals, per
+// output parity class (by, bx), a 3x3 pad-1 correlation of the input with
+// T[ty][tx] = sum_{cy,cx} V[cy][cx] * K[1+2ty-by-cy][1+2tx-bx-cx]
+// (V = spatially flipped weight, K = blur kernel, terms outside K dropped).
+void orc_tsubcf(const float *W, const float *K, int IC, int OC, float *tsub) {
+    const size_t R = (size_t) IC * 9;
+#pragma omp parallel for schedule(static)
+    for (int o = 0; o < OC; o++) {
+        for (int i = 0; i < IC; i++) {
+            const float *pw = W + ((size_t) o * IC + i) * 9;
+            for (int by = 0; by < 2; by++)
+                for (int bx = 0; bx < 2; bx++) {
+                    float *dstc = tsub + (size_t) ((by * 2 + bx) * OC + o) * R;
+                    for (int ty = 0; ty < 3; ty++)
+                        for (int tx = 0; tx < 3; tx++) {
+                            double acc = 0;
+                            for (int cy = 0; cy < 3; cy++) {
+                                const int ay = 1 + 2 * ty - by - cy;
+                                if (ay < 0 || ay > 3) continue;
+                                for (int cx = 0; cx < 3; cx++) {
+                                    const int ax = 1 + 2 * tx - bx - cx;
+                                    if (ax < 0 || ax > 3) continue;
+                                    const float v = pw[(2 - cy) * 3 + (2 - cx)];
+                                    acc += (double) v * (double) K[ay * 4 + ax];
+                                }
+                            }
+                            dstc[i + (size_t) IC * (tx + 3 * ty)] = (float) acc;
+                        }
+                }
+        }
+    }
+}
+
+void orc_set_threads(int n) {
+    if (n > 0) omp_set_num_threads(n);
+}
+int orc_get_threads(void) { return omp_get_max_threads(); }
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// decoder
+// ---------------------------------------------------------------------------
+struct orc_dec {
+    std::map<std::string, int64_t> spec = expected_tensors();
+    std::map<std::string, std::vector<float>> t;
+    std::vector<float> feat[7];
+    std::map<std::string, std::vector<float>> saug, tsub;
+    std::map<std::string, std::vector<float>> taps;
+    bool prepared = false;
+    std::string err;
+
+    const std::vector<float> &get(const std::string &n) const { return t.at(n); }
+
+    // s = Wmod * latent + bmod (src/motion_dec.cpp:267-272)
+    std::vector<float> style_of(const std::string &base, const float *lat) const {
+        const std::vector<float> &Wm = get(base + ".modulation.weight");
+        const std::vector<float> &bm = get(base + ".modulation.bias");
+        const int IC = (int) bm.size();
+        std::vector<float> s((size_t) IC);
+        for (int i = 0; i < IC; i++) {
+            double a = 0;
+            const float *w = Wm.data() + (size_t) i * 512;
+            for (int k = 0; k < 512; k++) a += (double) w[k] * lat[k];
+            s[(size_t) i] = (float) a + bm[(size_t) i];
+        }
+        return s;
+    }
+    // den = sqrt(S_aug [s^2; 1]) (src/motion_dec.cpp:275-280)
+    std::vector<float> demod_den(const std::string &wname, const std::vector<float> &s) const {
+        const std::vector<float> &sa = saug.at(wname);
+        const int IC = (int) s.size();
+        const int OC = (int) (sa.size() / (IC + 1));
+        std::vector<float> den((size_t) OC);
+        for (int o = 0; o < OC; o++) {
+            const float *r = sa.data() + (size_t) o * (IC + 1);
+            double a = 0;
+            for (int i = 0; i < IC; i++) {
+                const float s2 = s[(size_t) i] * s[(size_t) i];
+                a += (double) r[i] * s2;
+            }
+            a += (double) r[IC];
+            den[(size_t) o] = sqrtf((float) a);
+        }
+        return den;
+    }
+    void tap(bool keep, const std::string &name, const float *p, size_t n) {
+        if (keep) taps[name].assign(p, p + n);
+    }
+};
+
+namespace {
+
+// modulated dense 3x3 conv, map-side style (src/motion_dec.cpp:597-608):
+// lrelu(conv(x*s, W)/den + bias)
+std::vector<float> styled_conv_exact(const orc_dec &d, const std::vector<float> &x, int IC,
+                                     int Hh, const std::string &base, const float *lat) {
+    const std::vector<float> s = d.style_of(base + ".conv", lat);
+    const std::vector<float> den = d.demod_den(base + ".conv.weight", s);
+    const std::vector<float> &W = d.get(base + ".conv.weight");
+    const std::vector<float> &ab = d.get(base + ".activate.bias");
+    const int OC = (int) ab.size();
+    const size_t P = (size_t) Hh * Hh;
+    std::vector<float> xs(x.size());
+    for (int i = 0; i < IC; i++)
+        for (size_t p = 0; p < P; p++) xs[i * P + p] = x[i * P + p] * s[(size_t) i];
+    std::vector<float> y((size_t) OC * P);
+    conv2d(xs.data(), IC, Hh, Hh, W.data(), OC, 3, 3, 1, 1, Hh, Hh, y.data());
+#pragma omp parallel for schedule(static)
+    for (int o = 0; o < OC; o++)
+        for (size_t p = 0; p < P; p++) {
+            const float v = y[o * P + p] / den[(size_t) o];
+            y[o * P + p] = lrelu(v + ab[(size_t) o], 0.2f);
+        }
+    return y;
+}
+
+// upsampling modulated conv.
+// mode 0 (src/motion_dec.cpp:609-627): zero-stuff x*s, pad (2,1), correlate
+// with the flipped weight, /den, blur pad (1,1), lrelu(+bias).
+// mode 1 (src/motion_dec.cpp:397-433): the composed sub-pixel kernel (tsubcf)
+// as one 3x3 pad-1 conv with 4*OC outputs, /den per class, sub-pixel shuffle,
+// lrelu(+bias).
+std::vector<float> styled_conv_up(const orc_dec &d, const std::vector<float> &x, int IC,
+                                  int Hh, const std::string &base, const float *lat,
+                                  int mode) {
+    const std::vector<float> s = d.style_of(base + ".conv", lat);
+    const std::vector<float> den = d.demod_den(base + ".conv.weight", s);
+    const std::vector<float> &W = d.get(base + ".conv.weight");
+    const std::vector<float> &ab = d.get(base + ".activate.bias");
+    const std::vector<float> &K = d.get(base + ".conv.blur.kernel");
+    const int OC = (int) ab.size();
+    const int H2 = 2 * Hh;
+    const size_t P = (size_t) Hh * Hh;
+    std::vector<float> out((size_t) OC * H2 * H2);
+    if (mode == 0) {
+        const int ZP = H2 + 3;  // zero-stuffed 2H, padded 2 before and 1 after
+        std::vector<float> zs((size_t) IC * ZP * ZP, 0.0f);
+        for (int i = 0; i < IC; i++)
+            for (int yy = 0; yy < Hh; yy++)
+                for (int xx = 0; xx < Hh; xx++)
+                    zs[((size_t) i * ZP + 2 * yy + 2) * ZP + 2 * xx + 2] =
+                        x[i * P + (size_t) yy * Hh + xx] * s[(size_t) i];
+        std::vector<float> wf(W.size());
+        for (int o = 0; o < OC; o++)
+            for (int i = 0; i < IC; i++)
+                for (int a = 0; a < 3; a++)
+                    for (int b = 0; b < 3; b++)
+                        wf[(((size_t) o * IC + i) * 3 + a) * 3 + b] =
+                            W[(((size_t) o * IC + i) * 3 + (2 - a)) * 3 + (2 - b)];
+        const int TO = H2 + 1;  // conv_transpose output size 2H+1
+        std::vector<float> y((size_t) OC * TO * TO);
+        conv2d(zs.data(), IC, ZP, ZP, wf.data(), OC, 3, 3, 0, 0, TO, TO, y.data());
+        // /den, then blur with pad (1,1): out[Y][X] = sum_{a,b} K[a][b] yp[Y+a][X+b]
+#pragma omp parallel for schedule(static)
+        for (int o = 0; o < OC; o++) {
+            float *yo = y.data() + (size_t) o * TO * TO;
+            for (size_t q = 0; q < (size_t) TO * TO; q++) yo[q] = yo[q] / den[(size_t) o];
+            for (int Y = 0; Y < H2; Y++)
+                for (int X = 0; X < H2; X++) {
+                    float acc = 0.0f;
+                    for (int a = 0; a < 4; a++) {
+                        const int sy = Y + a - 1;
+                        if (sy < 0 || sy >= TO) continue;
+                        for (int b = 0; b < 4; b++) {
+                            const int sx = X + b - 1;
+                            if (sx < 0 || sx >= TO) continue;
+                            acc += K[(size_t) a * 4 + b] * yo[(size_t) sy * TO + sx];
+                        }
+                    }
+                    out[((size_t) o * H2 + Y) * H2 + X] = lrelu(acc + ab[(size_t) o], 0.2f);
+                }
+        }
+    } else {
+        const std::vector<float> &T = d.tsub.at(base + ".conv.weight");
+        const size_t R = (size_t) IC * 9;
+        // spatial [4OC][IC][3][3] view of the cf-ordered rows
+        std::vector<float> w4((size_t) 4 * OC * R);
+        for (int q = 0; q < 4 * OC; q++)
+            for (int i = 0; i < IC; i++)
+                for (int kh = 0; kh < 3; kh++)
+                    for (int kw = 0; kw < 3; kw++)
+                        w4[(((size_t) q * IC + i) * 3 + kh) * 3 + kw] =
+                            T[(size_t) q * R + i + (size_t) IC * (kw + 3 * kh)];
+        std::vector<float> xs(x.size());
+        for (int i = 0; i < IC; i++)
+            for (size_t p = 0; p < P; p++) xs[i * P + p] = x[i * P + p] * s[(size_t) i];
+        std::vector<float> y4((size_t) 4 * OC * P);
+        conv2d(xs.data(), IC, Hh, Hh, w4.data(), 4 * OC, 3, 3, 1, 1, Hh, Hh, y4.data());
+#pragma omp parallel for schedule(static)
+        for (int o = 0; o < OC; o++)
+            for (int Y = 0; Y < H2; Y++)
+                for (int X = 0; X < H2; X++) {
+                    const int k = (Y & 1) * 2 + (X & 1);
+                    const float v = y4[((size_t) (k * OC + o)) * P + (size_t) (Y >> 1) * Hh + (X >> 1)] /
+                                    den[(size_t) o];
+                    out[((size_t) o * H2 + Y) * H2 + X] = lrelu(v + ab[(size_t) o], 0.2f);
+                }
+    }
+    return out;
+}
+
+}  // namespace
+
+extern "C" {
+
+orc_dec *orc_dec_create(void) { return new orc_dec(); }
+void orc_dec_destroy(orc_dec *d) { delete d; }
+const char *orc_dec_error(const orc_dec *d) { return d ? d->err.c_str() : "null decoder"; }
+
+int orc_dec_set(orc_dec *d, const char *name, const float *data, int64_t n) {
+    auto it = d->spec.find(name);
+    if (it == d->spec.end()) {
+        d->err = std::string("unknown tensor ") + name;
+        return -1;
+    }
+    if (it->second != n) {
+        d->err = std::string(name) + ": size mismatch";
+        return -1;
+    }
+    d->t[name].assign(data, data + n);
+    d->prepared = false;
+    return 0;
+}
+
+int orc_dec_set_feat(orc_dec *d, int j, const float *feat, int64_t n) {
+    if (j < 0 || j > 6) {
+        d->err = "feat level out of range";
+        return -1;
+    }
+    const int r = 8 << j;
+    if (n != (int64_t) ST_OC[j] * r * r) {
+        d->err = "feat size mismatch";
+        return -1;
+    }
+    d->feat[j].assign(feat, feat + n);
+    return 0;
+}
+
+int orc_dec_prepare(orc_dec *d) {
+    for (auto &kv : d->spec)
+        if (!d->t.count(kv.first)) {
+            d->err = "missing tensor " + kv.first;
+            return -1;
+        }
+    std::vector<std::string> convs = {"dec.conv1.conv.weight"};
+    for (int i = 0; i < 14; i++) convs.push_back("dec.convs." + std::to_string(i) + ".conv.weight");
+    for (size_t c = 0; c < convs.size(); c++) {
+        const std::string &nm = convs[c];
+        int IC = 512, OC = 512;
+        bool up = false;
+        if (c > 0) {
+            const int i = (int) c - 1, j = i / 2;
+            up = (i % 2) == 0;
+            IC = up ? ST_IC[j] : ST_OC[j];
+            OC = ST_OC[j];
+        }
+        const std::vector<float> &W = d->t[nm];
+        std::vector<float> &sa = d->saug[nm];
+        sa.assign((size_t) (IC + 1) * OC, 0.0f);
+        orc_saug(W.data(), IC, OC, sa.data());
+        if (up) {
+            const std::string kb = nm.substr(0, nm.size() - 6) + "blur.kernel";
+            std::vector<float> &ts = d->tsub[nm];
+            ts.assign((size_t) 4 * OC * 9 * IC, 0.0f);
+            orc_tsubcf(W.data(), d->t[kb].data(), IC, OC, ts.data());
+        }
+    }
+    d->prepared = true;
+    return 0;
+}
+
+// the decoder graph, src/motion_dec.cpp:794-888 (mode 0) with the fast graph's
+// sub-pixel up-conv as mode 1
+int orc_dec_decode(orc_dec *d, const float *lat, int mode, int keep, float *img) {
+    if (!d->prepared) {
+        d->err = "decoder not prepared";
+        return -1;
+    }
+    for (int j = 0; j < 7; j++)
+        if (d->feat[j].empty()) {
+            d->err = "feats not set";
+            return -1;
+        }
+    d->taps.clear();
+    // conv1 on the 4x4 constant input
+    std::vector<float> x = d->get("dec.input.input");
+    x = styled_conv_exact(*d, x, 512, 4, "dec.conv1", lat);
+    d->tap(keep, "conv1_4", x.data(), x.size());
+    std::vector<float> skip, skipf;  // rgb / flow accumulators, CHW [3][r][r]
+    int IC = 512;
+    for (int j = 0; j < 7; j++) {
+        const int r = 8 << j, OC = ST_OC[j];
+        const size_t N = (size_t) r * r;
+        char b1[32], b2[32], bf[32], br[32];
+        snprintf(b1, sizeof b1, "dec.convs.%d", 2 * j);
+        snprintf(b2, sizeof b2, "dec.convs.%d", 2 * j + 1);
+        snprintf(bf, sizeof bf, "dec.to_flows.%d", j);
+        snprintf(br, sizeof br, "dec.to_rgbs.%d", j);
+        const std::string R = "r" + std::to_string(r);
+
+        std::vector<float> out = styled_conv_up(*d, x, IC, r / 2, b1, lat, mode);
+        d->tap(keep, R + ".conv1", out.data(), out.size());
+        out = styled_conv_exact(*d, out, OC, r, b2, lat);
+        d->tap(keep, R + ".conv2", out.data(), out.size());
+
+        // ToFlow: 1x1 modulated conv (no demod) + bias + upsample2x(skip_flow)
+        const std::vector<float> fs = d->style_of(std::string(bf) + ".conv", lat);
+        const std::vector<float> &fW = d->get(std::string(bf) + ".conv.weight");
+        const std::vector<float> &fb = d->get(std::string(bf) + ".bias");
+        const std::vector<float> &fup = d->get(std::string(bf) + ".upsample.kernel");
+        std::vector<float> fl((size_t) 3 * N);
+#pragma omp parallel for schedule(static)
+        for (size_t p = 0; p < N; p++)
+            for (int k = 0; k < 3; k++) {
+                float a = 0.0f;
+                for (int c = 0; c < OC; c++)
+                    a += fW[(size_t) k * OC + c] * (out[(size_t) c * N + p] * fs[(size_t) c]);
+                fl[(size_t) k * N + p] = a + fb[(size_t) k];
+            }
+        if (!skipf.empty()) {
+            std::vector<float> up((size_t) 3 * N);
+            orc_upfirdn2x(skipf.data(), fup.data(), r / 2, r / 2, 3, up.data());
+            for (size_t i = 0; i < fl.size(); i++) fl[i] += up[i];
+        }
+        skipf = fl;
+        d->tap(keep, R + ".flowmap", fl.data(), fl.size());
+
+        // grid (identity grid lin = -1 + 2i/(r-1), motion_dec.cpp:710-719)
+        std::vector<double> lin((size_t) r);
+        for (int i = 0; i < r; i++) lin[(size_t) i] = -1.0 + 2.0 * i / (r - 1);
+        std::vector<float> grid((size_t) 2 * N), m(N);
+        for (int yy = 0; yy < r; yy++)
+            for (int xx = 0; xx < r; xx++) {
+                const size_t p = (size_t) yy * r + xx;
+                grid[2 * p + 0] = tanhf(fl[p]) + (float) lin[(size_t) xx];
+                grid[2 * p + 1] = tanhf(fl[N + p]) + (float) lin[(size_t) yy];
+                m[p] = 1.0f / (1.0f + expf(-fl[2 * N + p]));
+            }
+        d->tap(keep, R + ".grid", grid.data(), grid.size());
+
+        std::vector<float> samp_cl((size_t) OC * N);
+        orc_bilinear_gather(d->feat[j].data(), 0, OC, r, r, grid.data(), (int64_t) N, 0, 0,
+                            samp_cl.data());
+        std::vector<float> warp((size_t) OC * N), trunk((size_t) OC * N);
+#pragma omp parallel for schedule(static)
+        for (int c = 0; c < OC; c++)
+            for (size_t p = 0; p < N; p++) {
+                const float w = samp_cl[p * OC + c] * m[p];
+                warp[(size_t) c * N + p] = w;
+                trunk[(size_t) c * N + p] = w + out[(size_t) c * N + p] * (1.0f - m[p]);
+            }
+        d->tap(keep, R + ".warp", warp.data(), warp.size());
+        d->tap(keep, R + ".out", trunk.data(), trunk.size());
+
+        // ToRGB: 1x1 EqualConv + FusedLeakyReLU + bias + upsample2x(skip)
+        const std::vector<float> &rW = d->get(std::string(br) + ".conv.0.weight");
+        const std::vector<float> &rlb = d->get(std::string(br) + ".conv.1.bias");
+        const std::vector<float> &rb = d->get(std::string(br) + ".bias");
+        const std::vector<float> &rup = d->get(std::string(br) + ".upsample.kernel");
+        std::vector<float> rgb((size_t) 3 * N);
+#pragma omp parallel for schedule(static)
+        for (size_t p = 0; p < N; p++)
+            for (int k = 0; k < 3; k++) {
+                float a = 0.0f;
+                for (int c = 0; c < OC; c++) a += rW[(size_t) k * OC + c] * warp[(size_t) c * N + p];
+                rgb[(size_t) k * N + p] = lrelu(a + rlb[(size_t) k], 0.2f) + rb[(size_t) k];
+            }
+        if (!skip.empty()) {
+            std::vector<float> up((size_t) 3 * N);
+            orc_upfirdn2x(skip.data(), rup.data(), r / 2, r / 2, 3, up.data());
+            for (size_t i = 0; i < rgb.size(); i++) rgb[i] += up[i];
+        }
+        skip = rgb;
+        d->tap(keep, R + ".rgb", rgb.data(), rgb.size());
+
+        x.swap(trunk);
+        IC = OC;
+    }
+    if (img) memcpy(img, skip.data(), skip.size() * 4);
+    return 0;
+}
+
+int64_t orc_dec_tap(const orc_dec *d, const char *name, float *out, int64_t cap) {
+    auto it = d->taps.find(name);
+    if (it == d->taps.end()) return -1;
+    const int64_t n = (int64_t) it->second.size();
+    if (out && cap >= n) memcpy(out, it->second.data(), (size_t) n * 4);
+    return n;
+}
+
+}  // extern "C"

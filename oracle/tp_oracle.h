@@ -1,0 +1,92 @@
+/* CPU oracle for the talking-portrait motion decoder (motion_dec).
+ *
+ * TEST INFRASTRUCTURE ONLY. This library is the checker the parity tests,
+ * __graft_entry__.smoke() and bench.py's CPU-baseline leg compare against.
+ * Nothing in the product path (libtpmd.so, include/tpmd.h) links, loads or
+ * calls it.
+ *
+ * It restates, in plain C++ (f32 arithmetic, OpenMP), the reference's CPU
+ * semantics of:
+ *   - the patched ggml ops (patches/ggml-tp-ops.patch): bilinear_gather
+ *     (+_planar, +_sp), im2col_cf, bias_lrelu, subpix_lrelu, subpix_lrelu_cl,
+ *     upfirdn2x, clsp_mul, clsp_lerp, flow_grid;
+ *   - the load-time scale folding motion_ae_scale (src/motion_enc.cpp:14-45);
+ *   - the derived decoder weights of motion_dec::prepare
+ *     (src/motion_dec.cpp:31-226): S_aug, acf, tsubcf;
+ *   - the decoder graph: the exact/parity graph (src/motion_dec.cpp:794-888)
+ *     and a sub-pixel variant that uses the fast graph's composed up-conv
+ *     kernel (src/motion_dec.cpp:397-433) in place of zero-stuff+conv+blur.
+ *
+ * Parity pinning: the op restatements are checked against the reference's own
+ * op code (compiled from the patch by oracle/ref_build.py into oracle/_ref/)
+ * and against golden vectors generated from it (tests/golden/). The decoder
+ * graph as a whole has no reference-produced vectors (the reference's ggml
+ * submodule is absent, so the decoder cannot be built): its composition is
+ * cross-checked against an independent torch float64 formulation instead.
+ */
+#ifndef TP_ORACLE_H
+#define TP_ORACLE_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- patched-op restatements ---------------------------------------- */
+void orc_bilinear_gather(const void *feat, int feat_f16, int C, int W, int H,
+                         const float *grid, int64_t N, int planar, int sp,
+                         float *dst);
+void orc_im2col_cf(const float *src, int IC, int IW, int IH, int N, int KW,
+                   int KH, int s0, int s1, int p0, int p1, int d0, int d1,
+                   void *dst, int dst_f16);
+void orc_bias_lrelu(const float *x, const float *bias, const int64_t *ne,
+                    int axis, float slope, float *y);
+void orc_subpix_lrelu(const float *g0, const float *g1, const float *bias,
+                      int W, int H, int OC, float slope, float *y);
+void orc_subpix_lrelu_cl(const float *y4, const float *bias, int OC,
+                         int64_t N, int64_t B, int W, float slope, float *y);
+void orc_upfirdn2x(const float *x, const float *k4, int W, int H, int64_t CB,
+                   float *y);
+void orc_clsp_mul(const float *cl, const float *m, int C, int64_t N, float *y);
+void orc_clsp_lerp(const float *cl, const float *m, const float *o, int C,
+                   int64_t N, float *y);
+void orc_flow_grid(const float *fl, const float *xs, int64_t N, float *y);
+
+/* motion_ae_scale: multiplier folded into tensor `name` at load; ne is the
+ * ggml shape (ne[0] = torch's last dim), 4 entries. */
+double orc_scale_for(const char *name, const int64_t *ne);
+
+/* ---- derived weights (prepare) --------------------------------------- */
+/* S_aug [OC][IC+1]: 0.5*sum_k W^2, last column 0.5e-8 (float32 out). */
+void orc_saug(const float *W, int IC, int OC, float *saug);
+/* tsubcf [4*OC][9*IC], column q = k*OC + o, row r = ic + IC*(kw + 3*kh). */
+void orc_tsubcf(const float *W, const float *blur16, int IC, int OC, float *tsub);
+
+/* ---- decoder ----------------------------------------------------------- */
+typedef struct orc_dec orc_dec;
+orc_dec *orc_dec_create(void);
+void orc_dec_destroy(orc_dec *d);
+/* folded f32 tensor in torch element order; returns 0 or -1 (unknown name
+ * or size mismatch, message in orc_dec_error) */
+int orc_dec_set(orc_dec *d, const char *name, const float *data, int64_t n);
+/* feats[j]: [ST_OC[j], r*r] channel-last (pixel-major), r = 8<<j */
+int orc_dec_set_feat(orc_dec *d, int j, const float *feat, int64_t n);
+/* derive S_aug / tsubcf from the set weights */
+int orc_dec_prepare(orc_dec *d);
+/* mode 0: exact graph (zero-stuff + conv + blur up-convs);
+ * mode 1: sub-pixel composed up-conv kernel.
+ * style [512] -> img [3*512*512] (CHW). keep_taps: record taps. */
+int orc_dec_decode(orc_dec *d, const float *style, int mode, int keep_taps,
+                   float *img);
+/* copy a recorded tap (names as in src/motion_dec.cpp:805-883); returns
+ * its element count or -1 */
+int64_t orc_dec_tap(const orc_dec *d, const char *name, float *out, int64_t cap);
+const char *orc_dec_error(const orc_dec *d);
+void orc_set_threads(int n);
+int orc_get_threads(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

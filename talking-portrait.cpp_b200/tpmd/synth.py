@@ -1,0 +1,158 @@
+"""Seeded synthetic inputs for the motion decoder (motion_dec).
+
+The reference's decoder benchmarks run on a real portrait and real weights,
+which are not redistributable; these generators stand in for them with the
+same shapes and value distributions (random-init LIA/StyleGAN decoder):
+
+* raw weights: conv and modulation weights N(0, 1); modulation biases 1.0
+  (EqualLinear bias_init=1, the StyleGAN2 convention); every other bias 0 by
+  default (`bias_std` > 0 draws them N(0, bias_std) instead, which parity
+  tests use so the bias paths are exercised); blur / upsample kernels
+  [1,3,3,1] x [1,3,3,1], normalised, x4 (the up-sampling gain);
+  dec.input.input N(0, 1) [1, 512, 4, 4].
+* feats: the source-portrait feature pyramid, N(0, 1) maps [ST_OC[j], r*r]
+  (channel-last, pixel-major) for r = 8 << j.
+* styles: latent = w_src + Q @ alpha with w_src ~ N(0, 1)^512, Q the
+  orthonormal factor of a seeded N(0, 1) [512, 20] matrix, alpha ~ N(0, 0.5)
+  (0.5 is the standard deviation). For frame sequences alpha follows a random
+  walk with N(0, 0.05) steps clipped to [-3, 3].
+
+Tensor names and torch shapes are those of the reference's motion_ae GGUF
+(src/motion_dec.cpp:17-29, 267-272, 357-433, 829-883). `fold` applies the
+load-time scale folding (motion_ae_scale, src/motion_enc.cpp:14-45) exactly as
+the reference loader does: f32 data times (float) scale
+(src/gguf_load.cpp:178-183).
+"""
+from __future__ import annotations
+
+import numpy as np
+
+ST_IC = (512, 512, 512, 512, 256, 128, 64)
+ST_OC = (512, 512, 512, 256, 128, 64, 32)
+STYLE_DIM = 512
+N_DIRS = 20
+
+
+def blur_kernel4() -> np.ndarray:
+    k1 = np.array([1, 3, 3, 1], np.float32)
+    k = np.outer(k1, k1)
+    return (k / k.sum() * 4.0).astype(np.float32)
+
+
+def tensor_shapes() -> dict[str, tuple[int, ...]]:
+    """name -> torch shape (leading singleton of 5-D modconv weights squeezed)."""
+    s: dict[str, tuple[int, ...]] = {"dec.input.input": (1, 512, 4, 4)}
+
+    def modconv(base, ic, oc, k, blur):
+        s[base + ".conv.weight"] = (oc, ic, k, k)
+        s[base + ".conv.modulation.weight"] = (ic, STYLE_DIM)
+        s[base + ".conv.modulation.bias"] = (ic,)
+        if blur:
+            s[base + ".conv.blur.kernel"] = (4, 4)
+
+    modconv("dec.conv1", 512, 512, 3, False)
+    s["dec.conv1.activate.bias"] = (1, 512, 1, 1)
+    for i in range(14):
+        j, up = i // 2, i % 2 == 0
+        ic, oc = (ST_IC[j] if up else ST_OC[j]), ST_OC[j]
+        modconv(f"dec.convs.{i}", ic, oc, 3, up)
+        s[f"dec.convs.{i}.activate.bias"] = (1, oc, 1, 1)
+    for j in range(7):
+        oc = ST_OC[j]
+        modconv(f"dec.to_flows.{j}", oc, 3, 1, False)
+        s[f"dec.to_flows.{j}.bias"] = (1, 3, 1, 1)
+        s[f"dec.to_flows.{j}.upsample.kernel"] = (4, 4)
+        s[f"dec.to_rgbs.{j}.conv.0.weight"] = (3, oc, 1, 1)
+        s[f"dec.to_rgbs.{j}.conv.1.bias"] = (1, 3, 1, 1)
+        s[f"dec.to_rgbs.{j}.bias"] = (1, 3, 1, 1)
+        s[f"dec.to_rgbs.{j}.upsample.kernel"] = (4, 4)
+    return s
+
+
+def ggml_ne(shape: tuple[int, ...]) -> tuple[int, int, int, int]:
+    """ggml dims (fastest first) of a torch shape, padded to 4."""
+    ne = tuple(reversed(shape))
+    return tuple(list(ne) + [1] * (4 - len(ne)))[:4]
+
+
+def make_weights(seed: int = 0, bias_std: float = 0.0) -> dict[str, np.ndarray]:
+    """Raw (unfolded) f32 weights in torch shapes."""
+    rng = np.random.default_rng([seed, 1])
+    out: dict[str, np.ndarray] = {}
+    bk = blur_kernel4()
+    for name, shape in tensor_shapes().items():
+        if name.endswith(".kernel"):
+            out[name] = bk.copy()
+        elif name.endswith("modulation.bias"):
+            out[name] = np.ones(shape, np.float32)
+        elif name.endswith("bias"):
+            out[name] = (rng.standard_normal(shape, np.float32) * np.float32(bias_std)
+                         if bias_std > 0 else np.zeros(shape, np.float32))
+        else:
+            out[name] = rng.standard_normal(shape, np.float32)
+    return out
+
+
+def fold(raw: dict[str, np.ndarray], scale_for) -> dict[str, np.ndarray]:
+    """Apply motion_ae_scale: each tensor times (float) scale_for(name, ne)."""
+    return {n: (a.astype(np.float32) * np.float32(scale_for(n, ggml_ne(a.shape))))
+            for n, a in raw.items()}
+
+
+def make_feats(seed: int = 0, smooth: bool = True) -> list[np.ndarray]:
+    """feats[j]: [r*r, ST_OC[j]] float32 (channel-last), r = 8 << j.
+
+    smooth=True (default): per channel, N(0, 1) white noise low-pass filtered
+    by a periodic Gaussian of standard deviation r/16 pixels and renormalised
+    to zero mean and unit variance, i.e. N(0, 1) maps with the spatial
+    correlation an encoder's feature pyramid has. smooth=False: white noise.
+    White-noise maps make the decoder chaotic: the bilinear warp of an
+    uncorrelated map turns a grid rounding error of e (normalised units) into
+    an error of about e*r/2 in the sampled value, so rounding grows roughly
+    tenfold per level and two float32 formulations of the same graph end at a
+    frame cosine near 0.9. Parity gates are therefore evaluated on smooth
+    maps; throughput does not depend on the values.
+    """
+    rng = np.random.default_rng([seed, 2])
+    out = []
+    for j in range(7):
+        r, c = 8 << j, ST_OC[j]
+        x = rng.standard_normal((c, r, r))
+        if smooth:
+            f = np.fft.fftfreq(r)
+            sig = r / 16.0
+            g = np.exp(-2.0 * (np.pi * sig) ** 2 * (f[:, None] ** 2 + f[None, :] ** 2))
+            x = np.fft.ifft2(np.fft.fft2(x) * g).real
+            x = (x - x.mean(axis=(1, 2), keepdims=True)) / x.std(axis=(1, 2), keepdims=True)
+        out.append(np.ascontiguousarray(x.reshape(c, r * r).T).astype(np.float32))
+    return out
+
+
+def make_basis(seed: int = 0) -> tuple[np.ndarray, np.ndarray]:
+    rng = np.random.default_rng([seed, 3])
+    w_src = rng.standard_normal(STYLE_DIM).astype(np.float32)
+    q, _ = np.linalg.qr(rng.standard_normal((STYLE_DIM, N_DIRS)))
+    return w_src, q.astype(np.float32)
+
+
+def styles_config0(seed: int = 0, n: int = 1) -> np.ndarray:
+    """n independent frames: latent = w_src + Q @ alpha, alpha ~ N(0, 0.5)."""
+    w_src, q = make_basis(seed)
+    rng = np.random.default_rng([seed, 4])
+    alpha = rng.standard_normal((n, N_DIRS)).astype(np.float32) * np.float32(0.5)
+    return (w_src[None, :] + alpha @ q.T).astype(np.float32)
+
+
+def styles_walk(seed: int = 0, n: int = 50, clip: int = 0) -> np.ndarray:
+    """A clip of n frames whose alpha is a seeded random walk: start
+    N(0, 0.5), steps N(0, 0.05), clipped to [-3, 3]."""
+    w_src, q = make_basis(seed)
+    rng = np.random.default_rng([seed, 5, clip])
+    a = rng.standard_normal(N_DIRS).astype(np.float32) * np.float32(0.5)
+    steps = rng.standard_normal((n, N_DIRS)).astype(np.float32) * np.float32(0.05)
+    alphas = np.empty((n, N_DIRS), np.float32)
+    for t in range(n):
+        if t:
+            a = np.clip(a + steps[t], -3.0, 3.0).astype(np.float32)
+        alphas[t] = a
+    return (w_src[None, :] + alphas @ q.T).astype(np.float32)
