@@ -1,0 +1,349 @@
+"""Benchmark of the B200 motion decoder (mdec frames/s @512x512 f16).
+
+One step = one decode of a 50-frame chunk (f16 weights,
+per-frame styles from a seeded random walk, one shared source latent and
+feature pyramid, output [50, 3, 512, 512] f32) on every GPU. Multi-GPU runs
+(torchrun, one process per GPU) shard frames: each rank decodes its own
+50-frame chunk per step (weak scaling); the prepared weights and the feature
+pyramid are broadcast once from rank 0 over NCCL. No per-step collective.
+
+value   frames/s over all ranks, device-timed with CUDA events on the launch
+        stream, inputs and outputs resident in HBM, max over ranks.
+e2e     the same through the host C ABI (tpmd_decode): styles H2D from pinned
+        memory and every frame D2H into pinned memory inside the timed region.
+roofline  the dominant kernel (largest share of device time, timed live with
+        CUDA events around each launch) against MEASURED_PEAKS.json.
+cpu_baseline  the CPU oracle (restatement of the reference's CPU decoder) on
+        this host's cores, bounded sample, rank 0 at N=1 only.
+
+--impl reference  times that CPU restatement as the reference arm (the
+reference itself cannot be built: its ggml submodule is absent).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "talking-portrait.cpp_b200"))
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+
+METRIC = "mdec frames/s @512x512 f16"
+UNIT = "frames/s"
+PUBLISHED_FPS = 213.2  # GGML-CUDA f16 mdec, RTX 5070 Ti (reference docs/vulkan-perf.md:143)
+ST_IC = (512, 512, 512, 512, 256, 128, 64)
+ST_OC = (512, 512, 512, 256, 128, 64, 32)
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d["hbm_gbs"], d["bf16_tflops"], d.get("bf16_tflops_sustained", d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def kernel_work(name: str, nb: int, esz: int):
+    """algorithmic (flops, bytes) of one launch decoding nb frames"""
+    if name == "conv1":
+        flops = 2.0 * 16 * 512 * 4608 * nb
+        byts = nb * 16 * 512 * esz * 2 + 512 * 4608 * esz
+        return flops, byts
+    for pre, up in (("upconv_r", True), ("conv2_r", False)):
+        if name.startswith(pre):
+            r = int(name[len(pre):])
+            j = (r // 8).bit_length() - 1
+            ic, oc = (ST_IC[j], ST_OC[j]) if up else (ST_OC[j], ST_OC[j])
+            npix = (r // 2) ** 2 if up else r * r
+            n = 4 * oc if up else oc
+            flops = 2.0 * npix * n * 9 * ic * nb
+            byts = nb * (npix * ic + r * r * oc) * esz + n * 9 * ic * esz
+            return flops, byts
+    if name.startswith("tail_r"):
+        r = int(name[len("tail_r"):])
+        j = (r // 8).bit_length() - 1
+        oc = ST_OC[j]
+        last = j == 6
+        per = r * r * oc * esz * (1 if last else 2) + 3 * 4 * r * r * (1 if last else 2)
+        per += 2 * 3 * 4 * (r // 2) ** 2 if j else 0
+        return 0.0, nb * per + r * r * oc * esz
+    return 0.0, 0.0
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms"""
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        rows = []
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                rows.append((float(parts[0]), float(parts[1]), parts[4:8]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, fl in rows for i, f in enumerate(fl) if f.lower() == "active"})
+        return {"sm_mhz": float(np.median([r[0] for r in rows])), "sm_max_mhz": rows[0][1],
+                "reasons": reasons, "samples": len(rows)}
+
+
+def cpu_baseline(tensors, feats, styles, budget_s: float = 12.0):
+    """oracle sub-pixel graph (the reference CPU path's fast-graph math) on
+    all host cores: one warm-up frame, then frames until ~budget_s"""
+    import oracle as O
+    dec = O.Decoder(tensors, feats)
+    dec.decode(styles[0], mode=1)
+    n, t0 = 0, time.perf_counter()
+    while n < len(styles) and (time.perf_counter() - t0) < budget_s:
+        dec.decode(styles[n % len(styles)], mode=1)
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": n / dt, "unit": UNIT, "cores": O.threads(), "kind": "port",
+            "sample": f"{n} frames of config 2 (fp32, batch 1, 512x512) after 1 warm-up frame, "
+                      f"{dt:.1f} s wall clock, oracle sub-pixel graph"}
+
+
+def setup_inputs(rank: int, frames: int):
+    import tpmd
+    from tpmd import synth
+    raw = synth.make_weights(seed=0)
+    tensors = synth.fold(raw, tpmd.scale_for)
+    feats = synth.make_feats(seed=0)
+    styles = synth.styles_walk(seed=0, n=frames, clip=rank)
+    return tensors, feats, styles
+
+
+def run_reference(args, rank: int, world: int):
+    if rank != 0:
+        return
+    tensors, feats, styles = setup_inputs(0, max(8, args.warmup + args.steps))
+    import oracle as O
+    dec = O.Decoder(tensors, feats)
+    for i in range(args.warmup):
+        dec.decode(styles[i], mode=1)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        dec.decode(styles[(args.warmup + i) % len(styles)], mode=1)
+    dt = time.perf_counter() - t0
+    v = args.steps / dt
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * dt / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": "config 2 styles, one frame per step (CPU, fp32)",
+                       "global_batch": 1, "parallelism": "cpu"},
+            "cpu_baseline": {"value": v, "unit": UNIT, "cores": O.threads(), "kind": "port",
+                             "sample": f"{args.steps} frames, batch 1, oracle sub-pixel graph; "
+                                       "reference unbuildable (ggml submodule absent)"},
+            "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--batch", type=int, default=50)
+    ap.add_argument("--dtype", default="f16", choices=["f16", "f32"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+
+    import torch
+    import torch.distributed as dist
+    import tpmd
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    nb = args.batch
+    tensors, feats, styles = setup_inputs(rank, nb)
+    dtype = tpmd.DTYPE_F16 if args.dtype == "f16" else tpmd.DTYPE_F32
+    dec = tpmd.MotionDecoder(local, dtype, max_batch=nb)
+
+    # weights + feats: prepared on rank 0, broadcast once over NCCL
+    if rank == 0:
+        dec.set_tensors(tensors)
+        dec.prepare()
+        dec.set_feats(feats)
+    if world > 1:
+        for which in (0, 1):
+            ptr, n = dec.arena(which)
+
+            class _Arena:
+                __cuda_array_interface__ = {"shape": (n,), "typestr": "|u1", "data": (ptr, False),
+                                            "version": 3}
+            t = torch.as_tensor(_Arena(), device=f"cuda:{local}")
+            dist.broadcast(t, src=0)
+            torch.cuda.synchronize()
+            if rank != 0:
+                dec.adopt_arena(which)
+
+    stream = torch.cuda.Stream()  # the launch stream; CUDA events are recorded on it
+    s_d = torch.from_numpy(styles).cuda()
+    f_d = torch.empty((nb, 3, 512, 512), device="cuda")
+    torch.cuda.synchronize()
+
+    def step():
+        dec.decode_device(s_d.data_ptr(), nb, f_d.data_ptr(), stream.cuda_stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    # ---- device-timed region
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = world * nb * args.steps / (ms / 1000.0)
+
+    # ---- end to end through the host C ABI (pinned buffers)
+    s_h = torch.from_numpy(styles).pin_memory()
+    f_h = torch.empty((nb, 3, 512, 512), pin_memory=True)
+    dec.decode_ptr(s_h.data_ptr(), nb, f_h.data_ptr())
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        dec.decode_ptr(s_h.data_ptr(), nb, f_h.data_ptr())
+    dt = time.perf_counter() - t0
+    if world > 1:
+        t = torch.tensor([dt], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dt = float(t.item())
+    e2e = world * nb * args.steps / dt
+
+    # ---- live per-kernel timing (untimed pass) for the roofline
+    dec.profile_begin()
+    for _ in range(2):
+        step()
+    prof = dec.profile_end()
+    hbm, tf_burst, tf_sus, src = peaks()
+    esz = 2 if dtype == tpmd.DTYPE_F16 else 4
+    total = sum(v[1] for v in prof.values())
+    top = max(prof.items(), key=lambda kv: kv[1][1])
+    name, (launches, tot_ms) = top
+    avg_s = tot_ms / launches / 1000.0
+    flops, byts = kernel_work(name, nb, esz)
+    t_tensor = flops / (tf_sus * 1e12)
+    t_hbm = byts / (hbm * 1e9)
+    if t_tensor >= t_hbm:
+        roof = {"bound": "tensor", "achieved": flops / avg_s / 1e12, "peak": tf_sus, "unit": "TFLOP/s"}
+    else:
+        roof = {"bound": "hbm", "achieved": byts / avg_s / 1e9, "peak": hbm, "unit": "GB/s"}
+    roof["frac"] = roof["achieved"] / roof["peak"]
+    roof["kernel"] = name
+    roof["share"] = tot_ms / total
+    roof["peak_source"] = src + (" sustained bf16" if roof["bound"] == "tensor" else " copy")
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+    if os.path.exists(tp):
+        tj = json.load(open(tp))
+        if name in tj.get("bytes_per_frame", {}) and tj.get("conv") == ("tc" if dec_uses_tc() else "simt"):
+            traffic = tj["bytes_per_frame"][name] * nb
+    roof["traffic"] = traffic
+    kernels = {k: {"launches": v[0], "ms": round(v[1], 4), "share": round(v[1] / total, 4)}
+               for k, v in sorted(prof.items(), key=lambda kv: -kv[1][1])[:8]}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(tensors, feats, styles)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": value / PUBLISHED_FPS, "dtype": args.dtype,
+            "data": "synthetic (random-init decoder, smooth N(0,1) feats, random-walk styles)",
+            "config": {"workload": "config 2: 50-frame chunk per GPU, f16 weights, 512x512",
+                       "global_batch": nb * world, "frames_per_gpu_per_step": nb,
+                       "parallelism": f"frame-sharded x{world}",
+                       "l2": "no flush: per-step working set (~2 GB activations) exceeds the 126 MB L2",
+                       "conv": "tcgen05" if dec_uses_tc() else "simt"},
+            "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": nb * 512 * 4,
+                    "d2h_bytes_per_step": nb * 3 * 512 * 512 * 4},
+            "gpu_launches": dec.kernel_launches(nb) * args.steps * world,
+            "roofline": roof, "kernels": kernels, "clocks": clk.summary(),
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    dec.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def dec_uses_tc() -> bool:
+    return os.environ.get("TPMD_CONV", "tc" if TC_DEFAULT else "simt") == "tc"
+
+
+TC_DEFAULT = False
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,140 @@
+/* tpmd — B200-native motion decoder (motion_dec) for talking-portrait.
+ *
+ * C ABI over hand-written sm_100a CUDA kernels. Conventions follow the
+ * reference's public API (include/tp.h:1-9): no exceptions or aborts cross
+ * this boundary, opaque handle, caller-owned flat buffers, fixed-width types.
+ * Every int-returning entry point returns 0 on success and -1 on failure,
+ * with the message in tpmd_last_error(ctx). Frees are NULL-safe.
+ *
+ * A handle owns one GPU (one process per GPU for multi-GPU use), one CUDA
+ * stream and its device memory. It is single-threaded: one call at a time.
+ *
+ * Layouts (element order, fastest last, as a C array):
+ *   styles  [n][512]          float32, latent = appearance + r_d[t]
+ *   frames  [n][3][512][512]  float32, CHW (the reference's img output)
+ *   feats[j][r*r][ST_OC[j]]   float32, channel-last (pixel-major), r = 8<<j,
+ *                             ST_OC = {512,512,512,256,128,64,32}
+ */
+#ifndef TPMD_H
+#define TPMD_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TPMD_ABI_VERSION 1
+
+/* storage/compute type of weights, feats and activations */
+#define TPMD_DTYPE_F32 0 /* fp32 storage, fp32 FFMA convs (parity mode)     */
+#define TPMD_DTYPE_F16 1 /* f16 storage, tcgen05 f16 convs, f32 accumulate   */
+
+#define TPMD_N_LEVELS 7
+#define TPMD_STYLE_DIM 512
+#define TPMD_IMG 512
+
+typedef struct tpmd_ctx tpmd_ctx;
+
+int tpmd_abi_version(void);
+
+/* Create a decoder on CUDA device `device` able to decode up to `max_batch`
+ * frames per internal dispatch (the decode calls accept any n and loop).
+ * Replaces the decoder half of tp_ctx::load (src/tp.cpp:13-41: backend init,
+ * mdec.w binding) with ftype "f32" -> TPMD_DTYPE_F32, "f16" ->
+ * TPMD_DTYPE_F16. Returns NULL on failure; the reason is in
+ * tpmd_create_error() (this thread's last failed create). */
+tpmd_ctx *tpmd_create(int device, int dtype, int max_batch);
+const char *tpmd_create_error(void);
+void tpmd_destroy(tpmd_ctx *ctx);
+const char *tpmd_last_error(const tpmd_ctx *ctx);
+
+/* motion_ae_scale (src/motion_enc.cpp:14-45): the multiplier the loader
+ * folds into tensor `name` (ggml dims ne[0..3], ne[0] = torch's last dim). */
+double tpmd_scale_for(const char *name, const int64_t ne[4]);
+
+/* One scale-folded float32 tensor of the motion_ae "dec.*" set, in torch
+ * element order (what weights_t holds after load, src/gguf_load.cpp:160-196;
+ * 5-D modconv weights squeezed to [OC][IC][k][k]). Unknown names or wrong
+ * sizes fail. */
+int tpmd_set_tensor(tpmd_ctx *ctx, const char *name, const float *data, int64_t n);
+
+/* Derive the decoder's device weights from the set tensors: S_aug, the cf
+ * GEMM matrices and the sub-pixel up-conv matrices (motion_dec::prepare,
+ * src/motion_dec.cpp:31-226). Requires every tensor. */
+int tpmd_prepare(tpmd_ctx *ctx);
+
+/* Per-portrait feature pyramid (motion_dec::set_feats,
+ * src/motion_dec.cpp:1137-1160), host float32 as described above. */
+int tpmd_set_feats(tpmd_ctx *ctx, const float *const feats[TPMD_N_LEVELS]);
+
+/* Frames per internal dispatch (motion_dec::batch). */
+int tpmd_batch(const tpmd_ctx *ctx);
+
+/* styles (host) -> frames (host), n >= 1 frames; blocks until the frames
+ * are in `frames`. Page-locked `frames` memory lets the device-to-host copy
+ * overlap the next batch's compute. (motion_dec::decode_batch,
+ * src/motion_dec.cpp:1194-1220, without its fixed-batch restriction.) */
+int tpmd_decode(tpmd_ctx *ctx, const float *styles, int64_t n, float *frames);
+
+/* Same with device pointers, enqueued on `stream` (a cudaStream_t; NULL =
+ * the legacy default stream, as in CUDA's own APIs) without host
+ * synchronisation. */
+int tpmd_decode_device(tpmd_ctx *ctx, const float *styles_dev, int64_t n,
+                       float *frames_dev, void *stream);
+
+/* Device arenas: which = 0 prepared weights, 1 feats. A multi-GPU caller
+ * prepares / sets feats on one rank, broadcasts each arena's bytes to the
+ * other ranks (NCCL), and those ranks call tpmd_arena_adopt. */
+int tpmd_arena(tpmd_ctx *ctx, int which, void **dev_ptr, size_t *bytes);
+int tpmd_arena_adopt(tpmd_ctx *ctx, int which);
+
+/* Parity taps of one frame (the reference's tap mode, src/motion_dec.cpp
+ * :805-883, tools/tp-parity.cpp:235-287): decodes `style` (host [512])
+ * through level `level` (0..6, r = 8<<level) and copies that level's
+ * intermediates to host, CHW float32: conv1 [OC][r][r] (the up-conv output
+ * as stored, i.e. multiplied by conv2's style), conv2 [OC][r][r], flowmap
+ * [3][r][r] (level < 6), trunk [OC][r][r] (level < 6; multiplied by the next
+ * up-conv's style), rgb [3][r][r]. Any output pointer may be NULL. */
+int tpmd_decode_taps(tpmd_ctx *ctx, const float *style, int level, float *conv1,
+                     float *conv2, float *flowmap, float *trunk, float *rgb);
+
+/* Live per-kernel timing. Between begin and end, decodes launch kernels one
+ * by one (no CUDA graph) with CUDA events recorded on the launch stream around
+ * each; end synchronises and writes a JSON object
+ * {"<kernel>": [launches, total_ms], ...} into json (cap bytes). */
+int tpmd_profile_begin(tpmd_ctx *ctx);
+int tpmd_profile_end(tpmd_ctx *ctx, char *json, size_t cap);
+
+/* Kernel launches one decode of n frames issues (for accounting). */
+int64_t tpmd_kernel_launches(const tpmd_ctx *ctx, int64_t n);
+
+/* ---- op-level kernels with the patched-op semantics ------------------ */
+
+/* ggml_bilinear_gather / _planar / _sp (patches/ggml-tp-ops.patch:41-60,
+ * 104-111; CPU semantics patch:319-369): torch grid_sample (bilinear, zeros
+ * padding, align_corners=false) of a channel-last map feat [W*H][C] (f32, or
+ * f16 when feat_is_f16) at N grid points. grid: [N][2] (x, y) interleaved,
+ * or [2][N] planar when `planar`. dst: [N][C], or [C][N] when `out_sp`.
+ * All pointers are device memory; enqueued on `stream`. */
+int tpk_bilinear_gather(const void *feat, int feat_is_f16, int C, int W, int H,
+                        const float *grid, int64_t N, int planar, int out_sp,
+                        float *dst, void *stream);
+
+/* ggml_im2col_cf (patch:25-39, CPU patch:201-307, CUDA patch:827-904):
+ * src [N][IH][IW][IC] f32 (channels first in ggml terms: ic fastest) ->
+ * dst [N][OH][OW][KH*KW*IC] with row r = ic + IC*(kw + KW*kh), zeros outside
+ * the source, OW = (IW + 2*p0 - d0*(KW-1) - 1)/s0 + 1 (OH likewise).
+ * dst is f16 (round to nearest even) when dst_is_f16, else f32. */
+int tpk_im2col_cf(const float *src, int IC, int IW, int IH, int N, int KW, int KH,
+                  int s0, int s1, int p0, int p1, int d0, int d1, void *dst,
+                  int dst_is_f16, void *stream);
+
+/* Message of the last failed tpk_* call on this thread. */
+const char *tpk_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TPMD_H */

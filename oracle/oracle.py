@@ -16,6 +16,10 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "liboracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libtpref.so")
 
+# f16 emulation flags for Decoder.decode(mode=...), see tp_oracle.h
+F16_WEIGHTS, F16_FEATS, F16_ACTS, F16_OUT = 0x10, 0x20, 0x40, 0x80
+REF_F16 = F16_WEIGHTS | F16_FEATS | F16_ACTS  # the reference's f16 mode
+
 ST_IC = (512, 512, 512, 512, 256, 128, 64)
 ST_OC = (512, 512, 512, 256, 128, 64, 32)
 
@@ -54,6 +58,7 @@ def lib():
         L.orc_subpix_lrelu_cl.argtypes = [v, v, C.c_int, C.c_int64, C.c_int64, C.c_int,
                                           C.c_float, v]
         L.orc_upfirdn2x.argtypes = [v, v, C.c_int, C.c_int, C.c_int64, v]
+        L.orc_blur.argtypes = [v, v, C.c_int, C.c_int, C.c_int64, C.c_int, C.c_int, v]
         L.orc_clsp_mul.argtypes = [v, v, C.c_int, C.c_int64, v]
         L.orc_clsp_lerp.argtypes = [v, v, v, C.c_int, C.c_int64, v]
         L.orc_flow_grid.argtypes = [v, v, C.c_int64, v]
@@ -173,6 +178,14 @@ def upfirdn2x(x, k4, W, H, CB, impl="oracle"):
     out = np.empty(4 * W * H * CB, np.float32)
     L, pre = _L(impl)
     getattr(L, pre + "upfirdn2x")(_p(x), _p(k4), W, H, CB, _p(out))
+    return out
+
+
+def blur(x, k4, W, H, Cc, p0, p1):
+    """oracle Blur: x [C][H][W] -> [C][H+p0+p1-3][W+p0+p1-3]"""
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.empty((Cc, H + p0 + p1 - 3, W + p0 + p1 - 3), np.float32)
+    lib().orc_blur(_p(x), _p(np.ascontiguousarray(k4, np.float32)), W, H, Cc, p0, p1, _p(out))
     return out
 
 

@@ -31,6 +31,10 @@ inline uint16_t f2h(float f) {
     return h;
 }
 inline float lrelu(float v, float s) { return v > 0.0f ? v : s * v; }
+inline float r16(float v) { return (float) (_Float16) v; }
+void round16(std::vector<float> &v) {
+    for (auto &x : v) x = r16(x);
+}
 
 // One output row of a stride-1 2-D correlation for a block of `nb` output
 // channels: acc[o][ox] += sum_{ic,ky,kx} w[o][ic][ky][kx] * x[ic][iy][ox+kx-pl]
@@ -280,6 +284,30 @@ void orc_upfirdn2x(const float *x, const float *k4, int W, int H, int64_t CB,
     }
 }
 
+// upfirdn2d(up=1, pad=(p0,p1)) with a 4x4 FIR (the Blur module,
+// src/ops_common.h:39-43: pad_ext then depthwise correlation, no flip):
+// x [C][H][W] -> y [C][H+p0+p1-3][W+p0+p1-3].
+void orc_blur(const float *x, const float *k4, int W, int H, int64_t C, int p0, int p1,
+              float *y) {
+    const int OW = W + p0 + p1 - 3, OH = H + p0 + p1 - 3;
+#pragma omp parallel for schedule(static)
+    for (int64_t c = 0; c < C; c++)
+        for (int Y = 0; Y < OH; Y++)
+            for (int X = 0; X < OW; X++) {
+                float acc = 0.0f;
+                for (int a = 0; a < 4; a++) {
+                    const int sy = Y + a - p0;
+                    if (sy < 0 || sy >= H) continue;
+                    for (int b = 0; b < 4; b++) {
+                        const int sx = X + b - p0;
+                        if (sx < 0 || sx >= W) continue;
+                        acc += k4[a * 4 + b] * x[((size_t) c * H + sy) * W + sx];
+                    }
+                }
+                y[((size_t) c * OH + Y) * OW + X] = acc;
+            }
+}
+
 // channel-last -> spatial transpose times the mask, patch:578-601.
 void orc_clsp_mul(const float *cl, const float *m, int C, int64_t N, float *y) {
 #pragma omp parallel for collapse(2) schedule(static)
@@ -450,16 +478,23 @@ namespace {
 // modulated dense 3x3 conv, map-side style (src/motion_dec.cpp:597-608):
 // lrelu(conv(x*s, W)/den + bias)
 std::vector<float> styled_conv_exact(const orc_dec &d, const std::vector<float> &x, int IC,
-                                     int Hh, const std::string &base, const float *lat) {
+                                     int Hh, const std::string &base, const float *lat,
+                                     int flags) {
     const std::vector<float> s = d.style_of(base + ".conv", lat);
     const std::vector<float> den = d.demod_den(base + ".conv.weight", s);
-    const std::vector<float> &W = d.get(base + ".conv.weight");
+    std::vector<float> Wr;
+    if (flags & ORC_F16_WEIGHTS) {
+        Wr = d.get(base + ".conv.weight");
+        round16(Wr);
+    }
+    const std::vector<float> &W = (flags & ORC_F16_WEIGHTS) ? Wr : d.get(base + ".conv.weight");
     const std::vector<float> &ab = d.get(base + ".activate.bias");
     const int OC = (int) ab.size();
     const size_t P = (size_t) Hh * Hh;
     std::vector<float> xs(x.size());
     for (int i = 0; i < IC; i++)
         for (size_t p = 0; p < P; p++) xs[i * P + p] = x[i * P + p] * s[(size_t) i];
+    if (flags & ORC_F16_ACTS) round16(xs);
     std::vector<float> y((size_t) OC * P);
     conv2d(xs.data(), IC, Hh, Hh, W.data(), OC, 3, 3, 1, 1, Hh, Hh, y.data());
 #pragma omp parallel for schedule(static)
@@ -479,7 +514,7 @@ std::vector<float> styled_conv_exact(const orc_dec &d, const std::vector<float> 
 // lrelu(+bias).
 std::vector<float> styled_conv_up(const orc_dec &d, const std::vector<float> &x, int IC,
                                   int Hh, const std::string &base, const float *lat,
-                                  int mode) {
+                                  int mode, int flags) {
     const std::vector<float> s = d.style_of(base + ".conv", lat);
     const std::vector<float> den = d.demod_den(base + ".conv.weight", s);
     const std::vector<float> &W = d.get(base + ".conv.weight");
@@ -496,7 +531,8 @@ std::vector<float> styled_conv_up(const orc_dec &d, const std::vector<float> &x,
             for (int yy = 0; yy < Hh; yy++)
                 for (int xx = 0; xx < Hh; xx++)
                     zs[((size_t) i * ZP + 2 * yy + 2) * ZP + 2 * xx + 2] =
-                        x[i * P + (size_t) yy * Hh + xx] * s[(size_t) i];
+                        (flags & ORC_F16_ACTS) ? r16(x[i * P + (size_t) yy * Hh + xx] * s[(size_t) i])
+                                               : x[i * P + (size_t) yy * Hh + xx] * s[(size_t) i];
         std::vector<float> wf(W.size());
         for (int o = 0; o < OC; o++)
             for (int i = 0; i < IC; i++)
@@ -504,29 +540,23 @@ std::vector<float> styled_conv_up(const orc_dec &d, const std::vector<float> &x,
                     for (int b = 0; b < 3; b++)
                         wf[(((size_t) o * IC + i) * 3 + a) * 3 + b] =
                             W[(((size_t) o * IC + i) * 3 + (2 - a)) * 3 + (2 - b)];
+        if (flags & ORC_F16_WEIGHTS) round16(wf);
         const int TO = H2 + 1;  // conv_transpose output size 2H+1
         std::vector<float> y((size_t) OC * TO * TO);
         conv2d(zs.data(), IC, ZP, ZP, wf.data(), OC, 3, 3, 0, 0, TO, TO, y.data());
-        // /den, then blur with pad (1,1): out[Y][X] = sum_{a,b} K[a][b] yp[Y+a][X+b]
+        // /den, then Blur with pad (1,1) (src/motion_dec.cpp:623-625)
 #pragma omp parallel for schedule(static)
         for (int o = 0; o < OC; o++) {
             float *yo = y.data() + (size_t) o * TO * TO;
             for (size_t q = 0; q < (size_t) TO * TO; q++) yo[q] = yo[q] / den[(size_t) o];
-            for (int Y = 0; Y < H2; Y++)
-                for (int X = 0; X < H2; X++) {
-                    float acc = 0.0f;
-                    for (int a = 0; a < 4; a++) {
-                        const int sy = Y + a - 1;
-                        if (sy < 0 || sy >= TO) continue;
-                        for (int b = 0; b < 4; b++) {
-                            const int sx = X + b - 1;
-                            if (sx < 0 || sx >= TO) continue;
-                            acc += K[(size_t) a * 4 + b] * yo[(size_t) sy * TO + sx];
-                        }
-                    }
-                    out[((size_t) o * H2 + Y) * H2 + X] = lrelu(acc + ab[(size_t) o], 0.2f);
-                }
         }
+        orc_blur(y.data(), K.data(), TO, TO, OC, 1, 1, out.data());
+#pragma omp parallel for schedule(static)
+        for (int o = 0; o < OC; o++)
+            for (size_t q = 0; q < (size_t) H2 * H2; q++) {
+                float &v = out[(size_t) o * H2 * H2 + q];
+                v = lrelu(v + ab[(size_t) o], 0.2f);
+            }
     } else {
         const std::vector<float> &T = d.tsub.at(base + ".conv.weight");
         const size_t R = (size_t) IC * 9;
@@ -538,9 +568,11 @@ std::vector<float> styled_conv_up(const orc_dec &d, const std::vector<float> &x,
                     for (int kw = 0; kw < 3; kw++)
                         w4[(((size_t) q * IC + i) * 3 + kh) * 3 + kw] =
                             T[(size_t) q * R + i + (size_t) IC * (kw + 3 * kh)];
+        if (flags & ORC_F16_WEIGHTS) round16(w4);
         std::vector<float> xs(x.size());
         for (int i = 0; i < IC; i++)
             for (size_t p = 0; p < P; p++) xs[i * P + p] = x[i * P + p] * s[(size_t) i];
+        if (flags & ORC_F16_ACTS) round16(xs);
         std::vector<float> y4((size_t) 4 * OC * P);
         conv2d(xs.data(), IC, Hh, Hh, w4.data(), 4 * OC, 3, 3, 1, 1, Hh, Hh, y4.data());
 #pragma omp parallel for schedule(static)
@@ -640,8 +672,10 @@ int orc_dec_decode(orc_dec *d, const float *lat, int mode, int keep, float *img)
         }
     d->taps.clear();
     // conv1 on the 4x4 constant input
+    const int flags = mode & ~1;
+    mode &= 1;
     std::vector<float> x = d->get("dec.input.input");
-    x = styled_conv_exact(*d, x, 512, 4, "dec.conv1", lat);
+    x = styled_conv_exact(*d, x, 512, 4, "dec.conv1", lat, flags);
     d->tap(keep, "conv1_4", x.data(), x.size());
     std::vector<float> skip, skipf;  // rgb / flow accumulators, CHW [3][r][r]
     int IC = 512;
@@ -655,9 +689,10 @@ int orc_dec_decode(orc_dec *d, const float *lat, int mode, int keep, float *img)
         snprintf(br, sizeof br, "dec.to_rgbs.%d", j);
         const std::string R = "r" + std::to_string(r);
 
-        std::vector<float> out = styled_conv_up(*d, x, IC, r / 2, b1, lat, mode);
+        std::vector<float> out = styled_conv_up(*d, x, IC, r / 2, b1, lat, mode, flags);
         d->tap(keep, R + ".conv1", out.data(), out.size());
-        out = styled_conv_exact(*d, out, OC, r, b2, lat);
+        out = styled_conv_exact(*d, out, OC, r, b2, lat, flags);
+        if (flags & ORC_F16_OUT) round16(out);
         d->tap(keep, R + ".conv2", out.data(), out.size());
 
         // ToFlow: 1x1 modulated conv (no demod) + bias + upsample2x(skip_flow)
@@ -696,8 +731,13 @@ int orc_dec_decode(orc_dec *d, const float *lat, int mode, int keep, float *img)
         d->tap(keep, R + ".grid", grid.data(), grid.size());
 
         std::vector<float> samp_cl((size_t) OC * N);
-        orc_bilinear_gather(d->feat[j].data(), 0, OC, r, r, grid.data(), (int64_t) N, 0, 0,
-                            samp_cl.data());
+        std::vector<float> f16feat;
+        if (flags & ORC_F16_FEATS) {
+            f16feat = d->feat[j];
+            round16(f16feat);
+        }
+        orc_bilinear_gather((flags & ORC_F16_FEATS) ? f16feat.data() : d->feat[j].data(), 0, OC, r,
+                            r, grid.data(), (int64_t) N, 0, 0, samp_cl.data());
         std::vector<float> warp((size_t) OC * N), trunk((size_t) OC * N);
 #pragma omp parallel for schedule(static)
         for (int c = 0; c < OC; c++)

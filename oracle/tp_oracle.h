@@ -48,6 +48,8 @@ void orc_subpix_lrelu_cl(const float *y4, const float *bias, int OC,
                          int64_t N, int64_t B, int W, float slope, float *y);
 void orc_upfirdn2x(const float *x, const float *k4, int W, int H, int64_t CB,
                    float *y);
+void orc_blur(const float *x, const float *k4, int W, int H, int64_t C, int p0, int p1,
+              float *y);
 void orc_clsp_mul(const float *cl, const float *m, int C, int64_t N, float *y);
 void orc_clsp_lerp(const float *cl, const float *m, const float *o, int C,
                    int64_t N, float *y);
@@ -74,9 +76,20 @@ int orc_dec_set(orc_dec *d, const char *name, const float *data, int64_t n);
 int orc_dec_set_feat(orc_dec *d, int j, const float *feat, int64_t n);
 /* derive S_aug / tsubcf from the set weights */
 int orc_dec_prepare(orc_dec *d);
-/* mode 0: exact graph (zero-stuff + conv + blur up-convs);
- * mode 1: sub-pixel composed up-conv kernel.
+/* mode bit 0 clear: exact graph (zero-stuff + conv + blur up-convs);
+ *          set:   sub-pixel composed up-conv kernel.
+ * f16 emulation bits (round to nearest even at that point, compute in f32):
+ * ORC_F16_WEIGHTS conv weights, ORC_F16_FEATS feats, ORC_F16_ACTS every conv
+ * input (x * style), ORC_F16_OUT the conv2 output read by the level tail.
+ * WEIGHTS|FEATS|ACTS is the reference's f16 mode (f16 weights and feats,
+ * f16 im2col into f32-accumulating GEMMs, src/gguf_load.cpp:149-153,
+ * src/motion_dec.cpp:688,340-354); adding OUT matches storing the conv2
+ * output as f16.
  * style [512] -> img [3*512*512] (CHW). keep_taps: record taps. */
+#define ORC_F16_WEIGHTS 0x10
+#define ORC_F16_FEATS 0x20
+#define ORC_F16_ACTS 0x40
+#define ORC_F16_OUT 0x80
 int orc_dec_decode(orc_dec *d, const float *style, int mode, int keep_taps,
                    float *img);
 /* copy a recorded tap (names as in src/motion_dec.cpp:805-883); returns

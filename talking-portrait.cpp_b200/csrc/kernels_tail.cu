@@ -1,0 +1,238 @@
+// The per-level tail of the decoder, one pass per pixel (src/motion_dec.cpp
+// :829-885 exact graph; :1077-1108 fast graph): ToFlow 1x1 modulated conv +
+// bias + up-sampled flow skip, flow head (tanh + identity grid, sigmoid mask),
+// bilinear warp of the level's feats (grid_sample, zeros, align_corners=false
+// with the patched gather's arithmetic, patch:341-366), mask blend
+// (warp = sampled*m, trunk = warp + out*(1-m)), ToRGB 1x1 + FusedLeakyReLU +
+// bias + up-sampled rgb skip (upfirdn2d up=2 pad (2,1), patch:535-572).
+//
+// The reference runs this as ~12 separate graph nodes with transposes
+// (cl_to_sp, clsp_mul/lerp, flow_grid, upfirdn2x); here it is one HBM-bound
+// kernel: each pixel's channel vector is read once (conv2 output), its four
+// feat taps are read with 16-byte channel-last vector loads (feats are shared
+// by every frame of the batch, so they stay L2-resident), and the blended
+// trunk is written once, already multiplied by the next up-conv's style.
+//
+// Mapping: a pixel is handled by G = OC/CPL lanes, each owning CPL
+// consecutive channels; 32/G pixels per warp. Channel sums (ToFlow, ToRGB)
+// reduce across the G lanes with xor shuffles.
+#include "tpmd_internal.h"
+
+#include <algorithm>
+
+namespace tpmd {
+namespace {
+
+template <typename T, int CPL>
+struct chans;
+template <int CPL>
+struct chans<float, CPL> {
+    static __device__ __forceinline__ void load(const float *p, float *v) {
+#pragma unroll
+        for (int i = 0; i < CPL; i += 4) {
+            const float4 q = __ldg(reinterpret_cast<const float4 *>(p + i));
+            v[i] = q.x; v[i + 1] = q.y; v[i + 2] = q.z; v[i + 3] = q.w;
+        }
+    }
+    static __device__ __forceinline__ void store(float *p, const float *v) {
+#pragma unroll
+        for (int i = 0; i < CPL; i += 4)
+            *reinterpret_cast<float4 *>(p + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+    }
+};
+template <int CPL>
+struct chans<__half, CPL> {
+    static __device__ __forceinline__ void load(const __half *p, float *v) {
+#pragma unroll
+        for (int i = 0; i < CPL; i += 8) {
+            const uint4 q = __ldg(reinterpret_cast<const uint4 *>(p + i));
+            const __half2 *h = reinterpret_cast<const __half2 *>(&q);
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const float2 f = __half22float2(h[k]);
+                v[i + 2 * k] = f.x;
+                v[i + 2 * k + 1] = f.y;
+            }
+        }
+    }
+    static __device__ __forceinline__ void store(__half *p, const float *v) {
+#pragma unroll
+        for (int i = 0; i < CPL; i += 8) {
+            uint4 q;
+            __half2 *h = reinterpret_cast<__half2 *>(&q);
+#pragma unroll
+            for (int k = 0; k < 4; k++) h[k] = __floats2half2_rn(v[i + 2 * k], v[i + 2 * k + 1]);
+            *reinterpret_cast<uint4 *>(p + i) = q;
+        }
+    }
+};
+
+// upfirdn2d(up=2, pad=(2,1)) of one h x h plane at output (x, y), in the
+// reference op's tap order (patch:559-569)
+__device__ __forceinline__ float up2x(const float *__restrict__ src, const float *__restrict__ k4,
+                                      int x, int y, int h) {
+    float acc = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const int vy = y + j - 2;
+        if (vy < 0 || vy >= 2 * h || (vy & 1)) continue;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int vx = x + i - 2;
+            if (vx < 0 || vx >= 2 * h || (vx & 1)) continue;
+            acc = fmaf(__ldg(src + (vy >> 1) * h + (vx >> 1)), __ldg(k4 + i + 4 * j), acc);
+        }
+    }
+    return acc;
+}
+
+template <int G>
+__device__ __forceinline__ float group_sum(float v) {
+#pragma unroll
+    for (int o = G / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+template <typename T, int CPL, int G>
+__global__ void __launch_bounds__(256) tail_kernel(tail_params p) {
+    constexpr int PW = 32 / G;  // pixels per warp
+    __shared__ __align__(16) float s_fw[3][512];
+    __shared__ __align__(16) float s_rw[3][512];
+    const int OC = p.OC, r = p.r;
+    for (int i = threadIdx.x; i < 3 * OC; i += blockDim.x) {
+        s_fw[i / OC][i % OC] = p.fW[i];
+        s_rw[i / OC][i % OC] = p.rW[i];
+    }
+    __syncthreads();
+
+    const int lane = threadIdx.x & 31;
+    const int gl = lane % G, grp = lane / G;
+    const int c0 = gl * CPL;
+    const int64_t rr = (int64_t) r * r;
+    const int64_t npix = (int64_t) p.B * rr;
+    const int h = r / 2;
+    const int64_t warp0 = ((int64_t) blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int64_t nwarps = ((int64_t) gridDim.x * blockDim.x) >> 5;
+    const T *outp = (const T *) p.out;
+    const T *featp = (const T *) p.feat;
+
+    for (int64_t base = warp0 * PW; base < npix; base += nwarps * PW) {
+        const int64_t pix = base + grp;  // npix is a multiple of PW
+        const int64_t b = pix / rr;
+        const int pr = (int) (pix - b * rr);
+        const int y = pr / r, x = pr - (pr / r) * r;
+
+        float o[CPL], fs[CPL];
+        chans<T, CPL>::load(outp + pix * OC + c0, o);
+        chans<float, CPL>::load(p.fs + b * p.s_stride + c0, fs);
+        float f0 = 0.0f, f1 = 0.0f, f2 = 0.0f;
+#pragma unroll
+        for (int c = 0; c < CPL; c++) {
+            const float xs = o[c] * fs[c];
+            f0 = fmaf(s_fw[0][c0 + c], xs, f0);
+            f1 = fmaf(s_fw[1][c0 + c], xs, f1);
+            f2 = fmaf(s_fw[2][c0 + c], xs, f2);
+        }
+        float fl[3] = {group_sum<G>(f0), group_sum<G>(f1), group_sum<G>(f2)};
+#pragma unroll
+        for (int k = 0; k < 3; k++) {
+            fl[k] += __ldg(p.fb + k);
+            if (p.skipf_prev)
+                fl[k] += up2x(p.skipf_prev + (b * 3 + k) * (int64_t) h * h, p.fup, x, y, h);
+        }
+        if (p.skipf_out && gl == 0) {
+#pragma unroll
+            for (int k = 0; k < 3; k++) p.skipf_out[(b * 3 + k) * rr + pr] = fl[k];
+        }
+        const float gx = tanhf(fl[0]) + __ldg(p.lin + x);
+        const float gy = tanhf(fl[1]) + __ldg(p.lin + y);
+        const float m = 1.0f / (1.0f + expf(-fl[2]));
+
+        // bilinear taps, as the patched gather computes them
+        const float fx = fmaf((gx + 1.0f) * 0.5f, (float) r, -0.5f);
+        const float fy = fmaf((gy + 1.0f) * 0.5f, (float) r, -0.5f);
+        const bool sane = fabsf(fx) < 1.0e8f && fabsf(fy) < 1.0e8f;
+        const float flx = floorf(fx), fly = floorf(fy);
+        const int x0 = sane ? (int) flx : -4, y0 = sane ? (int) fly : -4;
+        const float wx = fx - flx, wy = fy - fly;
+        float smp[CPL];
+#pragma unroll
+        for (int c = 0; c < CPL; c++) smp[c] = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const int cx = x0 + (k & 1), cy = y0 + (k >> 1);
+            if (!sane || cx < 0 || cx >= r || cy < 0 || cy >= r) continue;
+            const float wgt = ((k & 1) ? wx : 1.0f - wx) * ((k >> 1) ? wy : 1.0f - wy);
+            float f[CPL];
+            chans<T, CPL>::load(featp + ((int64_t) cy * r + cx) * OC + c0, f);
+#pragma unroll
+            for (int c = 0; c < CPL; c++) smp[c] = fmaf(wgt, f[c], smp[c]);
+        }
+
+        const float om = 1.0f - m;
+        float g0 = 0.0f, g1 = 0.0f, g2 = 0.0f;
+#pragma unroll
+        for (int c = 0; c < CPL; c++) {
+            const float w = smp[c] * m;
+            g0 = fmaf(s_rw[0][c0 + c], w, g0);
+            g1 = fmaf(s_rw[1][c0 + c], w, g1);
+            g2 = fmaf(s_rw[2][c0 + c], w, g2);
+            smp[c] = w + o[c] * om;  // trunk
+        }
+        float rg[3] = {group_sum<G>(g0), group_sum<G>(g1), group_sum<G>(g2)};
+        if (gl == 0) {
+#pragma unroll
+            for (int k = 0; k < 3; k++) {
+                float v = rg[k] + __ldg(p.rlb + k);
+                v = (v > 0.0f ? v : 0.2f * v) + __ldg(p.rb + k);
+                if (p.skip_prev) v += up2x(p.skip_prev + (b * 3 + k) * (int64_t) h * h, p.rup, x, y, h);
+                p.skip_out[(b * 3 + k) * rr + pr] = v;
+            }
+        }
+        if (p.trunk) {
+            float sn[CPL];
+            chans<float, CPL>::load(p.snext + b * p.s_stride + c0, sn);
+#pragma unroll
+            for (int c = 0; c < CPL; c++) smp[c] *= sn[c];
+            chans<T, CPL>::store((T *) p.trunk + pix * OC + c0, smp);
+        }
+    }
+}
+
+template <typename T, int CPL, int G>
+cudaError_t run_tail(const tail_params &p, cudaStream_t st) {
+    constexpr int PW = 32 / G;
+    const int64_t npix = (int64_t) p.B * p.r * p.r;
+    const int64_t warps = (npix + PW - 1) / PW;
+    const int blocks = (int) std::min<int64_t>((warps + 7) / 8, 148 * 8);
+    tail_kernel<T, CPL, G><<<blocks, 256, 0, st>>>(p);
+    return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t dispatch_tail(const tail_params &p, cudaStream_t st) {
+    // CPL = max(channels per 16 bytes, OC/32) channels per lane, G = OC/CPL
+    constexpr bool H = sizeof(T) == 2;
+    switch (p.OC) {
+        case 512: return run_tail<T, 16, 32>(p, st);
+        case 256: return run_tail<T, 8, 32>(p, st);
+        case 128:
+            if constexpr (H) return run_tail<T, 8, 16>(p, st);
+            else return run_tail<T, 4, 32>(p, st);
+        case 64:
+            if constexpr (H) return run_tail<T, 8, 8>(p, st);
+            else return run_tail<T, 4, 16>(p, st);
+        case 32:
+            if constexpr (H) return run_tail<T, 8, 4>(p, st);
+            else return run_tail<T, 4, 8>(p, st);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_tail(bool f16, const tail_params &p, cudaStream_t st) {
+    return f16 ? dispatch_tail<__half>(p, st) : dispatch_tail<float>(p, st);
+}
+
+}  // namespace tpmd

@@ -1,0 +1,88 @@
+// Internal interfaces between the decoder's host orchestration
+// (tpmd_api.cpp) and its CUDA kernels. Not installed.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace tpmd {
+
+constexpr int N_LEVELS = 7;
+constexpr int STYLE_DIM = 512;
+constexpr int IMG = 512;
+// stage channels: convs[2j] IC->OC up-conv, convs[2j+1] OC->OC
+// (src/motion_dec.cpp:12-13)
+constexpr int ST_IC[N_LEVELS] = {512, 512, 512, 512, 256, 128, 64};
+constexpr int ST_OC[N_LEVELS] = {512, 512, 512, 256, 128, 64, 32};
+constexpr int N_CONVS = 15;  // conv1 + convs.0..13 (the demodulated convs)
+
+// One modulated 3x3 conv as an implicit GEMM over channel-last activations.
+//   x  [B][H][W][IC]  this conv's input, already multiplied by its style
+//   w  [N][9*IC]      N = OC (dense) or 4*OC (sub-pixel up-conv: column
+//                     q = k*OC + o, parity class k = 2*by + bx); row order
+//                     k = (kh*3 + kw)*IC + ic (the cf order r = ic + IC*(kw+3kh))
+//   y  [B][H][W][OC] (dense) or [B][2H][2W][OC] (up)
+// epilogue per output (b, o): v = acc * inv_den[b*den_stride + o] + bias[o];
+// v = lrelu(v, 0.2); v *= snext[b*snext_stride + o] when snext != nullptr.
+struct conv_params {
+    const void *x;
+    const void *w;
+    void *y;
+    int B, H, W, IC, OC;
+    const float *inv_den;
+    int den_stride;
+    const float *bias;
+    const float *snext;
+    int snext_stride;
+};
+
+// The per-level tail after conv2 (ToFlow, flow head, bilinear warp of the
+// level's feats, mask blend, ToRGB, skip up-sampling), per pixel of level r:
+//   fl_k  = sum_c fW[k][c]*(out[c]*fs[c]) + fb[k] + up2x(skipf_prev)[k]
+//   grid  = (tanh(fl_0) + lin[x], tanh(fl_1) + lin[y]);  m = sigmoid(fl_2)
+//   warp  = gather(feat, grid) * m;  trunk = warp + out*(1 - m)
+//   rgb_k = lrelu(sum_c rW[k][c]*warp[c] + rlb[k]) + rb[k] + up2x(skip_prev)[k]
+struct tail_params {
+    const void *out;        // [B][r][r][OC]   conv2 output
+    const void *feat;       // [r*r][OC]       level feats (same dtype)
+    int B, r, OC;
+    const float *fW;        // [3][OC]
+    const float *fs;        // ToFlow styles, fs[b*s_stride + c]
+    int s_stride;
+    const float *fb, *fup;  // [3], [16]
+    const float *skipf_prev;  // [B][3][r/2][r/2] or nullptr (level 0)
+    float *skipf_out;         // [B][3][r][r] or nullptr (last level)
+    const float *rW;        // [3][OC]
+    const float *rlb, *rb, *rup;
+    const float *skip_prev;   // [B][3][r/2][r/2] or nullptr
+    float *skip_out;          // [B][3][r][r] (the frames at r = 512)
+    const float *lin;         // [r] identity grid -1 + 2i/(r-1)
+    void *trunk;              // [B][r][r][OC] or nullptr (last level)
+    const float *snext;       // next up-conv style, snext[b*s_stride + c]
+};
+
+// launchers; `f16` selects the f16 (else f32) instantiation
+cudaError_t launch_style(const float *wmod, const float *bmod, int rows, const float *lat,
+                         int B, float *s_all, cudaStream_t st);
+struct den_table {
+    int n;                 // convs
+    int row0[N_CONVS + 1]; // first global row of each conv; row0[n] = total
+    int ic[N_CONVS];
+    int64_t saug_off[N_CONVS];  // float offset of the conv's S_aug in saug base
+    int s_off[N_CONVS];    // its input style offset within a frame's s_all row
+    int d_off[N_CONVS];    // its inv_den offset within a frame's row
+};
+cudaError_t launch_den(const float *saug, const den_table &t, const float *s_all, int s_stride,
+                       int B, float *inv_den, int d_stride, cudaStream_t st);
+cudaError_t launch_conv1_input(bool f16, const float *input, const float *s, int s_stride,
+                               int B, void *x0, cudaStream_t st);
+cudaError_t launch_conv_simt(bool f16, bool up, const conv_params &p, cudaStream_t st);
+cudaError_t launch_tail(bool f16, const tail_params &p, cudaStream_t st);
+
+// tcgen05 path (f16)
+cudaError_t launch_conv_tc(bool up, const conv_params &p, cudaStream_t st);
+bool conv_tc_supported(bool up, int IC, int OC);
+
+}  // namespace tpmd

@@ -1,0 +1,214 @@
+"""Python binding of libtpmd.so, the B200 motion decoder's C ABI
+(include/tpmd.h).
+
+This is a thin ctypes layer: every call goes through the C ABI into the
+sm_100a kernels. There is no CPU or PyTorch fallback: importing this module
+without the built library raises, and the decoder refuses GPUs other than
+sm_100.
+
+Device memory for the op-level entry points and for tpmd_decode_device is
+passed as torch CUDA tensors (their data_ptr) purely as the allocator; torch
+computes nothing here.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+from . import synth  # noqa: F401  (re-exported)
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(os.path.dirname(HERE), "libtpmd.so")
+
+DTYPE_F32 = 0
+DTYPE_F16 = 1
+N_LEVELS = 7
+STYLE_DIM = 512
+IMG = 512
+ST_IC = (512, 512, 512, 512, 256, 128, 64)
+ST_OC = (512, 512, 512, 256, 128, 64, 32)
+
+EXPORTS = ("tpmd_abi_version", "tpmd_create", "tpmd_create_error", "tpmd_destroy",
+           "tpmd_last_error", "tpmd_scale_for", "tpmd_set_tensor", "tpmd_prepare",
+           "tpmd_set_feats", "tpmd_batch", "tpmd_decode", "tpmd_decode_device",
+           "tpmd_arena", "tpmd_arena_adopt", "tpmd_decode_taps", "tpmd_profile_begin", "tpmd_profile_end",
+           "tpmd_kernel_launches",
+           "tpk_bilinear_gather", "tpk_im2col_cf", "tpk_last_error")
+
+_lib = None
+
+
+class TpmdError(RuntimeError):
+    pass
+
+
+def load_library(path: str = LIB_PATH):
+    """Load libtpmd.so; raises if it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(path):
+        raise ImportError(f"{path} is missing: build it with "
+                          "`python talking-portrait.cpp_b200/build.py` (no fallback exists)")
+    L = C.CDLL(path)
+    v, i64, cp = C.c_void_p, C.c_int64, C.c_char_p
+    L.tpmd_abi_version.restype = C.c_int
+    L.tpmd_create.argtypes = [C.c_int, C.c_int, C.c_int]
+    L.tpmd_create.restype = v
+    L.tpmd_create_error.restype = cp
+    L.tpmd_destroy.argtypes = [v]
+    L.tpmd_last_error.argtypes = [v]
+    L.tpmd_last_error.restype = cp
+    L.tpmd_scale_for.argtypes = [cp, v]
+    L.tpmd_scale_for.restype = C.c_double
+    L.tpmd_set_tensor.argtypes = [v, cp, v, i64]
+    L.tpmd_prepare.argtypes = [v]
+    L.tpmd_set_feats.argtypes = [v, C.POINTER(v)]
+    L.tpmd_batch.argtypes = [v]
+    L.tpmd_decode.argtypes = [v, v, i64, v]
+    L.tpmd_decode_device.argtypes = [v, v, i64, v, v]
+    L.tpmd_arena.argtypes = [v, C.c_int, C.POINTER(v), C.POINTER(C.c_size_t)]
+    L.tpmd_arena_adopt.argtypes = [v, C.c_int]
+    L.tpmd_decode_taps.argtypes = [v, v, C.c_int, v, v, v, v, v]
+    L.tpmd_profile_begin.argtypes = [v]
+    L.tpmd_profile_end.argtypes = [v, C.c_char_p, C.c_size_t]
+    L.tpmd_kernel_launches.argtypes = [v, i64]
+    L.tpmd_kernel_launches.restype = i64
+    L.tpk_bilinear_gather.argtypes = [v, C.c_int, C.c_int, C.c_int, C.c_int, v, i64, C.c_int,
+                                      C.c_int, v, v]
+    L.tpk_im2col_cf.argtypes = [v] + [C.c_int] * 12 + [v, C.c_int, v]
+    L.tpk_last_error.restype = cp
+    _lib = L
+    return L
+
+
+def _np_ptr(a: np.ndarray):
+    return a.ctypes.data_as(C.c_void_p)
+
+
+def scale_for(name: str, ne) -> float:
+    """motion_ae_scale (src/motion_enc.cpp:14-45) through the C ABI."""
+    ne = np.asarray(list(ne) + [1] * (4 - len(ne)), np.int64)
+    return load_library().tpmd_scale_for(name.encode(), _np_ptr(ne))
+
+
+class MotionDecoder:
+    """One decoder on one GPU (mirrors the reference's motion_dec:
+    prepare / set_feats / decode_batch, src/motion_dec.h:10-49)."""
+
+    def __init__(self, device: int = 0, dtype: int = DTYPE_F16, max_batch: int = 64):
+        self._L = load_library()
+        self._h = self._L.tpmd_create(device, dtype, max_batch)
+        if not self._h:
+            raise TpmdError(self._L.tpmd_create_error().decode())
+        self.dtype = dtype
+        self.batch = self._L.tpmd_batch(self._h)
+
+    def _check(self, rc: int):
+        if rc != 0:
+            raise TpmdError(self._L.tpmd_last_error(self._h).decode())
+
+    def set_tensors(self, tensors: dict):
+        for name, arr in tensors.items():
+            a = np.ascontiguousarray(arr, np.float32)
+            self._check(self._L.tpmd_set_tensor(self._h, name.encode(), _np_ptr(a), a.size))
+
+    def prepare(self):
+        self._check(self._L.tpmd_prepare(self._h))
+
+    def set_feats(self, feats):
+        arrs = [np.ascontiguousarray(f, np.float32) for f in feats]
+        ptrs = (C.c_void_p * N_LEVELS)(*[a.ctypes.data for a in arrs])
+        self._check(self._L.tpmd_set_feats(self._h, ptrs))
+
+    def decode(self, styles: np.ndarray, out: np.ndarray | None = None) -> np.ndarray:
+        """styles [n, 512] f32 (host) -> frames [n, 3, 512, 512] f32 (host)."""
+        styles = np.ascontiguousarray(styles, np.float32).reshape(-1, STYLE_DIM)
+        n = styles.shape[0]
+        if out is None:
+            out = np.empty((n, 3, IMG, IMG), np.float32)
+        assert out.flags.c_contiguous and out.dtype == np.float32 and out.size == n * 3 * IMG * IMG
+        self._check(self._L.tpmd_decode(self._h, _np_ptr(styles), n, _np_ptr(out)))
+        return out
+
+    def decode_ptr(self, styles_ptr: int, n: int, frames_ptr: int):
+        """host pointers (e.g. pinned torch tensors' data_ptr())"""
+        self._check(self._L.tpmd_decode(self._h, C.c_void_p(styles_ptr), n, C.c_void_p(frames_ptr)))
+
+    def decode_device(self, styles_ptr: int, n: int, frames_ptr: int, stream: int = 0):
+        """device pointers, enqueued on `stream` (cudaStream_t as int)"""
+        self._check(self._L.tpmd_decode_device(self._h, C.c_void_p(styles_ptr), n,
+                                               C.c_void_p(frames_ptr), C.c_void_p(stream)))
+
+    def taps(self, style: np.ndarray, level: int) -> dict:
+        """Parity taps of one frame at `level` (see tpmd_decode_taps)."""
+        r, oc = 8 << level, ST_OC[level]
+        st = np.ascontiguousarray(style, np.float32).reshape(STYLE_DIM)
+        out = {"conv1": np.empty((oc, r, r), np.float32), "conv2": np.empty((oc, r, r), np.float32),
+               "rgb": np.empty((3, r, r), np.float32)}
+        if level < N_LEVELS - 1:
+            out["flowmap"] = np.empty((3, r, r), np.float32)
+            out["trunk"] = np.empty((oc, r, r), np.float32)
+        p = lambda k: _np_ptr(out[k]) if k in out else None  # noqa: E731
+        self._check(self._L.tpmd_decode_taps(self._h, _np_ptr(st), level, p("conv1"), p("conv2"),
+                                             p("flowmap"), p("trunk"), p("rgb")))
+        return out
+
+    def arena(self, which: int) -> tuple[int, int]:
+        p, n = C.c_void_p(), C.c_size_t()
+        self._check(self._L.tpmd_arena(self._h, which, C.byref(p), C.byref(n)))
+        return p.value, n.value
+
+    def adopt_arena(self, which: int):
+        self._check(self._L.tpmd_arena_adopt(self._h, which))
+
+    def profile_begin(self):
+        self._check(self._L.tpmd_profile_begin(self._h))
+
+    def profile_end(self) -> dict:
+        """{kernel: (launches, total_ms)} timed with CUDA events since begin"""
+        import json
+        buf = C.create_string_buffer(1 << 16)
+        self._check(self._L.tpmd_profile_end(self._h, buf, len(buf)))
+        return {k: (v[0], v[1]) for k, v in json.loads(buf.value.decode()).items()}
+
+    def kernel_launches(self, n: int) -> int:
+        return self._L.tpmd_kernel_launches(self._h, n)
+
+    def close(self):
+        if getattr(self, "_h", None):
+            self._L.tpmd_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+
+def _tpk_check(rc: int):
+    if rc != 0:
+        raise TpmdError(load_library().tpk_last_error().decode())
+
+
+def bilinear_gather(feat, W: int, H: int, grid, out, planar=False, out_sp=False, stream=0):
+    """Device op with ggml_bilinear_gather semantics. feat [W*H, C] (torch CUDA
+    f32/f16), grid [N, 2] (or [2, N] planar) f32, out [N, C] (or [C, N])."""
+    import torch
+    C_ = feat.shape[-1]
+    N = grid.numel() // 2
+    _tpk_check(load_library().tpk_bilinear_gather(
+        C.c_void_p(feat.data_ptr()), int(feat.dtype == torch.float16), C_, W, H,
+        C.c_void_p(grid.data_ptr()), N, int(planar), int(out_sp), C.c_void_p(out.data_ptr()),
+        C.c_void_p(stream)))
+    return out
+
+
+def im2col_cf(src, IC, IW, IH, N, out, KW=3, KH=3, s0=1, s1=1, p0=1, p1=1, d0=1, d1=1,
+              stream=0):
+    """Device op with ggml_im2col_cf semantics (see include/tpmd.h)."""
+    import torch
+    _tpk_check(load_library().tpk_im2col_cf(
+        C.c_void_p(src.data_ptr()), IC, IW, IH, N, KW, KH, s0, s1, p0, p1, d0, d1,
+        C.c_void_p(out.data_ptr()), int(out.dtype == torch.float16), C.c_void_p(stream)))
+    return out

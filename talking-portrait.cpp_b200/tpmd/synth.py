@@ -75,8 +75,15 @@ def ggml_ne(shape: tuple[int, ...]) -> tuple[int, int, int, int]:
     return tuple(list(ne) + [1] * (4 - len(ne)))[:4]
 
 
-def make_weights(seed: int = 0, bias_std: float = 0.0) -> dict[str, np.ndarray]:
-    """Raw (unfolded) f32 weights in torch shapes."""
+def make_weights(seed: int = 0, bias_std: float = 0.0, flow_gain: float = 1.0) -> dict[str, np.ndarray]:
+    """Raw (unfolded) f32 weights in torch shapes.
+
+    flow_gain scales the ToFlow conv weights. 1.0 is the plain random init,
+    whose flow maps are large (|fl| ~ 2-5), saturate tanh and move every
+    sampling point by up to half the image; the decoder is then so sensitive
+    that the reference's own f16 arithmetic ends at SSIM ~0.95 against its
+    fp32 output. 0.25 keeps the flows in tanh's linear range, as a trained
+    model's are; parity gates use it (PARITY_FLOW_GAIN)."""
     rng = np.random.default_rng([seed, 1])
     out: dict[str, np.ndarray] = {}
     bk = blur_kernel4()
@@ -90,7 +97,12 @@ def make_weights(seed: int = 0, bias_std: float = 0.0) -> dict[str, np.ndarray]:
                          if bias_std > 0 else np.zeros(shape, np.float32))
         else:
             out[name] = rng.standard_normal(shape, np.float32)
+            if name.startswith("dec.to_flows.") and name.endswith(".conv.weight"):
+                out[name] *= np.float32(flow_gain)
     return out
+
+
+PARITY_FLOW_GAIN = 0.25
 
 
 def fold(raw: dict[str, np.ndarray], scale_for) -> dict[str, np.ndarray]:

@@ -1,0 +1,104 @@
+"""An independent float64 formulation of the motion decoder in torch (CPU),
+used only to cross-check the oracle's graph composition.
+
+It is written from the module definitions the reference's graph implements
+(StyleGAN2 / LIA Synthesis as described by src/motion_dec.cpp:794-888 and
+the folding notes of src/motion_enc.cpp:14-45), deliberately in the
+*unfolded* form: RAW weights with the Equal* runtime scales applied at run
+time, weight-side modulation and demodulation (w' = w*s,
+d = rsqrt(sum w'^2 + 1e-8)), FusedLeakyReLU as sqrt(2)*lrelu(x + b), the
+up-conv as torch.conv_transpose2d(stride 2) followed by Blur(pad 1, 1), the
+skip up-sampling as upfirdn2d(up=2, pad=(2,1)) and the warp as
+torch.nn.functional.grid_sample. None of the oracle's derived tensors (S_aug,
+tsubcf, folded scales) are used.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+ST_IC = (512, 512, 512, 512, 256, 128, 64)
+ST_OC = (512, 512, 512, 256, 128, 64, 32)
+
+
+def _t(a):
+    return torch.as_tensor(np.asarray(a), dtype=torch.float64)
+
+
+def _upfirdn(x, k, up, pad0, pad1):
+    """x [1, C, H, W]; zero-stuff by `up`, pad (pad0, pad1), correlate with k"""
+    c = x.shape[1]
+    if up > 1:
+        n, _, h, w = x.shape
+        z = torch.zeros(n, c, h * up, w * up, dtype=x.dtype)
+        z[:, :, ::up, ::up] = x
+        x = z
+    x = F.pad(x, (pad0, pad1, pad0, pad1))
+    kk = k.flip([0, 1])[None, None].repeat(c, 1, 1, 1)  # upfirdn2d convolves
+    return F.conv2d(x, kk, groups=c)
+
+
+class TorchLIA:
+    def __init__(self, raw: dict, feats: list):
+        self.w = {k: _t(v) for k, v in raw.items()}
+        # feats[j]: [r*r, C] channel-last -> [1, C, r, r]
+        self.feats = [_t(f).T.reshape(1, f.shape[1], 8 << j, 8 << j) for j, f in enumerate(feats)]
+
+    def _style(self, base, lat):
+        W = self.w[base + ".modulation.weight"]
+        b = self.w[base + ".modulation.bias"]
+        return lat @ (W * (1.0 / math.sqrt(W.shape[1]))).T + b
+
+    def _modconv(self, x, base, lat, demod=True, up=False):
+        W = self.w[base + ".weight"]  # [OC, IC, k, k]
+        oc, ic, k, _ = W.shape
+        s = self._style(base, lat)
+        w = W * (1.0 / math.sqrt(ic * k * k)) * s[None, :, None, None]
+        if demod:
+            d = torch.rsqrt((w ** 2).sum([1, 2, 3]) + 1e-8)
+            w = w * d[:, None, None, None]
+        if up:
+            y = F.conv_transpose2d(x, w.transpose(0, 1), stride=2)
+            return _upfirdn(y, self.w[base + ".blur.kernel"], 1, 1, 1)
+        return F.conv2d(x, w, padding=k // 2)
+
+    @staticmethod
+    def _flrelu(x, b):
+        return math.sqrt(2.0) * F.leaky_relu(x + b.reshape(1, -1, 1, 1), 0.2)
+
+    def decode(self, latent: np.ndarray) -> np.ndarray:
+        lat = _t(latent)
+        x = self.w["dec.input.input"]
+        x = self._flrelu(self._modconv(x, "dec.conv1.conv", lat), self.w["dec.conv1.activate.bias"])
+        skip = skip_f = None
+        for j in range(7):
+            r = 8 << j
+            b1, b2 = f"dec.convs.{2 * j}", f"dec.convs.{2 * j + 1}"
+            x = self._flrelu(self._modconv(x, b1 + ".conv", lat, up=True),
+                             self.w[b1 + ".activate.bias"])
+            out = self._flrelu(self._modconv(x, b2 + ".conv", lat), self.w[b2 + ".activate.bias"])
+            bf, br = f"dec.to_flows.{j}", f"dec.to_rgbs.{j}"
+            fl = self._modconv(out, bf + ".conv", lat, demod=False) + self.w[bf + ".bias"]
+            if skip_f is not None:
+                fl = fl + _upfirdn(skip_f, self.w[bf + ".upsample.kernel"], 2, 2, 1)
+            skip_f = fl
+            lin = torch.linspace(-1.0, 1.0, r, dtype=torch.float64)
+            gx = torch.tanh(fl[0, 0]) + lin[None, :]
+            gy = torch.tanh(fl[0, 1]) + lin[:, None]
+            m = torch.sigmoid(fl[0, 2])
+            grid = torch.stack([gx, gy], -1)[None]
+            sampled = F.grid_sample(self.feats[j], grid, mode="bilinear", padding_mode="zeros",
+                                    align_corners=False)
+            warp = sampled * m
+            trunk = warp + out * (1 - m)
+            Wr = self.w[br + ".conv.0.weight"]
+            rgb = F.conv2d(warp, Wr * (1.0 / math.sqrt(Wr.shape[1])))
+            rgb = self._flrelu(rgb, self.w[br + ".conv.1.bias"]) + self.w[br + ".bias"].reshape(1, 3, 1, 1)
+            if skip is not None:
+                rgb = rgb + _upfirdn(skip, self.w[br + ".upsample.kernel"], 2, 2, 1)
+            skip = rgb
+            x = trunk
+        return skip[0].numpy()
