@@ -343,7 +343,7 @@ def dec_uses_tc() -> bool:
     return os.environ.get("TPMD_CONV", "tc" if TC_DEFAULT else "simt") == "tc"
 
 
-TC_DEFAULT = False
+TC_DEFAULT = True
 
 if __name__ == "__main__":
     main()

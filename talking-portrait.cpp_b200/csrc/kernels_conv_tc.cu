@@ -1,7 +1,495 @@
-// tcgen05 implicit-GEMM modulated conv (f16): placeholder until the kernel lands.
+// Modulated 3x3 conv as a tcgen05 implicit GEMM (f16 in, f32 accumulate in
+// TMEM, f16 out) for sm_100a.
+//
+// GEMM view (as the SIMT kernel): M = input-grid pixels of the batch, N = OC
+// (dense) or 4*OC (sub-pixel up-conv: the conv_transpose+blur composition of
+// src/motion_dec.cpp:144-191 as four parity classes), K = 9*IC in the order
+// k = tap*IC + ic.
+//
+// Structure (one CTA per SM, persistent over tiles of 128 pixels x BN columns):
+//  * warp 0, one lane: TMA producer. Per k-step it loads the A tile as ONE
+//    4-D box {KC channels, bw, bh, bb} of the channel-last activation at the
+//    tap's shifted coordinates (x-1..x+1, y-1..y+1); TMA's zero fill of the
+//    out-of-range part IS the conv's padding, so no im2col buffer exists. The
+//    B tile is a 2-D box {KC, BN} of the [N][K] weight matrix. Both land in
+//    shared memory in the 128-byte (KC = 64) or 64-byte (KC = 32) swizzled
+//    K-major layout that tcgen05 descriptors address directly.
+//  * warp 1, one lane: issues tcgen05.mma (M=128, N=BN, K=16) into a TMEM
+//    accumulator, commits each stage back to the producer and each finished
+//    tile to the epilogue. Two accumulators (2*BN TMEM columns) let the
+//    epilogue of tile t overlap the MMAs of tile t+1.
+//  * warps 2-5: epilogue. Each warp reads its 32-lane quarter of TMEM
+//    (tcgen05.ld 32x32b), applies x inv_den[b][o] (demodulation with the
+//    FusedLeakyReLU gain folded), + bias, leaky ReLU 0.2, x the next conv's
+//    style, and stores f16 channel-last rows (sub-pixel scatter for the up-conv).
+// Every mbarrier wait is bounded (~2 s of %globaltimer); on expiry the kernel
+// sets *err, stops issuing work, waits (bounded) for its own copies and MMAs
+// in flight, frees its TMEM and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
 #include "tpmd_internal.h"
 
 namespace tpmd {
-bool conv_tc_supported(bool, int, int) { return false; }
-cudaError_t launch_conv_tc(bool, const conv_params &, cudaStream_t) { return cudaErrorNotSupported; }
+namespace {
+
+constexpr int TC_THREADS = 192;
+constexpr int BM = 128;
+
+struct tc_params {
+    int B, H, W, IC, OC, N;
+    int kiters, cpt;           // k-steps per tile, channel chunks per tap
+    int bw, bh, bb;            // pixel box of one M tile
+    int tiles_x, tiles_y, tiles_n;
+    int64_t num_tiles;
+    __half *y;
+    const float *inv_den;
+    int den_stride;
+    const float *bias;
+    const float *snext;
+    int snext_stride;
+    int *err;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return (uint32_t) __cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// bounded phase wait: false after ~2 s without completion
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+    if (mbar_try(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    for (;;) {
+        for (int i = 0; i < 64; i++)
+            if (mbar_try(bar, parity)) return true;
+        if (global_ns() - t0 > 2000000000ull) return false;
+    }
+}
+
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap *tm, uint32_t bar, int c0,
+                                            int c1, int c2, int c3) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(dst),
+        "l"((uint64_t) tm), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+        : "memory");
+}
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *tm, uint32_t bar, int c0,
+                                            int c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+        "l"((uint64_t) tm), "r"(bar), "r"(c0), "r"(c1)
+        : "memory");
+}
+
+// shared-memory matrix descriptor, K-major swizzled canonical layout:
+// start address >> 4, LBO = 1 (unused when swizzled), SBO = bytes between
+// 8-row groups, version 1 (sm_100), layout type (2: 128B swizzle, 4: 64B)
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t sbo, uint32_t layout) {
+    uint64_t d = (uint64_t) ((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t) 1u << 16;
+    d |= (uint64_t) ((sbo >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t) 1u << 46;
+    d |= (uint64_t) layout << 61;
+    return d;
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+    const uint32_t mask = 0;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(mask));
+}
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                 : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, "
+        "%13, %14, %15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+          "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+template <int BN, int KC>
+struct tc_cfg {
+    static constexpr int A_BYTES = BM * KC * 2;
+    static constexpr int B_BYTES = BN * KC * 2;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int STAGES = (196608 / STAGE_BYTES) > 8 ? 8 : (196608 / STAGE_BYTES);
+    static constexpr uint32_t TMEM_COLS = 2 * BN;  // two accumulators; 64..512, a power of 2
+    static constexpr uint32_t LAYOUT = KC == 64 ? 2u : 4u;
+    static constexpr uint32_t SBO = KC == 64 ? 1024u : 512u;
+    // kind::f16 instruction descriptor: D f32, A/B f16, both K-major, N, M
+    static constexpr uint32_t IDESC =
+        (1u << 4) | ((uint32_t) (BN >> 3) << 17) | ((uint32_t) (BM >> 4) << 24);
+    static constexpr int NBARS = 2 * STAGES + 5;
+    static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + NBARS * 8 + 16;
+};
+
+struct tile_pos {
+    int n0, b0, y0, x0;
+};
+__device__ __forceinline__ tile_pos tile_of(const tc_params &p, int64_t t, int BN) {
+    tile_pos r;
+    const int nt = (int) (t % p.tiles_n);
+    const int64_t m = t / p.tiles_n;
+    const int xt = (int) (m % p.tiles_x);
+    const int64_t m2 = m / p.tiles_x;
+    const int yt = (int) (m2 % p.tiles_y);
+    const int bt = (int) (m2 / p.tiles_y);
+    r.n0 = nt * BN;
+    r.x0 = xt * p.bw;
+    r.y0 = yt * p.bh;
+    r.b0 = bt * p.bb;
+    return r;
+}
+
+template <int BN, int KC, bool UP>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+               const tc_params p) {
+    using cfg = tc_cfg<BN, KC>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = (uint8_t *) (((uintptr_t) smem_raw + 1023) & ~(uintptr_t) 1023);
+    uint8_t *sA = smem;
+    uint8_t *sB = smem + cfg::STAGES * cfg::A_BYTES;
+    uint64_t *bars = (uint64_t *) (smem + cfg::STAGES * cfg::STAGE_BYTES);
+    uint32_t *tmem_slot = (uint32_t *) (bars + cfg::NBARS);
+    auto full = [&](int s) { return smem_u32(&bars[s]); };
+    auto empty = [&](int s) { return smem_u32(&bars[cfg::STAGES + s]); };
+    auto tfull = [&](int a) { return smem_u32(&bars[2 * cfg::STAGES + a]); };
+    auto tempty = [&](int a) { return smem_u32(&bars[2 * cfg::STAGES + 2 + a]); };
+    const uint32_t drain = smem_u32(&bars[2 * cfg::STAGES + 4]);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < cfg::STAGES; s++) {
+            mbar_init(full(s), 1);
+            mbar_init(empty(s), 1);
+        }
+        for (int a = 0; a < 2; a++) {
+            mbar_init(tfull(a), 1);
+            mbar_init(tempty(a), 4);
+        }
+        mbar_init(drain, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(tmem_slot)),
+                     "r"(cfg::TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---- TMA producer
+            uint32_t it = 0;
+            bool ok = true;
+            for (int64_t t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+                const tile_pos tp = tile_of(p, t, BN);
+                for (int kk = 0; kk < p.kiters; kk++, it++) {
+                    const int s = it % cfg::STAGES;
+                    const uint32_t ph = (it / cfg::STAGES) & 1;
+                    if (!mbar_wait(empty(s), ph ^ 1)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(full(s), cfg::STAGE_BYTES);
+                    const int tap = kk / p.cpt, c = kk - tap * p.cpt;
+                    const int kh = tap / 3, kw = tap - kh * 3;
+                    tma_load_4d(smem_u32(sA + s * cfg::A_BYTES), &tmA, full(s), c * KC, tp.x0 + kw - 1,
+                                tp.y0 + kh - 1, tp.b0);
+                    tma_load_2d(smem_u32(sB + s * cfg::B_BYTES), &tmB, full(s), tap * p.IC + c * KC,
+                                tp.n0);
+                }
+            }
+            if (!ok) {
+                atomicExch(p.err, 1);
+                // let the loads already issued land before shared memory goes away
+                for (int s = 0; s < cfg::STAGES && (uint32_t) s < it; s++) {
+                    const uint32_t last = it - 1 - ((it - 1 - s) % cfg::STAGES);
+                    mbar_wait(full(s), (last / cfg::STAGES) & 1);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---- MMA issuer
+            uint32_t it = 0, tcount = 0;
+            bool ok = true;
+            for (int64_t t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x, tcount++) {
+                const int a = tcount & 1;
+                if (!mbar_wait(tempty(a), ((tcount >> 1) & 1) ^ 1)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + a * BN;
+                for (int kk = 0; kk < p.kiters; kk++, it++) {
+                    const int s = it % cfg::STAGES;
+                    if (!mbar_wait(full(s), (it / cfg::STAGES) & 1)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint64_t ad = smem_desc(smem_u32(sA + s * cfg::A_BYTES), cfg::SBO, cfg::LAYOUT);
+                    const uint64_t bd = smem_desc(smem_u32(sB + s * cfg::B_BYTES), cfg::SBO, cfg::LAYOUT);
+#pragma unroll
+                    for (int k = 0; k < KC / 16; k++)  // +32 bytes along K per step
+                        umma_f16(d_tmem, ad + 2 * k, bd + 2 * k, cfg::IDESC, (kk | k) != 0);
+                    umma_commit(empty(s));
+                }
+                if (!ok) break;
+                umma_commit(tfull(a));
+            }
+            if (!ok) atomicExch(p.err, 1);
+            umma_commit(drain);  // completes when every MMA issued here has
+            mbar_wait(drain, 0);
+        }
+    } else {
+        // ---- epilogue: warps 2..5, TMEM lane quarter = warp % 4
+        const int q = warp & 3;
+        const int row = q * 32 + lane;
+        const int bx = row % p.bw, by = (row / p.bw) % p.bh, bz = row / (p.bw * p.bh);
+        uint32_t tcount = 0;
+        for (int64_t t = blockIdx.x; t < p.num_tiles; t += gridDim.x, tcount++) {
+            const int a = tcount & 1;
+            const bool ok = __all_sync(0xffffffffu, mbar_wait(tfull(a), (tcount >> 1) & 1));
+            if (!ok) {
+                if (lane == 0) atomicExch(p.err, 1);
+                break;
+            }
+            tc_fence_after();
+            const tile_pos tp = tile_of(p, t, BN);
+            const int b = tp.b0 + bz, y = tp.y0 + by, x = tp.x0 + bx;
+            const bool valid = b < p.B;
+            const uint32_t taddr = tmem_base + ((uint32_t) (q * 32) << 16) + a * BN;
+#pragma unroll 1
+            for (int c0 = 0; c0 < BN; c0 += 16) {
+                uint32_t r[16];
+                tmem_ld16(taddr + c0, r);
+                if (!valid) continue;
+                const int n = tp.n0 + c0;
+                const int o0 = UP ? n % p.OC : n;
+                float den[16], bias[16], sn[16];
+                const float4 *dp = reinterpret_cast<const float4 *>(p.inv_den + (int64_t) b * p.den_stride + o0);
+                const float4 *bp = reinterpret_cast<const float4 *>(p.bias + o0);
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const float4 dv = __ldg(dp + i), bv = __ldg(bp + i);
+                    den[4 * i] = dv.x; den[4 * i + 1] = dv.y; den[4 * i + 2] = dv.z; den[4 * i + 3] = dv.w;
+                    bias[4 * i] = bv.x; bias[4 * i + 1] = bv.y; bias[4 * i + 2] = bv.z; bias[4 * i + 3] = bv.w;
+                }
+                if (p.snext) {
+                    const float4 *sp = reinterpret_cast<const float4 *>(p.snext + (int64_t) b * p.snext_stride + o0);
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        const float4 sv = __ldg(sp + i);
+                        sn[4 * i] = sv.x; sn[4 * i + 1] = sv.y; sn[4 * i + 2] = sv.z; sn[4 * i + 3] = sv.w;
+                    }
+                }
+                uint4 pk[2];
+                __half2 *h2 = reinterpret_cast<__half2 *>(pk);
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    float v0 = fmaf(__uint_as_float(r[2 * i]), den[2 * i], bias[2 * i]);
+                    float v1 = fmaf(__uint_as_float(r[2 * i + 1]), den[2 * i + 1], bias[2 * i + 1]);
+                    v0 = v0 > 0.0f ? v0 : 0.2f * v0;
+                    v1 = v1 > 0.0f ? v1 : 0.2f * v1;
+                    if (p.snext) {
+                        v0 *= sn[2 * i];
+                        v1 *= sn[2 * i + 1];
+                    }
+                    h2[i] = __floats2half2_rn(v0, v1);
+                }
+                int64_t dst;
+                if (UP) {
+                    const int cls = n / p.OC;
+                    const int Y = 2 * y + (cls >> 1), X = 2 * x + (cls & 1);
+                    dst = (((int64_t) b * 2 * p.H + Y) * 2 * p.W + X) * p.OC + o0;
+                } else {
+                    dst = (((int64_t) b * p.H + y) * p.W + x) * p.OC + o0;
+                }
+                uint4 *yp = reinterpret_cast<uint4 *>(p.y + dst);
+                yp[0] = pk[0];
+                yp[1] = pk[1];
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(tempty(a));
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                     "r"(cfg::TMEM_COLS)
+                     : "memory");
+}
+
+// ---- host side ------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (PFN_cuTensorMapEncodeTiled_v12000) ptr;
+    });
+    return fn;
+}
+
+int sm_count() {
+    static int n = 0;
+    if (!n) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (n <= 0) n = 148;
+    }
+    return n;
+}
+
+template <int BN, int KC, bool UP>
+cudaError_t run_tc(const conv_params &cp, int *err, cudaStream_t st) {
+    using cfg = tc_cfg<BN, KC>;
+    auto enc = encode_fn();
+    if (!enc) return cudaErrorNotSupported;
+    tc_params p{};
+    p.B = cp.B;
+    p.H = cp.H;
+    p.W = cp.W;
+    p.IC = cp.IC;
+    p.OC = cp.OC;
+    p.N = UP ? 4 * cp.OC : cp.OC;
+    p.cpt = cp.IC / KC;
+    p.kiters = 9 * p.cpt;
+    p.bw = cp.W < BM ? cp.W : BM;
+    p.bh = cp.H < BM / p.bw ? cp.H : BM / p.bw;
+    p.bb = BM / (p.bw * p.bh);
+    p.tiles_x = cp.W / p.bw;
+    p.tiles_y = cp.H / p.bh;
+    p.tiles_n = p.N / BN;
+    const int tiles_b = (cp.B + p.bb - 1) / p.bb;
+    p.num_tiles = (int64_t) tiles_b * p.tiles_y * p.tiles_x * p.tiles_n;
+    p.y = (__half *) cp.y;
+    p.inv_den = cp.inv_den;
+    p.den_stride = cp.den_stride;
+    p.bias = cp.bias;
+    p.snext = cp.snext;
+    p.snext_stride = cp.snext_stride;
+    p.err = err;
+
+    CUtensorMap tmA, tmB;
+    {
+        const cuuint64_t dims[4] = {(cuuint64_t) cp.IC, (cuuint64_t) cp.W, (cuuint64_t) cp.H,
+                                    (cuuint64_t) cp.B};
+        const cuuint64_t strides[3] = {(cuuint64_t) cp.IC * 2, (cuuint64_t) cp.W * cp.IC * 2,
+                                       (cuuint64_t) cp.H * cp.W * cp.IC * 2};
+        const cuuint32_t box[4] = {(cuuint32_t) KC, (cuuint32_t) p.bw, (cuuint32_t) p.bh,
+                                   (cuuint32_t) p.bb};
+        const cuuint32_t es[4] = {1, 1, 1, 1};
+        if (enc(&tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, (void *) cp.x, dims, strides, box, es,
+                CU_TENSOR_MAP_INTERLEAVE_NONE,
+                KC == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return cudaErrorInvalidValue;
+    }
+    {
+        const int K = 9 * cp.IC;
+        const cuuint64_t dims[2] = {(cuuint64_t) K, (cuuint64_t) p.N};
+        const cuuint64_t strides[1] = {(cuuint64_t) K * 2};
+        const cuuint32_t box[2] = {(cuuint32_t) KC, (cuuint32_t) BN};
+        const cuuint32_t es[2] = {1, 1};
+        if (enc(&tmB, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void *) cp.w, dims, strides, box, es,
+                CU_TENSOR_MAP_INTERLEAVE_NONE,
+                KC == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return cudaErrorInvalidValue;
+    }
+    static uint64_t attr_set = 0;  // one bit per device
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!(attr_set >> (dev & 63) & 1)) {
+        const cudaError_t e = cudaFuncSetAttribute(conv_tc_kernel<BN, KC, UP>,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, cfg::SMEM);
+        if (e != cudaSuccess) return e;
+        attr_set |= 1ull << (dev & 63);
+    }
+    const int grid = (int) (p.num_tiles < sm_count() ? p.num_tiles : sm_count());
+    conv_tc_kernel<BN, KC, UP><<<grid, TC_THREADS, cfg::SMEM, st>>>(tmA, tmB, p);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+bool conv_tc_supported(bool up, int IC, int OC) {
+    const int N = up ? 4 * OC : OC;
+    if (IC % 32 != 0 || OC % 16 != 0) return false;
+    if (IC == 32) return !up && N == 32;
+    return IC % 64 == 0 && (N >= 256 ? N % 256 == 0 : (N == 128 || N == 64));
+}
+
+cudaError_t launch_conv_tc(bool up, const conv_params &p, cudaStream_t st) {
+    const int N = up ? 4 * p.OC : p.OC;
+    if (!conv_tc_supported(up, p.IC, p.OC) || !p.err) return cudaErrorInvalidValue;
+    if (p.IC == 32) return run_tc<32, 32, false>(p, p.err, st);
+    if (N >= 256) return up ? run_tc<256, 64, true>(p, p.err, st) : run_tc<256, 64, false>(p, p.err, st);
+    if (N == 128) return up ? run_tc<128, 64, true>(p, p.err, st) : run_tc<128, 64, false>(p, p.err, st);
+    return up ? run_tc<64, 64, true>(p, p.err, st) : run_tc<64, 64, false>(p, p.err, st);
+}
+
 }  // namespace tpmd

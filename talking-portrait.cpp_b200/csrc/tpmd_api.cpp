@@ -95,6 +95,7 @@ struct tpmd_ctx {
     void *actA = nullptr, *actB = nullptr, *actC = nullptr;
     float *sf[2] = {nullptr, nullptr}, *sk[2] = {nullptr, nullptr};
     float *frames_d[2] = {nullptr, nullptr};  // device staging for host decode
+    int *err_flag = nullptr;                   // set by kernels whose bounded waits expired
 
     std::list<graph_entry> graphs;  // most recently used first
 
@@ -288,6 +289,7 @@ bool alloc_workspace(tpmd_ctx *c) {
     take(B * skip * 4);
     take(B * frame * 4);
     take(B * frame * 4);
+    take(256);
     if (!c->ck(cudaMalloc(&c->ws, off), "cudaMalloc(workspace)")) return false;
     c->ws_bytes = off;
     char *p = (char *) c->ws;
@@ -305,7 +307,8 @@ bool alloc_workspace(tpmd_ctx *c) {
     c->sk[1] = (float *) (p + offs[i++]);
     c->frames_d[0] = (float *) (p + offs[i++]);
     c->frames_d[1] = (float *) (p + offs[i++]);
-    return true;
+    c->err_flag = (int *) (p + offs[i++]);
+    return c->ck(cudaMemset(c->err_flag, 0, 256), "cudaMemset");
 }
 
 void to_half(const float *src, size_t n, __half *dst) {
@@ -441,8 +444,10 @@ tpmd_ctx *tpmd_create(int device, int dtype, int max_batch) {
     c->dtype = dtype;
     c->f16 = dtype == TPMD_DTYPE_F16;
     c->max_batch = max_batch;
-    const char *cv = getenv("TPMD_CONV");  // A/B knob: "tc" / "simt"
-    c->use_tc = c->f16 && cv && strcmp(cv, "tc") == 0;
+    // f16 convs run on tcgen05; TPMD_CONV=simt selects the FFMA kernels
+    // instead (an A/B knob, like the reference's TP_MDEC_* switches)
+    const char *cv = getenv("TPMD_CONV");
+    c->use_tc = c->f16 && !(cv && strcmp(cv, "simt") == 0);
     c->use_graph = getenv("TPMD_NO_GRAPH") == nullptr;
     c->spec = tensor_spec();
     build_layout(c);
@@ -664,6 +669,7 @@ bool enqueue_chunk(tpmd_ctx *c, const float *styles, int64_t nb, float *out, cud
         p.bias = c->Wf(L.abias);
         p.snext = snext;
         p.snext_stride = c->S_TOT;
+        p.err = c->err_flag;
         std::string name = k == 0 ? "conv1" : (L.up ? "upconv_r" : "conv2_r") +
                                                    std::to_string(L.up ? 2 * Hh : Hh);
         return launch(c, name, st, [&] {
@@ -740,6 +746,17 @@ bool run_chunk(tpmd_ctx *c, const float *styles, int64_t nb, float *out, cudaStr
     return c->ck(cudaGraphLaunch(exec, st), "cudaGraphLaunch");
 }
 
+// a kernel reports an expired bounded wait through the device flag
+bool device_ok(tpmd_ctx *c) {
+    int flag = 0;
+    if (!c->ck(cudaMemcpy(&flag, c->err_flag, 4, cudaMemcpyDeviceToHost), "error flag D2H")) return false;
+    if (flag) {
+        cudaMemset(c->err_flag, 0, 4);
+        return c->fail("a decoder kernel timed out waiting on its pipeline (results invalid)");
+    }
+    return true;
+}
+
 bool ready(tpmd_ctx *c) {
     if (!c->wready) return c->fail("weights not prepared (tpmd_prepare)");
     if (!c->fready) return c->fail("feats not set (tpmd_set_feats)");
@@ -777,7 +794,7 @@ int tpmd_decode_taps(tpmd_ctx *c, const float *style, int level, float *conv1, f
                                c->stream),
                "style H2D") ||
         !enqueue_chunk(c, c->styles_d[0], 1, c->frames_d[0], c->stream, level) ||
-        !c->ck(cudaStreamSynchronize(c->stream), "sync"))
+        !c->ck(cudaStreamSynchronize(c->stream), "sync") || !device_ok(c))
         return -1;
     const int r = 8 << level, OC = ST_OC[level];
     const size_t n = (size_t) r * r * OC;
@@ -873,7 +890,7 @@ int tpmd_decode(tpmd_ctx *c, const float *styles, int64_t n, float *frames) {
             return -1;
     }
     if (!c->ck(cudaStreamSynchronize(c->copy_stream), "sync") ||
-        !c->ck(cudaStreamSynchronize(c->stream), "sync"))
+        !c->ck(cudaStreamSynchronize(c->stream), "sync") || !device_ok(c))
         return -1;
     return 0;
 }

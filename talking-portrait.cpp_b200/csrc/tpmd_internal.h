@@ -36,6 +36,7 @@ struct conv_params {
     const float *bias;
     const float *snext;
     int snext_stride;
+    int *err;  // device flag a kernel sets when a bounded wait expires
 };
 
 // The per-level tail after conv2 (ToFlow, flow head, bilinear warp of the

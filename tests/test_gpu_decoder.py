@@ -152,3 +152,29 @@ def test_stress_random_init(stress_model):
         print(f"stress frame {i}: f32 cos {c32:.7f}; f16 ssim {s16:.4f} vs reference-f16 {sref:.4f}")
         assert c32 >= 0.9999
         assert s16 >= sref - 0.01
+
+
+def _dec_with_conv(model, kind):
+    import os
+    old = os.environ.get("TPMD_CONV")
+    os.environ["TPMD_CONV"] = kind
+    try:
+        return make_dec(model, tpmd.DTYPE_F16)
+    finally:
+        if old is None:
+            del os.environ["TPMD_CONV"]
+        else:
+            os.environ["TPMD_CONV"] = old
+
+
+@pytest.mark.parametrize("level", range(7))
+def test_tcgen05_matches_simt_f16(model, level):
+    """the tcgen05 convs against the FFMA convs on identical f16 storage:
+    only the accumulation order differs"""
+    tc, simt = _dec_with_conv(model, "tc"), _dec_with_conv(model, "simt")
+    lat = model["styles"][0]
+    a, b = tc.taps(lat, level), simt.taps(lat, level)
+    for k in a:
+        c = cosine(a[k], b[k])
+        print(f"level {level} {k}: tc vs simt cos {c:.9f} max-abs {max_abs(a[k], b[k]):.3e}")
+        assert c >= 0.9999, (level, k, c)
