@@ -110,6 +110,26 @@ int tpmd_profile_end(tpmd_ctx *ctx, char *json, size_t cap);
 /* Kernel launches one decode of n frames issues (for accounting). */
 int64_t tpmd_kernel_launches(const tpmd_ctx *ctx, int64_t n);
 
+/* Decode without allocating anything. This entry point has no counterpart
+ * in the reference; it exists for callers that must not allocate GPU memory
+ * at decode time: code running while a CUDA graph is being captured (where
+ * cudaMalloc is not allowed), real-time frame loops that cannot risk an
+ * allocator stall or failure mid-stream, and hosts whose memory manager owns
+ * the whole GPU and forbids other allocations. Instead of the handle's
+ * workspace it uses one static device array of 48 MiB inside this library,
+ * enough for one f16 frame, so it accepts n = 1 frame per call on a handle
+ * created with TPMD_DTYPE_F16 and rejects anything larger with an error.
+ * Every GPU that loads the library holds the array until process exit. The
+ * first call on each device looks up the array's device address (make that
+ * first call before any stream capture); later calls only enqueue kernels on
+ * `stream` (NULL = legacy default stream), without host synchronisation. All
+ * calls share the array and it keeps the last call's contents, so calls whose
+ * work overlaps on the GPU (other streams, other threads, other handles on
+ * the same device) race and corrupt each other's frames. Pointers are device
+ * memory: styles_dev [n][512], frames_dev [n][3][512][512]. */
+int tpmd_decode_noalloc(tpmd_ctx *ctx, const float *styles_dev, int64_t n,
+                        float *frames_dev, void *stream);
+
 /* ---- op-level kernels with the patched-op semantics ------------------ */
 
 /* ggml_bilinear_gather / _planar / _sp (patches/ggml-tp-ops.patch:41-60,

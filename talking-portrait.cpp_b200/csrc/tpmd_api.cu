@@ -23,6 +23,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <list>
+#include <mutex>
 #include <map>
 #include <new>
 #include <string>
@@ -53,6 +54,15 @@ struct conv_layout {
 struct stage_layout {
     size_t fW = 0, fb = 0, fup = 0, rW = 0, rlb = 0, rb = 0, rup = 0, lin = 0;
     int fs_off = 0;  // ToFlow style offset
+};
+
+// the per-decode scratch a chunk runs in: the handle's workspace, or the
+// static array of tpmd_decode_noalloc
+struct ws_view {
+    float *s_all, *inv_den;
+    void *actA, *actB, *actC;
+    float *sf[2], *sk[2];
+    int *err;
 };
 
 struct graph_entry {
@@ -618,6 +628,11 @@ namespace {
 
 // Enqueue the decode of nb frames: styles (device, [nb][512]) -> out (device,
 // [nb][3][512][512]).
+ws_view ctx_ws(const tpmd_ctx *c) {
+    return ws_view{c->s_all, c->inv_den, c->actA, c->actB, c->actC,
+                   {c->sf[0], c->sf[1]}, {c->sk[0], c->sk[1]}, c->err_flag};
+}
+
 // one kernel launch, bracketed by CUDA events while profiling
 template <typename F>
 bool launch(tpmd_ctx *c, const std::string &name, cudaStream_t st, F &&fn) {
@@ -635,23 +650,23 @@ bool launch(tpmd_ctx *c, const std::string &name, cudaStream_t st, F &&fn) {
     return true;
 }
 
-bool enqueue_chunk(tpmd_ctx *c, const float *styles, int64_t nb, float *out, cudaStream_t st,
-                   int last_level = N_LEVELS - 1) {
+bool enqueue_chunk(tpmd_ctx *c, const ws_view &w, const float *styles, int64_t nb, float *out,
+                   cudaStream_t st, int last_level = N_LEVELS - 1) {
     const bool h = c->f16;
     const int B = (int) nb;
     if (!launch(c, "style", st, [&] {
             return launch_style(c->Wf(c->off_wmod), c->Wf(c->off_bmod), c->S_TOT, styles, B,
-                                c->s_all, st);
+                                w.s_all, st);
         }))
         return false;
     if (!launch(c, "den", st, [&] {
-            return launch_den((const float *) c->warena, c->dtab, c->s_all, c->S_TOT, B,
-                              c->inv_den, c->D_TOT, st);
+            return launch_den((const float *) c->warena, c->dtab, w.s_all, c->S_TOT, B,
+                              w.inv_den, c->D_TOT, st);
         }))
         return false;
     if (!launch(c, "conv1_input", st, [&] {
-            return launch_conv1_input(h, c->Wf(c->off_input), c->s_all + c->conv[0].s_off,
-                                      c->S_TOT, B, c->actA, st);
+            return launch_conv1_input(h, c->Wf(c->off_input), w.s_all + c->conv[0].s_off,
+                                      c->S_TOT, B, w.actA, st);
         }))
         return false;
     auto conv = [&](int k, const void *x, void *y, int Hh, const float *snext) {
@@ -664,12 +679,12 @@ bool enqueue_chunk(tpmd_ctx *c, const float *styles, int64_t nb, float *out, cud
         p.H = p.W = Hh;
         p.IC = L.IC;
         p.OC = L.OC;
-        p.inv_den = c->inv_den + L.d_off;
+        p.inv_den = w.inv_den + L.d_off;
         p.den_stride = c->D_TOT;
         p.bias = c->Wf(L.abias);
         p.snext = snext;
         p.snext_stride = c->S_TOT;
-        p.err = c->err_flag;
+        p.err = w.err;
         std::string name = k == 0 ? "conv1" : (L.up ? "upconv_r" : "conv2_r") +
                                                    std::to_string(L.up ? 2 * Hh : Hh);
         return launch(c, name, st, [&] {
@@ -677,38 +692,38 @@ bool enqueue_chunk(tpmd_ctx *c, const float *styles, int64_t nb, float *out, cud
         });
     };
     // conv1: 4x4 map, output x style of convs.0 -> trunk buffer
-    if (!conv(0, c->actA, c->actB, 4, c->s_all + c->conv[1].s_off)) return false;
+    if (!conv(0, w.actA, w.actB, 4, w.s_all + c->conv[1].s_off)) return false;
     for (int j = 0; j <= last_level; j++) {
         const int r = 8 << j;
         const conv_layout &Lu = c->conv[1 + 2 * j], &Ld = c->conv[2 + 2 * j];
         // up-conv: trunk (x its style) -> c1 (x conv2's style)
-        if (!conv(1 + 2 * j, c->actB, c->actC, r / 2, c->s_all + Ld.s_off)) return false;
+        if (!conv(1 + 2 * j, w.actB, w.actC, r / 2, w.s_all + Ld.s_off)) return false;
         // conv2: c1 -> out (unscaled, read by the tail)
-        if (!conv(2 + 2 * j, c->actC, c->actA, r, nullptr)) return false;
+        if (!conv(2 + 2 * j, w.actC, w.actA, r, nullptr)) return false;
         (void) Lu;
         const stage_layout &S = c->stage[j];
         tail_params t{};
-        t.out = c->actA;
+        t.out = w.actA;
         t.feat = (const char *) c->farena + c->feat_off[j];
         t.B = B;
         t.r = r;
         t.OC = ST_OC[j];
         t.fW = c->Wf(S.fW);
-        t.fs = c->s_all + S.fs_off;
+        t.fs = w.s_all + S.fs_off;
         t.s_stride = c->S_TOT;
         t.fb = c->Wf(S.fb);
         t.fup = c->Wf(S.fup);
-        t.skipf_prev = j == 0 ? nullptr : c->sf[(j - 1) & 1];
-        t.skipf_out = j == N_LEVELS - 1 ? nullptr : c->sf[j & 1];
+        t.skipf_prev = j == 0 ? nullptr : w.sf[(j - 1) & 1];
+        t.skipf_out = j == N_LEVELS - 1 ? nullptr : w.sf[j & 1];
         t.rW = c->Wf(S.rW);
         t.rlb = c->Wf(S.rlb);
         t.rb = c->Wf(S.rb);
         t.rup = c->Wf(S.rup);
-        t.skip_prev = j == 0 ? nullptr : c->sk[(j - 1) & 1];
-        t.skip_out = j == N_LEVELS - 1 ? out : c->sk[j & 1];
+        t.skip_prev = j == 0 ? nullptr : w.sk[(j - 1) & 1];
+        t.skip_out = j == N_LEVELS - 1 ? out : w.sk[j & 1];
         t.lin = c->Wf(S.lin);
-        t.trunk = j == N_LEVELS - 1 ? nullptr : c->actB;
-        t.snext = j == N_LEVELS - 1 ? nullptr : c->s_all + c->conv[3 + 2 * j].s_off;
+        t.trunk = j == N_LEVELS - 1 ? nullptr : w.actB;
+        t.snext = j == N_LEVELS - 1 ? nullptr : w.s_all + c->conv[3 + 2 * j].s_off;
         if (!launch(c, "tail_r" + std::to_string(r), st, [&] { return launch_tail(h, t, st); }))
             return false;
     }
@@ -716,7 +731,7 @@ bool enqueue_chunk(tpmd_ctx *c, const float *styles, int64_t nb, float *out, cud
 }
 
 bool run_chunk(tpmd_ctx *c, const float *styles, int64_t nb, float *out, cudaStream_t st) {
-    if (!c->use_graph || c->profiling) return enqueue_chunk(c, styles, nb, out, st);
+    if (!c->use_graph || c->profiling) return enqueue_chunk(c, ctx_ws(c), styles, nb, out, st);
     for (auto it = c->graphs.begin(); it != c->graphs.end(); ++it) {
         if (it->nb == nb && it->styles == styles && it->out == out) {
             c->graphs.splice(c->graphs.begin(), c->graphs, it);
@@ -727,7 +742,7 @@ bool run_chunk(tpmd_ctx *c, const float *styles, int64_t nb, float *out, cudaStr
     if (!c->ck(cudaStreamBeginCapture(c->cap_stream, cudaStreamCaptureModeThreadLocal),
                "begin capture"))
         return false;
-    const bool ok = enqueue_chunk(c, styles, nb, out, c->cap_stream);
+    const bool ok = enqueue_chunk(c, ctx_ws(c), styles, nb, out, c->cap_stream);
     const cudaError_t e = cudaStreamEndCapture(c->cap_stream, &g);
     if (!ok) {
         if (g) cudaGraphDestroy(g);
@@ -793,7 +808,7 @@ int tpmd_decode_taps(tpmd_ctx *c, const float *style, int level, float *conv1, f
         !c->ck(cudaMemcpyAsync(c->styles_d[0], style, STYLE_DIM * 4, cudaMemcpyHostToDevice,
                                c->stream),
                "style H2D") ||
-        !enqueue_chunk(c, c->styles_d[0], 1, c->frames_d[0], c->stream, level) ||
+        !enqueue_chunk(c, ctx_ws(c), c->styles_d[0], 1, c->frames_d[0], c->stream, level) ||
         !c->ck(cudaStreamSynchronize(c->stream), "sync") || !device_ok(c))
         return -1;
     const int r = 8 << level, OC = ST_OC[level];
@@ -896,3 +911,87 @@ int tpmd_decode(tpmd_ctx *c, const float *styles, int64_t n, float *frames) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Decoding without any allocation: the per-decode scratch lives in a static
+// device array of this library instead of the handle's workspace.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr size_t NOALLOC_BYTES = (size_t) 48 << 20;  // 48 MiB: one f16 frame's scratch
+constexpr int NOALLOC_MAX_FRAMES = 1;
+
+// Shared by every call on a device and kept between calls.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[NOALLOC_BYTES];
+
+std::mutex g_noalloc_mu;
+void *g_noalloc_addr[64] = {nullptr};  // device address of the array, per device
+
+// carve one frame's workspace out of the static array; false if it does not fit
+bool noalloc_view(const tpmd_ctx *c, char *base, ws_view &w) {
+    size_t a, b, cc;
+    act_sizes(a, b, cc);
+    const size_t skip = (size_t) 3 * 256 * 256;
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        char *p = base + off;
+        off = align256(off + bytes);
+        return p;
+    };
+    w.s_all = (float *) take((size_t) c->S_TOT * 4);
+    w.inv_den = (float *) take((size_t) c->D_TOT * 4);
+    w.actA = take(a * c->esz());
+    w.actB = take(b * c->esz());
+    w.actC = take(cc * c->esz());
+    for (int i = 0; i < 2; i++) w.sf[i] = (float *) take(skip * 4);
+    for (int i = 0; i < 2; i++) w.sk[i] = (float *) take(skip * 4);
+    w.err = (int *) take(256);
+    return off <= NOALLOC_BYTES;
+}
+
+}  // namespace
+
+extern "C" int tpmd_decode_noalloc(tpmd_ctx *c, const float *styles_dev, int64_t n,
+                                   float *frames_dev, void *stream) {
+    if (!c) return -1;
+    if (!styles_dev || !frames_dev) return c->fail("tpmd_decode_noalloc: null pointer"), -1;
+    if (n < 1 || n > NOALLOC_MAX_FRAMES)
+        return c->fail("tpmd_decode_noalloc: n = " + std::to_string(n) +
+                       " frames exceeds its static scratch (at most " +
+                       std::to_string(NOALLOC_MAX_FRAMES) + " frame per call)"),
+               -1;
+    if (!c->f16)
+        return c->fail("tpmd_decode_noalloc: the static scratch holds f16 activations only "
+                       "(create the handle with TPMD_DTYPE_F16)"),
+               -1;
+    if (!ready(c)) return -1;
+    if (c->device < 0 || c->device >= 64) return c->fail("tpmd_decode_noalloc: device index"), -1;
+    if (!c->ck(cudaSetDevice(c->device), "cudaSetDevice")) return -1;
+    char *base = nullptr;
+    {
+        // once per device, with that device current: the host-side name of the
+        // array is not a device address, so ask the runtime for the real one
+        std::lock_guard<std::mutex> lk(g_noalloc_mu);
+        if (!g_noalloc_addr[c->device]) {
+            void *p = nullptr;
+            const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+            if (e != cudaSuccess)
+                return c->fail(std::string("tpmd_decode_noalloc: cudaGetSymbolAddress: ") +
+                               cudaGetErrorString(e)),
+                       -1;
+            g_noalloc_addr[c->device] = p;
+        }
+        base = (char *) g_noalloc_addr[c->device];
+    }
+    ws_view w;
+    if (!noalloc_view(c, base, w)) return c->fail("tpmd_decode_noalloc: scratch layout too large"), -1;
+    cudaStream_t st = (cudaStream_t) stream;
+    // the error flag must start each call at zero; everything else is written
+    // before it is read
+    if (!c->ck(cudaMemsetAsync(w.err, 0, sizeof(int), st), "cudaMemsetAsync")) return -1;
+    const bool prof = c->profiling;
+    c->profiling = false;  // no events: they would be allocations
+    const bool ok = enqueue_chunk(c, w, styles_dev, n, frames_dev, st);
+    c->profiling = prof;
+    return ok ? 0 : -1;
+}

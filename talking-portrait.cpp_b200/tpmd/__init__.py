@@ -34,7 +34,7 @@ EXPORTS = ("tpmd_abi_version", "tpmd_create", "tpmd_create_error", "tpmd_destroy
            "tpmd_last_error", "tpmd_scale_for", "tpmd_set_tensor", "tpmd_prepare",
            "tpmd_set_feats", "tpmd_batch", "tpmd_decode", "tpmd_decode_device",
            "tpmd_arena", "tpmd_arena_adopt", "tpmd_decode_taps", "tpmd_profile_begin", "tpmd_profile_end",
-           "tpmd_kernel_launches",
+           "tpmd_kernel_launches", "tpmd_decode_noalloc",
            "tpk_bilinear_gather", "tpk_im2col_cf", "tpk_last_error")
 
 _lib = None
@@ -75,6 +75,7 @@ def load_library(path: str = LIB_PATH):
     L.tpmd_profile_begin.argtypes = [v]
     L.tpmd_profile_end.argtypes = [v, C.c_char_p, C.c_size_t]
     L.tpmd_kernel_launches.argtypes = [v, i64]
+    L.tpmd_decode_noalloc.argtypes = [v, v, i64, v, v]
     L.tpmd_kernel_launches.restype = i64
     L.tpk_bilinear_gather.argtypes = [v, C.c_int, C.c_int, C.c_int, C.c_int, v, i64, C.c_int,
                                       C.c_int, v, v]
