@@ -56,6 +56,13 @@ def kernel_work(name: str, nb: int, esz: int):
         flops = 2.0 * 16 * 512 * 4608 * nb
         byts = nb * 16 * 512 * esz * 2 + 512 * 4608 * esz
         return flops, byts
+    if name.startswith("conv2tail_r"):  # conv2 with the level tail fused
+        r = int(name[len("conv2tail_r"):])
+        f, b = kernel_work(f"conv2_r{r}", nb, esz)
+        f2, b2 = kernel_work(f"tail_r{r}", nb, esz)
+        j = (r // 8).bit_length() - 1
+        # the conv2 output never reaches HBM: drop its write and the tail's read
+        return f, b + b2 - 2 * nb * r * r * ST_OC[j] * esz
     for pre, up in (("upconv_r", True), ("conv2_r", False)):
         if name.startswith(pre):
             r = int(name[len(pre):])

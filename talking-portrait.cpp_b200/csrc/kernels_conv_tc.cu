@@ -35,7 +35,6 @@
 namespace tpmd {
 namespace {
 
-constexpr int TC_THREADS = 192;
 constexpr int BM = 128;
 
 struct tc_params {
@@ -51,6 +50,17 @@ struct tc_params {
     const float *snext;
     int snext_stride;
     int *err;
+    // fused level tail (conv2 kernels of the levels with OC <= 256)
+    const __half *feat;
+    const float *fW, *fs;
+    int s_stride;
+    const float *fb, *fup, *skipf_prev;
+    float *skipf_out;
+    const float *rW, *rlb, *rb, *rup, *skip_prev;
+    float *skip_out;
+    const float *lin;
+    __half *trunk;
+    const float *tsn;  // next up-conv style, multiplied into the trunk
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -152,20 +162,27 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-template <int BN, int KC>
+template <int BN, int KC, int NACC, bool TAIL>
 struct tc_cfg {
     static constexpr int A_BYTES = BM * KC * 2;
     static constexpr int B_BYTES = BN * KC * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int STAGES = (196608 / STAGE_BYTES) > 8 ? 8 : (196608 / STAGE_BYTES);
-    static constexpr uint32_t TMEM_COLS = 2 * BN;  // two accumulators; 64..512, a power of 2
+    // fused tail: the ToRGB weights [3][BN], shared by all epilogue groups
+    static constexpr int EXTRA = TAIL ? 3 * BN * 4 : 0;
+    static constexpr int STAGES =
+        ((212992 - EXTRA) / STAGE_BYTES) > 8 ? 8 : ((212992 - EXTRA) / STAGE_BYTES);
+    static constexpr uint32_t TMEM_COLS = NACC * BN;  // one accumulator per epilogue group
+    static constexpr int THREADS = 64 + 128 * NACC;
     static constexpr uint32_t LAYOUT = KC == 64 ? 2u : 4u;
     static constexpr uint32_t SBO = KC == 64 ? 1024u : 512u;
     // kind::f16 instruction descriptor: D f32, A/B f16, both K-major, N, M
     static constexpr uint32_t IDESC =
         (1u << 4) | ((uint32_t) (BN >> 3) << 17) | ((uint32_t) (BM >> 4) << 24);
-    static constexpr int NBARS = 2 * STAGES + 5;
-    static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + NBARS * 8 + 16;
+    static constexpr int NBARS = 2 * STAGES + 2 * NACC + 1;
+    static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + EXTRA + NBARS * 8 + 16;
+    static_assert((TMEM_COLS & (TMEM_COLS - 1)) == 0 && TMEM_COLS >= 32 && TMEM_COLS <= 512, "TMEM");
+    static_assert(SMEM <= 232448, "shared memory");
+    static_assert(STAGES >= 2, "pipeline depth");
 };
 
 struct tile_pos {
@@ -186,22 +203,81 @@ __device__ __forceinline__ tile_pos tile_of(const tc_params &p, int64_t t, int B
     return r;
 }
 
-template <int BN, int KC, bool UP>
-__global__ void __launch_bounds__(TC_THREADS, 1)
+// upfirdn2d(up=2, pad=(2,1)) of an h x h plane at output (x, y): the two
+// source rows/columns of matching parity, in the reference op's tap order
+// (patch:559-569, rows outer, columns inner)
+__device__ __forceinline__ float up2x_at(const float *__restrict__ src, const float *__restrict__ k4,
+                                         int x, int y, int h) {
+    const int px = x & 1, py = y & 1, nx = x >> 1, ny = y >> 1;
+    float acc = 0.0f;
+#pragma unroll
+    for (int a = 0; a < 2; a++) {
+        const int sy = ny + py - 1 + a;
+        if (sy < 0 || sy >= h) continue;
+#pragma unroll
+        for (int b = 0; b < 2; b++) {
+            const int sx = nx + px - 1 + b;
+            if (sx < 0 || sx >= h) continue;
+            acc = fmaf(__ldg(src + sy * h + sx), __ldg(k4 + (px + 2 * b) + 4 * (py + 2 * a)), acc);
+        }
+    }
+    return acc;
+}
+
+// 16 consecutive floats (64-byte aligned) through the read-only path
+__device__ __forceinline__ void ld_f16x(const float *p, float *v) {
+    const float4 *q = reinterpret_cast<const float4 *>(p);
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const float4 u = __ldg(q + j);
+        v[4 * j] = u.x;
+        v[4 * j + 1] = u.y;
+        v[4 * j + 2] = u.z;
+        v[4 * j + 3] = u.w;
+    }
+}
+
+__device__ __forceinline__ void ld_half16(const __half *p, float *v) {
+    const uint4 *q = reinterpret_cast<const uint4 *>(p);
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+        const uint4 u = __ldg(q + j);
+        const __half2 *h = reinterpret_cast<const __half2 *>(&u);
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const float2 f = __half22float2(h[k]);
+            v[8 * j + 2 * k] = f.x;
+            v[8 * j + 2 * k + 1] = f.y;
+        }
+    }
+}
+__device__ __forceinline__ void st_half16(__half *p, const float *v) {
+    uint4 pk[2];
+    __half2 *h2 = reinterpret_cast<__half2 *>(pk);
+#pragma unroll
+    for (int i = 0; i < 8; i++) h2[i] = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+    uint4 *q = reinterpret_cast<uint4 *>(p);
+    q[0] = pk[0];
+    q[1] = pk[1];
+}
+
+template <int BN, int KC, bool UP, int NACC, bool TAIL>
+__global__ void __launch_bounds__(tc_cfg<BN, KC, NACC, TAIL>::THREADS, 1)
 conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const tc_params p) {
-    using cfg = tc_cfg<BN, KC>;
+    using cfg = tc_cfg<BN, KC, NACC, TAIL>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = (uint8_t *) (((uintptr_t) smem_raw + 1023) & ~(uintptr_t) 1023);
     uint8_t *sA = smem;
     uint8_t *sB = smem + cfg::STAGES * cfg::A_BYTES;
-    uint64_t *bars = (uint64_t *) (smem + cfg::STAGES * cfg::STAGE_BYTES);
+    float *sx = (float *) (smem + cfg::STAGES * cfg::STAGE_BYTES);  // TAIL constants
+    uint64_t *bars = (uint64_t *) (smem + cfg::STAGES * cfg::STAGE_BYTES + cfg::EXTRA);
     uint32_t *tmem_slot = (uint32_t *) (bars + cfg::NBARS);
     auto full = [&](int s) { return smem_u32(&bars[s]); };
     auto empty = [&](int s) { return smem_u32(&bars[cfg::STAGES + s]); };
     auto tfull = [&](int a) { return smem_u32(&bars[2 * cfg::STAGES + a]); };
-    auto tempty = [&](int a) { return smem_u32(&bars[2 * cfg::STAGES + 2 + a]); };
-    const uint32_t drain = smem_u32(&bars[2 * cfg::STAGES + 4]);
+    auto tempty = [&](int a) { return smem_u32(&bars[2 * cfg::STAGES + NACC + a]); };
+    const uint32_t drain = smem_u32(&bars[2 * cfg::STAGES + 2 * NACC]);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
@@ -209,13 +285,16 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             mbar_init(full(s), 1);
             mbar_init(empty(s), 1);
         }
-        for (int a = 0; a < 2; a++) {
+        for (int a = 0; a < NACC; a++) {
             mbar_init(tfull(a), 1);
             mbar_init(tempty(a), 4);
         }
         mbar_init(drain, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (TAIL) {
+        for (int i = threadIdx.x; i < 3 * BN; i += blockDim.x) sx[i] = __ldg(p.rW + i);
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -263,12 +342,12 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            // ---- MMA issuer
-            uint32_t it = 0, tcount = 0;
+            // ---- MMA issuer: tile k of this CTA accumulates into buffer k % NACC
+            uint32_t it = 0, k = 0;
             bool ok = true;
-            for (int64_t t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x, tcount++) {
-                const int a = tcount & 1;
-                if (!mbar_wait(tempty(a), ((tcount >> 1) & 1) ^ 1)) {
+            for (int64_t t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x, k++) {
+                const int a = k % NACC;
+                if (!mbar_wait(tempty(a), ((k / NACC) & 1) ^ 1)) {
                     ok = false;
                     break;
                 }
@@ -284,8 +363,8 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     const uint64_t ad = smem_desc(smem_u32(sA + s * cfg::A_BYTES), cfg::SBO, cfg::LAYOUT);
                     const uint64_t bd = smem_desc(smem_u32(sB + s * cfg::B_BYTES), cfg::SBO, cfg::LAYOUT);
 #pragma unroll
-                    for (int k = 0; k < KC / 16; k++)  // +32 bytes along K per step
-                        umma_f16(d_tmem, ad + 2 * k, bd + 2 * k, cfg::IDESC, (kk | k) != 0);
+                    for (int kx = 0; kx < KC / 16; kx++)  // +32 bytes along K per step
+                        umma_f16(d_tmem, ad + 2 * kx, bd + 2 * kx, cfg::IDESC, (kk | kx) != 0);
                     umma_commit(empty(s));
                 }
                 if (!ok) break;
@@ -296,14 +375,18 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             mbar_wait(drain, 0);
         }
     } else {
-        // ---- epilogue: warps 2..5, TMEM lane quarter = warp % 4
+        // ---- epilogue group g = (warp-2)/4 owns accumulator g and the CTA's
+        // tiles k = g, g+NACC, ...; each warp reads TMEM lane quarter warp % 4
+        const int g = (warp - 2) >> 2;
         const int q = warp & 3;
         const int row = q * 32 + lane;
         const int bx = row % p.bw, by = (row / p.bw) % p.bh, bz = row / (p.bw * p.bh);
-        uint32_t tcount = 0;
-        for (int64_t t = blockIdx.x; t < p.num_tiles; t += gridDim.x, tcount++) {
-            const int a = tcount & 1;
-            const bool ok = __all_sync(0xffffffffu, mbar_wait(tfull(a), (tcount >> 1) & 1));
+        const uint32_t taddr0 = tmem_base + ((uint32_t) (q * 32) << 16) + g * BN;
+        const float *s_rw = sx;
+        uint32_t k = g;
+        for (int64_t t = blockIdx.x + (int64_t) g * gridDim.x; t < p.num_tiles;
+             t += (int64_t) NACC * gridDim.x, k += NACC) {
+            const bool ok = __all_sync(0xffffffffu, mbar_wait(tfull(g), (k / NACC) & 1));
             if (!ok) {
                 if (lane == 0) atomicExch(p.err, 1);
                 break;
@@ -311,61 +394,157 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             tc_fence_after();
             const tile_pos tp = tile_of(p, t, BN);
             const int b = tp.b0 + bz, y = tp.y0 + by, x = tp.x0 + bx;
-            const bool valid = b < p.B;
-            const uint32_t taddr = tmem_base + ((uint32_t) (q * 32) << 16) + a * BN;
+            if constexpr (!TAIL) {
+                const bool valid = b < p.B;
 #pragma unroll 1
-            for (int c0 = 0; c0 < BN; c0 += 16) {
-                uint32_t r[16];
-                tmem_ld16(taddr + c0, r);
-                if (!valid) continue;
-                const int n = tp.n0 + c0;
-                const int o0 = UP ? n % p.OC : n;
-                float den[16], bias[16], sn[16];
-                const float4 *dp = reinterpret_cast<const float4 *>(p.inv_den + (int64_t) b * p.den_stride + o0);
-                const float4 *bp = reinterpret_cast<const float4 *>(p.bias + o0);
-#pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    const float4 dv = __ldg(dp + i), bv = __ldg(bp + i);
-                    den[4 * i] = dv.x; den[4 * i + 1] = dv.y; den[4 * i + 2] = dv.z; den[4 * i + 3] = dv.w;
-                    bias[4 * i] = bv.x; bias[4 * i + 1] = bv.y; bias[4 * i + 2] = bv.z; bias[4 * i + 3] = bv.w;
-                }
-                if (p.snext) {
-                    const float4 *sp = reinterpret_cast<const float4 *>(p.snext + (int64_t) b * p.snext_stride + o0);
+                for (int c0 = 0; c0 < BN; c0 += 16) {
+                    uint32_t r[16];
+                    tmem_ld16(taddr0 + c0, r);
+                    if (!valid) continue;
+                    const int n = tp.n0 + c0;
+                    const int o0 = UP ? n % p.OC : n;
+                    float den[16], bias[16], sn[16];
+                    const float4 *dp =
+                        reinterpret_cast<const float4 *>(p.inv_den + (int64_t) b * p.den_stride + o0);
+                    const float4 *bp = reinterpret_cast<const float4 *>(p.bias + o0);
 #pragma unroll
                     for (int i = 0; i < 4; i++) {
-                        const float4 sv = __ldg(sp + i);
-                        sn[4 * i] = sv.x; sn[4 * i + 1] = sv.y; sn[4 * i + 2] = sv.z; sn[4 * i + 3] = sv.w;
+                        const float4 dv = __ldg(dp + i), bv = __ldg(bp + i);
+                        den[4 * i] = dv.x; den[4 * i + 1] = dv.y; den[4 * i + 2] = dv.z; den[4 * i + 3] = dv.w;
+                        bias[4 * i] = bv.x; bias[4 * i + 1] = bv.y; bias[4 * i + 2] = bv.z; bias[4 * i + 3] = bv.w;
                     }
-                }
-                uint4 pk[2];
-                __half2 *h2 = reinterpret_cast<__half2 *>(pk);
-#pragma unroll
-                for (int i = 0; i < 8; i++) {
-                    float v0 = fmaf(__uint_as_float(r[2 * i]), den[2 * i], bias[2 * i]);
-                    float v1 = fmaf(__uint_as_float(r[2 * i + 1]), den[2 * i + 1], bias[2 * i + 1]);
-                    v0 = v0 > 0.0f ? v0 : 0.2f * v0;
-                    v1 = v1 > 0.0f ? v1 : 0.2f * v1;
                     if (p.snext) {
-                        v0 *= sn[2 * i];
-                        v1 *= sn[2 * i + 1];
+                        const float4 *sp =
+                            reinterpret_cast<const float4 *>(p.snext + (int64_t) b * p.snext_stride + o0);
+#pragma unroll
+                        for (int i = 0; i < 4; i++) {
+                            const float4 sv = __ldg(sp + i);
+                            sn[4 * i] = sv.x; sn[4 * i + 1] = sv.y; sn[4 * i + 2] = sv.z; sn[4 * i + 3] = sv.w;
+                        }
                     }
-                    h2[i] = __floats2half2_rn(v0, v1);
+                    float v[16];
+#pragma unroll
+                    for (int i = 0; i < 16; i++) {
+                        float a = fmaf(__uint_as_float(r[i]), den[i], bias[i]);
+                        a = a > 0.0f ? a : 0.2f * a;
+                        v[i] = p.snext ? a * sn[i] : a;
+                    }
+                    int64_t dst;
+                    if (UP) {
+                        const int cls = n / p.OC;
+                        const int Y = 2 * y + (cls >> 1), X = 2 * x + (cls & 1);
+                        dst = (((int64_t) b * 2 * p.H + Y) * 2 * p.W + X) * p.OC + o0;
+                    } else {
+                        dst = (((int64_t) b * p.H + y) * p.W + x) * p.OC + o0;
+                    }
+                    st_half16(p.y + dst, v);
                 }
-                int64_t dst;
-                if (UP) {
-                    const int cls = n / p.OC;
-                    const int Y = 2 * y + (cls >> 1), X = 2 * x + (cls & 1);
-                    dst = (((int64_t) b * 2 * p.H + Y) * 2 * p.W + X) * p.OC + o0;
-                } else {
-                    dst = (((int64_t) b * p.H + y) * p.W + x) * p.OC + o0;
+            } else {
+                // ---- conv2 + level tail (one tile = 128 pixels of one frame,
+                // BN = OC: every channel of a pixel is in this thread's TMEM lane)
+                const float *fden = p.inv_den + (int64_t) b * p.den_stride;
+                const float *ffs = p.fs + (int64_t) b * p.s_stride;
+                const float *fsn = p.trunk ? p.tsn + (int64_t) b * p.s_stride : nullptr;
+                const int r = p.W, h = r >> 1;
+                const int64_t pix = ((int64_t) b * p.H + y) * p.W + x;
+                // pass 1: conv2 output (f32, never stored) -> ToFlow sums
+                float f0 = 0.0f, f1 = 0.0f, f2 = 0.0f;
+#pragma unroll 1
+                for (int c0 = 0; c0 < BN; c0 += 16) {
+                    uint32_t rr[16];
+                    tmem_ld16(taddr0 + c0, rr);
+                    float den[16], bias[16], fsv[16], v[16];
+                    ld_f16x(fden + c0, den);
+                    ld_f16x(p.bias + c0, bias);
+                    ld_f16x(ffs + c0, fsv);
+#pragma unroll
+                    for (int i = 0; i < 16; i++) {
+                        float a = fmaf(__uint_as_float(rr[i]), den[i], bias[i]);
+                        a = a > 0.0f ? a : 0.2f * a;
+                        v[i] = a;
+                        const float xs = a * fsv[i];  // ToFlow input: out * style
+                        f0 = fmaf(__ldg(p.fW + c0 + i), xs, f0);
+                        f1 = fmaf(__ldg(p.fW + BN + c0 + i), xs, f1);
+                        f2 = fmaf(__ldg(p.fW + 2 * BN + c0 + i), xs, f2);
+                    }
+                    if (p.y) st_half16(p.y + pix * BN + c0, v);  // conv2 tap (debug)
                 }
-                uint4 *yp = reinterpret_cast<uint4 *>(p.y + dst);
-                yp[0] = pk[0];
-                yp[1] = pk[1];
+                float fl[3] = {f0 + __ldg(p.fb), f1 + __ldg(p.fb + 1), f2 + __ldg(p.fb + 2)};
+                if (p.skipf_prev) {
+#pragma unroll
+                    for (int kk = 0; kk < 3; kk++)
+                        fl[kk] += up2x_at(p.skipf_prev + ((int64_t) b * 3 + kk) * h * h, p.fup, x, y, h);
+                }
+                const int64_t rr2 = (int64_t) r * r;
+                if (p.skipf_out) {
+#pragma unroll
+                    for (int kk = 0; kk < 3; kk++) p.skipf_out[((int64_t) b * 3 + kk) * rr2 + (int64_t) y * r + x] = fl[kk];
+                }
+                const float gx = tanhf(fl[0]) + __ldg(p.lin + x);
+                const float gy = tanhf(fl[1]) + __ldg(p.lin + y);
+                const float m = 1.0f / (1.0f + expf(-fl[2]));
+                const float om = 1.0f - m;
+                // bilinear taps, as the patched gather computes them (patch:341-358)
+                const float fx = fmaf((gx + 1.0f) * 0.5f, (float) r, -0.5f);
+                const float fy = fmaf((gy + 1.0f) * 0.5f, (float) r, -0.5f);
+                const bool sane = fabsf(fx) < 1.0e8f && fabsf(fy) < 1.0e8f;
+                const float flx = floorf(fx), fly = floorf(fy);
+                const int x0 = sane ? (int) flx : -4, y0 = sane ? (int) fly : -4;
+                const float wx = fx - flx, wy = fy - fly;
+                int trow[4];
+                float twt[4];
+#pragma unroll
+                for (int kk = 0; kk < 4; kk++) {
+                    const int cx = x0 + (kk & 1), cy = y0 + (kk >> 1);
+                    trow[kk] = (sane && cx >= 0 && cx < r && cy >= 0 && cy < r) ? cy * r + cx : -1;
+                    twt[kk] = ((kk & 1) ? wx : 1.0f - wx) * ((kk >> 1) ? wy : 1.0f - wy);
+                }
+                // pass 2: gather, blend, ToRGB sums, trunk
+                float g0 = 0.0f, g1 = 0.0f, g2 = 0.0f;
+#pragma unroll 1
+                for (int c0 = 0; c0 < BN; c0 += 16) {
+                    uint32_t rr[16];
+                    tmem_ld16(taddr0 + c0, rr);
+                    float smp[16];
+#pragma unroll
+                    for (int i = 0; i < 16; i++) smp[i] = 0.0f;
+#pragma unroll
+                    for (int kk = 0; kk < 4; kk++) {
+                        if (trow[kk] < 0) continue;
+                        float f[16];
+                        ld_half16(p.feat + (int64_t) trow[kk] * BN + c0, f);
+#pragma unroll
+                        for (int i = 0; i < 16; i++) smp[i] = fmaf(twt[kk], f[i], smp[i]);
+                    }
+                    float den[16], bias[16], sn[16];
+                    ld_f16x(fden + c0, den);
+                    ld_f16x(p.bias + c0, bias);
+                    if (fsn) ld_f16x(fsn + c0, sn);
+#pragma unroll
+                    for (int i = 0; i < 16; i++) {
+                        float a = fmaf(__uint_as_float(rr[i]), den[i], bias[i]);
+                        a = a > 0.0f ? a : 0.2f * a;
+                        const float w = smp[i] * m;
+                        g0 = fmaf(s_rw[c0 + i], w, g0);
+                        g1 = fmaf(s_rw[BN + c0 + i], w, g1);
+                        g2 = fmaf(s_rw[2 * BN + c0 + i], w, g2);
+                        smp[i] = w + a * om;  // trunk
+                        if (fsn) smp[i] *= sn[i];  // x next up-conv style
+                    }
+                    if (p.trunk) st_half16(p.trunk + pix * BN + c0, smp);
+                }
+                const float rg[3] = {g0, g1, g2};
+#pragma unroll
+                for (int kk = 0; kk < 3; kk++) {
+                    float v = rg[kk] + __ldg(p.rlb + kk);
+                    v = (v > 0.0f ? v : 0.2f * v) + __ldg(p.rb + kk);
+                    if (p.skip_prev) v += up2x_at(p.skip_prev + ((int64_t) b * 3 + kk) * h * h, p.rup, x, y, h);
+                    p.skip_out[((int64_t) b * 3 + kk) * rr2 + (int64_t) y * r + x] = v;
+                }
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(tempty(a));
+            if (lane == 0) mbar_arrive(tempty(g));
         }
     }
     tc_fence_before();
@@ -403,9 +582,9 @@ int sm_count() {
     return n;
 }
 
-template <int BN, int KC, bool UP>
-cudaError_t run_tc(const conv_params &cp, int *err, cudaStream_t st) {
-    using cfg = tc_cfg<BN, KC>;
+template <int BN, int KC, bool UP, int NACC, bool TAIL>
+cudaError_t run_tc(const conv_params &cp, const tail_params *tl, cudaStream_t st) {
+    using cfg = tc_cfg<BN, KC, NACC, TAIL>;
     auto enc = encode_fn();
     if (!enc) return cudaErrorNotSupported;
     tc_params p{};
@@ -431,7 +610,28 @@ cudaError_t run_tc(const conv_params &cp, int *err, cudaStream_t st) {
     p.bias = cp.bias;
     p.snext = cp.snext;
     p.snext_stride = cp.snext_stride;
-    p.err = err;
+    p.err = cp.err;
+    if (TAIL) {
+        // one frame per tile and the whole channel range in one tile
+        if (!tl || p.bb != 1 || p.tiles_n != 1 || tl->OC != BN || tl->r != cp.W) return cudaErrorInvalidValue;
+        p.feat = (const __half *) tl->feat;
+        p.fW = tl->fW;
+        p.fs = tl->fs;
+        p.s_stride = tl->s_stride;
+        p.fb = tl->fb;
+        p.fup = tl->fup;
+        p.skipf_prev = tl->skipf_prev;
+        p.skipf_out = tl->skipf_out;
+        p.rW = tl->rW;
+        p.rlb = tl->rlb;
+        p.rb = tl->rb;
+        p.rup = tl->rup;
+        p.skip_prev = tl->skip_prev;
+        p.skip_out = tl->skip_out;
+        p.lin = tl->lin;
+        p.trunk = (__half *) tl->trunk;
+        p.tsn = tl->snext;
+    }
 
     CUtensorMap tmA, tmB;
     {
@@ -464,13 +664,13 @@ cudaError_t run_tc(const conv_params &cp, int *err, cudaStream_t st) {
     int dev = 0;
     cudaGetDevice(&dev);
     if (!(attr_set >> (dev & 63) & 1)) {
-        const cudaError_t e = cudaFuncSetAttribute(conv_tc_kernel<BN, KC, UP>,
+        const cudaError_t e = cudaFuncSetAttribute(conv_tc_kernel<BN, KC, UP, NACC, TAIL>,
                                                    cudaFuncAttributeMaxDynamicSharedMemorySize, cfg::SMEM);
         if (e != cudaSuccess) return e;
         attr_set |= 1ull << (dev & 63);
     }
     const int grid = (int) (p.num_tiles < sm_count() ? p.num_tiles : sm_count());
-    conv_tc_kernel<BN, KC, UP><<<grid, TC_THREADS, cfg::SMEM, st>>>(tmA, tmB, p);
+    conv_tc_kernel<BN, KC, UP, NACC, TAIL><<<grid, cfg::THREADS, cfg::SMEM, st>>>(tmA, tmB, p);
     return cudaGetLastError();
 }
 
@@ -486,10 +686,28 @@ bool conv_tc_supported(bool up, int IC, int OC) {
 cudaError_t launch_conv_tc(bool up, const conv_params &p, cudaStream_t st) {
     const int N = up ? 4 * p.OC : p.OC;
     if (!conv_tc_supported(up, p.IC, p.OC) || !p.err) return cudaErrorInvalidValue;
-    if (p.IC == 32) return run_tc<32, 32, false>(p, p.err, st);
-    if (N >= 256) return up ? run_tc<256, 64, true>(p, p.err, st) : run_tc<256, 64, false>(p, p.err, st);
-    if (N == 128) return up ? run_tc<128, 64, true>(p, p.err, st) : run_tc<128, 64, false>(p, p.err, st);
-    return up ? run_tc<64, 64, true>(p, p.err, st) : run_tc<64, 64, false>(p, p.err, st);
+    if (p.IC == 32) return run_tc<32, 32, false, 4, false>(p, nullptr, st);
+    if (N >= 256)
+        return up ? run_tc<256, 64, true, 2, false>(p, nullptr, st)
+                  : run_tc<256, 64, false, 2, false>(p, nullptr, st);
+    if (N == 128)
+        return up ? run_tc<128, 64, true, 4, false>(p, nullptr, st)
+                  : run_tc<128, 64, false, 4, false>(p, nullptr, st);
+    return up ? run_tc<64, 64, true, 4, false>(p, nullptr, st) : run_tc<64, 64, false, 4, false>(p, nullptr, st);
+}
+
+bool conv_tail_tc_supported(int IC, int OC, int r) {
+    return IC == OC && (OC == 32 || OC == 64 || OC == 128 || OC == 256) && r >= 64;
+}
+
+cudaError_t launch_conv_tail_tc(const conv_params &p, const tail_params &t, cudaStream_t st) {
+    if (!conv_tail_tc_supported(p.IC, p.OC, p.W) || !p.err || p.H != p.W) return cudaErrorInvalidValue;
+    switch (p.OC) {
+        case 32: return run_tc<32, 32, false, 4, true>(p, &t, st);
+        case 64: return run_tc<64, 64, false, 4, true>(p, &t, st);
+        case 128: return run_tc<128, 64, false, 4, true>(p, &t, st);
+        default: return run_tc<256, 64, false, 2, true>(p, &t, st);
+    }
 }
 
 }  // namespace tpmd

@@ -616,10 +616,18 @@ int tpmd_arena_adopt(tpmd_ctx *c, int which) {
     return 0;
 }
 
+}  // extern "C"
+namespace {
+bool fused_level(const tpmd_ctx *c, int j);
+}
+extern "C" {
+
 static int64_t tpmd_kernel_launches_impl(const tpmd_ctx *c, int64_t n) {
     if (!c || n <= 0) return 0;
     const int64_t chunks = (n + c->max_batch - 1) / c->max_batch;
-    return chunks * (4 + 3 * N_LEVELS);
+    int per = 4 + 3 * N_LEVELS;
+    for (int j = 0; j < N_LEVELS; j++) per -= fused_level(c, j) ? 1 : 0;
+    return chunks * per;
 }
 
 }  // extern "C"
@@ -650,8 +658,13 @@ bool launch(tpmd_ctx *c, const std::string &name, cudaStream_t st, F &&fn) {
     return true;
 }
 
+// levels whose conv2 runs with the level tail fused into its epilogue
+bool fused_level(const tpmd_ctx *c, int j) {
+    return c->use_tc && conv_tail_tc_supported(ST_OC[j], ST_OC[j], 8 << j);
+}
+
 bool enqueue_chunk(tpmd_ctx *c, const ws_view &w, const float *styles, int64_t nb, float *out,
-                   cudaStream_t st, int last_level = N_LEVELS - 1) {
+                   cudaStream_t st, int last_level = N_LEVELS - 1, bool keep_conv2 = false) {
     const bool h = c->f16;
     const int B = (int) nb;
     if (!launch(c, "style", st, [&] {
@@ -669,7 +682,7 @@ bool enqueue_chunk(tpmd_ctx *c, const ws_view &w, const float *styles, int64_t n
                                       c->S_TOT, B, w.actA, st);
         }))
         return false;
-    auto conv = [&](int k, const void *x, void *y, int Hh, const float *snext) {
+    auto conv_p = [&](int k, const void *x, void *y, int Hh, const float *snext) {
         const conv_layout &L = c->conv[k];
         conv_params p{};
         p.x = x;
@@ -685,6 +698,11 @@ bool enqueue_chunk(tpmd_ctx *c, const ws_view &w, const float *styles, int64_t n
         p.snext = snext;
         p.snext_stride = c->S_TOT;
         p.err = w.err;
+        return p;
+    };
+    auto conv = [&](int k, const void *x, void *y, int Hh, const float *snext) {
+        const conv_layout &L = c->conv[k];
+        const conv_params p = conv_p(k, x, y, Hh, snext);
         std::string name = k == 0 ? "conv1" : (L.up ? "upconv_r" : "conv2_r") +
                                                    std::to_string(L.up ? 2 * Hh : Hh);
         return launch(c, name, st, [&] {
@@ -698,9 +716,10 @@ bool enqueue_chunk(tpmd_ctx *c, const ws_view &w, const float *styles, int64_t n
         const conv_layout &Lu = c->conv[1 + 2 * j], &Ld = c->conv[2 + 2 * j];
         // up-conv: trunk (x its style) -> c1 (x conv2's style)
         if (!conv(1 + 2 * j, w.actB, w.actC, r / 2, w.s_all + Ld.s_off)) return false;
-        // conv2: c1 -> out (unscaled, read by the tail)
-        if (!conv(2 + 2 * j, w.actC, w.actA, r, nullptr)) return false;
         (void) Lu;
+        const bool fused = fused_level(c, j);
+        // conv2: c1 -> out (unscaled, read by the tail)
+        if (!fused && !conv(2 + 2 * j, w.actC, w.actA, r, nullptr)) return false;
         const stage_layout &S = c->stage[j];
         tail_params t{};
         t.out = w.actA;
@@ -724,8 +743,14 @@ bool enqueue_chunk(tpmd_ctx *c, const ws_view &w, const float *styles, int64_t n
         t.lin = c->Wf(S.lin);
         t.trunk = j == N_LEVELS - 1 ? nullptr : w.actB;
         t.snext = j == N_LEVELS - 1 ? nullptr : w.s_all + c->conv[3 + 2 * j].s_off;
-        if (!launch(c, "tail_r" + std::to_string(r), st, [&] { return launch_tail(h, t, st); }))
+        if (fused) {
+            const conv_params p = conv_p(2 + 2 * j, w.actC, keep_conv2 ? w.actA : nullptr, r, nullptr);
+            if (!launch(c, "conv2tail_r" + std::to_string(r), st,
+                        [&] { return launch_conv_tail_tc(p, t, st); }))
+                return false;
+        } else if (!launch(c, "tail_r" + std::to_string(r), st, [&] { return launch_tail(h, t, st); })) {
             return false;
+        }
     }
     return true;
 }
@@ -808,7 +833,7 @@ int tpmd_decode_taps(tpmd_ctx *c, const float *style, int level, float *conv1, f
         !c->ck(cudaMemcpyAsync(c->styles_d[0], style, STYLE_DIM * 4, cudaMemcpyHostToDevice,
                                c->stream),
                "style H2D") ||
-        !enqueue_chunk(c, ctx_ws(c), c->styles_d[0], 1, c->frames_d[0], c->stream, level) ||
+        !enqueue_chunk(c, ctx_ws(c), c->styles_d[0], 1, c->frames_d[0], c->stream, level, true) ||
         !c->ck(cudaStreamSynchronize(c->stream), "sync") || !device_ok(c))
         return -1;
     const int r = 8 << level, OC = ST_OC[level];

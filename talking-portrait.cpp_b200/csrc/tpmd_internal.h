@@ -85,5 +85,10 @@ cudaError_t launch_tail(bool f16, const tail_params &p, cudaStream_t st);
 // tcgen05 path (f16)
 cudaError_t launch_conv_tc(bool up, const conv_params &p, cudaStream_t st);
 bool conv_tc_supported(bool up, int IC, int OC);
+// conv2 with the level tail fused into its epilogue (levels with OC <= 256):
+// the tail reads the conv2 output from TMEM in f32; p.y, when not null, also
+// receives the conv2 output (f16) for parity taps
+cudaError_t launch_conv_tail_tc(const conv_params &p, const tail_params &t, cudaStream_t st);
+bool conv_tail_tc_supported(int IC, int OC, int r);
 
 }  // namespace tpmd

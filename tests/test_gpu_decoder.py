@@ -129,9 +129,12 @@ def test_errors_are_reported(model):
         d.decode(model["styles"][:1])
 
 
-def test_kernel_launch_count(dec16):
-    assert dec16.kernel_launches(8) == 25
-    assert dec16.kernel_launches(9) == 50
+def test_kernel_launch_count(dec16, dec32):
+    # style, den, conv1 input, conv1, then per level up-conv, conv2, tail;
+    # with tcgen05 the four levels with OC <= 256 fuse conv2 and tail
+    assert dec32.kernel_launches(8) == 25
+    assert dec16.kernel_launches(8) == 21
+    assert dec16.kernel_launches(9) == 42
 
 
 def test_stress_random_init(stress_model):
