@@ -42,7 +42,7 @@ struct tc_params {
     int kiters, cpt;           // k-steps per tile, channel chunks per tap
     int bw, bh, bb;            // pixel box of one M tile
     int tiles_x, tiles_y, tiles_n;
-    int64_t num_tiles;
+    int num_tiles;
     __half *y;
     const float *inv_den;
     int den_stride;
@@ -164,13 +164,20 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
 
 template <int BN, int KC, int NACC, bool TAIL>
 struct tc_cfg {
-    static constexpr int A_BYTES = BM * KC * 2;
-    static constexpr int B_BYTES = BN * KC * 2;
+    // taps per pipeline stage: narrow layers put a whole kernel row (3 taps)
+    // in one stage, so the per-stage barrier round trip is paid 3x less often
+    static constexpr int TPS = BN <= 128 ? 3 : 1;
+    static constexpr int A_TAP = BM * KC * 2;   // one tap's A tile
+    static constexpr int B_TAP = BN * KC * 2;   // one tap's B tile
+    static constexpr int A_BYTES = TPS * A_TAP;
+    static constexpr int B_BYTES = TPS * B_TAP;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    // fused tail: the ToRGB weights [3][BN], shared by all epilogue groups
-    static constexpr int EXTRA = TAIL ? 3 * BN * 4 : 0;
+    // fused tail: the ToFlow and ToRGB weights [3][BN] each, shared by all
+    // epilogue groups
+    static constexpr int EXTRA = TAIL ? 6 * BN * 4 : 0;
+    // as deep as shared memory allows (small stages hide more TMA latency)
     static constexpr int STAGES =
-        ((212992 - EXTRA) / STAGE_BYTES) > 8 ? 8 : ((212992 - EXTRA) / STAGE_BYTES);
+        ((212992 - EXTRA) / STAGE_BYTES) > 20 ? 20 : ((212992 - EXTRA) / STAGE_BYTES);
     static constexpr uint32_t TMEM_COLS = NACC * BN;  // one accumulator per epilogue group
     static constexpr int THREADS = 64 + 128 * NACC;
     static constexpr uint32_t LAYOUT = KC == 64 ? 2u : 4u;
@@ -188,40 +195,19 @@ struct tc_cfg {
 struct tile_pos {
     int n0, b0, y0, x0;
 };
-__device__ __forceinline__ tile_pos tile_of(const tc_params &p, int64_t t, int BN) {
+__device__ __forceinline__ tile_pos tile_of(const tc_params &p, int t, int BN) {
     tile_pos r;
-    const int nt = (int) (t % p.tiles_n);
-    const int64_t m = t / p.tiles_n;
-    const int xt = (int) (m % p.tiles_x);
-    const int64_t m2 = m / p.tiles_x;
-    const int yt = (int) (m2 % p.tiles_y);
-    const int bt = (int) (m2 / p.tiles_y);
+    const int nt = t % p.tiles_n;
+    const int m = t / p.tiles_n;
+    const int xt = m % p.tiles_x;
+    const int m2 = m / p.tiles_x;
+    const int yt = m2 % p.tiles_y;
+    const int bt = m2 / p.tiles_y;
     r.n0 = nt * BN;
     r.x0 = xt * p.bw;
     r.y0 = yt * p.bh;
     r.b0 = bt * p.bb;
     return r;
-}
-
-// upfirdn2d(up=2, pad=(2,1)) of an h x h plane at output (x, y): the two
-// source rows/columns of matching parity, in the reference op's tap order
-// (patch:559-569, rows outer, columns inner)
-__device__ __forceinline__ float up2x_at(const float *__restrict__ src, const float *__restrict__ k4,
-                                         int x, int y, int h) {
-    const int px = x & 1, py = y & 1, nx = x >> 1, ny = y >> 1;
-    float acc = 0.0f;
-#pragma unroll
-    for (int a = 0; a < 2; a++) {
-        const int sy = ny + py - 1 + a;
-        if (sy < 0 || sy >= h) continue;
-#pragma unroll
-        for (int b = 0; b < 2; b++) {
-            const int sx = nx + px - 1 + b;
-            if (sx < 0 || sx >= h) continue;
-            acc = fmaf(__ldg(src + sy * h + sx), __ldg(k4 + (px + 2 * b) + 4 * (py + 2 * a)), acc);
-        }
-    }
-    return acc;
 }
 
 // 16 consecutive floats (64-byte aligned) through the read-only path
@@ -293,8 +279,11 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
-    if (TAIL) {
-        for (int i = threadIdx.x; i < 3 * BN; i += blockDim.x) sx[i] = __ldg(p.rW + i);
+    if (TAIL) {  // sx[0..3BN): ToRGB weights, sx[3BN..6BN): ToFlow weights
+        for (int i = threadIdx.x; i < 3 * BN; i += blockDim.x) {
+            sx[i] = __ldg(p.rW + i);
+            sx[3 * BN + i] = __ldg(p.fW + i);
+        }
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -310,25 +299,37 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 
     if (warp == 0) {
         if (lane == 0) {
-            // ---- TMA producer
+            // ---- TMA producer: counters only, no division per k-step
             uint32_t it = 0;
+            int s = 0;
+            uint32_t ph = 0;
             bool ok = true;
-            for (int64_t t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+            const uint32_t sA0 = smem_u32(sA), sB0 = smem_u32(sB);
+            for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
                 const tile_pos tp = tile_of(p, t, BN);
-                for (int kk = 0; kk < p.kiters; kk++, it++) {
-                    const int s = it % cfg::STAGES;
-                    const uint32_t ph = (it / cfg::STAGES) & 1;
-                    if (!mbar_wait(empty(s), ph ^ 1)) {
-                        ok = false;
-                        break;
+                for (int kh = 0; kh < 3 && ok; kh++) {
+                    for (int c = 0; c < p.cpt && ok; c++) {
+                        for (int kw0 = 0; kw0 < 3; kw0 += cfg::TPS, it++) {
+                            if (!mbar_wait(empty(s), ph ^ 1)) {
+                                ok = false;
+                                break;
+                            }
+                            mbar_expect_tx(full(s), cfg::STAGE_BYTES);
+#pragma unroll
+                            for (int i = 0; i < cfg::TPS; i++) {
+                                const int kw = kw0 + i;
+                                tma_load_4d(sA0 + s * cfg::A_BYTES + i * cfg::A_TAP, &tmA, full(s), c * KC,
+                                            tp.x0 + kw - 1, tp.y0 + kh - 1, tp.b0);
+                                // weight column of (tap, chunk): tap * IC + c * KC
+                                tma_load_2d(sB0 + s * cfg::B_BYTES + i * cfg::B_TAP, &tmB, full(s),
+                                            (kh * 3 + kw) * p.IC + c * KC, tp.n0);
+                            }
+                            if (++s == cfg::STAGES) {
+                                s = 0;
+                                ph ^= 1;
+                            }
+                        }
                     }
-                    mbar_expect_tx(full(s), cfg::STAGE_BYTES);
-                    const int tap = kk / p.cpt, c = kk - tap * p.cpt;
-                    const int kh = tap / 3, kw = tap - kh * 3;
-                    tma_load_4d(smem_u32(sA + s * cfg::A_BYTES), &tmA, full(s), c * KC, tp.x0 + kw - 1,
-                                tp.y0 + kh - 1, tp.b0);
-                    tma_load_2d(smem_u32(sB + s * cfg::B_BYTES), &tmB, full(s), tap * p.IC + c * KC,
-                                tp.n0);
                 }
             }
             if (!ok) {
@@ -343,32 +344,46 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     } else if (warp == 1) {
         if (lane == 0) {
             // ---- MMA issuer: tile k of this CTA accumulates into buffer k % NACC
-            uint32_t it = 0, k = 0;
+            int s = 0, a = 0;
+            uint32_t ph = 0, aph = 0;
             bool ok = true;
-            for (int64_t t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x, k++) {
-                const int a = k % NACC;
-                if (!mbar_wait(tempty(a), ((k / NACC) & 1) ^ 1)) {
+            // descriptors of stage 0; stage s adds its byte offset >> 4 to the
+            // start-address field (shared addresses stay below 2^18)
+            const uint64_t ad0 = smem_desc(smem_u32(sA), cfg::SBO, cfg::LAYOUT);
+            const uint64_t bd0 = smem_desc(smem_u32(sB), cfg::SBO, cfg::LAYOUT);
+            for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+                if (!mbar_wait(tempty(a), aph ^ 1)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + a * BN;
-                for (int kk = 0; kk < p.kiters; kk++, it++) {
-                    const int s = it % cfg::STAGES;
-                    if (!mbar_wait(full(s), (it / cfg::STAGES) & 1)) {
+                for (int kk = 0; kk < p.kiters; kk++) {
+                    if (!mbar_wait(full(s), ph)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint64_t ad = smem_desc(smem_u32(sA + s * cfg::A_BYTES), cfg::SBO, cfg::LAYOUT);
-                    const uint64_t bd = smem_desc(smem_u32(sB + s * cfg::B_BYTES), cfg::SBO, cfg::LAYOUT);
+                    const uint64_t ad = ad0 + (uint64_t) ((s * cfg::A_BYTES) >> 4);
+                    const uint64_t bd = bd0 + (uint64_t) ((s * cfg::B_BYTES) >> 4);
 #pragma unroll
-                    for (int kx = 0; kx < KC / 16; kx++)  // +32 bytes along K per step
-                        umma_f16(d_tmem, ad + 2 * kx, bd + 2 * kx, cfg::IDESC, (kk | kx) != 0);
+                    for (int i = 0; i < cfg::TPS; i++)
+#pragma unroll
+                        for (int kx = 0; kx < KC / 16; kx++)  // +32 bytes along K per step
+                            umma_f16(d_tmem, ad + ((i * cfg::A_TAP) >> 4) + 2 * kx,
+                                     bd + ((i * cfg::B_TAP) >> 4) + 2 * kx, cfg::IDESC, (kk | i | kx) != 0);
                     umma_commit(empty(s));
+                    if (++s == cfg::STAGES) {
+                        s = 0;
+                        ph ^= 1;
+                    }
                 }
                 if (!ok) break;
                 umma_commit(tfull(a));
+                if (++a == NACC) {
+                    a = 0;
+                    aph ^= 1;
+                }
             }
             if (!ok) atomicExch(p.err, 1);
             umma_commit(drain);  // completes when every MMA issued here has
@@ -382,10 +397,9 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         const int row = q * 32 + lane;
         const int bx = row % p.bw, by = (row / p.bw) % p.bh, bz = row / (p.bw * p.bh);
         const uint32_t taddr0 = tmem_base + ((uint32_t) (q * 32) << 16) + g * BN;
-        const float *s_rw = sx;
+        const float *s_rw = sx, *s_fw = sx + 3 * BN;
         uint32_t k = g;
-        for (int64_t t = blockIdx.x + (int64_t) g * gridDim.x; t < p.num_tiles;
-             t += (int64_t) NACC * gridDim.x, k += NACC) {
+        for (int t = blockIdx.x + g * gridDim.x; t < p.num_tiles; t += NACC * gridDim.x, k += NACC) {
             const bool ok = __all_sync(0xffffffffu, mbar_wait(tfull(g), (k / NACC) & 1));
             if (!ok) {
                 if (lane == 0) atomicExch(p.err, 1);
@@ -463,17 +477,38 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                         a = a > 0.0f ? a : 0.2f * a;
                         v[i] = a;
                         const float xs = a * fsv[i];  // ToFlow input: out * style
-                        f0 = fmaf(__ldg(p.fW + c0 + i), xs, f0);
-                        f1 = fmaf(__ldg(p.fW + BN + c0 + i), xs, f1);
-                        f2 = fmaf(__ldg(p.fW + 2 * BN + c0 + i), xs, f2);
+                        f0 = fmaf(s_fw[c0 + i], xs, f0);
+                        f1 = fmaf(s_fw[BN + c0 + i], xs, f1);
+                        f2 = fmaf(s_fw[2 * BN + c0 + i], xs, f2);
                     }
                     if (p.y) st_half16(p.y + pix * BN + c0, v);  // conv2 tap (debug)
                 }
+                // up-sampling taps of (x, y): the same four source offsets and
+                // kernel indices serve all three channels of both skips
+                int uoff[4], uk[4];
+                {
+                    const int px = x & 1, py = y & 1, nx = x >> 1, ny = y >> 1;
+#pragma unroll
+                    for (int a = 0; a < 2; a++)
+#pragma unroll
+                        for (int bb = 0; bb < 2; bb++) {
+                            const int sy = ny + py - 1 + a, sx2 = nx + px - 1 + bb;
+                            const bool in = sy >= 0 && sy < h && sx2 >= 0 && sx2 < h;
+                            uoff[2 * a + bb] = in ? sy * h + sx2 : -1;
+                            uk[2 * a + bb] = (px + 2 * bb) + 4 * (py + 2 * a);
+                        }
+                }
+                auto up2 = [&](const float *plane, const float *k4) {
+                    float acc = 0.0f;
+#pragma unroll
+                    for (int i = 0; i < 4; i++)
+                        if (uoff[i] >= 0) acc = fmaf(__ldg(plane + uoff[i]), __ldg(k4 + uk[i]), acc);
+                    return acc;
+                };
                 float fl[3] = {f0 + __ldg(p.fb), f1 + __ldg(p.fb + 1), f2 + __ldg(p.fb + 2)};
                 if (p.skipf_prev) {
 #pragma unroll
-                    for (int kk = 0; kk < 3; kk++)
-                        fl[kk] += up2x_at(p.skipf_prev + ((int64_t) b * 3 + kk) * h * h, p.fup, x, y, h);
+                    for (int kk = 0; kk < 3; kk++) fl[kk] += up2(p.skipf_prev + ((int64_t) b * 3 + kk) * h * h, p.fup);
                 }
                 const int64_t rr2 = (int64_t) r * r;
                 if (p.skipf_out) {
@@ -499,12 +534,14 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     trow[kk] = (sane && cx >= 0 && cx < r && cy >= 0 && cy < r) ? cy * r + cx : -1;
                     twt[kk] = ((kk & 1) ? wx : 1.0f - wx) * ((kk >> 1) ? wy : 1.0f - wy);
                 }
-                // pass 2: gather, blend, ToRGB sums, trunk
+                // pass 2: gather, blend, ToRGB sums, trunk. The last level has
+                // no trunk, so it needs neither the conv2 output nor TMEM here.
+                const bool need_out = p.trunk != nullptr;
                 float g0 = 0.0f, g1 = 0.0f, g2 = 0.0f;
 #pragma unroll 1
                 for (int c0 = 0; c0 < BN; c0 += 16) {
                     uint32_t rr[16];
-                    tmem_ld16(taddr0 + c0, rr);
+                    if (need_out) tmem_ld16(taddr0 + c0, rr);
                     float smp[16];
 #pragma unroll
                     for (int i = 0; i < 16; i++) smp[i] = 0.0f;
@@ -516,10 +553,20 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 #pragma unroll
                         for (int i = 0; i < 16; i++) smp[i] = fmaf(twt[kk], f[i], smp[i]);
                     }
+                    if (!need_out) {
+#pragma unroll
+                        for (int i = 0; i < 16; i++) {
+                            const float w = smp[i] * m;
+                            g0 = fmaf(s_rw[c0 + i], w, g0);
+                            g1 = fmaf(s_rw[BN + c0 + i], w, g1);
+                            g2 = fmaf(s_rw[2 * BN + c0 + i], w, g2);
+                        }
+                        continue;
+                    }
                     float den[16], bias[16], sn[16];
                     ld_f16x(fden + c0, den);
                     ld_f16x(p.bias + c0, bias);
-                    if (fsn) ld_f16x(fsn + c0, sn);
+                    ld_f16x(fsn + c0, sn);
 #pragma unroll
                     for (int i = 0; i < 16; i++) {
                         float a = fmaf(__uint_as_float(rr[i]), den[i], bias[i]);
@@ -528,17 +575,16 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                         g0 = fmaf(s_rw[c0 + i], w, g0);
                         g1 = fmaf(s_rw[BN + c0 + i], w, g1);
                         g2 = fmaf(s_rw[2 * BN + c0 + i], w, g2);
-                        smp[i] = w + a * om;  // trunk
-                        if (fsn) smp[i] *= sn[i];  // x next up-conv style
+                        smp[i] = (w + a * om) * sn[i];  // trunk x next up-conv style
                     }
-                    if (p.trunk) st_half16(p.trunk + pix * BN + c0, smp);
+                    st_half16(p.trunk + pix * BN + c0, smp);
                 }
                 const float rg[3] = {g0, g1, g2};
 #pragma unroll
                 for (int kk = 0; kk < 3; kk++) {
                     float v = rg[kk] + __ldg(p.rlb + kk);
                     v = (v > 0.0f ? v : 0.2f * v) + __ldg(p.rb + kk);
-                    if (p.skip_prev) v += up2x_at(p.skip_prev + ((int64_t) b * 3 + kk) * h * h, p.rup, x, y, h);
+                    if (p.skip_prev) v += up2(p.skip_prev + ((int64_t) b * 3 + kk) * h * h, p.rup);
                     p.skip_out[((int64_t) b * 3 + kk) * rr2 + (int64_t) y * r + x] = v;
                 }
             }
@@ -595,7 +641,7 @@ cudaError_t run_tc(const conv_params &cp, const tail_params *tl, cudaStream_t st
     p.OC = cp.OC;
     p.N = UP ? 4 * cp.OC : cp.OC;
     p.cpt = cp.IC / KC;
-    p.kiters = 9 * p.cpt;
+    p.kiters = 9 * p.cpt / cfg::TPS;  // pipeline stages per tile
     p.bw = cp.W < BM ? cp.W : BM;
     p.bh = cp.H < BM / p.bw ? cp.H : BM / p.bw;
     p.bb = BM / (p.bw * p.bh);
@@ -603,7 +649,9 @@ cudaError_t run_tc(const conv_params &cp, const tail_params *tl, cudaStream_t st
     p.tiles_y = cp.H / p.bh;
     p.tiles_n = p.N / BN;
     const int tiles_b = (cp.B + p.bb - 1) / p.bb;
-    p.num_tiles = (int64_t) tiles_b * p.tiles_y * p.tiles_x * p.tiles_n;
+    const int64_t nt = (int64_t) tiles_b * p.tiles_y * p.tiles_x * p.tiles_n;
+    if (nt >= (1ll << 30)) return cudaErrorInvalidValue;
+    p.num_tiles = (int) nt;
     p.y = (__half *) cp.y;
     p.inv_den = cp.inv_den;
     p.den_stride = cp.den_stride;

@@ -33,13 +33,22 @@ style_kernel(const float *__restrict__ wmod, const float *__restrict__ bmod, int
 #pragma unroll
     for (int i = 0; i < STYLE_DIM / 32; i++) w[i] = __ldg(wmod + (int64_t) row * STYLE_DIM + lane + 32 * i);
     const float bias = __ldg(bmod + row);
-    for (int b = 0; b < B; b++) {
-        const float *l = lat + (int64_t) b * STYLE_DIM;
-        float a = 0.0f;
+    // four frames per pass: independent loads and reductions overlap
+    for (int b0 = 0; b0 < B; b0 += 4) {
+        float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-        for (int i = 0; i < STYLE_DIM / 32; i++) a = fmaf(w[i], __ldg(l + lane + 32 * i), a);
-        a = warp_sum(a);
-        if (lane == 0) s_all[(int64_t) b * rows + row] = a + bias;
+        for (int f = 0; f < 4; f++) {
+            if (b0 + f >= B) continue;
+            const float *l = lat + (int64_t) (b0 + f) * STYLE_DIM;
+#pragma unroll
+            for (int i = 0; i < STYLE_DIM / 32; i++) a[f] = fmaf(w[i], __ldg(l + lane + 32 * i), a[f]);
+        }
+#pragma unroll
+        for (int f = 0; f < 4; f++) a[f] = warp_sum(a[f]);
+        if (lane < 4 && b0 + lane < B) {
+            const float v = lane == 0 ? a[0] : lane == 1 ? a[1] : lane == 2 ? a[2] : a[3];
+            s_all[(int64_t) (b0 + lane) * rows + row] = v + bias;
+        }
     }
 }
 
@@ -60,18 +69,26 @@ den_kernel(const float *__restrict__ saug, den_table t, const float *__restrict_
 #pragma unroll
     for (int i = 0; i < MAXPER; i++) w[i] = i < per ? __ldg(r + lane + 32 * i) : 0.0f;
     const float eps = __ldg(r + IC);
-    for (int b = 0; b < B; b++) {
-        const float *s = s_all + (int64_t) b * s_stride + t.s_off[c];
-        float a = 0.0f;
+    for (int b0 = 0; b0 < B; b0 += 4) {  // four frames per pass
+        float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-        for (int i = 0; i < MAXPER; i++) {
-            if (i < per) {
-                const float v = __ldg(s + lane + 32 * i);
-                a = fmaf(w[i], v * v, a);
+        for (int f = 0; f < 4; f++) {
+            if (b0 + f >= B) continue;
+            const float *s = s_all + (int64_t) (b0 + f) * s_stride + t.s_off[c];
+#pragma unroll
+            for (int i = 0; i < MAXPER; i++) {
+                if (i < per) {
+                    const float v = __ldg(s + lane + 32 * i);
+                    a[f] = fmaf(w[i], v * v, a[f]);
+                }
             }
         }
-        a = warp_sum(a) + eps;
-        if (lane == 0) inv_den[(int64_t) b * d_stride + t.d_off[c] + o] = 1.0f / sqrtf(a);
+#pragma unroll
+        for (int f = 0; f < 4; f++) a[f] = warp_sum(a[f]) + eps;
+        if (lane < 4 && b0 + lane < B) {
+            const float v = lane == 0 ? a[0] : lane == 1 ? a[1] : lane == 2 ? a[2] : a[3];
+            inv_den[(int64_t) (b0 + lane) * d_stride + t.d_off[c] + o] = 1.0f / sqrtf(v);
+        }
     }
 }
 
