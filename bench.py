@@ -140,6 +140,7 @@ def cpu_baseline(tensors, feats, styles, budget_s: float = 12.0):
     """oracle sub-pixel graph (the reference CPU path's fast-graph math) on
     all host cores: one warm-up frame, then frames until ~budget_s"""
     import oracle as O
+    O.set_threads(os.cpu_count() or 1)  # torchrun exports OMP_NUM_THREADS=1
     dec = O.Decoder(tensors, feats)
     dec.decode(styles[0], mode=1)
     n, t0 = 0, time.perf_counter()
@@ -167,6 +168,7 @@ def run_reference(args, rank: int, world: int):
         return
     tensors, feats, styles = setup_inputs(0, max(8, args.warmup + args.steps))
     import oracle as O
+    O.set_threads(os.cpu_count() or 1)  # all host threads (torchrun exports OMP_NUM_THREADS=1)
     dec = O.Decoder(tensors, feats)
     for i in range(args.warmup):
         dec.decode(styles[i], mode=1)
@@ -197,6 +199,8 @@ def main():
     ap.add_argument("--batch", type=int, default=50)
     ap.add_argument("--dtype", default="f16", choices=["f16", "f32"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--clip", type=int, default=0,
+                    help="config 3: decode a clip of this many frames sharded across ranks per step")
     args = ap.parse_args()
 
     rank = int(os.environ.get("RANK", "0"))
@@ -209,6 +213,7 @@ def main():
     import torch
     import torch.distributed as dist
     import tpmd
+    from tpmd import multi, synth
 
     torch.cuda.set_device(local)
     if world > 1:
@@ -226,25 +231,24 @@ def main():
         dec.prepare()
         dec.set_feats(feats)
     if world > 1:
-        for which in (0, 1):
-            ptr, n = dec.arena(which)
-
-            class _Arena:
-                __cuda_array_interface__ = {"shape": (n,), "typestr": "|u1", "data": (ptr, False),
-                                            "version": 3}
-            t = torch.as_tensor(_Arena(), device=f"cuda:{local}")
-            dist.broadcast(t, src=0)
-            torch.cuda.synchronize()
-            if rank != 0:
-                dec.adopt_arena(which)
+        multi.share_decoder(dec, rank, torch.device("cuda", local))
 
     stream = torch.cuda.Stream()  # the launch stream; CUDA events are recorded on it
-    s_d = torch.from_numpy(styles).cuda()
-    f_d = torch.empty((nb, 3, 512, 512), device="cuda")
+    if args.clip:
+        # config 3: a clip of args.clip frames sharded by frame across ranks
+        lo, hi = multi.frame_range(args.clip, world, rank)
+        clip_styles = synth.styles_walk(seed=0, n=args.clip)[lo:hi]
+        styles = clip_styles if hi > lo else styles[:1]
+        parts = multi.sub_batches(0, len(styles), nb)
+    else:
+        parts = [(0, nb)]
+    s_d = torch.from_numpy(np.ascontiguousarray(styles)).cuda()
+    f_d = torch.empty((max(b - a for a, b in parts), 3, 512, 512), device="cuda")
     torch.cuda.synchronize()
 
     def step():
-        dec.decode_device(s_d.data_ptr(), nb, f_d.data_ptr(), stream.cuda_stream)
+        for a, b in parts:
+            dec.decode_device(s_d.data_ptr() + a * 512 * 4, b - a, f_d.data_ptr(), stream.cuda_stream)
 
     for _ in range(args.warmup):
         step()
@@ -267,25 +271,23 @@ def main():
     barrier()
     ms = e0.elapsed_time(e1)
     if world > 1:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    value = world * nb * args.steps / (ms / 1000.0)
+        ms = multi.max_over_ranks(ms, torch.device("cuda", local))
+    frames_per_step = args.clip if args.clip else world * nb
+    value = frames_per_step * args.steps / (ms / 1000.0)
 
     # ---- end to end through the host C ABI (pinned buffers)
-    s_h = torch.from_numpy(styles).pin_memory()
-    f_h = torch.empty((nb, 3, 512, 512), pin_memory=True)
-    dec.decode_ptr(s_h.data_ptr(), nb, f_h.data_ptr())
+    n_mine = len(styles) if args.clip else nb
+    s_h = torch.from_numpy(np.ascontiguousarray(styles[:n_mine])).pin_memory()
+    f_h = torch.empty((n_mine, 3, 512, 512), pin_memory=True)
+    dec.decode_ptr(s_h.data_ptr(), n_mine, f_h.data_ptr())
     barrier()
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        dec.decode_ptr(s_h.data_ptr(), nb, f_h.data_ptr())
+        dec.decode_ptr(s_h.data_ptr(), n_mine, f_h.data_ptr())
     dt = time.perf_counter() - t0
     if world > 1:
-        t = torch.tensor([dt], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        dt = float(t.item())
-    e2e = world * nb * args.steps / dt
+        dt = multi.max_over_ranks(dt, torch.device("cuda", local))
+    e2e = frames_per_step * args.steps / dt
 
     # ---- live per-kernel timing (untimed pass) for the roofline
     dec.profile_begin()
@@ -327,16 +329,19 @@ def main():
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": value / PUBLISHED_FPS, "dtype": args.dtype,
+            "scaling": "strong" if args.clip else "weak", "vs_baseline": value / PUBLISHED_FPS,
+            "dtype": args.dtype,
             "data": "synthetic (random-init decoder, smooth N(0,1) feats, random-walk styles)",
-            "config": {"workload": "config 2: 50-frame chunk per GPU, f16 weights, 512x512",
-                       "global_batch": nb * world, "frames_per_gpu_per_step": nb,
+            "config": {"workload": (f"config 3: {args.clip}-frame clip sharded by frame, sub-batches of "
+                                    f"<= {nb}, f16 weights, 512x512") if args.clip else
+                                   "config 2: 50-frame chunk per GPU, f16 weights, 512x512",
+                       "global_batch": frames_per_step, "frames_per_gpu_per_step": n_mine,
                        "parallelism": f"frame-sharded x{world}",
                        "l2": "no flush: per-step working set (~2 GB activations) exceeds the 126 MB L2",
                        "conv": "tcgen05" if dec_uses_tc() else "simt"},
-            "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": nb * 512 * 4,
-                    "d2h_bytes_per_step": nb * 3 * 512 * 512 * 4},
-            "gpu_launches": dec.kernel_launches(nb) * args.steps * world,
+            "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": frames_per_step * 512 * 4,
+                    "d2h_bytes_per_step": frames_per_step * 3 * 512 * 512 * 4},
+            "gpu_launches": sum(dec.kernel_launches(b - a) for a, b in parts) * args.steps * world,
             "roofline": roof, "kernels": kernels, "clocks": clk.summary(),
             "cpu_baseline": cpu,
         }

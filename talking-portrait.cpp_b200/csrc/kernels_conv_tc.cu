@@ -162,22 +162,28 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-template <int BN, int KC, int NACC, bool TAIL>
+template <int BN, int KC, int NACC, bool TAIL, bool BRES>
 struct tc_cfg {
-    // taps per pipeline stage: narrow layers put a whole kernel row (3 taps)
-    // in one stage, so the per-stage barrier round trip is paid 3x less often
-    static constexpr int TPS = BN <= 128 ? 3 : 1;
     static constexpr int A_TAP = BM * KC * 2;   // one tap's A tile
     static constexpr int B_TAP = BN * KC * 2;   // one tap's B tile
-    static constexpr int A_BYTES = TPS * A_TAP;
-    static constexpr int B_BYTES = TPS * B_TAP;
-    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     // fused tail: the ToFlow and ToRGB weights [3][BN] each, shared by all
     // epilogue groups
     static constexpr int EXTRA = TAIL ? 6 * BN * 4 : 0;
+    // BRES: the whole weight matrix (9 taps x one KC chunk) stays resident in
+    // shared memory for the kernel's lifetime instead of being re-loaded for
+    // every pixel tile; stages then carry only A
+    static constexpr int B_RES = BRES ? 9 * B_TAP : 0;
+    static constexpr int BUDGET = 212992 - EXTRA - B_RES;
+    // taps per pipeline stage: narrow layers put a whole kernel row (3 taps)
+    // in one stage, so the per-stage barrier round trip is paid 3x less often
+    static constexpr int TPS =
+        BRES ? (BUDGET / (3 * A_TAP) >= 3 ? 3 : 1) : (BN <= 128 ? 3 : 1);
+    static constexpr int A_BYTES = TPS * A_TAP;
+    static constexpr int B_BYTES = BRES ? 0 : TPS * B_TAP;  // per stage
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     // as deep as shared memory allows (small stages hide more TMA latency)
-    static constexpr int STAGES =
-        ((212992 - EXTRA) / STAGE_BYTES) > 20 ? 20 : ((212992 - EXTRA) / STAGE_BYTES);
+    static constexpr int STAGES = (BUDGET / STAGE_BYTES) > 20 ? 20 : (BUDGET / STAGE_BYTES);
+    static constexpr int B_REGION = BRES ? B_RES : STAGES * B_BYTES;
     static constexpr uint32_t TMEM_COLS = NACC * BN;  // one accumulator per epilogue group
     static constexpr int THREADS = 64 + 128 * NACC;
     static constexpr uint32_t LAYOUT = KC == 64 ? 2u : 4u;
@@ -185,8 +191,8 @@ struct tc_cfg {
     // kind::f16 instruction descriptor: D f32, A/B f16, both K-major, N, M
     static constexpr uint32_t IDESC =
         (1u << 4) | ((uint32_t) (BN >> 3) << 17) | ((uint32_t) (BM >> 4) << 24);
-    static constexpr int NBARS = 2 * STAGES + 2 * NACC + 1;
-    static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + EXTRA + NBARS * 8 + 16;
+    static constexpr int NBARS = 2 * STAGES + 2 * NACC + 2;
+    static constexpr int SMEM = 1024 + STAGES * A_BYTES + B_REGION + EXTRA + NBARS * 8 + 16;
     static_assert((TMEM_COLS & (TMEM_COLS - 1)) == 0 && TMEM_COLS >= 32 && TMEM_COLS <= 512, "TMEM");
     static_assert(SMEM <= 232448, "shared memory");
     static_assert(STAGES >= 2, "pipeline depth");
@@ -247,23 +253,24 @@ __device__ __forceinline__ void st_half16(__half *p, const float *v) {
     q[1] = pk[1];
 }
 
-template <int BN, int KC, bool UP, int NACC, bool TAIL>
-__global__ void __launch_bounds__(tc_cfg<BN, KC, NACC, TAIL>::THREADS, 1)
+template <int BN, int KC, bool UP, int NACC, bool TAIL, bool BRES>
+__global__ void __launch_bounds__(tc_cfg<BN, KC, NACC, TAIL, BRES>::THREADS, 1)
 conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const tc_params p) {
-    using cfg = tc_cfg<BN, KC, NACC, TAIL>;
+    using cfg = tc_cfg<BN, KC, NACC, TAIL, BRES>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = (uint8_t *) (((uintptr_t) smem_raw + 1023) & ~(uintptr_t) 1023);
     uint8_t *sA = smem;
     uint8_t *sB = smem + cfg::STAGES * cfg::A_BYTES;
-    float *sx = (float *) (smem + cfg::STAGES * cfg::STAGE_BYTES);  // TAIL constants
-    uint64_t *bars = (uint64_t *) (smem + cfg::STAGES * cfg::STAGE_BYTES + cfg::EXTRA);
+    float *sx = (float *) (sB + cfg::B_REGION);  // TAIL constants
+    uint64_t *bars = (uint64_t *) (sB + cfg::B_REGION + cfg::EXTRA);
     uint32_t *tmem_slot = (uint32_t *) (bars + cfg::NBARS);
     auto full = [&](int s) { return smem_u32(&bars[s]); };
     auto empty = [&](int s) { return smem_u32(&bars[cfg::STAGES + s]); };
     auto tfull = [&](int a) { return smem_u32(&bars[2 * cfg::STAGES + a]); };
     auto tempty = [&](int a) { return smem_u32(&bars[2 * cfg::STAGES + NACC + a]); };
     const uint32_t drain = smem_u32(&bars[2 * cfg::STAGES + 2 * NACC]);
+    const uint32_t bres_bar = smem_u32(&bars[2 * cfg::STAGES + 2 * NACC + 1]);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
@@ -276,6 +283,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             mbar_init(tempty(a), 4);
         }
         mbar_init(drain, 1);
+        mbar_init(bres_bar, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
@@ -305,6 +313,10 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             uint32_t ph = 0;
             bool ok = true;
             const uint32_t sA0 = smem_u32(sA), sB0 = smem_u32(sB);
+            if (BRES) {  // the nine weight taps, once
+                mbar_expect_tx(bres_bar, cfg::B_RES);
+                for (int i = 0; i < 9; i++) tma_load_2d(sB0 + i * cfg::B_TAP, &tmB, bres_bar, i * p.IC, 0);
+            }
             for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
                 const tile_pos tp = tile_of(p, t, BN);
                 for (int kh = 0; kh < 3 && ok; kh++) {
@@ -321,8 +333,9 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                                 tma_load_4d(sA0 + s * cfg::A_BYTES + i * cfg::A_TAP, &tmA, full(s), c * KC,
                                             tp.x0 + kw - 1, tp.y0 + kh - 1, tp.b0);
                                 // weight column of (tap, chunk): tap * IC + c * KC
-                                tma_load_2d(sB0 + s * cfg::B_BYTES + i * cfg::B_TAP, &tmB, full(s),
-                                            (kh * 3 + kw) * p.IC + c * KC, tp.n0);
+                                if (!BRES)
+                                    tma_load_2d(sB0 + s * cfg::B_BYTES + i * cfg::B_TAP, &tmB, full(s),
+                                                (kh * 3 + kw) * p.IC + c * KC, tp.n0);
                             }
                             if (++s == cfg::STAGES) {
                                 s = 0;
@@ -339,6 +352,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     const uint32_t last = it - 1 - ((it - 1 - s) % cfg::STAGES);
                     mbar_wait(full(s), (last / cfg::STAGES) & 1);
                 }
+                if (BRES) mbar_wait(bres_bar, 0);
             }
         }
     } else if (warp == 1) {
@@ -351,6 +365,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             // start-address field (shared addresses stay below 2^18)
             const uint64_t ad0 = smem_desc(smem_u32(sA), cfg::SBO, cfg::LAYOUT);
             const uint64_t bd0 = smem_desc(smem_u32(sB), cfg::SBO, cfg::LAYOUT);
+            if (BRES && !mbar_wait(bres_bar, 0)) ok = false;
             for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
                 if (!mbar_wait(tempty(a), aph ^ 1)) {
                     ok = false;
@@ -358,14 +373,16 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + a * BN;
-                for (int kk = 0; kk < p.kiters; kk++) {
+                int tap0 = 0;  // first tap of the stage (BRES: its resident B tile)
+                for (int kk = 0; kk < p.kiters; kk++, tap0 += cfg::TPS) {
                     if (!mbar_wait(full(s), ph)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
                     const uint64_t ad = ad0 + (uint64_t) ((s * cfg::A_BYTES) >> 4);
-                    const uint64_t bd = bd0 + (uint64_t) ((s * cfg::B_BYTES) >> 4);
+                    const uint64_t bd = BRES ? bd0 + (uint64_t) ((tap0 * cfg::B_TAP) >> 4)
+                                             : bd0 + (uint64_t) ((s * cfg::B_BYTES) >> 4);
 #pragma unroll
                     for (int i = 0; i < cfg::TPS; i++)
 #pragma unroll
@@ -628,9 +645,9 @@ int sm_count() {
     return n;
 }
 
-template <int BN, int KC, bool UP, int NACC, bool TAIL>
+template <int BN, int KC, bool UP, int NACC, bool TAIL, bool BRES = false>
 cudaError_t run_tc(const conv_params &cp, const tail_params *tl, cudaStream_t st) {
-    using cfg = tc_cfg<BN, KC, NACC, TAIL>;
+    using cfg = tc_cfg<BN, KC, NACC, TAIL, BRES>;
     auto enc = encode_fn();
     if (!enc) return cudaErrorNotSupported;
     tc_params p{};
@@ -652,6 +669,7 @@ cudaError_t run_tc(const conv_params &cp, const tail_params *tl, cudaStream_t st
     const int64_t nt = (int64_t) tiles_b * p.tiles_y * p.tiles_x * p.tiles_n;
     if (nt >= (1ll << 30)) return cudaErrorInvalidValue;
     p.num_tiles = (int) nt;
+    if (BRES && (p.cpt != 1 || p.tiles_n != 1)) return cudaErrorInvalidValue;  // 9 taps x 1 chunk, 1 N tile
     p.y = (__half *) cp.y;
     p.inv_den = cp.inv_den;
     p.den_stride = cp.den_stride;
@@ -712,13 +730,13 @@ cudaError_t run_tc(const conv_params &cp, const tail_params *tl, cudaStream_t st
     int dev = 0;
     cudaGetDevice(&dev);
     if (!(attr_set >> (dev & 63) & 1)) {
-        const cudaError_t e = cudaFuncSetAttribute(conv_tc_kernel<BN, KC, UP, NACC, TAIL>,
+        const cudaError_t e = cudaFuncSetAttribute(conv_tc_kernel<BN, KC, UP, NACC, TAIL, BRES>,
                                                    cudaFuncAttributeMaxDynamicSharedMemorySize, cfg::SMEM);
         if (e != cudaSuccess) return e;
         attr_set |= 1ull << (dev & 63);
     }
     const int grid = (int) (p.num_tiles < sm_count() ? p.num_tiles : sm_count());
-    conv_tc_kernel<BN, KC, UP, NACC, TAIL><<<grid, cfg::THREADS, cfg::SMEM, st>>>(tmA, tmB, p);
+    conv_tc_kernel<BN, KC, UP, NACC, TAIL, BRES><<<grid, cfg::THREADS, cfg::SMEM, st>>>(tmA, tmB, p);
     return cudaGetLastError();
 }
 
@@ -738,6 +756,7 @@ cudaError_t launch_conv_tc(bool up, const conv_params &p, cudaStream_t st) {
     if (N >= 256)
         return up ? run_tc<256, 64, true, 2, false>(p, nullptr, st)
                   : run_tc<256, 64, false, 2, false>(p, nullptr, st);
+    if (N == 128 && up && p.IC == 64) return run_tc<128, 64, true, 4, false, true>(p, nullptr, st);
     if (N == 128)
         return up ? run_tc<128, 64, true, 4, false>(p, nullptr, st)
                   : run_tc<128, 64, false, 4, false>(p, nullptr, st);
@@ -751,7 +770,7 @@ bool conv_tail_tc_supported(int IC, int OC, int r) {
 cudaError_t launch_conv_tail_tc(const conv_params &p, const tail_params &t, cudaStream_t st) {
     if (!conv_tail_tc_supported(p.IC, p.OC, p.W) || !p.err || p.H != p.W) return cudaErrorInvalidValue;
     switch (p.OC) {
-        case 32: return run_tc<32, 32, false, 4, true>(p, &t, st);
+        case 32: return run_tc<32, 32, false, 4, true, true>(p, &t, st);
         case 64: return run_tc<64, 64, false, 4, true>(p, &t, st);
         case 128: return run_tc<128, 64, false, 4, true>(p, &t, st);
         default: return run_tc<256, 64, false, 2, true>(p, &t, st);
