@@ -314,10 +314,13 @@ def main():
     traffic = None
     tp = os.path.join(ROOT, "profiles", "ncu_traffic.json")
     if os.path.exists(tp):
+        # ncu DRAM bytes of this kernel from a batch-8 capture, scaled to this
+        # launch: the feats are read once per launch, the rest per frame
         tj = json.load(open(tp))
-        if name in tj.get("bytes_per_frame", {}) and tj.get("conv") == ("tc" if dec_uses_tc() else "simt"):
-            traffic = tj["bytes_per_frame"][name] * nb
+        if tj.get("kernel") == name and tj.get("conv") == ("tc" if dec_uses_tc() else "simt"):
+            traffic = tj["fixed_bytes"] + tj["bytes_per_frame"] * nb
     roof["traffic"] = traffic
+    roof["algorithmic_bytes"] = byts
     kernels = {k: {"launches": v[0], "ms": round(v[1], 4), "share": round(v[1] / total, 4)}
                for k, v in sorted(prof.items(), key=lambda kv: -kv[1][1])[:8]}
 
