@@ -162,10 +162,17 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-template <int BN, int KC, int NACC, bool TAIL, bool BRES>
+template <int BN, int KC, int NACC, bool TAIL, bool BRES, bool HALO = false>
 struct tc_cfg {
     static constexpr int A_TAP = BM * KC * 2;   // one tap's A tile
     static constexpr int B_TAP = BN * KC * 2;   // one tap's B tile
+    // HALO: a tile is one 128-pixel row; per kernel row one TMA box of the
+    // 130 pixels x-1..x+128 serves all three horizontal taps, each tap's A
+    // operand being the same box started 0, 1 or 2 rows later (a descriptor
+    // offset; swizzling follows absolute shared addresses). 136 rows are
+    // reserved per box to keep the next box 1024-byte aligned.
+    static constexpr int HALO_ROWS = BM + 2;
+    static constexpr int A_HALO = 136 * KC * 2;
     // fused tail: the ToFlow and ToRGB weights [3][BN] each, shared by all
     // epilogue groups
     static constexpr int EXTRA = TAIL ? 6 * BN * 4 : 0;
@@ -177,10 +184,12 @@ struct tc_cfg {
     // taps per pipeline stage: narrow layers put a whole kernel row (3 taps)
     // in one stage, so the per-stage barrier round trip is paid 3x less often
     static constexpr int TPS =
-        BRES ? (BUDGET / (3 * A_TAP) >= 3 ? 3 : 1) : (BN <= 128 ? 3 : 1);
-    static constexpr int A_BYTES = TPS * A_TAP;
+        HALO ? 3 : BRES ? (BUDGET / (3 * A_TAP) >= 3 ? 3 : 1) : (BN <= 128 ? 3 : 1);
+    static constexpr int A_BYTES = HALO ? A_HALO : TPS * A_TAP;     // per stage (space)
+    static constexpr int A_TX = HALO ? HALO_ROWS * KC * 2 : A_BYTES;  // per stage (loaded)
     static constexpr int B_BYTES = BRES ? 0 : TPS * B_TAP;  // per stage
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int STAGE_TX = A_TX + B_BYTES;
     // as deep as shared memory allows (small stages hide more TMA latency)
     static constexpr int STAGES = (BUDGET / STAGE_BYTES) > 20 ? 20 : (BUDGET / STAGE_BYTES);
     static constexpr int B_REGION = BRES ? B_RES : STAGES * B_BYTES;
@@ -253,11 +262,11 @@ __device__ __forceinline__ void st_half16(__half *p, const float *v) {
     q[1] = pk[1];
 }
 
-template <int BN, int KC, bool UP, int NACC, bool TAIL, bool BRES>
-__global__ void __launch_bounds__(tc_cfg<BN, KC, NACC, TAIL, BRES>::THREADS, 1)
+template <int BN, int KC, bool UP, int NACC, bool TAIL, bool BRES, bool HALO>
+__global__ void __launch_bounds__(tc_cfg<BN, KC, NACC, TAIL, BRES, HALO>::THREADS, 1)
 conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const tc_params p) {
-    using cfg = tc_cfg<BN, KC, NACC, TAIL, BRES>;
+    using cfg = tc_cfg<BN, KC, NACC, TAIL, BRES, HALO>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = (uint8_t *) (((uintptr_t) smem_raw + 1023) & ~(uintptr_t) 1023);
     uint8_t *sA = smem;
@@ -326,12 +335,16 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                                 ok = false;
                                 break;
                             }
-                            mbar_expect_tx(full(s), cfg::STAGE_BYTES);
+                            mbar_expect_tx(full(s), cfg::STAGE_TX);
+                            if (HALO)  // pixels x0-1 .. x0+128 of the kernel row's input row
+                                tma_load_4d(sA0 + s * cfg::A_BYTES, &tmA, full(s), c * KC, tp.x0 - 1,
+                                            tp.y0 + kh - 1, tp.b0);
 #pragma unroll
                             for (int i = 0; i < cfg::TPS; i++) {
                                 const int kw = kw0 + i;
-                                tma_load_4d(sA0 + s * cfg::A_BYTES + i * cfg::A_TAP, &tmA, full(s), c * KC,
-                                            tp.x0 + kw - 1, tp.y0 + kh - 1, tp.b0);
+                                if (!HALO)
+                                    tma_load_4d(sA0 + s * cfg::A_BYTES + i * cfg::A_TAP, &tmA, full(s),
+                                                c * KC, tp.x0 + kw - 1, tp.y0 + kh - 1, tp.b0);
                                 // weight column of (tap, chunk): tap * IC + c * KC
                                 if (!BRES)
                                     tma_load_2d(sB0 + s * cfg::B_BYTES + i * cfg::B_TAP, &tmB, full(s),
@@ -387,7 +400,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     for (int i = 0; i < cfg::TPS; i++)
 #pragma unroll
                         for (int kx = 0; kx < KC / 16; kx++)  // +32 bytes along K per step
-                            umma_f16(d_tmem, ad + ((i * cfg::A_TAP) >> 4) + 2 * kx,
+                            umma_f16(d_tmem, ad + ((i * (HALO ? KC * 2 : cfg::A_TAP)) >> 4) + 2 * kx,
                                      bd + ((i * cfg::B_TAP) >> 4) + 2 * kx, cfg::IDESC, (kk | i | kx) != 0);
                     umma_commit(empty(s));
                     if (++s == cfg::STAGES) {
@@ -645,9 +658,9 @@ int sm_count() {
     return n;
 }
 
-template <int BN, int KC, bool UP, int NACC, bool TAIL, bool BRES = false>
+template <int BN, int KC, bool UP, int NACC, bool TAIL, bool BRES = false, bool HALO = false>
 cudaError_t run_tc(const conv_params &cp, const tail_params *tl, cudaStream_t st) {
-    using cfg = tc_cfg<BN, KC, NACC, TAIL, BRES>;
+    using cfg = tc_cfg<BN, KC, NACC, TAIL, BRES, HALO>;
     auto enc = encode_fn();
     if (!enc) return cudaErrorNotSupported;
     tc_params p{};
@@ -670,6 +683,7 @@ cudaError_t run_tc(const conv_params &cp, const tail_params *tl, cudaStream_t st
     if (nt >= (1ll << 30)) return cudaErrorInvalidValue;
     p.num_tiles = (int) nt;
     if (BRES && (p.cpt != 1 || p.tiles_n != 1)) return cudaErrorInvalidValue;  // 9 taps x 1 chunk, 1 N tile
+    if (HALO && (p.bw != BM || p.bh != 1 || p.bb != 1)) return cudaErrorInvalidValue;  // one-row tiles
     p.y = (__half *) cp.y;
     p.inv_den = cp.inv_den;
     p.den_stride = cp.den_stride;
@@ -705,8 +719,8 @@ cudaError_t run_tc(const conv_params &cp, const tail_params *tl, cudaStream_t st
                                     (cuuint64_t) cp.B};
         const cuuint64_t strides[3] = {(cuuint64_t) cp.IC * 2, (cuuint64_t) cp.W * cp.IC * 2,
                                        (cuuint64_t) cp.H * cp.W * cp.IC * 2};
-        const cuuint32_t box[4] = {(cuuint32_t) KC, (cuuint32_t) p.bw, (cuuint32_t) p.bh,
-                                   (cuuint32_t) p.bb};
+        const cuuint32_t box[4] = {(cuuint32_t) KC, (cuuint32_t) (HALO ? cfg::HALO_ROWS : p.bw),
+                                   (cuuint32_t) p.bh, (cuuint32_t) p.bb};
         const cuuint32_t es[4] = {1, 1, 1, 1};
         if (enc(&tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, (void *) cp.x, dims, strides, box, es,
                 CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -730,13 +744,13 @@ cudaError_t run_tc(const conv_params &cp, const tail_params *tl, cudaStream_t st
     int dev = 0;
     cudaGetDevice(&dev);
     if (!(attr_set >> (dev & 63) & 1)) {
-        const cudaError_t e = cudaFuncSetAttribute(conv_tc_kernel<BN, KC, UP, NACC, TAIL, BRES>,
+        const cudaError_t e = cudaFuncSetAttribute(conv_tc_kernel<BN, KC, UP, NACC, TAIL, BRES, HALO>,
                                                    cudaFuncAttributeMaxDynamicSharedMemorySize, cfg::SMEM);
         if (e != cudaSuccess) return e;
         attr_set |= 1ull << (dev & 63);
     }
     const int grid = (int) (p.num_tiles < sm_count() ? p.num_tiles : sm_count());
-    conv_tc_kernel<BN, KC, UP, NACC, TAIL, BRES><<<grid, cfg::THREADS, cfg::SMEM, st>>>(tmA, tmB, p);
+    conv_tc_kernel<BN, KC, UP, NACC, TAIL, BRES, HALO><<<grid, cfg::THREADS, cfg::SMEM, st>>>(tmA, tmB, p);
     return cudaGetLastError();
 }
 
@@ -756,7 +770,10 @@ cudaError_t launch_conv_tc(bool up, const conv_params &p, cudaStream_t st) {
     if (N >= 256)
         return up ? run_tc<256, 64, true, 2, false>(p, nullptr, st)
                   : run_tc<256, 64, false, 2, false>(p, nullptr, st);
-    if (N == 128 && up && p.IC == 64) return run_tc<128, 64, true, 4, false, true>(p, nullptr, st);
+    if (N == 128 && up && p.IC == 64) {
+        if (p.W >= BM) return run_tc<128, 64, true, 4, false, true, true>(p, nullptr, st);
+        return run_tc<128, 64, true, 4, false, true>(p, nullptr, st);
+    }
     if (N == 128)
         return up ? run_tc<128, 64, true, 4, false>(p, nullptr, st)
                   : run_tc<128, 64, false, 4, false>(p, nullptr, st);
@@ -769,10 +786,17 @@ bool conv_tail_tc_supported(int IC, int OC, int r) {
 
 cudaError_t launch_conv_tail_tc(const conv_params &p, const tail_params &t, cudaStream_t st) {
     if (!conv_tail_tc_supported(p.IC, p.OC, p.W) || !p.err || p.H != p.W) return cudaErrorInvalidValue;
+    const bool halo = p.W >= BM;  // one-row tiles: taps share a halo box
     switch (p.OC) {
-        case 32: return run_tc<32, 32, false, 4, true, true>(p, &t, st);
-        case 64: return run_tc<64, 64, false, 4, true>(p, &t, st);
-        case 128: return run_tc<128, 64, false, 4, true>(p, &t, st);
+        case 32:
+            return halo ? run_tc<32, 32, false, 4, true, true, true>(p, &t, st)
+                        : run_tc<32, 32, false, 4, true, true>(p, &t, st);
+        case 64:
+            return halo ? run_tc<64, 64, false, 4, true, false, true>(p, &t, st)
+                        : run_tc<64, 64, false, 4, true>(p, &t, st);
+        case 128:
+            return halo ? run_tc<128, 64, false, 4, true, false, true>(p, &t, st)
+                        : run_tc<128, 64, false, 4, true>(p, &t, st);
         default: return run_tc<256, 64, false, 2, true>(p, &t, st);
     }
 }
