@@ -61,6 +61,7 @@ struct tc_params {
     const float *lin;
     __half *trunk;
     const float *tsn;  // next up-conv style, multiplied into the trunk
+    const float4 *proj;  // last level: ToRGB conv.0 applied to the feats per pixel
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -568,8 +569,23 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 // no trunk, so it needs neither the conv2 output nor TMEM here.
                 const bool need_out = p.trunk != nullptr;
                 float g0 = 0.0f, g1 = 0.0f, g2 = 0.0f;
+                if (!need_out && p.proj) {
+                    // ToRGB of the gathered channels = gather of the projected
+                    // feats (both linear): four 16-byte taps instead of 4 x BN
+#pragma unroll
+                    for (int kk = 0; kk < 4; kk++) {
+                        if (trow[kk] < 0) continue;
+                        const float4 q = __ldg(p.proj + trow[kk]);
+                        g0 = fmaf(twt[kk], q.x, g0);
+                        g1 = fmaf(twt[kk], q.y, g1);
+                        g2 = fmaf(twt[kk], q.z, g2);
+                    }
+                    g0 *= m;
+                    g1 *= m;
+                    g2 *= m;
+                }
 #pragma unroll 1
-                for (int c0 = 0; c0 < BN; c0 += 16) {
+                for (int c0 = 0; c0 < BN && (need_out || !p.proj); c0 += 16) {
                     uint32_t rr[16];
                     if (need_out) tmem_ld16(taddr0 + c0, rr);
                     float smp[16];
@@ -711,6 +727,7 @@ cudaError_t run_tc(const conv_params &cp, const tail_params *tl, cudaStream_t st
         p.lin = tl->lin;
         p.trunk = (__half *) tl->trunk;
         p.tsn = tl->snext;
+        p.proj = tl->proj;
     }
 
     CUtensorMap tmA, tmB;

@@ -229,10 +229,44 @@ cudaError_t dispatch_tail(const tail_params &p, cudaStream_t st) {
     }
 }
 
+// ToRGB's 1x1 conv (before its bias and activation) is linear, and so is
+// the bilinear gather: rW . gather(feat) = gather(rW . feat). Where nothing
+// else reads the gathered channels (the last level, which has no trunk), the
+// tail gathers this 3-channel projection of the portrait's feats instead of
+// all C channels; it is computed once per portrait.
+__device__ __forceinline__ float to_f(float v) { return v; }
+__device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
+
+template <typename T>
+__global__ void project_feats_kernel(const T *__restrict__ feat, int64_t npx, int C,
+                                     const float *__restrict__ rW, float4 *__restrict__ proj) {
+    for (int64_t i = (int64_t) blockIdx.x * blockDim.x + threadIdx.x; i < npx;
+         i += (int64_t) gridDim.x * blockDim.x) {
+        float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f;
+        for (int c = 0; c < C; c++) {
+            const float f = to_f(feat[i * C + c]);
+            a0 = fmaf(__ldg(rW + c), f, a0);
+            a1 = fmaf(__ldg(rW + C + c), f, a1);
+            a2 = fmaf(__ldg(rW + 2 * C + c), f, a2);
+        }
+        proj[i] = make_float4(a0, a1, a2, 0.0f);
+    }
+}
+
 }  // namespace
 
 cudaError_t launch_tail(bool f16, const tail_params &p, cudaStream_t st) {
     return f16 ? dispatch_tail<__half>(p, st) : dispatch_tail<float>(p, st);
+}
+
+cudaError_t launch_project_feats(bool f16, const void *feat, int64_t npx, int C, const float *rW,
+                                 float4 *proj, cudaStream_t st) {
+    const int blocks = (int) std::min<int64_t>((npx + 255) / 256, 148 * 8);
+    if (f16)
+        project_feats_kernel<__half><<<blocks, 256, 0, st>>>((const __half *) feat, npx, C, rW, proj);
+    else
+        project_feats_kernel<float><<<blocks, 256, 0, st>>>((const float *) feat, npx, C, rW, proj);
+    return cudaGetLastError();
 }
 
 }  // namespace tpmd

@@ -96,6 +96,10 @@ struct tpmd_ctx {
     void *warena = nullptr, *farena = nullptr;
     size_t wbytes = 0, fbytes = 0;
     bool wready = false, fready = false;
+    // the last level's feats projected by its ToRGB conv.0 weights; lives
+    // after the feats arena (not broadcast: every rank derives its own)
+    float4 *proj = nullptr;
+    bool pready = false;
 
     // workspace
     void *ws = nullptr;
@@ -466,7 +470,10 @@ tpmd_ctx *tpmd_create(int device, int dtype, int max_batch) {
               c->ck(cudaStreamCreateWithFlags(&c->copy_stream, cudaStreamNonBlocking), "stream") &&
               c->ck(cudaStreamCreateWithFlags(&c->cap_stream, cudaStreamNonBlocking), "stream") &&
               c->ck(cudaMalloc(&c->warena, c->wbytes), "cudaMalloc(weights)") &&
-              c->ck(cudaMalloc(&c->farena, c->fbytes), "cudaMalloc(feats)") && alloc_workspace(c);
+              c->ck(cudaMalloc(&c->farena, c->fbytes + (size_t) 512 * 512 * sizeof(float4)),
+                    "cudaMalloc(feats)") &&
+              alloc_workspace(c);
+    if (ok) c->proj = (float4 *) ((char *) c->farena + c->fbytes);
     for (int i = 0; ok && i < 2; i++)
         ok = c->ck(cudaEventCreateWithFlags(&c->ev_done[i], cudaEventDisableTiming), "event") &&
              c->ck(cudaEventCreateWithFlags(&c->ev_copied[i], cudaEventDisableTiming), "event");
@@ -521,6 +528,25 @@ int tpmd_set_tensor(tpmd_ctx *c, const char *name, const float *data, int64_t n)
     return 0;
 }
 
+}  // extern "C"
+namespace {
+// Recomputed whenever the weights or the feats change (both must be set).
+bool make_proj(tpmd_ctx *c) {
+    c->pready = false;
+    if (!c->wready || !c->fready) return true;
+    const int j = N_LEVELS - 1, r = 8 << j;
+    if (!c->ck(cudaSetDevice(c->device), "cudaSetDevice") ||
+        !c->ck(launch_project_feats(c->f16, (const char *) c->farena + c->feat_off[j], (int64_t) r * r,
+                                    ST_OC[j], c->Wf(c->stage[j].rW), c->proj, c->stream),
+               "project feats") ||
+        !c->ck(cudaStreamSynchronize(c->stream), "project feats"))
+        return false;
+    c->pready = true;
+    return true;
+}
+}  // namespace
+extern "C" {
+
 int tpmd_prepare(tpmd_ctx *c) {
     if (!c) return -1;
     for (auto &kv : c->spec)
@@ -572,7 +598,7 @@ int tpmd_prepare(tpmd_ctx *c) {
                "upload weights"))
         return -1;
     c->wready = true;
-    return 0;
+    return make_proj(c) ? 0 : -1;
 }
 
 int tpmd_set_feats(tpmd_ctx *c, const float *const feats[TPMD_N_LEVELS]) {
@@ -592,7 +618,7 @@ int tpmd_set_feats(tpmd_ctx *c, const float *const feats[TPMD_N_LEVELS]) {
                "upload feats"))
         return -1;
     c->fready = true;
-    return 0;
+    return make_proj(c) ? 0 : -1;
 }
 
 int tpmd_batch(const tpmd_ctx *c) { return c ? c->max_batch : -1; }
@@ -613,7 +639,7 @@ int tpmd_arena_adopt(tpmd_ctx *c, int which) {
         c->fready = true;
     else
         return c->fail("tpmd_arena_adopt: bad argument"), -1;
-    return 0;
+    return make_proj(c) ? 0 : -1;
 }
 
 }  // extern "C"
@@ -743,6 +769,7 @@ bool enqueue_chunk(tpmd_ctx *c, const ws_view &w, const float *styles, int64_t n
         t.lin = c->Wf(S.lin);
         t.trunk = j == N_LEVELS - 1 ? nullptr : w.actB;
         t.snext = j == N_LEVELS - 1 ? nullptr : w.s_all + c->conv[3 + 2 * j].s_off;
+        t.proj = j == N_LEVELS - 1 ? c->proj : nullptr;
         if (fused) {
             const conv_params p = conv_p(2 + 2 * j, w.actC, keep_conv2 ? w.actA : nullptr, r, nullptr);
             if (!launch(c, "conv2tail_r" + std::to_string(r), st,
@@ -800,6 +827,7 @@ bool device_ok(tpmd_ctx *c) {
 bool ready(tpmd_ctx *c) {
     if (!c->wready) return c->fail("weights not prepared (tpmd_prepare)");
     if (!c->fready) return c->fail("feats not set (tpmd_set_feats)");
+    if (!c->pready) return c->fail("feats projection missing (set the feats again)");
     return true;
 }
 

@@ -62,6 +62,7 @@ struct tail_params {
     const float *lin;         // [r] identity grid -1 + 2i/(r-1)
     void *trunk;              // [B][r][r][OC] or nullptr (last level)
     const float *snext;       // next up-conv style, snext[b*s_stride + c]
+    const float4 *proj;       // [r*r] rW . feat per feats pixel (.w = 0), or nullptr
 };
 
 // launchers; `f16` selects the f16 (else f32) instantiation
@@ -81,6 +82,9 @@ cudaError_t launch_conv1_input(bool f16, const float *input, const float *s, int
                                int B, void *x0, cudaStream_t st);
 cudaError_t launch_conv_simt(bool f16, bool up, const conv_params &p, cudaStream_t st);
 cudaError_t launch_tail(bool f16, const tail_params &p, cudaStream_t st);
+// proj[i] = (rW[0] . feat[i], rW[1] . feat[i], rW[2] . feat[i], 0) over C channels
+cudaError_t launch_project_feats(bool f16, const void *feat, int64_t npx, int C, const float *rW,
+                                 float4 *proj, cudaStream_t st);
 
 // tcgen05 path (f16)
 cudaError_t launch_conv_tc(bool up, const conv_params &p, cudaStream_t st);
