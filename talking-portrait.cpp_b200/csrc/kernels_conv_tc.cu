@@ -42,6 +42,7 @@ struct tc_params {
     int kiters, cpt;           // k-steps per tile, channel chunks per tap
     int bw, bh, bb;            // pixel box of one M tile
     int tiles_x, tiles_y, tiles_n;
+    int lg_x, lg_y, lg_n;      // their log2
     int num_tiles;
     __half *y;
     const float *inv_den;
@@ -162,6 +163,17 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
         : "r"(taddr));
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+        "%12, %13, %14, %15, %16};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+        "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
 
 template <int BN, int KC, int NACC, bool TAIL, bool BRES, bool HALO = false>
 struct tc_cfg {
@@ -176,7 +188,7 @@ struct tc_cfg {
     static constexpr int A_HALO = 136 * KC * 2;
     // fused tail: the ToFlow and ToRGB weights [3][BN] each, shared by all
     // epilogue groups
-    static constexpr int EXTRA = TAIL ? 6 * BN * 4 : 0;
+    static constexpr int EXTRA = TAIL ? (3 * BN + 32) * 4 : 0;  // ToFlow weights, up kernels
     // BRES: the whole weight matrix (9 taps x one KC chunk) stays resident in
     // shared memory for the kernel's lifetime instead of being re-loaded for
     // every pixel tile; stages then carry only A
@@ -211,14 +223,15 @@ struct tc_cfg {
 struct tile_pos {
     int n0, b0, y0, x0;
 };
+// tile counts along n, x and y are powers of two (log2 in lg_*)
 __device__ __forceinline__ tile_pos tile_of(const tc_params &p, int t, int BN) {
     tile_pos r;
-    const int nt = t % p.tiles_n;
-    const int m = t / p.tiles_n;
-    const int xt = m % p.tiles_x;
-    const int m2 = m / p.tiles_x;
-    const int yt = m2 % p.tiles_y;
-    const int bt = m2 / p.tiles_y;
+    const int nt = t & (p.tiles_n - 1);
+    const int m = t >> p.lg_n;
+    const int xt = m & (p.tiles_x - 1);
+    const int m2 = m >> p.lg_x;
+    const int yt = m2 & (p.tiles_y - 1);
+    const int bt = m2 >> p.lg_y;
     r.n0 = nt * BN;
     r.x0 = xt * p.bw;
     r.y0 = yt * p.bh;
@@ -297,10 +310,11 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
-    if (TAIL) {  // sx[0..3BN): ToRGB weights, sx[3BN..6BN): ToFlow weights
-        for (int i = threadIdx.x; i < 3 * BN; i += blockDim.x) {
-            sx[i] = __ldg(p.rW + i);
-            sx[3 * BN + i] = __ldg(p.fW + i);
+    if (TAIL) {  // sx[0..3BN): ToFlow weights, then the flow and rgb up-sampling kernels
+        for (int i = threadIdx.x; i < 3 * BN; i += blockDim.x) sx[i] = __ldg(p.fW + i);
+        for (int i = threadIdx.x; i < 16; i += blockDim.x) {
+            sx[3 * BN + i] = __ldg(p.fup + i);
+            sx[3 * BN + 16 + i] = __ldg(p.rup + i);
         }
     }
     if (warp == 1) {
@@ -428,17 +442,56 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         const int row = q * 32 + lane;
         const int bx = row % p.bw, by = (row / p.bw) % p.bh, bz = row / (p.bw * p.bh);
         const uint32_t taddr0 = tmem_base + ((uint32_t) (q * 32) << 16) + g * BN;
-        const float *s_rw = sx, *s_fw = sx + 3 * BN;
+        const float *s_fw = sx, *s_up = sx + 3 * BN;
         uint32_t k = g;
         for (int t = blockIdx.x + g * gridDim.x; t < p.num_tiles; t += NACC * gridDim.x, k += NACC) {
+            const tile_pos tp = tile_of(p, t, BN);
+            const int b = tp.b0 + bz, y = tp.y0 + by, x = tp.x0 + bx;
+            // TAIL: the up-sampled flow and rgb skips depend on the pixel only;
+            // their loads are issued before the wait for the accumulator
+            float skf[3] = {0.0f, 0.0f, 0.0f}, skr[3] = {0.0f, 0.0f, 0.0f};
+            if constexpr (TAIL) {
+                const int h = p.W >> 1;
+                const int px = x & 1, py = y & 1, nx = x >> 1, ny = y >> 1;
+                int uoff[4];
+                float ukf[4], ukr[4];
+#pragma unroll
+                for (int a = 0; a < 2; a++)
+#pragma unroll
+                    for (int bb = 0; bb < 2; bb++) {
+                        const int sy = ny + py - 1 + a, sx2 = nx + px - 1 + bb;
+                        const bool in = sy >= 0 && sy < h && sx2 >= 0 && sx2 < h;
+                        const int uk = (px + 2 * bb) + 4 * (py + 2 * a);
+                        uoff[2 * a + bb] = in ? sy * h + sx2 : -1;
+                        ukf[2 * a + bb] = s_up[uk];
+                        ukr[2 * a + bb] = s_up[16 + uk];
+                    }
+                const int64_t hh = (int64_t) h * h;
+                if (p.skipf_prev) {
+#pragma unroll
+                    for (int kk = 0; kk < 3; kk++) {
+                        const float *pl = p.skipf_prev + ((int64_t) b * 3 + kk) * hh;
+#pragma unroll
+                        for (int i = 0; i < 4; i++)
+                            if (uoff[i] >= 0) skf[kk] = fmaf(__ldg(pl + uoff[i]), ukf[i], skf[kk]);
+                    }
+                }
+                if (p.skip_prev) {
+#pragma unroll
+                    for (int kk = 0; kk < 3; kk++) {
+                        const float *pl = p.skip_prev + ((int64_t) b * 3 + kk) * hh;
+#pragma unroll
+                        for (int i = 0; i < 4; i++)
+                            if (uoff[i] >= 0) skr[kk] = fmaf(__ldg(pl + uoff[i]), ukr[i], skr[kk]);
+                    }
+                }
+            }
             const bool ok = __all_sync(0xffffffffu, mbar_wait(tfull(g), (k / NACC) & 1));
             if (!ok) {
                 if (lane == 0) atomicExch(p.err, 1);
                 break;
             }
             tc_fence_after();
-            const tile_pos tp = tile_of(p, t, BN);
-            const int b = tp.b0 + bz, y = tp.y0 + by, x = tp.x0 + bx;
             if constexpr (!TAIL) {
                 const bool valid = b < p.B;
 #pragma unroll 1
@@ -490,9 +543,13 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 const float *fden = p.inv_den + (int64_t) b * p.den_stride;
                 const float *ffs = p.fs + (int64_t) b * p.s_stride;
                 const float *fsn = p.trunk ? p.tsn + (int64_t) b * p.s_stride : nullptr;
-                const int r = p.W, h = r >> 1;
+                const int r = p.W;
                 const int64_t pix = ((int64_t) b * p.H + y) * p.W + x;
-                // pass 1: conv2 output (f32, never stored) -> ToFlow sums
+                // the last level has no trunk: it needs neither the conv2 output
+                // nor TMEM after pass 1
+                const bool need_out = p.trunk != nullptr;
+                // pass 1: conv2 output (f32, never stored) -> ToFlow sums; the
+                // activation goes back into TMEM for pass 2
                 float f0 = 0.0f, f1 = 0.0f, f2 = 0.0f;
 #pragma unroll 1
                 for (int c0 = 0; c0 < BN; c0 += 16) {
@@ -507,40 +564,19 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                         float a = fmaf(__uint_as_float(rr[i]), den[i], bias[i]);
                         a = a > 0.0f ? a : 0.2f * a;
                         v[i] = a;
+                        rr[i] = __float_as_uint(a);
                         const float xs = a * fsv[i];  // ToFlow input: out * style
                         f0 = fmaf(s_fw[c0 + i], xs, f0);
                         f1 = fmaf(s_fw[BN + c0 + i], xs, f1);
                         f2 = fmaf(s_fw[2 * BN + c0 + i], xs, f2);
                     }
+                    if (need_out) tmem_st16(taddr0 + c0, rr);
                     if (p.y) st_half16(p.y + pix * BN + c0, v);  // conv2 tap (debug)
                 }
-                // up-sampling taps of (x, y): the same four source offsets and
-                // kernel indices serve all three channels of both skips
-                int uoff[4], uk[4];
-                {
-                    const int px = x & 1, py = y & 1, nx = x >> 1, ny = y >> 1;
-#pragma unroll
-                    for (int a = 0; a < 2; a++)
-#pragma unroll
-                        for (int bb = 0; bb < 2; bb++) {
-                            const int sy = ny + py - 1 + a, sx2 = nx + px - 1 + bb;
-                            const bool in = sy >= 0 && sy < h && sx2 >= 0 && sx2 < h;
-                            uoff[2 * a + bb] = in ? sy * h + sx2 : -1;
-                            uk[2 * a + bb] = (px + 2 * bb) + 4 * (py + 2 * a);
-                        }
-                }
-                auto up2 = [&](const float *plane, const float *k4) {
-                    float acc = 0.0f;
-#pragma unroll
-                    for (int i = 0; i < 4; i++)
-                        if (uoff[i] >= 0) acc = fmaf(__ldg(plane + uoff[i]), __ldg(k4 + uk[i]), acc);
-                    return acc;
-                };
+                if (need_out) tmem_wait_st();
                 float fl[3] = {f0 + __ldg(p.fb), f1 + __ldg(p.fb + 1), f2 + __ldg(p.fb + 2)};
-                if (p.skipf_prev) {
 #pragma unroll
-                    for (int kk = 0; kk < 3; kk++) fl[kk] += up2(p.skipf_prev + ((int64_t) b * 3 + kk) * h * h, p.fup);
-                }
+                for (int kk = 0; kk < 3; kk++) fl[kk] += skf[kk];
                 const int64_t rr2 = (int64_t) r * r;
                 if (p.skipf_out) {
 #pragma unroll
@@ -565,29 +601,22 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     trow[kk] = (sane && cx >= 0 && cx < r && cy >= 0 && cy < r) ? cy * r + cx : -1;
                     twt[kk] = ((kk & 1) ? wx : 1.0f - wx) * ((kk >> 1) ? wy : 1.0f - wy);
                 }
-                // pass 2: gather, blend, ToRGB sums, trunk. The last level has
-                // no trunk, so it needs neither the conv2 output nor TMEM here.
-                const bool need_out = p.trunk != nullptr;
+                // ToRGB of the gathered channels = gather of the feats projected
+                // by ToRGB's 1x1 conv (both linear): four 16-byte taps
                 float g0 = 0.0f, g1 = 0.0f, g2 = 0.0f;
-                if (!need_out && p.proj) {
-                    // ToRGB of the gathered channels = gather of the projected
-                    // feats (both linear): four 16-byte taps instead of 4 x BN
 #pragma unroll
-                    for (int kk = 0; kk < 4; kk++) {
-                        if (trow[kk] < 0) continue;
-                        const float4 q = __ldg(p.proj + trow[kk]);
-                        g0 = fmaf(twt[kk], q.x, g0);
-                        g1 = fmaf(twt[kk], q.y, g1);
-                        g2 = fmaf(twt[kk], q.z, g2);
-                    }
-                    g0 *= m;
-                    g1 *= m;
-                    g2 *= m;
+                for (int kk = 0; kk < 4; kk++) {
+                    if (trow[kk] < 0) continue;
+                    const float4 pq = __ldg(p.proj + trow[kk]);
+                    g0 = fmaf(twt[kk], pq.x, g0);
+                    g1 = fmaf(twt[kk], pq.y, g1);
+                    g2 = fmaf(twt[kk], pq.z, g2);
                 }
+                // pass 2 (levels with a trunk): gather, blend, trunk
 #pragma unroll 1
-                for (int c0 = 0; c0 < BN && (need_out || !p.proj); c0 += 16) {
+                for (int c0 = 0; c0 < BN && need_out; c0 += 16) {
                     uint32_t rr[16];
-                    if (need_out) tmem_ld16(taddr0 + c0, rr);
+                    tmem_ld16(taddr0 + c0, rr);
                     float smp[16];
 #pragma unroll
                     for (int i = 0; i < 16; i++) smp[i] = 0.0f;
@@ -599,38 +628,21 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 #pragma unroll
                         for (int i = 0; i < 16; i++) smp[i] = fmaf(twt[kk], f[i], smp[i]);
                     }
-                    if (!need_out) {
-#pragma unroll
-                        for (int i = 0; i < 16; i++) {
-                            const float w = smp[i] * m;
-                            g0 = fmaf(s_rw[c0 + i], w, g0);
-                            g1 = fmaf(s_rw[BN + c0 + i], w, g1);
-                            g2 = fmaf(s_rw[2 * BN + c0 + i], w, g2);
-                        }
-                        continue;
-                    }
-                    float den[16], bias[16], sn[16];
-                    ld_f16x(fden + c0, den);
-                    ld_f16x(p.bias + c0, bias);
+                    float sn[16];
                     ld_f16x(fsn + c0, sn);
 #pragma unroll
                     for (int i = 0; i < 16; i++) {
-                        float a = fmaf(__uint_as_float(rr[i]), den[i], bias[i]);
-                        a = a > 0.0f ? a : 0.2f * a;
                         const float w = smp[i] * m;
-                        g0 = fmaf(s_rw[c0 + i], w, g0);
-                        g1 = fmaf(s_rw[BN + c0 + i], w, g1);
-                        g2 = fmaf(s_rw[2 * BN + c0 + i], w, g2);
-                        smp[i] = (w + a * om) * sn[i];  // trunk x next up-conv style
+                        smp[i] = (w + __uint_as_float(rr[i]) * om) * sn[i];  // trunk x next up-conv style
                     }
                     st_half16(p.trunk + pix * BN + c0, smp);
                 }
-                const float rg[3] = {g0, g1, g2};
+                const float rg[3] = {g0 * m, g1 * m, g2 * m};
 #pragma unroll
                 for (int kk = 0; kk < 3; kk++) {
                     float v = rg[kk] + __ldg(p.rlb + kk);
                     v = (v > 0.0f ? v : 0.2f * v) + __ldg(p.rb + kk);
-                    if (p.skip_prev) v += up2(p.skip_prev + ((int64_t) b * 3 + kk) * h * h, p.rup);
+                    if (p.skip_prev) v += skr[kk];
                     p.skip_out[((int64_t) b * 3 + kk) * rr2 + (int64_t) y * r + x] = v;
                 }
             }
@@ -649,6 +661,13 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 }
 
 // ---- host side ------------------------------------------------------------
+int ilog2(int v) {  // log2 of a power of two, else -1
+    if (v <= 0 || (v & (v - 1))) return -1;
+    int l = 0;
+    while ((1 << l) < v) l++;
+    return l;
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
     static std::once_flag once;
@@ -694,6 +713,10 @@ cudaError_t run_tc(const conv_params &cp, const tail_params *tl, cudaStream_t st
     p.tiles_x = cp.W / p.bw;
     p.tiles_y = cp.H / p.bh;
     p.tiles_n = p.N / BN;
+    p.lg_x = ilog2(p.tiles_x);
+    p.lg_y = ilog2(p.tiles_y);
+    p.lg_n = ilog2(p.tiles_n);
+    if (p.lg_x < 0 || p.lg_y < 0 || p.lg_n < 0 || p.N % BN) return cudaErrorInvalidValue;
     const int tiles_b = (cp.B + p.bb - 1) / p.bb;
     const int64_t nt = (int64_t) tiles_b * p.tiles_y * p.tiles_x * p.tiles_n;
     if (nt >= (1ll << 30)) return cudaErrorInvalidValue;
@@ -709,7 +732,8 @@ cudaError_t run_tc(const conv_params &cp, const tail_params *tl, cudaStream_t st
     p.err = cp.err;
     if (TAIL) {
         // one frame per tile and the whole channel range in one tile
-        if (!tl || p.bb != 1 || p.tiles_n != 1 || tl->OC != BN || tl->r != cp.W) return cudaErrorInvalidValue;
+        if (!tl || !tl->proj || p.bb != 1 || p.tiles_n != 1 || tl->OC != BN || tl->r != cp.W)
+            return cudaErrorInvalidValue;
         p.feat = (const __half *) tl->feat;
         p.fW = tl->fW;
         p.fs = tl->fs;

@@ -40,6 +40,12 @@ namespace {
 thread_local std::string g_create_err;
 
 size_t align256(size_t v) { return (v + 255) & ~(size_t) 255; }
+// pixels over all levels (8x8 .. 512x512): one projected-feats float4 each
+size_t proj_count() {
+    size_t n = 0;
+    for (int j = 0; j < N_LEVELS; j++) n += (size_t) (8 << j) * (8 << j);
+    return n;
+}
 
 struct conv_layout {
     std::string name;  // weight tensor name
@@ -96,9 +102,11 @@ struct tpmd_ctx {
     void *warena = nullptr, *farena = nullptr;
     size_t wbytes = 0, fbytes = 0;
     bool wready = false, fready = false;
-    // the last level's feats projected by its ToRGB conv.0 weights; lives
-    // after the feats arena (not broadcast: every rank derives its own)
+    // each level's feats projected by its ToRGB conv.0 weights ([r*r] float4
+    // per level); lives after the feats arena (not broadcast: every rank
+    // derives its own)
     float4 *proj = nullptr;
+    size_t proj_off[N_LEVELS] = {0};  // in float4
     bool pready = false;
 
     // workspace
@@ -470,10 +478,17 @@ tpmd_ctx *tpmd_create(int device, int dtype, int max_batch) {
               c->ck(cudaStreamCreateWithFlags(&c->copy_stream, cudaStreamNonBlocking), "stream") &&
               c->ck(cudaStreamCreateWithFlags(&c->cap_stream, cudaStreamNonBlocking), "stream") &&
               c->ck(cudaMalloc(&c->warena, c->wbytes), "cudaMalloc(weights)") &&
-              c->ck(cudaMalloc(&c->farena, c->fbytes + (size_t) 512 * 512 * sizeof(float4)),
+              c->ck(cudaMalloc(&c->farena, c->fbytes + proj_count() * sizeof(float4)),
                     "cudaMalloc(feats)") &&
               alloc_workspace(c);
-    if (ok) c->proj = (float4 *) ((char *) c->farena + c->fbytes);
+    if (ok) {
+        c->proj = (float4 *) ((char *) c->farena + c->fbytes);
+        size_t o = 0;
+        for (int j = 0; j < N_LEVELS; j++) {
+            c->proj_off[j] = o;
+            o += (size_t) (8 << j) * (8 << j);
+        }
+    }
     for (int i = 0; ok && i < 2; i++)
         ok = c->ck(cudaEventCreateWithFlags(&c->ev_done[i], cudaEventDisableTiming), "event") &&
              c->ck(cudaEventCreateWithFlags(&c->ev_copied[i], cudaEventDisableTiming), "event");
@@ -534,13 +549,16 @@ namespace {
 bool make_proj(tpmd_ctx *c) {
     c->pready = false;
     if (!c->wready || !c->fready) return true;
-    const int j = N_LEVELS - 1, r = 8 << j;
-    if (!c->ck(cudaSetDevice(c->device), "cudaSetDevice") ||
-        !c->ck(launch_project_feats(c->f16, (const char *) c->farena + c->feat_off[j], (int64_t) r * r,
-                                    ST_OC[j], c->Wf(c->stage[j].rW), c->proj, c->stream),
-               "project feats") ||
-        !c->ck(cudaStreamSynchronize(c->stream), "project feats"))
-        return false;
+    if (!c->ck(cudaSetDevice(c->device), "cudaSetDevice")) return false;
+    for (int j = 0; j < N_LEVELS; j++) {
+        const int r = 8 << j;
+        if (!c->ck(launch_project_feats(c->f16, (const char *) c->farena + c->feat_off[j],
+                                        (int64_t) r * r, ST_OC[j], c->Wf(c->stage[j].rW),
+                                        c->proj + c->proj_off[j], c->stream),
+                   "project feats"))
+            return false;
+    }
+    if (!c->ck(cudaStreamSynchronize(c->stream), "project feats")) return false;
     c->pready = true;
     return true;
 }
@@ -769,7 +787,7 @@ bool enqueue_chunk(tpmd_ctx *c, const ws_view &w, const float *styles, int64_t n
         t.lin = c->Wf(S.lin);
         t.trunk = j == N_LEVELS - 1 ? nullptr : w.actB;
         t.snext = j == N_LEVELS - 1 ? nullptr : w.s_all + c->conv[3 + 2 * j].s_off;
-        t.proj = j == N_LEVELS - 1 ? c->proj : nullptr;
+        t.proj = c->proj + c->proj_off[j];
         if (fused) {
             const conv_params p = conv_p(2 + 2 * j, w.actC, keep_conv2 ? w.actA : nullptr, r, nullptr);
             if (!launch(c, "conv2tail_r" + std::to_string(r), st,
