@@ -175,7 +175,7 @@ __device__ __forceinline__ void tmem_wait_st() {
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
-template <int BN, int KC, int NACC, bool TAIL, bool BRES, bool HALO = false>
+template <int BN, int KC, int NACC, bool TAIL, bool BRES, bool HALO = false, int RPS = 1>
 struct tc_cfg {
     static constexpr int A_TAP = BM * KC * 2;   // one tap's A tile
     static constexpr int B_TAP = BN * KC * 2;   // one tap's B tile
@@ -198,9 +198,12 @@ struct tc_cfg {
     // in one stage, so the per-stage barrier round trip is paid 3x less often
     static constexpr int TPS =
         HALO ? 3 : BRES ? (BUDGET / (3 * A_TAP) >= 3 ? 3 : 1) : (BN <= 128 ? 3 : 1);
-    static constexpr int A_BYTES = HALO ? A_HALO : TPS * A_TAP;     // per stage (space)
-    static constexpr int A_TX = HALO ? HALO_ROWS * KC * 2 : A_BYTES;  // per stage (loaded)
-    static constexpr int B_BYTES = BRES ? 0 : TPS * B_TAP;  // per stage
+    // RPS: kernel rows per stage (HALO with resident weights only); a stage
+    // then holds RPS halo boxes and TAPS = 3 * RPS taps, fewer commits per tile
+    static constexpr int TAPS = HALO ? 3 * RPS : TPS;
+    static constexpr int A_BYTES = HALO ? RPS * A_HALO : TPS * A_TAP;     // per stage (space)
+    static constexpr int A_TX = HALO ? RPS * HALO_ROWS * KC * 2 : A_BYTES;  // per stage (loaded)
+    static constexpr int B_BYTES = BRES ? 0 : TAPS * B_TAP;  // per stage
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int STAGE_TX = A_TX + B_BYTES;
     // as deep as shared memory allows (small stages hide more TMA latency)
@@ -218,6 +221,7 @@ struct tc_cfg {
     static_assert((TMEM_COLS & (TMEM_COLS - 1)) == 0 && TMEM_COLS >= 32 && TMEM_COLS <= 512, "TMEM");
     static_assert(SMEM <= 232448, "shared memory");
     static_assert(STAGES >= 2, "pipeline depth");
+    static_assert(RPS == 1 || (RPS == 3 && HALO && BRES), "rows per stage");
 };
 
 struct tile_pos {
@@ -276,11 +280,11 @@ __device__ __forceinline__ void st_half16(__half *p, const float *v) {
     q[1] = pk[1];
 }
 
-template <int BN, int KC, bool UP, int NACC, bool TAIL, bool BRES, bool HALO>
-__global__ void __launch_bounds__(tc_cfg<BN, KC, NACC, TAIL, BRES, HALO>::THREADS, 1)
+template <int BN, int KC, bool UP, int NACC, bool TAIL, bool BRES, bool HALO, int RPS>
+__global__ void __launch_bounds__(tc_cfg<BN, KC, NACC, TAIL, BRES, HALO, RPS>::THREADS, 1)
 conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const tc_params p) {
-    using cfg = tc_cfg<BN, KC, NACC, TAIL, BRES, HALO>;
+    using cfg = tc_cfg<BN, KC, NACC, TAIL, BRES, HALO, RPS>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = (uint8_t *) (((uintptr_t) smem_raw + 1023) & ~(uintptr_t) 1023);
     uint8_t *sA = smem;
@@ -343,7 +347,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             }
             for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
                 const tile_pos tp = tile_of(p, t, BN);
-                for (int kh = 0; kh < 3 && ok; kh++) {
+                for (int kh = 0; kh < 3 && ok; kh += RPS) {
                     for (int c = 0; c < p.cpt && ok; c++) {
                         for (int kw0 = 0; kw0 < 3; kw0 += cfg::TPS, it++) {
                             if (!mbar_wait(empty(s), ph ^ 1)) {
@@ -351,9 +355,11 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                                 break;
                             }
                             mbar_expect_tx(full(s), cfg::STAGE_TX);
-                            if (HALO)  // pixels x0-1 .. x0+128 of the kernel row's input row
-                                tma_load_4d(sA0 + s * cfg::A_BYTES, &tmA, full(s), c * KC, tp.x0 - 1,
-                                            tp.y0 + kh - 1, tp.b0);
+                            if (HALO)  // pixels x0-1 .. x0+128 of the kernel rows' input rows
+#pragma unroll
+                                for (int r = 0; r < RPS; r++)
+                                    tma_load_4d(sA0 + s * cfg::A_BYTES + r * cfg::A_HALO, &tmA, full(s),
+                                                c * KC, tp.x0 - 1, tp.y0 + kh + r - 1, tp.b0);
 #pragma unroll
                             for (int i = 0; i < cfg::TPS; i++) {
                                 const int kw = kw0 + i;
@@ -402,7 +408,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + a * BN;
                 int tap0 = 0;  // first tap of the stage (BRES: its resident B tile)
-                for (int kk = 0; kk < p.kiters; kk++, tap0 += cfg::TPS) {
+                for (int kk = 0; kk < p.kiters; kk++, tap0 += cfg::TAPS) {
                     if (!mbar_wait(full(s), ph)) {
                         ok = false;
                         break;
@@ -412,10 +418,12 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     const uint64_t bd = BRES ? bd0 + (uint64_t) ((tap0 * cfg::B_TAP) >> 4)
                                              : bd0 + (uint64_t) ((s * cfg::B_BYTES) >> 4);
 #pragma unroll
-                    for (int i = 0; i < cfg::TPS; i++)
+                    for (int i = 0; i < cfg::TAPS; i++)
 #pragma unroll
                         for (int kx = 0; kx < KC / 16; kx++)  // +32 bytes along K per step
-                            umma_f16(d_tmem, ad + ((i * (HALO ? KC * 2 : cfg::A_TAP)) >> 4) + 2 * kx,
+                            umma_f16(d_tmem,
+                                     ad + (((HALO ? (i / 3) * cfg::A_HALO + (i % 3) * KC * 2 : i * cfg::A_TAP)) >> 4) +
+                                         2 * kx,
                                      bd + ((i * cfg::B_TAP) >> 4) + 2 * kx, cfg::IDESC, (kk | i | kx) != 0);
                     umma_commit(empty(s));
                     if (++s == cfg::STAGES) {
@@ -693,9 +701,9 @@ int sm_count() {
     return n;
 }
 
-template <int BN, int KC, bool UP, int NACC, bool TAIL, bool BRES = false, bool HALO = false>
+template <int BN, int KC, bool UP, int NACC, bool TAIL, bool BRES = false, bool HALO = false, int RPS = 1>
 cudaError_t run_tc(const conv_params &cp, const tail_params *tl, cudaStream_t st) {
-    using cfg = tc_cfg<BN, KC, NACC, TAIL, BRES, HALO>;
+    using cfg = tc_cfg<BN, KC, NACC, TAIL, BRES, HALO, RPS>;
     auto enc = encode_fn();
     if (!enc) return cudaErrorNotSupported;
     tc_params p{};
@@ -706,7 +714,7 @@ cudaError_t run_tc(const conv_params &cp, const tail_params *tl, cudaStream_t st
     p.OC = cp.OC;
     p.N = UP ? 4 * cp.OC : cp.OC;
     p.cpt = cp.IC / KC;
-    p.kiters = 9 * p.cpt / cfg::TPS;  // pipeline stages per tile
+    p.kiters = 9 * p.cpt / cfg::TAPS;  // pipeline stages per tile
     p.bw = cp.W < BM ? cp.W : BM;
     p.bh = cp.H < BM / p.bw ? cp.H : BM / p.bw;
     p.bb = BM / (p.bw * p.bh);
@@ -785,13 +793,13 @@ cudaError_t run_tc(const conv_params &cp, const tail_params *tl, cudaStream_t st
     int dev = 0;
     cudaGetDevice(&dev);
     if (!(attr_set >> (dev & 63) & 1)) {
-        const cudaError_t e = cudaFuncSetAttribute(conv_tc_kernel<BN, KC, UP, NACC, TAIL, BRES, HALO>,
+        const cudaError_t e = cudaFuncSetAttribute(conv_tc_kernel<BN, KC, UP, NACC, TAIL, BRES, HALO, RPS>,
                                                    cudaFuncAttributeMaxDynamicSharedMemorySize, cfg::SMEM);
         if (e != cudaSuccess) return e;
         attr_set |= 1ull << (dev & 63);
     }
     const int grid = (int) (p.num_tiles < sm_count() ? p.num_tiles : sm_count());
-    conv_tc_kernel<BN, KC, UP, NACC, TAIL, BRES, HALO><<<grid, cfg::THREADS, cfg::SMEM, st>>>(tmA, tmB, p);
+    conv_tc_kernel<BN, KC, UP, NACC, TAIL, BRES, HALO, RPS><<<grid, cfg::THREADS, cfg::SMEM, st>>>(tmA, tmB, p);
     return cudaGetLastError();
 }
 
@@ -830,7 +838,7 @@ cudaError_t launch_conv_tail_tc(const conv_params &p, const tail_params &t, cuda
     const bool halo = p.W >= BM;  // one-row tiles: taps share a halo box
     switch (p.OC) {
         case 32:
-            return halo ? run_tc<32, 32, false, 4, true, true, true>(p, &t, st)
+            return halo ? run_tc<32, 32, false, 4, true, true, true, 3>(p, &t, st)
                         : run_tc<32, 32, false, 4, true, true>(p, &t, st);
         case 64:
             return halo ? run_tc<64, 64, false, 4, true, false, true>(p, &t, st)
