@@ -207,7 +207,9 @@ struct tc_cfg {
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int STAGE_TX = A_TX + B_BYTES;
     // as deep as shared memory allows (small stages hide more TMA latency)
-    static constexpr int STAGES = (BUDGET / STAGE_BYTES) > 20 ? 20 : (BUDGET / STAGE_BYTES);
+    // an even count: stages are released to the producer in pairs (one
+    // tcgen05.commit per two stages)
+    static constexpr int STAGES = ((BUDGET / STAGE_BYTES) > 20 ? 20 : (BUDGET / STAGE_BYTES)) & ~1;
     static constexpr int B_REGION = BRES ? B_RES : STAGES * B_BYTES;
     static constexpr uint32_t TMEM_COLS = NACC * BN;  // one accumulator per epilogue group
     static constexpr int THREADS = 64 + 128 * NACC;
@@ -293,7 +295,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     uint64_t *bars = (uint64_t *) (sB + cfg::B_REGION + cfg::EXTRA);
     uint32_t *tmem_slot = (uint32_t *) (bars + cfg::NBARS);
     auto full = [&](int s) { return smem_u32(&bars[s]); };
-    auto empty = [&](int s) { return smem_u32(&bars[cfg::STAGES + s]); };
+    auto empty = [&](int s) { return smem_u32(&bars[cfg::STAGES + (s >> 1)]); };  // per stage pair
     auto tfull = [&](int a) { return smem_u32(&bars[2 * cfg::STAGES + a]); };
     auto tempty = [&](int a) { return smem_u32(&bars[2 * cfg::STAGES + NACC + a]); };
     const uint32_t drain = smem_u32(&bars[2 * cfg::STAGES + 2 * NACC]);
@@ -303,7 +305,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     if (threadIdx.x == 0) {
         for (int s = 0; s < cfg::STAGES; s++) {
             mbar_init(full(s), 1);
-            mbar_init(empty(s), 1);
+            if (!(s & 1)) mbar_init(empty(s), 1);
         }
         for (int a = 0; a < NACC; a++) {
             mbar_init(tfull(a), 1);
@@ -350,7 +352,8 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 for (int kh = 0; kh < 3 && ok; kh += RPS) {
                     for (int c = 0; c < p.cpt && ok; c++) {
                         for (int kw0 = 0; kw0 < 3; kw0 += cfg::TPS, it++) {
-                            if (!mbar_wait(empty(s), ph ^ 1)) {
+                            // an odd stage was released together with the even one before it
+                            if (!(s & 1) && !mbar_wait(empty(s), ph ^ 1)) {
                                 ok = false;
                                 break;
                             }
@@ -425,7 +428,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                                      ad + (((HALO ? (i / 3) * cfg::A_HALO + (i % 3) * KC * 2 : i * cfg::A_TAP)) >> 4) +
                                          2 * kx,
                                      bd + ((i * cfg::B_TAP) >> 4) + 2 * kx, cfg::IDESC, (kk | i | kx) != 0);
-                    umma_commit(empty(s));
+                    if (s & 1) umma_commit(empty(s));  // releases stages s-1 and s
                     if (++s == cfg::STAGES) {
                         s = 0;
                         ph ^= 1;
