@@ -44,6 +44,11 @@ struct motion_dec_b200 {
     bool set_tensor(const std::string &name, const float *data, int64_t n, std::string &err) {
         return ok(tpmd_set_tensor(ctx, name.c_str(), data, n), err);
     }
+    // the decoder's tensors straight from motion_ae_{f32,f16}.gguf (scale
+    // folding included), in place of the set_tensor loop
+    bool load_gguf(const std::string &path, std::string &err) {
+        return ok(tpmd_load_gguf(ctx, path.c_str()), err);
+    }
     bool prepare(std::string &err) { return ok(tpmd_prepare(ctx), err); }
 
     // motion_dec::build: the decode plan needs no graph construction here

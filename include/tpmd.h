@@ -60,6 +60,29 @@ double tpmd_scale_for(const char *name, const int64_t ne[4]);
  * sizes fail. */
 int tpmd_set_tensor(tpmd_ctx *ctx, const char *name, const float *data, int64_t n);
 
+/* GGUF v3 reader (weights_t::load, src/gguf_load.cpp:50-197): parses the
+ * file at `path`, checks general.architecture against `expect_arch` (NULL:
+ * no check) and calls `cb` once per tensor in file order with its ggml dims
+ * ne[4] (fastest first, unit dims beyond the fourth dropped) and its
+ * elements as float32 in torch order (f16 converted exactly), multiplied by
+ * tpmd_scale_for(name, ne) when `fold_scales` is nonzero (motion_ae_scale,
+ * as tp_ctx::load folds it, src/tp.cpp:32-34). `data` is valid during the
+ * call only; a nonzero return from `cb` stops the read with an error. The
+ * reference's acceptance rules are kept: version 3, value types
+ * u32/i32/f32/bool/string, element types f32/f16, at most four non-unit
+ * dims, 32-byte data alignment. Needs no GPU. On failure returns -1 and
+ * writes the message (truncated to err_len, NUL-terminated) into `err`. */
+typedef int (*tpmd_gguf_tensor_fn)(void *user, const char *name, const int64_t ne[4],
+                                   const float *data, int64_t n);
+int tpmd_gguf_read(const char *path, const char *expect_arch, int fold_scales,
+                   tpmd_gguf_tensor_fn cb, void *user, char *err, size_t err_len);
+
+/* The decoder half of tp_ctx::load (src/tp.cpp:32-38): reads the
+ * motion_ae_{f32,f16}.gguf file (architecture "float-motion-ae"), folds
+ * motion_ae_scale and hands every "dec.*" tensor except dec.direction to
+ * tpmd_set_tensor; encoder tensors are skipped. Call tpmd_prepare next. */
+int tpmd_load_gguf(tpmd_ctx *ctx, const char *path);
+
 /* Derive the decoder's device weights from the set tensors: S_aug, the cf
  * GEMM matrices and the sub-pixel up-conv matrices (motion_dec::prepare,
  * src/motion_dec.cpp:31-226). Requires every tensor. */

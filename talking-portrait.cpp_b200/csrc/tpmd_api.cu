@@ -432,6 +432,16 @@ tpmd_ctx::~tpmd_ctx() {
 
 extern "C" {
 
+}  // extern "C"
+
+// error text for entry points implemented in other files
+__attribute__((visibility("hidden"))) int tpmd_ctx_fail(tpmd_ctx *c, const char *msg) {
+    if (c) c->fail(msg);
+    return -1;
+}
+
+extern "C" {
+
 int tpmd_abi_version(void) { return TPMD_ABI_VERSION; }
 
 const char *tpmd_create_error(void) { return g_create_err.c_str(); }

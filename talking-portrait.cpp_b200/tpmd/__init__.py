@@ -34,7 +34,7 @@ EXPORTS = ("tpmd_abi_version", "tpmd_create", "tpmd_create_error", "tpmd_destroy
            "tpmd_last_error", "tpmd_scale_for", "tpmd_set_tensor", "tpmd_prepare",
            "tpmd_set_feats", "tpmd_batch", "tpmd_decode", "tpmd_decode_device",
            "tpmd_arena", "tpmd_arena_adopt", "tpmd_decode_taps", "tpmd_profile_begin", "tpmd_profile_end",
-           "tpmd_kernel_launches", "tpmd_decode_noalloc",
+           "tpmd_kernel_launches", "tpmd_decode_noalloc", "tpmd_gguf_read", "tpmd_load_gguf",
            "tpk_bilinear_gather", "tpk_im2col_cf", "tpk_last_error")
 
 _lib = None
@@ -77,12 +77,40 @@ def load_library(path: str = LIB_PATH):
     L.tpmd_kernel_launches.argtypes = [v, i64]
     L.tpmd_decode_noalloc.argtypes = [v, v, i64, v, v]
     L.tpmd_kernel_launches.restype = i64
+    L.tpmd_gguf_read.argtypes = [cp, cp, C.c_int, GGUF_TENSOR_FN, v, C.c_char_p, C.c_size_t]
+    L.tpmd_load_gguf.argtypes = [v, cp]
     L.tpk_bilinear_gather.argtypes = [v, C.c_int, C.c_int, C.c_int, C.c_int, v, i64, C.c_int,
                                       C.c_int, v, v]
     L.tpk_im2col_cf.argtypes = [v] + [C.c_int] * 12 + [v, C.c_int, v]
     L.tpk_last_error.restype = cp
     _lib = L
     return L
+
+
+GGUF_TENSOR_FN = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_char_p, C.POINTER(C.c_int64),
+                             C.POINTER(C.c_float), C.c_int64)
+
+
+def gguf_read(path: str, expect_arch: str | None = None, fold: bool = True) -> dict:
+    """Every tensor of a GGUF v3 file as {name: (ne, float32 array)} through
+    tpmd_gguf_read (src/gguf_load.cpp:50-197 semantics); ne is the ggml dims
+    tuple (fastest first), the array is flat in torch element order, scale
+    folded with motion_ae_scale when `fold`."""
+    L = load_library()
+    out: dict = {}
+
+    def cb(_user, name, ne, data, n):
+        out[name.decode()] = (tuple(ne[i] for i in range(4)),
+                              np.ctypeslib.as_array(data, shape=(n,)).copy())
+        return 0
+
+    fn = GGUF_TENSOR_FN(cb)
+    err = C.create_string_buffer(1024)
+    rc = L.tpmd_gguf_read(path.encode(), expect_arch.encode() if expect_arch else None,
+                          1 if fold else 0, fn, None, err, len(err))
+    if rc != 0:
+        raise TpmdError(err.value.decode())
+    return out
 
 
 def _np_ptr(a: np.ndarray):
@@ -115,6 +143,11 @@ class MotionDecoder:
         for name, arr in tensors.items():
             a = np.ascontiguousarray(arr, np.float32)
             self._check(self._L.tpmd_set_tensor(self._h, name.encode(), _np_ptr(a), a.size))
+
+    def load_gguf(self, path: str):
+        """The decoder's tensors from a motion_ae GGUF file (tp_ctx::load,
+        src/tp.cpp:32-38); call prepare() next."""
+        self._check(self._L.tpmd_load_gguf(self._h, path.encode()))
 
     def prepare(self):
         self._check(self._L.tpmd_prepare(self._h))
