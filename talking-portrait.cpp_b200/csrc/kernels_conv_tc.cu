@@ -43,6 +43,7 @@ struct tc_params {
     int bw, bh, bb;            // pixel box of one M tile
     int tiles_x, tiles_y, tiles_n;
     int lg_x, lg_y, lg_n;      // their log2
+    int lg_oc;                 // log2 of OC (sub-pixel class of column n = n >> lg_oc)
     int num_tiles;
     __half *y;
     const float *inv_den;
@@ -505,48 +506,59 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             tc_fence_after();
             if constexpr (!TAIL) {
                 const bool valid = b < p.B;
+                // the tile's columns are ncls sub-pixel classes (UP) of `span`
+                // channels each, column = class * OC + channel; a channel's
+                // per-frame constants are loaded once for all its classes
+                const int span = UP ? (BN < p.OC ? BN : p.OC) : BN;
+                const int ncls = BN / span;
+                const int cls0 = UP ? tp.n0 >> p.lg_oc : 0;
+                const int obase = UP ? tp.n0 & (p.OC - 1) : tp.n0;
 #pragma unroll 1
-                for (int c0 = 0; c0 < BN; c0 += 16) {
-                    uint32_t r[16];
-                    tmem_ld16(taddr0 + c0, r);
-                    if (!valid) continue;
-                    const int n = tp.n0 + c0;
-                    const int o0 = UP ? n % p.OC : n;
+                for (int c0 = 0; c0 < span; c0 += 16) {
+                    const int o0 = obase + c0;
                     float den[16], bias[16], sn[16];
-                    const float4 *dp =
-                        reinterpret_cast<const float4 *>(p.inv_den + (int64_t) b * p.den_stride + o0);
-                    const float4 *bp = reinterpret_cast<const float4 *>(p.bias + o0);
-#pragma unroll
-                    for (int i = 0; i < 4; i++) {
-                        const float4 dv = __ldg(dp + i), bv = __ldg(bp + i);
-                        den[4 * i] = dv.x; den[4 * i + 1] = dv.y; den[4 * i + 2] = dv.z; den[4 * i + 3] = dv.w;
-                        bias[4 * i] = bv.x; bias[4 * i + 1] = bv.y; bias[4 * i + 2] = bv.z; bias[4 * i + 3] = bv.w;
-                    }
-                    if (p.snext) {
-                        const float4 *sp =
-                            reinterpret_cast<const float4 *>(p.snext + (int64_t) b * p.snext_stride + o0);
+                    if (valid) {
+                        const float4 *dp =
+                            reinterpret_cast<const float4 *>(p.inv_den + (int64_t) b * p.den_stride + o0);
+                        const float4 *bp = reinterpret_cast<const float4 *>(p.bias + o0);
 #pragma unroll
                         for (int i = 0; i < 4; i++) {
-                            const float4 sv = __ldg(sp + i);
-                            sn[4 * i] = sv.x; sn[4 * i + 1] = sv.y; sn[4 * i + 2] = sv.z; sn[4 * i + 3] = sv.w;
+                            const float4 dv = __ldg(dp + i), bv = __ldg(bp + i);
+                            den[4 * i] = dv.x; den[4 * i + 1] = dv.y; den[4 * i + 2] = dv.z; den[4 * i + 3] = dv.w;
+                            bias[4 * i] = bv.x; bias[4 * i + 1] = bv.y; bias[4 * i + 2] = bv.z; bias[4 * i + 3] = bv.w;
+                        }
+                        if (p.snext) {
+                            const float4 *sp =
+                                reinterpret_cast<const float4 *>(p.snext + (int64_t) b * p.snext_stride + o0);
+#pragma unroll
+                            for (int i = 0; i < 4; i++) {
+                                const float4 sv = __ldg(sp + i);
+                                sn[4 * i] = sv.x; sn[4 * i + 1] = sv.y; sn[4 * i + 2] = sv.z; sn[4 * i + 3] = sv.w;
+                            }
                         }
                     }
-                    float v[16];
+#pragma unroll 1
+                    for (int k = 0; k < ncls; k++) {
+                        uint32_t r[16];
+                        tmem_ld16(taddr0 + k * span + c0, r);
+                        if (!valid) continue;
+                        float v[16];
 #pragma unroll
-                    for (int i = 0; i < 16; i++) {
-                        float a = fmaf(__uint_as_float(r[i]), den[i], bias[i]);
-                        a = a > 0.0f ? a : 0.2f * a;
-                        v[i] = p.snext ? a * sn[i] : a;
+                        for (int i = 0; i < 16; i++) {
+                            float a = fmaf(__uint_as_float(r[i]), den[i], bias[i]);
+                            a = fmaxf(a, 0.2f * a);  // leaky relu, slope 0.2
+                            v[i] = p.snext ? a * sn[i] : a;
+                        }
+                        int64_t dst;
+                        if (UP) {
+                            const int cls = cls0 + k;
+                            const int Y = 2 * y + (cls >> 1), X = 2 * x + (cls & 1);
+                            dst = (((int64_t) b * 2 * p.H + Y) * 2 * p.W + X) * p.OC + o0;
+                        } else {
+                            dst = (((int64_t) b * p.H + y) * p.W + x) * p.OC + o0;
+                        }
+                        st_half16(p.y + dst, v);
                     }
-                    int64_t dst;
-                    if (UP) {
-                        const int cls = n / p.OC;
-                        const int Y = 2 * y + (cls >> 1), X = 2 * x + (cls & 1);
-                        dst = (((int64_t) b * 2 * p.H + Y) * 2 * p.W + X) * p.OC + o0;
-                    } else {
-                        dst = (((int64_t) b * p.H + y) * p.W + x) * p.OC + o0;
-                    }
-                    st_half16(p.y + dst, v);
                 }
             } else {
                 // ---- conv2 + level tail (one tile = 128 pixels of one frame,
@@ -727,7 +739,9 @@ cudaError_t run_tc(const conv_params &cp, const tail_params *tl, cudaStream_t st
     p.lg_x = ilog2(p.tiles_x);
     p.lg_y = ilog2(p.tiles_y);
     p.lg_n = ilog2(p.tiles_n);
-    if (p.lg_x < 0 || p.lg_y < 0 || p.lg_n < 0 || p.N % BN) return cudaErrorInvalidValue;
+    p.lg_oc = ilog2(cp.OC);
+    if (p.lg_x < 0 || p.lg_y < 0 || p.lg_n < 0 || p.lg_oc < 0 || p.N % BN) return cudaErrorInvalidValue;
+    if (UP && (BN % 16 || (BN > cp.OC && BN % cp.OC))) return cudaErrorInvalidValue;
     const int tiles_b = (cp.B + p.bb - 1) / p.bb;
     const int64_t nt = (int64_t) tiles_b * p.tiles_y * p.tiles_x * p.tiles_n;
     if (nt >= (1ll << 30)) return cudaErrorInvalidValue;
