@@ -474,9 +474,10 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                         const int sy = ny + py - 1 + a, sx2 = nx + px - 1 + bb;
                         const bool in = sy >= 0 && sy < h && sx2 >= 0 && sx2 < h;
                         const int uk = (px + 2 * bb) + 4 * (py + 2 * a);
-                        uoff[2 * a + bb] = in ? sy * h + sx2 : -1;
-                        ukf[2 * a + bb] = s_up[uk];
-                        ukr[2 * a + bb] = s_up[16 + uk];
+                        // taps outside the map read pixel 0 with weight 0 (no branches)
+                        uoff[2 * a + bb] = in ? sy * h + sx2 : 0;
+                        ukf[2 * a + bb] = in ? s_up[uk] : 0.0f;
+                        ukr[2 * a + bb] = in ? s_up[16 + uk] : 0.0f;
                     }
                 const int64_t hh = (int64_t) h * h;
                 if (p.skipf_prev) {
@@ -485,7 +486,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                         const float *pl = p.skipf_prev + ((int64_t) b * 3 + kk) * hh;
 #pragma unroll
                         for (int i = 0; i < 4; i++)
-                            if (uoff[i] >= 0) skf[kk] = fmaf(__ldg(pl + uoff[i]), ukf[i], skf[kk]);
+                            skf[kk] = fmaf(__ldg(pl + uoff[i]), ukf[i], skf[kk]);
                     }
                 }
                 if (p.skip_prev) {
@@ -494,7 +495,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                         const float *pl = p.skip_prev + ((int64_t) b * 3 + kk) * hh;
 #pragma unroll
                         for (int i = 0; i < 4; i++)
-                            if (uoff[i] >= 0) skr[kk] = fmaf(__ldg(pl + uoff[i]), ukr[i], skr[kk]);
+                            skr[kk] = fmaf(__ldg(pl + uoff[i]), ukr[i], skr[kk]);
                     }
                 }
             }
@@ -621,15 +622,16 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 #pragma unroll
                 for (int kk = 0; kk < 4; kk++) {
                     const int cx = x0 + (kk & 1), cy = y0 + (kk >> 1);
-                    trow[kk] = (sane && cx >= 0 && cx < r && cy >= 0 && cy < r) ? cy * r + cx : -1;
-                    twt[kk] = ((kk & 1) ? wx : 1.0f - wx) * ((kk >> 1) ? wy : 1.0f - wy);
+                    // a tap outside the map (zeros padding) reads pixel 0 with weight 0
+                    const bool in = sane && cx >= 0 && cx < r && cy >= 0 && cy < r;
+                    trow[kk] = in ? cy * r + cx : 0;
+                    twt[kk] = in ? ((kk & 1) ? wx : 1.0f - wx) * ((kk >> 1) ? wy : 1.0f - wy) : 0.0f;
                 }
                 // ToRGB of the gathered channels = gather of the feats projected
                 // by ToRGB's 1x1 conv (both linear): four 16-byte taps
                 float g0 = 0.0f, g1 = 0.0f, g2 = 0.0f;
 #pragma unroll
                 for (int kk = 0; kk < 4; kk++) {
-                    if (trow[kk] < 0) continue;
                     const float4 pq = __ldg(p.proj + trow[kk]);
                     g0 = fmaf(twt[kk], pq.x, g0);
                     g1 = fmaf(twt[kk], pq.y, g1);
@@ -645,7 +647,6 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     for (int i = 0; i < 16; i++) smp[i] = 0.0f;
 #pragma unroll
                     for (int kk = 0; kk < 4; kk++) {
-                        if (trow[kk] < 0) continue;
                         float f[16];
                         ld_half16(p.feat + (int64_t) trow[kk] * BN + c0, f);
 #pragma unroll
@@ -858,7 +859,7 @@ cudaError_t launch_conv_tail_tc(const conv_params &p, const tail_params &t, cuda
             return halo ? run_tc<32, 32, false, 4, true, true, true, 3>(p, &t, st)
                         : run_tc<32, 32, false, 4, true, true>(p, &t, st);
         case 64:
-            return halo ? run_tc<64, 64, false, 4, true, false, true>(p, &t, st)
+            return halo ? run_tc<64, 64, false, 4, true, true, true, 3>(p, &t, st)
                         : run_tc<64, 64, false, 4, true>(p, &t, st);
         case 128:
             return halo ? run_tc<128, 64, false, 4, true, false, true>(p, &t, st)
