@@ -85,26 +85,68 @@ def kernel_work(name: str, nb: int, esz: int):
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms"""
+    """SM clock and clock-event (throttle) reasons of this rank's GPU, read
+    through NVML (read-only queries) while the timed work runs: `poll_until`
+    samples every few ms until the given CUDA event completes, so even a
+    short timed region gets samples taken under load. Falls back to an
+    nvidia-smi process sampling every 100 ms when NVML is unavailable."""
+
+    REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40),
+               ("sw_thermal_slowdown", 0x20), ("sw_power_cap", 0x4))
 
     def __init__(self, gpu: int):
         self.gpu = gpu
+        self.nv = None
+        self.h = None
         self.proc = None
         self.lines: list[str] = []
+        self.rows: list[tuple[float, float, list[str]]] = []
 
     def __enter__(self):
-        q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={q}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
-            self.t.start()
-        except OSError:
-            self.proc = None
+            import pynvml as nv
+            nv.nvmlInit()
+            h = None
+            try:  # the CUDA device's PCI address names the NVML device exactly
+                import torch
+                pr = torch.cuda.get_device_properties(self.gpu)
+                bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+                h = nv.nvmlDeviceGetHandleByPciBusId(bus)
+            except Exception:
+                h = nv.nvmlDeviceGetHandleByIndex(self.gpu)
+            self.nv, self.h = nv, h
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+        except Exception:
+            self.nv = None
+            q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+            try:
+                self.proc = subprocess.Popen(
+                    ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                     "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                self.t = threading.Thread(target=self._read, daemon=True)
+                self.t.start()
+            except OSError:
+                self.proc = None
         return self
+
+    def sample(self):
+        if self.nv is None:
+            return
+        try:
+            mhz = float(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+            bits = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+        except Exception:
+            return
+        self.rows.append((mhz, self.max_mhz, [n for n, b in self.REASONS if bits & b]))
+
+    def poll_until(self, event, period_s: float = 0.003):
+        """Sample until `event` (recorded after the timed work) completes."""
+        self.sample()
+        while not event.query():
+            time.sleep(period_s)
+            self.sample()
 
     def _read(self):
         for line in self.proc.stdout:
@@ -119,21 +161,23 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self):
-        rows = []
+        rows = list(self.rows)
+        names = [n for n, _ in self.REASONS]
         for ln in self.lines:
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 8:
                 continue
             try:
-                rows.append((float(parts[0]), float(parts[1]), parts[4:8]))
+                rows.append((float(parts[0]), float(parts[1]),
+                             [names[i] for i, f in enumerate(parts[4:8]) if f.lower() == "active"]))
             except ValueError:
                 continue
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for _, _, fl in rows for i, f in enumerate(fl) if f.lower() == "active"})
+        reasons = sorted({r for _, _, rs in rows for r in rs})
         return {"sm_mhz": float(np.median([r[0] for r in rows])), "sm_max_mhz": rows[0][1],
-                "reasons": reasons, "samples": len(rows)}
+                "reasons": reasons, "samples": len(rows),
+                "source": "nvml" if self.rows else "nvidia-smi"}
 
 
 def cpu_baseline(tensors, feats, styles, budget_s: float = 12.0):
@@ -267,6 +311,7 @@ def main():
         for _ in range(args.steps):
             step()
         e1.record(stream)
+        clk.poll_until(e1)
         torch.cuda.synchronize()
     barrier()
     ms = e0.elapsed_time(e1)
