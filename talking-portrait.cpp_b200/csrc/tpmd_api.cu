@@ -852,6 +852,34 @@ bool device_ok(tpmd_ctx *c) {
     return true;
 }
 
+// Sub-batches of a host decode. The frame copy (D2H) of one sub-batch
+// overlaps the compute of the next, so only the last copy is exposed: whole
+// max_batch chunks first, then the last chunk split into shrinking parts
+// (ratio about 0.62, the copy/compute time ratio per frame with margin) so
+// the exposed copy is small while each copy still hides under the next
+// part's compute. TPMD_SUBBATCH=k forces equal parts of k frames.
+std::vector<int64_t> sub_batch_plan(int64_t n, int64_t max_batch) {
+    std::vector<int64_t> plan;
+    if (const char *e = getenv("TPMD_SUBBATCH")) {
+        const int64_t k = std::max<int64_t>(1, std::min<int64_t>(max_batch, atoll(e)));
+        for (int64_t f = 0; f < n; f += k) plan.push_back(std::min<int64_t>(k, n - f));
+        return plan;
+    }
+    const int64_t tail = std::min<int64_t>(n, max_batch);
+    for (int64_t f = 0; f < n - tail; f += max_batch) plan.push_back(std::min<int64_t>(max_batch, n - tail - f));
+    const int parts = tail >= 16 ? 4 : tail >= 4 ? 2 : 1;
+    double w[4], wsum = 0.0;
+    for (int i = 0; i < parts; i++) wsum += (w[i] = std::pow(0.62, i));
+    int64_t left = tail;
+    for (int i = 0; i < parts; i++) {
+        int64_t k = i + 1 == parts ? left : std::max<int64_t>(1, std::llround(tail * w[i] / wsum));
+        k = std::min<int64_t>(k, left - (parts - 1 - i));  // leave at least one frame per later part
+        plan.push_back(k);
+        left -= k;
+    }
+    return plan;
+}
+
 bool ready(tpmd_ctx *c) {
     if (!c->wready) return c->fail("weights not prepared (tpmd_prepare)");
     if (!c->fready) return c->fail("feats not set (tpmd_set_feats)");
@@ -964,13 +992,11 @@ int tpmd_decode(tpmd_ctx *c, const float *styles, int64_t n, float *frames) {
     if (!ready(c)) return -1;
     if (!c->ck(cudaSetDevice(c->device), "cudaSetDevice")) return -1;
     const size_t fsz = (size_t) 3 * IMG * IMG;
-    // sub-batches: about four per call (so the frame copy of one overlaps the
-    // compute of the next), at most max_batch frames each
-    int64_t sub = std::min<int64_t>(c->max_batch, std::max<int64_t>(1, (n + 3) / 4));
-    if (const char *e = getenv("TPMD_SUBBATCH")) sub = std::max<int64_t>(1, std::min<int64_t>(c->max_batch, atoll(e)));
+    const std::vector<int64_t> plan = sub_batch_plan(n, c->max_batch);
     int k = 0;
-    for (int64_t f0 = 0; f0 < n; f0 += sub, k ^= 1) {
-        const int64_t nb = std::min<int64_t>(sub, n - f0);
+    int64_t f0 = 0;
+    for (size_t i = 0; i < plan.size(); f0 += plan[i], i++, k ^= 1) {
+        const int64_t nb = plan[i];
         // staging buffer k is free once its previous frame copy finished
         if (!c->ck(cudaStreamWaitEvent(c->stream, c->ev_copied[k], 0), "wait") ||
             !c->ck(cudaMemcpyAsync(c->styles_d[k], styles + f0 * STYLE_DIM,
