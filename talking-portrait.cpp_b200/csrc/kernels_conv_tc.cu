@@ -586,7 +586,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 #pragma unroll
                     for (int i = 0; i < 16; i++) {
                         float a = fmaf(__uint_as_float(rr[i]), den[i], bias[i]);
-                        a = a > 0.0f ? a : 0.2f * a;
+                        a = fmaxf(a, 0.2f * a);  // leaky relu, slope 0.2
                         v[i] = a;
                         rr[i] = __float_as_uint(a);
                         const float xs = a * fsv[i];  // ToFlow input: out * style
@@ -665,7 +665,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 #pragma unroll
                 for (int kk = 0; kk < 3; kk++) {
                     float v = rg[kk] + __ldg(p.rlb + kk);
-                    v = (v > 0.0f ? v : 0.2f * v) + __ldg(p.rb + kk);
+                    v = fmaxf(v, 0.2f * v) + __ldg(p.rb + kk);
                     if (p.skip_prev) v += skr[kk];
                     p.skip_out[((int64_t) b * 3 + kk) * rr2 + (int64_t) y * r + x] = v;
                 }
