@@ -92,6 +92,13 @@ int tpmd_prepare(tpmd_ctx *ctx);
  * src/motion_dec.cpp:1137-1160), host float32 as described above. */
 int tpmd_set_feats(tpmd_ctx *ctx, const float *const feats[TPMD_N_LEVELS]);
 
+/* The same pyramid from device memory on this decoder's GPU (f32,
+ * channel-last, e.g. tpme_feat_device after a tpme_run), converted in place
+ * on `stream` (NULL: the legacy default stream); returns after the copy.
+ * The motion_enc -> motion_dec hand-off of src/pipeline.cpp:153-160 without
+ * the host round trip; the reference has no counterpart. */
+int tpmd_set_feats_device(tpmd_ctx *ctx, const float *const feats_dev[TPMD_N_LEVELS], void *stream);
+
 /* Frames per internal dispatch (motion_dec::batch). */
 int tpmd_batch(const tpmd_ctx *ctx);
 

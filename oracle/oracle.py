@@ -76,6 +76,12 @@ def lib():
         L.orc_dec_tap.restype = C.c_int64
         L.orc_dec_error.argtypes = [v]
         L.orc_dec_error.restype = C.c_char_p
+        L.orc_enc_create.restype = v
+        L.orc_enc_destroy.argtypes = [v]
+        L.orc_enc_set.argtypes = [v, C.c_char_p, v, C.c_int64]
+        L.orc_enc_run.argtypes = [v, v, v, v, v, C.POINTER(v)]
+        L.orc_enc_error.argtypes = [v]
+        L.orc_enc_error.restype = C.c_char_p
         L.orc_set_threads.argtypes = [C.c_int]
         L.orc_get_threads.restype = C.c_int
         _lib = L
@@ -266,6 +272,33 @@ class Decoder:
     def __del__(self):
         if getattr(self, "_h", None):
             self._L.orc_dec_destroy(self._h)
+            self._h = None
+
+
+class Encoder:
+    """The motion encoder restatement (motion_enc::run, src/motion_enc.cpp:46-184)
+    over scale-folded host tensors (enc.* and dec.direction.Q)."""
+
+    def __init__(self, tensors: dict):
+        self._L = lib()
+        self._h = self._L.orc_enc_create()
+        for n, a in tensors.items():
+            a = np.ascontiguousarray(a, np.float32)
+            if self._L.orc_enc_set(self._h, n.encode(), _p(a), a.size) != 0:
+                raise RuntimeError(self._L.orc_enc_error(self._h).decode())
+
+    def run(self, image: np.ndarray) -> dict:
+        img = np.ascontiguousarray(image, np.float32)
+        app, lam, mot = np.empty(512, np.float32), np.empty(20, np.float32), np.empty(512, np.float32)
+        feats = [np.empty(((8 << j) ** 2, ST_OC[j]), np.float32) for j in range(7)]
+        ptrs = (C.c_void_p * 7)(*[f.ctypes.data for f in feats])
+        if self._L.orc_enc_run(self._h, _p(img), _p(app), _p(lam), _p(mot), ptrs) != 0:
+            raise RuntimeError(self._L.orc_enc_error(self._h).decode())
+        return dict(appearance=app, lam=lam, motion=mot, feats=feats)
+
+    def __del__(self):
+        if getattr(self, "_h", None):
+            self._L.orc_enc_destroy(self._h)
             self._h = None
 
 

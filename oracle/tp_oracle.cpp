@@ -786,3 +786,193 @@ int64_t orc_dec_tap(const orc_dec *d, const char *name, float *out, int64_t cap)
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// motion encoder (src/motion_enc.cpp:46-184, ops src/ops_common.h:12-43)
+// ---------------------------------------------------------------------------
+namespace {
+
+const int ENC_IN[7] = {32, 64, 128, 256, 512, 512, 512};    // motion_enc.cpp:46
+const int ENC_OUT[7] = {64, 128, 256, 512, 512, 512, 512};  // motion_enc.cpp:47
+
+std::map<std::string, int64_t> encoder_tensors() {
+    std::map<std::string, int64_t> m;
+    char nm[64];
+    m["enc.net_app.convs.0.0.weight"] = 32 * 3;
+    m["enc.net_app.convs.0.1.bias"] = 32;
+    for (int i = 1; i <= 7; i++) {
+        const int64_t C = ENC_IN[i - 1], Co = ENC_OUT[i - 1];
+        auto put = [&](const char *suffix, int64_t n) {
+            snprintf(nm, sizeof nm, "enc.net_app.convs.%d.%s", i, suffix);
+            m[nm] = n;
+        };
+        put("conv1.0.weight", C * C * 9);
+        put("conv1.1.bias", C);
+        put("conv2.0.kernel", 16);
+        put("conv2.1.weight", Co * C * 9);
+        put("conv2.2.bias", Co);
+        put("skip.0.kernel", 16);
+        put("skip.1.weight", Co * C);
+    }
+    m["enc.net_app.convs.8.weight"] = (int64_t) 512 * 512 * 16;
+    for (int i = 0; i < 5; i++) {
+        const int64_t out = i == 4 ? 20 : 512;
+        snprintf(nm, sizeof nm, "enc.fc.%d.weight", i);
+        m[nm] = out * 512;
+        snprintf(nm, sizeof nm, "enc.fc.%d.bias", i);
+        m[nm] = out;
+    }
+    m["dec.direction.Q"] = 512 * 20;
+    return m;
+}
+
+// y[OC][OH][OW] = corr2d(x[IC][IH][IW], w[OC][IC][K][K]) with stride s and
+// zero padding p on every side (ggml_im2col + mul_mat, src/ops_common.h:12-26)
+void conv2d_s(const float *x, int IC, int IH, int IW, const float *w, int OC, int K, int s,
+              int p, int OH, int OW, float *y) {
+    if (s == 1) {
+        conv2d(x, IC, IH, IW, w, OC, K, K, p, p, OH, OW, y);
+        return;
+    }
+#pragma omp parallel for collapse(2) schedule(dynamic, 4)
+    for (int o = 0; o < OC; o++)
+        for (int oy = 0; oy < OH; oy++) {
+            float *out = y + ((size_t) o * OH + oy) * OW;
+            for (int ox = 0; ox < OW; ox++) out[ox] = 0.0f;
+            for (int ic = 0; ic < IC; ic++)
+                for (int ky = 0; ky < K; ky++) {
+                    const int iy = oy * s + ky - p;
+                    if (iy < 0 || iy >= IH) continue;
+                    const float *row = x + ((size_t) ic * IH + iy) * IW;
+                    for (int kx = 0; kx < K; kx++) {
+                        const float wv = w[(((size_t) o * IC + ic) * K + ky) * K + kx];
+                        for (int ox = 0; ox < OW; ox++) {
+                            const int ix = ox * s + kx - p;
+                            if (ix >= 0 && ix < IW) out[ox] += wv * row[ix];
+                        }
+                    }
+                }
+        }
+}
+
+// FusedLeakyReLU with its sqrt2 folded upstream: lrelu(x + b), slope 0.2
+void bias_lrelu_chw(std::vector<float> &x, const std::vector<float> &b, size_t P) {
+    const int C = (int) b.size();
+#pragma omp parallel for schedule(static)
+    for (int c = 0; c < C; c++)
+        for (size_t q = 0; q < P; q++) x[c * P + q] = lrelu(x[c * P + q] + b[(size_t) c], 0.2f);
+}
+
+}  // namespace
+
+struct orc_enc {
+    std::map<std::string, int64_t> spec = encoder_tensors();
+    std::map<std::string, std::vector<float>> t;
+    std::string err;
+    const std::vector<float> &get(const std::string &n) const { return t.at(n); }
+};
+
+extern "C" {
+
+orc_enc *orc_enc_create(void) { return new orc_enc(); }
+void orc_enc_destroy(orc_enc *e) { delete e; }
+const char *orc_enc_error(const orc_enc *e) { return e ? e->err.c_str() : "null encoder"; }
+
+int orc_enc_set(orc_enc *e, const char *name, const float *data, int64_t n) {
+    auto it = e->spec.find(name);
+    if (it == e->spec.end() || it->second != n) {
+        e->err = std::string("orc_enc_set: unknown tensor or size mismatch: ") + name;
+        return -1;
+    }
+    e->t[name].assign(data, data + n);
+    return 0;
+}
+
+int orc_enc_run(orc_enc *e, const float *image, float *appearance, float *lambda, float *motion,
+                float *const feats[7]) {
+    for (auto &kv : e->spec)
+        if (!e->t.count(kv.first)) {
+            e->err = "orc_enc_run: missing tensor " + kv.first;
+            return -1;
+        }
+    // stem: 1x1 conv 3 -> 32 + FLReLU at 512x512
+    int H = 512;
+    std::vector<float> x((size_t) 32 * H * H);
+    conv2d_s(image, 3, H, H, e->get("enc.net_app.convs.0.0.weight").data(), 32, 1, 1, 0, H, H,
+             x.data());
+    bias_lrelu_chw(x, e->get("enc.net_app.convs.0.1.bias"), (size_t) H * H);
+    std::vector<std::vector<float>> pyr;
+    pyr.push_back(x);
+    char nm[96];
+    for (int i = 1; i <= 7; i++) {
+        const int C = ENC_IN[i - 1], Co = ENC_OUT[i - 1];
+        auto T = [&](const char *suffix) -> const std::vector<float> & {
+            snprintf(nm, sizeof nm, "enc.net_app.convs.%d.%s", i, suffix);
+            return e->get(nm);
+        };
+        const size_t P = (size_t) H * H;
+        const int h = H / 2;
+        // main: conv1 (3x3, pad 1) + FLReLU, Blur pad (2,2), conv2 (3x3 s2) + FLReLU
+        std::vector<float> x1((size_t) C * P);
+        conv2d_s(x.data(), C, H, H, T("conv1.0.weight").data(), C, 3, 1, 1, H, H, x1.data());
+        bias_lrelu_chw(x1, T("conv1.1.bias"), P);
+        const int Hb = H + 1;  // H + 2 + 2 - 3
+        std::vector<float> xb((size_t) C * Hb * Hb);
+        orc_blur(x1.data(), T("conv2.0.kernel").data(), H, H, C, 2, 2, xb.data());
+        std::vector<float> x2((size_t) Co * h * h);
+        conv2d_s(xb.data(), C, Hb, Hb, T("conv2.1.weight").data(), Co, 3, 2, 0, h, h, x2.data());
+        bias_lrelu_chw(x2, T("conv2.2.bias"), (size_t) h * h);
+        // skip: Blur pad (1,1), 1x1 stride-2 conv (1/sqrt2 folded into it)
+        const int Hs = H - 1;  // H + 1 + 1 - 3
+        std::vector<float> sb((size_t) C * Hs * Hs);
+        orc_blur(x.data(), T("skip.0.kernel").data(), H, H, C, 1, 1, sb.data());
+        std::vector<float> sk((size_t) Co * h * h);
+        conv2d_s(sb.data(), C, Hs, Hs, T("skip.1.weight").data(), Co, 1, 2, 0, h, h, sk.data());
+        for (size_t q = 0; q < x2.size(); q++) x2[q] += sk[q];
+        x.swap(x2);
+        H = h;
+        pyr.push_back(x);
+    }
+    // 4x4 valid conv on the 4x4 map -> appearance [512]
+    std::vector<float> app(512);
+    conv2d_s(x.data(), 512, 4, 4, e->get("enc.net_app.convs.8.weight").data(), 512, 4, 1, 0, 1, 1,
+             app.data());
+    // five plain EqualLinears (scale folded): h = W h + b
+    std::vector<float> hcur = app;
+    for (int i = 0; i < 5; i++) {
+        snprintf(nm, sizeof nm, "enc.fc.%d.weight", i);
+        const std::vector<float> &W = e->get(nm);
+        snprintf(nm, sizeof nm, "enc.fc.%d.bias", i);
+        const std::vector<float> &b = e->get(nm);
+        const int out = (int) b.size();
+        std::vector<float> nh((size_t) out);
+        for (int o = 0; o < out; o++) {
+            float a = 0.0f;
+            for (int k = 0; k < 512; k++) a += W[(size_t) o * 512 + k] * hcur[(size_t) k];
+            nh[(size_t) o] = a + b[(size_t) o];
+        }
+        hcur.swap(nh);
+    }
+    // motion = Q lambda, Q [512][20]
+    const std::vector<float> &Q = e->get("dec.direction.Q");
+    if (appearance) memcpy(appearance, app.data(), 512 * 4);
+    if (lambda) memcpy(lambda, hcur.data(), 20 * 4);
+    if (motion)
+        for (int r = 0; r < 512; r++) {
+            float a = 0.0f;
+            for (int k = 0; k < 20; k++) a += Q[(size_t) r * 20 + k] * hcur[(size_t) k];
+            motion[r] = a;
+        }
+    // feats[j] = conv{6-j}, channel-last [r*r][C]
+    for (int j = 0; j < 7; j++) {
+        if (!feats || !feats[j]) continue;
+        const std::vector<float> &f = pyr[(size_t) (6 - j)];
+        const int r = 8 << j, Cj = (int) (f.size() / ((size_t) r * r));
+        for (int c = 0; c < Cj; c++)
+            for (int q = 0; q < r * r; q++) feats[j][(size_t) q * Cj + c] = f[(size_t) c * r * r + q];
+    }
+    return 0;
+}
+
+}  // extern "C"
+

@@ -99,6 +99,24 @@ const char *orc_dec_error(const orc_dec *d);
 void orc_set_threads(int n);
 int orc_get_threads(void);
 
+/* ---- motion encoder (motion_enc::run, src/motion_enc.cpp:46-184) -------
+ * Stem EqualConv2d(3,32,1) + FusedLeakyReLU; seven ResBlocks (3x3 conv +
+ * FLReLU; Blur pad (2,2) + 3x3 stride-2 conv + FLReLU; skip: Blur pad (1,1)
+ * + 1x1 stride-2 conv; sum); a 4x4 valid conv -> appearance [512]; five
+ * plain EqualLinears -> lambda [20]; motion = Q lambda [512]. Tensors are
+ * the scale-folded f32 host copies (motion_ae_scale folds the FLReLU sqrt2
+ * and the ResBlock 1/sqrt2, src/motion_enc.cpp:9-45), torch element order.
+ * image: [3][512][512] CHW (ggml [512,512,3,1]); feats[j]: [r*r][ST_OC[j]]
+ * channel-last, r = 8<<j, = menc conv{6-j} (src/motion_enc.cpp:146-155);
+ * any output pointer may be NULL. */
+typedef struct orc_enc orc_enc;
+orc_enc *orc_enc_create(void);
+void orc_enc_destroy(orc_enc *e);
+int orc_enc_set(orc_enc *e, const char *name, const float *data, int64_t n);
+int orc_enc_run(orc_enc *e, const float *image, float *appearance, float *lambda,
+                float *motion, float *const feats[7]);
+const char *orc_enc_error(const orc_enc *e);
+
 #ifdef __cplusplus
 }
 #endif

@@ -649,6 +649,24 @@ int tpmd_set_feats(tpmd_ctx *c, const float *const feats[TPMD_N_LEVELS]) {
     return make_proj(c) ? 0 : -1;
 }
 
+int tpmd_set_feats_device(tpmd_ctx *c, const float *const feats_dev[TPMD_N_LEVELS], void *stream) {
+    if (!c) return -1;
+    if (!feats_dev) return c->fail("tpmd_set_feats_device: null feats"), -1;
+    for (int j = 0; j < N_LEVELS; j++)
+        if (!feats_dev[j]) return c->fail("tpmd_set_feats_device: null level"), -1;
+    cudaStream_t st = (cudaStream_t) stream;
+    if (!c->ck(cudaSetDevice(c->device), "cudaSetDevice")) return -1;
+    for (int j = 0; j < N_LEVELS; j++) {
+        const int64_t n = (int64_t) (8 << j) * (8 << j) * ST_OC[j];
+        if (!c->ck(launch_convert_feats(feats_dev[j], n, c->f16, (char *) c->farena + c->feat_off[j], st),
+                   "convert feats"))
+            return -1;
+    }
+    if (!c->ck(cudaStreamSynchronize(st), "convert feats")) return -1;
+    c->fready = true;
+    return make_proj(c) ? 0 : -1;
+}
+
 int tpmd_batch(const tpmd_ctx *c) { return c ? c->max_batch : -1; }
 
 int tpmd_arena(tpmd_ctx *c, int which, void **dev_ptr, size_t *bytes) {

@@ -82,6 +82,31 @@ cudaError_t launch_conv1_input(bool f16, const float *input, const float *s, int
                                int B, void *x0, cudaStream_t st);
 cudaError_t launch_conv_simt(bool f16, bool up, const conv_params &p, cudaStream_t st);
 cudaError_t launch_tail(bool f16, const tail_params &p, cudaStream_t st);
+// ---- motion encoder (f32, batch 1, channel-last) ----
+struct enc_conv_params {
+    const float *x;        // [IH][IW][IC]
+    int IH, IW, IC;
+    const float *w;        // [OC][K*K*IC], k = (kh*K + kw)*IC + ic
+    int OC, K, stride, pad;
+    int OH, OW;
+    const float *bias;     // [OC] or nullptr
+    int lrelu;             // leaky relu 0.2 after the bias
+    const float *res;      // [OH][OW][OC] added last, or nullptr (may alias y)
+    float *y;              // [OH][OW][OC]
+};
+struct enc_head_params {
+    const float *W[5], *b[5];  // EqualLinears, [out][512]
+    const float *Q;            // [512][20]
+};
+cudaError_t launch_enc_stem(const float *img, const float *w, const float *b, float *y, cudaStream_t st);
+cudaError_t launch_enc_conv(const enc_conv_params &p, cudaStream_t st);
+cudaError_t launch_enc_blur(const float *x, int IH, int IW, int C, const float *k4, int p0, int p1, float *y,
+                            cudaStream_t st);
+cudaError_t launch_enc_head(const float *app, const enc_head_params &h, float *lam, float *motion,
+                            cudaStream_t st);
+// f32 channel-last feats -> the decoder's feats storage (f16 or f32)
+cudaError_t launch_convert_feats(const float *src, int64_t n, bool f16, void *dst, cudaStream_t st);
+
 // proj[i] = (rW[0] . feat[i], rW[1] . feat[i], rW[2] . feat[i], 0) over C channels
 cudaError_t launch_project_feats(bool f16, const void *feat, int64_t npx, int C, const float *rW,
                                  float4 *proj, cudaStream_t st);

@@ -35,6 +35,8 @@ EXPORTS = ("tpmd_abi_version", "tpmd_create", "tpmd_create_error", "tpmd_destroy
            "tpmd_set_feats", "tpmd_batch", "tpmd_decode", "tpmd_decode_device",
            "tpmd_arena", "tpmd_arena_adopt", "tpmd_decode_taps", "tpmd_profile_begin", "tpmd_profile_end",
            "tpmd_kernel_launches", "tpmd_decode_noalloc", "tpmd_gguf_read", "tpmd_load_gguf",
+           "tpmd_set_feats_device", "tpme_create", "tpme_create_error", "tpme_destroy", "tpme_last_error",
+           "tpme_set_tensor", "tpme_load_gguf", "tpme_prepare", "tpme_run", "tpme_feat_device",
            "tpk_bilinear_gather", "tpk_im2col_cf", "tpk_last_error")
 
 _lib = None
@@ -79,6 +81,18 @@ def load_library(path: str = LIB_PATH):
     L.tpmd_kernel_launches.restype = i64
     L.tpmd_gguf_read.argtypes = [cp, cp, C.c_int, GGUF_TENSOR_FN, v, C.c_char_p, C.c_size_t]
     L.tpmd_load_gguf.argtypes = [v, cp]
+    L.tpmd_set_feats_device.argtypes = [v, C.POINTER(v), v]
+    L.tpme_create.argtypes = [C.c_int]
+    L.tpme_create.restype = v
+    L.tpme_create_error.restype = cp
+    L.tpme_destroy.argtypes = [v]
+    L.tpme_last_error.argtypes = [v]
+    L.tpme_last_error.restype = cp
+    L.tpme_set_tensor.argtypes = [v, cp, v, i64]
+    L.tpme_load_gguf.argtypes = [v, cp]
+    L.tpme_prepare.argtypes = [v]
+    L.tpme_run.argtypes = [v, v, v, v, v, C.POINTER(v)]
+    L.tpme_feat_device.argtypes = [v, C.c_int, C.POINTER(v), C.POINTER(i64)]
     L.tpk_bilinear_gather.argtypes = [v, C.c_int, C.c_int, C.c_int, C.c_int, v, i64, C.c_int,
                                       C.c_int, v, v]
     L.tpk_im2col_cf.argtypes = [v] + [C.c_int] * 12 + [v, C.c_int, v]
@@ -151,6 +165,12 @@ class MotionDecoder:
 
     def prepare(self):
         self._check(self._L.tpmd_prepare(self._h))
+
+    def set_feats_device(self, ptrs, stream: int = 0):
+        """The pyramid from device pointers (f32 channel-last), e.g.
+        MotionEncoder.feat_ptrs() after a run."""
+        arr = (C.c_void_p * N_LEVELS)(*ptrs)
+        self._check(self._L.tpmd_set_feats_device(self._h, arr, stream or None))
 
     def set_feats(self, feats):
         arrs = [np.ascontiguousarray(f, np.float32) for f in feats]
@@ -246,3 +266,59 @@ def im2col_cf(src, IC, IW, IH, N, out, KW=3, KH=3, s0=1, s1=1, p0=1, p1=1, d0=1,
         C.c_void_p(src.data_ptr()), IC, IW, IH, N, KW, KH, s0, s1, p0, p1, d0, d1,
         C.c_void_p(out.data_ptr()), int(out.dtype == torch.float16), C.c_void_p(stream)))
     return out
+
+
+class MotionEncoder:
+    """The motion encoder on one GPU (mirrors motion_enc::run,
+    src/motion_enc.cpp:46-184): image -> appearance, lambda, motion, feats."""
+
+    def __init__(self, device: int = 0):
+        self._L = load_library()
+        self._h = self._L.tpme_create(device)
+        if not self._h:
+            raise TpmdError(self._L.tpme_create_error().decode())
+
+    def _check(self, rc: int):
+        if rc != 0:
+            raise TpmdError(self._L.tpme_last_error(self._h).decode())
+
+    def set_tensors(self, tensors: dict):
+        for name, arr in tensors.items():
+            a = np.ascontiguousarray(arr, np.float32)
+            self._check(self._L.tpme_set_tensor(self._h, name.encode(), _np_ptr(a), a.size))
+
+    def load_gguf(self, path: str):
+        self._check(self._L.tpme_load_gguf(self._h, path.encode()))
+
+    def prepare(self):
+        self._check(self._L.tpme_prepare(self._h))
+
+    def run(self, image: np.ndarray, want_feats: bool = True) -> dict:
+        img = np.ascontiguousarray(image, np.float32)
+        if img.shape != (3, 512, 512):
+            raise ValueError("image must be [3, 512, 512] float32 CHW")
+        app, lam, mot = np.empty(512, np.float32), np.empty(20, np.float32), np.empty(512, np.float32)
+        feats = [np.empty(((8 << j) ** 2, ST_OC[j]), np.float32) for j in range(N_LEVELS)] if want_feats else None
+        ptrs = (C.c_void_p * N_LEVELS)(*[f.ctypes.data for f in feats]) if want_feats else None
+        self._check(self._L.tpme_run(self._h, _np_ptr(img), _np_ptr(app), _np_ptr(lam), _np_ptr(mot), ptrs))
+        return dict(appearance=app, lam=lam, motion=mot, feats=feats)
+
+    def feat_ptrs(self) -> list[int]:
+        out = []
+        for j in range(N_LEVELS):
+            p, n = C.c_void_p(), C.c_int64()
+            self._check(self._L.tpme_feat_device(self._h, j, C.byref(p), C.byref(n)))
+            out.append(p.value)
+        return out
+
+    def close(self):
+        if getattr(self, "_h", None):
+            self._L.tpme_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+

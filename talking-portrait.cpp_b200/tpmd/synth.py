@@ -168,3 +168,71 @@ def styles_walk(seed: int = 0, n: int = 50, clip: int = 0) -> np.ndarray:
             a = np.clip(a + steps[t], -3.0, 3.0).astype(np.float32)
         alphas[t] = a
     return (w_src[None, :] + alphas @ q.T).astype(np.float32)
+
+
+ENC_IN = (32, 64, 128, 256, 512, 512, 512)
+ENC_OUT = (64, 128, 256, 512, 512, 512, 512)
+
+
+def encoder_shapes() -> dict[str, tuple[int, ...]]:
+    """name -> torch shape of the motion encoder's tensors (enc.* and the
+    baked direction basis dec.direction.Q), src/motion_enc.cpp:46-140."""
+    p = "enc.net_app.convs."
+    s: dict[str, tuple[int, ...]] = {p + "0.0.weight": (32, 3, 1, 1), p + "0.1.bias": (1, 32, 1, 1)}
+    for i in range(1, 8):
+        c, co = ENC_IN[i - 1], ENC_OUT[i - 1]
+        b = f"{p}{i}."
+        s[b + "conv1.0.weight"] = (c, c, 3, 3)
+        s[b + "conv1.1.bias"] = (1, c, 1, 1)
+        s[b + "conv2.0.kernel"] = (4, 4)
+        s[b + "conv2.1.weight"] = (co, c, 3, 3)
+        s[b + "conv2.2.bias"] = (1, co, 1, 1)
+        s[b + "skip.0.kernel"] = (4, 4)
+        s[b + "skip.1.weight"] = (co, c, 1, 1)
+    s[p + "8.weight"] = (512, 512, 4, 4)
+    for i in range(5):
+        out = 20 if i == 4 else 512
+        s[f"enc.fc.{i}.weight"] = (out, 512)
+        s[f"enc.fc.{i}.bias"] = (out,)
+    s["dec.direction.Q"] = (512, 20)
+    return s
+
+
+def make_encoder_weights(seed: int = 0, bias_std: float = 0.1) -> dict[str, np.ndarray]:
+    """Raw (unfolded) encoder weights: N(0,1) conv and linear weights (the
+    Equal* convention: the runtime scale is 1/sqrt(fan_in)), N(0, bias_std)
+    biases, the normalised [1,3,3,1] outer-product blur (sum 1, as the
+    downsampling Blur uses it), Q with orthonormal columns (QR of a seeded
+    N(0,1) [512, 20] matrix)."""
+    rng = np.random.default_rng([seed, 7])
+    k1 = np.array([1, 3, 3, 1], np.float64)
+    k = np.outer(k1, k1)
+    k = (k / k.sum()).astype(np.float32)
+    out: dict[str, np.ndarray] = {}
+    for name, shape in encoder_shapes().items():
+        if name.endswith(".kernel"):
+            out[name] = k.copy()
+        elif name == "dec.direction.Q":
+            q, _ = np.linalg.qr(rng.standard_normal(shape))
+            out[name] = q.astype(np.float32)
+        elif name.endswith(".bias"):
+            out[name] = (rng.standard_normal(shape) * bias_std).astype(np.float32)
+        else:
+            out[name] = rng.standard_normal(shape).astype(np.float32)
+    return out
+
+
+def make_image(seed: int = 0) -> np.ndarray:
+    """A smooth synthetic portrait-sized image [3, 512, 512] in [-1, 1]: a
+    few random low-frequency cosines per channel plus mild noise."""
+    rng = np.random.default_rng([seed, 8])
+    yy, xx = np.meshgrid(np.arange(512) / 512.0, np.arange(512) / 512.0, indexing="ij")
+    img = np.zeros((3, 512, 512), np.float64)
+    for c in range(3):
+        for _ in range(6):
+            fx, fy = rng.uniform(0.5, 6.0, 2)
+            ph = rng.uniform(0, 2 * np.pi)
+            img[c] += rng.uniform(0.1, 0.3) * np.cos(2 * np.pi * (fx * xx + fy * yy) + ph)
+        img[c] += 0.05 * rng.standard_normal((512, 512))
+    return np.clip(img, -1.0, 1.0).astype(np.float32)
+

@@ -17,8 +17,9 @@ from tpmd import synth
 
 
 def declared_symbols():
-    src = open(os.path.join(ROOT, "include", "tpmd.h")).read()
-    return sorted(set(re.findall(r"\b((?:tpmd|tpk)_[a-z0-9_]+)\s*\(", src)))
+    src = "".join(open(os.path.join(ROOT, "include", h)).read()
+                  for h in ("tpmd.h", "tpme.h"))
+    return sorted(set(re.findall(r"\b((?:tpmd|tpme|tpk)_[a-z0-9_]+)\s*\(", src)))
 
 
 def test_exports_every_declared_symbol():

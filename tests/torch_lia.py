@@ -102,3 +102,56 @@ class TorchLIA:
             skip = rgb
             x = trunk
         return skip[0].numpy()
+
+
+ENC_IN = (32, 64, 128, 256, 512, 512, 512)
+ENC_OUT = (64, 128, 256, 512, 512, 512, 512)
+
+
+class TorchEncoder:
+    """The LIA appearance encoder (EncoderApp) + fc chain + direction, in
+    float64 torch and the unfolded form: RAW weights with the EqualConv2d /
+    EqualLinear runtime scales 1/sqrt(fan_in) applied at run time,
+    FusedLeakyReLU as sqrt(2)*lrelu(x + b), ResBlock output (main + skip) /
+    sqrt(2), Blur as upfirdn2d with pads (2, 2) before the stride-2 3x3 conv
+    and (1, 1) before the stride-2 1x1 skip conv (the graph of
+    src/motion_enc.cpp:46-184 before its load-time folding)."""
+
+    def __init__(self, raw: dict):
+        self.w = {k: _t(v) for k, v in raw.items()}
+
+    def _conv(self, x, name, stride=1, pad=0):
+        W = self.w[name]
+        fan = W.shape[1] * W.shape[2] * W.shape[3]
+        return F.conv2d(x, W * (1.0 / math.sqrt(fan)), stride=stride, padding=pad)
+
+    @staticmethod
+    def _flrelu(x, b):
+        return math.sqrt(2.0) * F.leaky_relu(x + b.reshape(1, -1, 1, 1), 0.2)
+
+    def run(self, image: np.ndarray) -> dict:
+        """image [3, 512, 512] -> appearance [512], lambda [20], motion [512],
+        feats[j] [r*r, C] channel-last (menc conv{6-j})"""
+        p = "enc.net_app.convs."
+        x = self._flrelu(self._conv(_t(image)[None], p + "0.0.weight"), self.w[p + "0.1.bias"])
+        pyr = [x]
+        for i in range(1, 8):
+            b = f"{p}{i}."
+            h = self._flrelu(self._conv(x, b + "conv1.0.weight", pad=1), self.w[b + "conv1.1.bias"])
+            h = _upfirdn(h, self.w[b + "conv2.0.kernel"], 1, 2, 2)
+            h = self._flrelu(self._conv(h, b + "conv2.1.weight", stride=2), self.w[b + "conv2.2.bias"])
+            s = _upfirdn(x, self.w[b + "skip.0.kernel"], 1, 1, 1)
+            s = self._conv(s, b + "skip.1.weight", stride=2)
+            x = (h + s) / math.sqrt(2.0)
+            pyr.append(x)
+        app = self._conv(x, p + "8.weight")[0, :, 0, 0]
+        h = app
+        for i in range(5):
+            W = self.w[f"enc.fc.{i}.weight"]
+            h = h @ (W * (1.0 / math.sqrt(W.shape[1]))).T + self.w[f"enc.fc.{i}.bias"]
+        motion = self.w["dec.direction.Q"] @ h
+        feats = []
+        for j in range(7):
+            f = pyr[6 - j][0]
+            feats.append(f.reshape(f.shape[0], -1).T.numpy())
+        return dict(appearance=app.numpy(), lam=h.numpy(), motion=motion.numpy(), feats=feats)
