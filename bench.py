@@ -234,6 +234,67 @@ def run_reference(args, rank: int, world: int):
     print(json.dumps(line), flush=True)
 
 
+def run_encoder(args):
+    """The motion encoder, one portrait per step on cuda:0, wall clock
+    around the blocking tpme_run. `value`: the image H2D, the encoder and the
+    small outputs D2H, with the pyramid left on the device (the pipeline's
+    path: the decoder takes it through tpmd_set_feats_device); `e2e`: the
+    same plus the D2H of all seven feature maps into host arrays. The CPU
+    baseline is the oracle's restatement on the host cores."""
+    import torch
+    import tpmd
+    import oracle as O
+    from tpmd import synth
+    raw = synth.make_encoder_weights(0)
+    w = synth.fold(raw, tpmd.scale_for)
+    img = synth.make_image(0)
+    enc = tpmd.MotionEncoder(0)
+    enc.set_tensors(w)
+    enc.prepare()
+    for _ in range(args.warmup):
+        enc.run(img)
+    torch.cuda.synchronize()
+    with ClockSampler(0) as clk:
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            enc.run(img)
+            clk.sample()
+        dt = (time.perf_counter() - t0) / args.steps
+    ms_e2e = dt * 1e3
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        enc.run(img, want_feats=False)
+    ms_dev = (time.perf_counter() - t0) / args.steps * 1e3
+    cpu = None
+    if not args.no_cpu_baseline:
+        O.set_threads(os.cpu_count() or 1)
+        oe = O.Encoder(synth.fold(raw, O.scale_for))
+        t0 = time.perf_counter()
+        oe.run(img)
+        cpu = (time.perf_counter() - t0) * 1e3
+    flop = 0.0  # 2*MACs of the convs and linears per portrait
+    H = 512
+    flop += 2.0 * H * H * 32 * 3
+    for i in range(7):
+        c, co, h = synth.ENC_IN[i], synth.ENC_OUT[i], H // 2
+        flop += 2.0 * H * H * c * c * 9 + 2.0 * h * h * co * c * 9 + 2.0 * h * h * co * c
+        H = h
+    flop += 2.0 * 512 * 512 * 16 + 2.0 * (4 * 512 * 512 + 20 * 512)
+    line = {"metric": "menc ms/portrait @512x512 f32", "value": ms_dev, "unit": "ms",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": False,
+            "dtype": "f32", "data": "synthetic (random-init encoder, smooth synthetic image)",
+            "config": {"workload": "motion encoder, one 512x512 portrait per step", "global_batch": 1},
+            "achieved_tflops": flop / (ms_dev * 1e-3) / 1e12,
+            "e2e": {"value": ms_e2e, "unit": "ms", "h2d_bytes_per_step": 3 * 512 * 512 * 4,
+                    "d2h_bytes_per_step": 4 * (512 + 20 + 512 + sum(((8 << j) ** 2) * s for j, s in
+                                                                   enumerate(synth.ST_OC)))},
+            "reference_published_ms": 14.3,
+            "clocks": clk.summary(),
+            "cpu_baseline": None if cpu is None else {"value": cpu, "unit": "ms", "cores": O.threads(),
+                                                      "kind": "port", "sample": "1 portrait"}}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -245,7 +306,13 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--clip", type=int, default=0,
                     help="config 3: decode a clip of this many frames sharded across ranks per step")
+    ap.add_argument("--path", default="decoder", choices=["decoder", "encoder"],
+                    help="encoder: time the motion encoder (once-per-portrait step before the "
+                         "decoder) instead of the decoder; one GPU")
     args = ap.parse_args()
+    if args.path == "encoder":
+        run_encoder(args)
+        return
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
