@@ -77,6 +77,14 @@ typedef int (*tpmd_gguf_tensor_fn)(void *user, const char *name, const int64_t n
 int tpmd_gguf_read(const char *path, const char *expect_arch, int fold_scales,
                    tpmd_gguf_tensor_fn cb, void *user, char *err, size_t err_len);
 
+/* The key/value section only (weights_t::kv_num / kv_str,
+ * src/gguf_load.cpp:82-96): `cb` gets every key in file order with its
+ * GGUF value type (4 u32, 5 i32, 6 f32, 7 bool: `num`; 8 string: `str`,
+ * valid during the call); a nonzero return stops with an error. */
+typedef int (*tpmd_gguf_kv_fn)(void *user, const char *key, int type, double num, const char *str);
+int tpmd_gguf_read_kv(const char *path, const char *expect_arch, tpmd_gguf_kv_fn cb, void *user, char *err,
+                      size_t err_len);
+
 /* The decoder half of tp_ctx::load (src/tp.cpp:32-38): reads the
  * motion_ae_{f32,f16}.gguf file (architecture "float-motion-ae"), folds
  * motion_ae_scale and hands every "dec.*" tensor except dec.direction to

@@ -82,6 +82,14 @@ def lib():
         L.orc_enc_run.argtypes = [v, v, v, v, v, C.POINTER(v)]
         L.orc_enc_error.argtypes = [v]
         L.orc_enc_error.restype = C.c_char_p
+        L.orc_fmt_create.argtypes = [v]
+        L.orc_fmt_create.restype = v
+        L.orc_fmt_destroy.argtypes = [v]
+        L.orc_fmt_set.argtypes = [v, C.c_char_p, v, C.c_int64]
+        L.orc_fmt_forward.argtypes = [v, v, v, C.c_float, v]
+        L.orc_fmt_sample.argtypes = [v, v, v, v, v, v, C.c_int, v]
+        L.orc_fmt_error.argtypes = [v]
+        L.orc_fmt_error.restype = C.c_char_p
         L.orc_set_threads.argtypes = [C.c_int]
         L.orc_get_threads.restype = C.c_int
         _lib = L
@@ -299,6 +307,50 @@ class Encoder:
     def __del__(self):
         if getattr(self, "_h", None):
             self._L.orc_enc_destroy(self._h)
+            self._h = None
+
+
+class FmtConfig(C.Structure):
+    """orc_fmt_config: the FMT's float.fmt.* hyper-parameters."""
+    _fields_ = [(n, C.c_int) for n in ("dim_h", "depth", "n_heads", "dim_w", "dim_a", "dim_e",
+                                       "chunk_frames", "prev_frames", "attn_window", "t_freq_dim", "nfe")] + \
+               [(n, C.c_float) for n in ("mlp_ratio", "ln_eps", "a_cfg", "e_cfg")]
+
+
+class Fmt:
+    """The flow-matching transformer restatement (src/fmt.cpp:9-211) and its
+    chunk sampler (src/pipeline.cpp:15-91), f32."""
+
+    def __init__(self, cfg: dict, tensors: dict):
+        self._L = lib()
+        self.cfg = FmtConfig(**cfg)
+        self._h = self._L.orc_fmt_create(C.byref(self.cfg))
+        for n, a in tensors.items():
+            a = np.ascontiguousarray(a, np.float32)
+            if self._L.orc_fmt_set(self._h, n.encode(), _p(a), a.size) != 0:
+                raise RuntimeError(self._L.orc_fmt_error(self._h).decode())
+
+    def forward(self, x60, cond, t: float) -> np.ndarray:
+        c = self.cfg
+        T = c.chunk_frames + c.prev_frames
+        x60 = np.ascontiguousarray(x60, np.float32)
+        cond = np.ascontiguousarray(cond, np.float32)
+        v = np.empty((3, T, c.dim_w), np.float32)
+        if self._L.orc_fmt_forward(self._h, _p(x60), _p(cond), float(t), _p(v)) != 0:
+            raise RuntimeError(self._L.orc_fmt_error(self._h).decode())
+        return v
+
+    def sample(self, wr, prev_wa, cond_audio, prev_x, x0, emotion: int) -> np.ndarray:
+        c = self.cfg
+        a = [np.ascontiguousarray(z, np.float32) for z in (wr, prev_wa, cond_audio, prev_x, x0)]
+        out = np.empty((c.chunk_frames, c.dim_w), np.float32)
+        if self._L.orc_fmt_sample(self._h, *[_p(z) for z in a], int(emotion), _p(out)) != 0:
+            raise RuntimeError(self._L.orc_fmt_error(self._h).decode())
+        return out
+
+    def __del__(self):
+        if getattr(self, "_h", None):
+            self._L.orc_fmt_destroy(self._h)
             self._h = None
 
 

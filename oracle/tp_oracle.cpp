@@ -976,3 +976,234 @@ int orc_enc_run(orc_enc *e, const float *image, float *appearance, float *lambda
 
 }  // extern "C"
 
+// ---------------------------------------------------------------------------
+// flow-matching transformer (src/fmt.cpp:9-211) and chunk sampler
+// (src/pipeline.cpp:15-91)
+// ---------------------------------------------------------------------------
+namespace {
+
+// y[m][n] = sum_k x[m][k] W[n][k] + b[n]  (torch Linear, W [N][K])
+void linear_rows(const float *x, int M, int K, const float *W, const float *b, int N, float *y) {
+#pragma omp parallel for collapse(2) schedule(static)
+    for (int m = 0; m < M; m++)
+        for (int n = 0; n < N; n++) {
+            const float *xr = x + (size_t) m * K, *wr = W + (size_t) n * K;
+            float a = 0.0f;
+            for (int k = 0; k < K; k++) a += xr[k] * wr[k];
+            y[(size_t) m * N + n] = a + (b ? b[n] : 0.0f);
+        }
+}
+inline float silu(float v) { return v / (1.0f + expf(-v)); }
+inline float gelu_tanh(float v) {
+    const float c = 0.7978845608028654f;  // sqrt(2/pi)
+    return 0.5f * v * (1.0f + tanhf(c * (v + 0.044715f * v * v * v)));
+}
+// ggml_norm (no affine) then the adaLN modulation h*scale + h + shift
+void norm_modulate(const float *x, int M, int H, float eps, const float *mod, int mod_stride,
+                   int shift_off, int scale_off, float *y) {
+#pragma omp parallel for schedule(static)
+    for (int m = 0; m < M; m++) {
+        const float *r = x + (size_t) m * H;
+        double mean = 0;
+        for (int i = 0; i < H; i++) mean += r[i];
+        mean /= H;
+        double var = 0;
+        for (int i = 0; i < H; i++) var += (r[i] - mean) * (r[i] - mean);
+        var /= H;
+        const float inv = (float) (1.0 / sqrt(var + eps));
+        const float *md = mod + (size_t) m * mod_stride;
+        for (int i = 0; i < H; i++) {
+            const float h = (float) (r[i] - mean) * inv;
+            y[(size_t) m * H + i] = h * md[scale_off + i] + h + md[shift_off + i];
+        }
+    }
+}
+
+}  // namespace
+
+struct orc_fmt {
+    orc_fmt_config c{};
+    int T = 0, CD = 0, FF = 0;
+    std::map<std::string, int64_t> spec;
+    std::map<std::string, std::vector<float>> t;
+    std::string err;
+    const std::vector<float> &get(const std::string &n) const { return t.at(n); }
+};
+
+extern "C" {
+
+orc_fmt *orc_fmt_create(const orc_fmt_config *cfg) {
+    orc_fmt *f = new orc_fmt();
+    f->c = *cfg;
+    const int H = cfg->dim_h;
+    f->T = cfg->chunk_frames + cfg->prev_frames;
+    f->CD = cfg->dim_w + cfg->dim_a + cfg->dim_e;
+    f->FF = (int) (H * cfg->mlp_ratio);
+    auto lin = [&](const std::string &n, int64_t out, int64_t in) {
+        f->spec[n + ".weight"] = out * in;
+        f->spec[n + ".bias"] = out;
+    };
+    lin("t_embedder.mlp.0", H, cfg->t_freq_dim);
+    lin("t_embedder.mlp.2", H, H);
+    lin("c_embedder", H, f->CD);
+    lin("x_embedder.proj", H, cfg->dim_w);
+    f->spec["pos_embed"] = (int64_t) f->T * H;
+    for (int i = 0; i < cfg->depth; i++) {
+        const std::string b = "blocks." + std::to_string(i) + ".";
+        lin(b + "adaLN_modulation.1", 6 * H, H);
+        lin(b + "attn.qkv", 3 * H, H);
+        lin(b + "attn.proj", H, H);
+        lin(b + "mlp.fc1", f->FF, H);
+        lin(b + "mlp.fc2", H, f->FF);
+    }
+    lin("decoder.adaLN_modulation.1", 2 * H, H);
+    lin("decoder.linear", cfg->dim_w, H);
+    return f;
+}
+void orc_fmt_destroy(orc_fmt *f) { delete f; }
+const char *orc_fmt_error(const orc_fmt *f) { return f ? f->err.c_str() : "null fmt"; }
+
+int orc_fmt_set(orc_fmt *f, const char *name, const float *data, int64_t n) {
+    auto it = f->spec.find(name);
+    if (it == f->spec.end() || it->second != n) {
+        f->err = std::string("orc_fmt_set: unknown tensor or size mismatch: ") + name;
+        return -1;
+    }
+    f->t[name].assign(data, data + n);
+    return 0;
+}
+
+int orc_fmt_forward(orc_fmt *f, const float *x60, const float *cond, float tt, float *v) {
+    for (auto &kv : f->spec)
+        if (!f->t.count(kv.first)) {
+            f->err = "orc_fmt_forward: missing tensor " + kv.first;
+            return -1;
+        }
+    const orc_fmt_config &c = f->c;
+    const int H = c.dim_h, T = f->T, B = 3, M = B * T, nh = c.n_heads, hd = H / nh;
+    // timestep embedding: GLIDE sinusoid, freq_k = exp(-ln(10000) k / half)
+    const int half = c.t_freq_dim / 2;
+    std::vector<float> tf((size_t) c.t_freq_dim);
+    for (int k = 0; k < half; k++) {
+        const float fr = (float) exp(-log(10000.0) * (double) k / (double) half);
+        tf[(size_t) k] = cosf(tt * fr);
+        tf[(size_t) (half + k)] = sinf(tt * fr);
+    }
+    std::vector<float> te0((size_t) H), te((size_t) H);
+    linear_rows(tf.data(), 1, c.t_freq_dim, f->get("t_embedder.mlp.0.weight").data(),
+                f->get("t_embedder.mlp.0.bias").data(), H, te0.data());
+    for (float &q : te0) q = silu(q);
+    linear_rows(te0.data(), 1, H, f->get("t_embedder.mlp.2.weight").data(),
+                f->get("t_embedder.mlp.2.bias").data(), H, te.data());
+    // conditioning: silu(c_embedder(cond) + t_emb) per (branch, frame)
+    std::vector<float> sc((size_t) M * H);
+    linear_rows(cond, M, f->CD, f->get("c_embedder.weight").data(), f->get("c_embedder.bias").data(), H,
+                sc.data());
+    for (int m = 0; m < M; m++)
+        for (int i = 0; i < H; i++) sc[(size_t) m * H + i] = silu(sc[(size_t) m * H + i] + te[(size_t) i]);
+    // tokens: x_embedder(x60) + pos, the same rows in every branch
+    std::vector<float> x1((size_t) T * H), x((size_t) M * H);
+    linear_rows(x60, T, c.dim_w, f->get("x_embedder.proj.weight").data(),
+                f->get("x_embedder.proj.bias").data(), H, x1.data());
+    const std::vector<float> &pos = f->get("pos_embed");
+    for (int b = 0; b < B; b++)
+        for (int r = 0; r < T; r++)
+            for (int i = 0; i < H; i++)
+                x[((size_t) b * T + r) * H + i] = x1[(size_t) r * H + i] + pos[(size_t) r * H + i];
+    std::vector<float> mod((size_t) M * 6 * H), h((size_t) M * H), qkv((size_t) M * 3 * H),
+        att((size_t) M * H), o((size_t) M * H), m1((size_t) M * f->FF);
+    const float scale = 1.0f / sqrtf((float) hd);
+    for (int l = 0; l < c.depth; l++) {
+        const std::string bn = "blocks." + std::to_string(l) + ".";
+        auto W = [&](const std::string &n) { return f->get(bn + n + ".weight").data(); };
+        auto Bv = [&](const std::string &n) { return f->get(bn + n + ".bias").data(); };
+        linear_rows(sc.data(), M, H, W("adaLN_modulation.1"), Bv("adaLN_modulation.1"), 6 * H, mod.data());
+        // attention branch (chunks: shift, scale, gate for msa then for mlp)
+        norm_modulate(x.data(), M, H, c.ln_eps, mod.data(), 6 * H, 0, H, h.data());
+        linear_rows(h.data(), M, H, W("attn.qkv"), Bv("attn.qkv"), 3 * H, qkv.data());
+        // banded mask: row i attends cols [max(0,i-w), i+w+1), scale 1/sqrt(hd)
+#pragma omp parallel for collapse(3) schedule(static)
+        for (int b = 0; b < B; b++)
+            for (int hh = 0; hh < nh; hh++)
+                for (int i = 0; i < T; i++) {
+                    const int j0 = std::max(0, i - c.attn_window), j1 = std::min(T, i + c.attn_window + 1);
+                    const float *q = qkv.data() + ((size_t) b * T + i) * 3 * H + hh * hd;
+                    float sc_[64];
+                    float mx = -INFINITY;
+                    for (int j = j0; j < j1; j++) {
+                        const float *k = qkv.data() + ((size_t) b * T + j) * 3 * H + H + hh * hd;
+                        float a = 0.0f;
+                        for (int d = 0; d < hd; d++) a += q[d] * k[d];
+                        sc_[j - j0] = a * scale;
+                        mx = std::max(mx, sc_[j - j0]);
+                    }
+                    float sum = 0.0f;
+                    for (int j = j0; j < j1; j++) sum += (sc_[j - j0] = expf(sc_[j - j0] - mx));
+                    float *out = att.data() + ((size_t) b * T + i) * H + hh * hd;
+                    for (int d = 0; d < hd; d++) out[d] = 0.0f;
+                    for (int j = j0; j < j1; j++) {
+                        const float pj = sc_[j - j0] / sum;
+                        const float *vv = qkv.data() + ((size_t) b * T + j) * 3 * H + 2 * H + hh * hd;
+                        for (int d = 0; d < hd; d++) out[d] += pj * vv[d];
+                    }
+                }
+        linear_rows(att.data(), M, H, W("attn.proj"), Bv("attn.proj"), H, o.data());
+        for (int m = 0; m < M; m++)
+            for (int i = 0; i < H; i++)
+                x[(size_t) m * H + i] += mod[(size_t) m * 6 * H + 2 * H + i] * o[(size_t) m * H + i];
+        // MLP branch (tanh GELU)
+        norm_modulate(x.data(), M, H, c.ln_eps, mod.data(), 6 * H, 3 * H, 4 * H, h.data());
+        linear_rows(h.data(), M, H, W("mlp.fc1"), Bv("mlp.fc1"), f->FF, m1.data());
+        for (float &q : m1) q = gelu_tanh(q);
+        linear_rows(m1.data(), M, f->FF, W("mlp.fc2"), Bv("mlp.fc2"), H, o.data());
+        for (int m = 0; m < M; m++)
+            for (int i = 0; i < H; i++)
+                x[(size_t) m * H + i] += mod[(size_t) m * 6 * H + 5 * H + i] * o[(size_t) m * H + i];
+    }
+    std::vector<float> fm((size_t) M * 2 * H);
+    linear_rows(sc.data(), M, H, f->get("decoder.adaLN_modulation.1.weight").data(),
+                f->get("decoder.adaLN_modulation.1.bias").data(), 2 * H, fm.data());
+    norm_modulate(x.data(), M, H, c.ln_eps, fm.data(), 2 * H, 0, H, h.data());
+    linear_rows(h.data(), M, H, f->get("decoder.linear.weight").data(), f->get("decoder.linear.bias").data(),
+                c.dim_w, v);
+    return 0;
+}
+
+int orc_fmt_sample(orc_fmt *f, const float *wr, const float *prev_wa, const float *cond_audio,
+                   const float *prev_x, const float *x0, int emotion, float *motion) {
+    const orc_fmt_config &c = f->c;
+    const int T = f->T, P = c.prev_frames, CF = c.chunk_frames, D = c.dim_w, CD = f->CD;
+    // condition rows [wr | wa | we] per branch: uncond nulls the current
+    // frames' wa and we, audio-only nulls we; prev_wa rows stay in all
+    std::vector<float> cond((size_t) 3 * T * CD, 0.0f);
+    for (int b = 0; b < 3; b++)
+        for (int fr = 0; fr < T; fr++) {
+            float *row = cond.data() + ((size_t) b * T + fr) * CD;
+            memcpy(row, wr, (size_t) D * 4);
+            const float *wa = fr < P ? prev_wa + (size_t) fr * D : cond_audio + (size_t) (fr - P) * D;
+            if (!(b == 0 && fr >= P)) memcpy(row + D, wa, (size_t) D * 4);
+            if (b == 1 && emotion >= 0 && emotion < c.dim_e) row[D + c.dim_a + emotion] = 1.0f;
+        }
+    std::vector<float> x((size_t) CF * D), x60((size_t) T * D), v((size_t) 3 * T * D);
+    memcpy(x.data(), x0, x.size() * 4);
+    memcpy(x60.data(), prev_x, (size_t) P * D * 4);
+    for (int s = 0; s < c.nfe - 1; s++) {
+        memcpy(x60.data() + (size_t) P * D, x.data(), x.size() * 4);
+        const float t0 = (float) ((double) s / (double) (c.nfe - 1));
+        const float t1 = (float) ((double) (s + 1) / (double) (c.nfe - 1));
+        if (orc_fmt_forward(f, x60.data(), cond.data(), t0, v.data()) != 0) return -1;
+        const float *u = v.data(), *fu = v.data() + (size_t) T * D, *a = v.data() + (size_t) 2 * T * D;
+        const float dt = t1 - t0;
+        for (int fr = 0; fr < CF; fr++)
+            for (int i = 0; i < D; i++) {
+                const size_t q = (size_t) (P + fr) * D + i;
+                const float vc = (u[q] + c.a_cfg * (a[q] - u[q])) + c.e_cfg * (fu[q] - a[q]);
+                x[(size_t) fr * D + i] = x[(size_t) fr * D + i] + dt * vc;
+            }
+    }
+    memcpy(motion, x.data(), x.size() * 4);
+    return 0;
+}
+
+}  // extern "C"
+

@@ -117,6 +117,30 @@ int orc_enc_run(orc_enc *e, const float *image, float *appearance, float *lambda
                 float *motion, float *const feats[7]);
 const char *orc_enc_error(const orc_enc *e);
 
+/* ---- flow-matching transformer (fmt_model, src/fmt.cpp:9-211) and its
+ * chunk sampler (sample_chunk_ex, src/pipeline.cpp:15-91) ------------------
+ * Dimensions as the GGUF's float.fmt.* keys give them. Tensors f32, torch
+ * element order: t_embedder.mlp.{0,2}, c_embedder, x_embedder.proj,
+ * pos_embed [1][T][H], blocks.i.{adaLN_modulation.1, attn.qkv, attn.proj,
+ * mlp.fc1, mlp.fc2}, decoder.{adaLN_modulation.1, linear} (.weight/.bias). */
+typedef struct {
+    int dim_h, depth, n_heads, dim_w, dim_a, dim_e;
+    int chunk_frames, prev_frames, attn_window, t_freq_dim, nfe;
+    float mlp_ratio, ln_eps, a_cfg, e_cfg;
+} orc_fmt_config;
+typedef struct orc_fmt orc_fmt;
+orc_fmt *orc_fmt_create(const orc_fmt_config *cfg);
+void orc_fmt_destroy(orc_fmt *f);
+int orc_fmt_set(orc_fmt *f, const char *name, const float *data, int64_t n);
+/* one CFG-batched forward: x60 [T][dim_w], cond [3][T][dim_w+dim_a+dim_e],
+ * t in [0,1] -> v [3][T][dim_w] (uncond, full, audio-only) */
+int orc_fmt_forward(orc_fmt *f, const float *x60, const float *cond, float t, float *v);
+/* one 50-frame chunk: wr [dim_w], prev_wa / prev_x [P][dim_w], cond_audio /
+ * x0 [CF][dim_w], emotion (-1: none) -> motion [CF][dim_w] */
+int orc_fmt_sample(orc_fmt *f, const float *wr, const float *prev_wa, const float *cond_audio,
+                   const float *prev_x, const float *x0, int emotion, float *motion);
+const char *orc_fmt_error(const orc_fmt *f);
+
 #ifdef __cplusplus
 }
 #endif

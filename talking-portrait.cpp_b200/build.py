@@ -25,7 +25,7 @@ FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O3",
 
 def _compile(src: str) -> str:
     obj = os.path.join(OBJ, os.path.basename(src) + ".o")
-    deps = [src] + glob.glob(os.path.join(CSRC, "*.h")) + [os.path.join(HERE, "..", "include", "tpmd.h")]
+    deps = [src] + glob.glob(os.path.join(CSRC, "*.h")) + glob.glob(os.path.join(HERE, "..", "include", "*.h"))
     if os.path.exists(obj) and os.path.getmtime(obj) >= max(os.path.getmtime(d) for d in deps):
         return obj
     cmd = [NVCC] + FLAGS + ["-c", src, "-o", obj]
@@ -45,7 +45,9 @@ def build(verbose: bool = False) -> str:
     with cf.ThreadPoolExecutor(max_workers=os.cpu_count() or 4) as ex:
         objs = list(ex.map(_compile, srcs))
     if not os.path.exists(SO) or os.path.getmtime(SO) < max(os.path.getmtime(o) for o in objs):
-        cmd = [NVCC] + ARCH + ["-shared", "-cudart", "static", "-o", SO] + objs + ["-lpthread"]
+        # cuBLAS (dynamic, from the CUDA toolkit) serves the FMT sampler's plain linears
+        cmd = [NVCC] + ARCH + ["-shared", "-cudart", "static", "-o", SO] + objs + \
+              ["-lcublas", "-lpthread", "-Xlinker", "-rpath=/usr/local/cuda/lib64"]
         subprocess.run(cmd, check=True)
     if verbose:
         print(f"built {SO}")

@@ -1,0 +1,269 @@
+// Kernels of the flow-matching transformer (fmt_model::forward,
+// src/fmt.cpp:64-211) and its Euler/CFG sampler (src/pipeline.cpp:15-91),
+// around the plain linears (cuBLAS, tpfm_api.cu). Tokens are rows m = b*T + f
+// of the three CFG branches b (uncond, full, audio-only) and T frames; every
+// activation is row-major [M][width] float32 unless it feeds a GEMM, where it
+// is written in the GEMM's input type TIN (float or __half). GEMMs run
+// without bias; the kernel consuming a GEMM output adds the bias.
+#include "tpmd_internal.h"
+
+#include <algorithm>
+
+namespace tpmd {
+namespace {
+
+template <typename T>
+__device__ __forceinline__ T cvt(float v);
+template <>
+__device__ __forceinline__ float cvt<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __half cvt<__half>(float v) { return __float2half_rn(v); }
+
+__device__ __forceinline__ float silu(float v) { return v / (1.0f + expf(-v)); }
+__device__ __forceinline__ float gelu_tanh(float v) {
+    const float c = 0.7978845608028654f;  // sqrt(2/pi)
+    return 0.5f * v * (1.0f + tanhf(c * (v + 0.044715f * v * v * v)));
+}
+
+__device__ __forceinline__ float block_sum(float v, float *red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
+    __syncthreads();
+    if (l == 0) red[w] = v;
+    __syncthreads();
+    float s = 0.0f;
+    for (int i = 0; i < nw; i++) s += red[i];
+    return s;
+}
+
+// y[n] = act(W[n] . x + b[n]), one warp per row (the timestep MLP, M = 1)
+__global__ void __launch_bounds__(256) gemv_kernel(const float *__restrict__ W, const float *__restrict__ x,
+                                                   const float *__restrict__ b, int N, int K, int act_silu,
+                                                   float *__restrict__ y) {
+    const int lane = threadIdx.x & 31, n = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (n >= N) return;
+    float a = 0.0f;
+    for (int k = lane; k < K; k += 32) a = fmaf(__ldg(W + (int64_t) n * K + k), __ldg(x + k), a);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+    if (lane == 0) {
+        a += __ldg(b + n);
+        y[n] = act_silu ? silu(a) : a;
+    }
+}
+
+// sc[m][i] = silu(clin[m][i] + bc[i] + te[i])
+template <typename TIN>
+__global__ void cond_silu_kernel(const float *__restrict__ clin, const float *__restrict__ bc,
+                                 const float *__restrict__ te, int M, int H, TIN *__restrict__ sc) {
+    const int64_t n = (int64_t) M * H;
+    for (int64_t e = (int64_t) blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t) gridDim.x * blockDim.x) {
+        const int i = (int) (e % H);
+        sc[e] = cvt<TIN>(silu(clin[e] + __ldg(bc + i) + __ldg(te + i)));
+    }
+}
+
+// x[b][f][i] = x1[f][i] + bx[i] + pos[f][i] for the three branches
+__global__ void embed_x_kernel(const float *__restrict__ x1, const float *__restrict__ bx,
+                               const float *__restrict__ pos, int T, int H, float *__restrict__ x) {
+    const int64_t n = (int64_t) T * H;
+    for (int64_t e = (int64_t) blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t) gridDim.x * blockDim.x) {
+        const float v = x1[e] + __ldg(bx + e % H) + __ldg(pos + e);
+        x[e] = v;
+        x[n + e] = v;
+        x[2 * n + e] = v;
+    }
+}
+
+// h = LN(x) * (1 + scale) + shift per row (ggml_norm: no affine; mean and
+// variance in two passes), scale/shift = mod[m][off..] + bmod[off..]
+template <typename TIN>
+__global__ void __launch_bounds__(256) norm_mod_kernel(const float *__restrict__ x, int H, float eps,
+                                                       const float *__restrict__ mod,
+                                                       const float *__restrict__ bmod, int mod_stride,
+                                                       int shift_off, int scale_off, TIN *__restrict__ h) {
+    __shared__ float red[32];
+    const int m = blockIdx.x;
+    const float *r = x + (int64_t) m * H;
+    float s = 0.0f;
+    for (int i = threadIdx.x; i < H; i += blockDim.x) s += r[i];
+    const float mean = block_sum(s, red) / (float) H;
+    float q = 0.0f;
+    for (int i = threadIdx.x; i < H; i += blockDim.x) {
+        const float d = r[i] - mean;
+        q = fmaf(d, d, q);
+    }
+    const float var = block_sum(q, red) / (float) H;
+    const float inv = 1.0f / sqrtf(var + eps);
+    const float *md = mod + (int64_t) m * mod_stride;
+    for (int i = threadIdx.x; i < H; i += blockDim.x) {
+        const float v = (r[i] - mean) * inv;
+        const float sc = md[scale_off + i] + __ldg(bmod + scale_off + i);
+        const float sh = md[shift_off + i] + __ldg(bmod + shift_off + i);
+        h[(int64_t) m * H + i] = cvt<TIN>(v * sc + v + sh);
+    }
+}
+
+// banded self-attention per (branch, head, query row i): keys j with
+// |i - j| <= window (the additive -inf mask elsewhere contributes nothing),
+// scores q.k / sqrt(hd), softmax, weighted sum of v. One warp per query;
+// qkv = GEMM output + bias, row m = [q | k | v] of width 3H.
+template <typename TIN>
+__global__ void __launch_bounds__(256) attn_kernel(const float *__restrict__ qkv, const float *__restrict__ bqkv,
+                                                   int T, int H, int nh, int window, TIN *__restrict__ out) {
+    const int lane = threadIdx.x & 31;
+    const int g = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int hd = H / nh;
+    if (g >= 3 * nh * T) return;
+    const int i = g % T, head = (g / T) % nh, b = g / (T * nh);
+    const int j0 = max(0, i - window), j1 = min(T, i + window + 1);
+    const float scale = 1.0f / sqrtf((float) hd);
+    const float *qrow = qkv + ((int64_t) b * T + i) * 3 * H + head * hd;
+    float sc[16];
+    float mx = -INFINITY;
+    for (int j = j0; j < j1; j++) {
+        const float *krow = qkv + ((int64_t) b * T + j) * 3 * H + H + head * hd;
+        float a = 0.0f;
+        for (int d = lane; d < hd; d += 32)
+            a = fmaf(qrow[d] + __ldg(bqkv + head * hd + d), krow[d] + __ldg(bqkv + H + head * hd + d), a);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+        sc[j - j0] = a * scale;
+        mx = fmaxf(mx, sc[j - j0]);
+    }
+    float sum = 0.0f;
+    for (int j = j0; j < j1; j++) sum += (sc[j - j0] = expf(sc[j - j0] - mx));
+    for (int d = lane; d < hd; d += 32) {
+        float a = 0.0f;
+        for (int j = j0; j < j1; j++)
+            a = fmaf(sc[j - j0] / sum, qkv[((int64_t) b * T + j) * 3 * H + 2 * H + head * hd + d] +
+                                           __ldg(bqkv + 2 * H + head * hd + d),
+                     a);
+        out[((int64_t) b * T + i) * H + head * hd + d] = cvt<TIN>(a);
+    }
+}
+
+// x += (mod[m][gate] + bmod[gate]) * (o + bo)
+__global__ void gate_residual_kernel(float *__restrict__ x, const float *__restrict__ o,
+                                     const float *__restrict__ bo, const float *__restrict__ mod,
+                                     const float *__restrict__ bmod, int mod_stride, int gate_off, int M, int H) {
+    const int64_t n = (int64_t) M * H;
+    for (int64_t e = (int64_t) blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t) gridDim.x * blockDim.x) {
+        const int64_t m = e / H;
+        const int i = (int) (e % H);
+        const float g = mod[m * mod_stride + gate_off + i] + __ldg(bmod + gate_off + i);
+        x[e] += g * (o[e] + __ldg(bo + i));
+    }
+}
+
+// y = gelu_tanh(a + b)
+template <typename TIN>
+__global__ void gelu_kernel(const float *__restrict__ a, const float *__restrict__ b, int M, int N,
+                            TIN *__restrict__ y) {
+    const int64_t n = (int64_t) M * N;
+    for (int64_t e = (int64_t) blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t) gridDim.x * blockDim.x)
+        y[e] = cvt<TIN>(gelu_tanh(a[e] + __ldg(b + e % N)));
+}
+
+// v = out + b; per current frame f: vc = (u + a_cfg (a - u)) + e_cfg (fu - a);
+// x[f] += dt * vc; the next forward's x60 rows P.. are the new x
+__global__ void cfg_euler_kernel(const float *__restrict__ vout, const float *__restrict__ bv, int T, int P,
+                                 int D, float a_cfg, float e_cfg, float dt, float *__restrict__ x,
+                                 float *__restrict__ x60) {
+    const int CF = T - P;
+    const int64_t n = (int64_t) CF * D;
+    const int64_t br = (int64_t) T * D;
+    for (int64_t e = (int64_t) blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t) gridDim.x * blockDim.x) {
+        const int i = (int) (e % D);
+        const int64_t q = (int64_t) P * D + e;
+        const float bb = __ldg(bv + i);
+        const float u = vout[q] + bb, fu = vout[br + q] + bb, a = vout[2 * br + q] + bb;
+        const float vc = (u + a_cfg * (a - u)) + e_cfg * (fu - a);
+        const float nx = x[e] + dt * vc;
+        x[e] = nx;
+        x60[q] = nx;
+    }
+}
+
+// v_out = out + b (the plain forward's output)
+__global__ void add_bias_kernel(const float *__restrict__ a, const float *__restrict__ b, int M, int N,
+                                float *__restrict__ y) {
+    const int64_t n = (int64_t) M * N;
+    for (int64_t e = (int64_t) blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t) gridDim.x * blockDim.x)
+        y[e] = a[e] + __ldg(b + e % N);
+}
+
+__global__ void to_half_kernel(const float *__restrict__ a, int64_t n, __half *__restrict__ y) {
+    for (int64_t e = (int64_t) blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t) gridDim.x * blockDim.x)
+        y[e] = __float2half_rn(a[e]);
+}
+
+inline int grid_for(int64_t n) { return (int) std::min<int64_t>((n + 255) / 256, 148 * 8); }
+
+}  // namespace
+
+cudaError_t fmt_gemv(const float *W, const float *x, const float *b, int N, int K, bool silu_act, float *y,
+                     cudaStream_t st) {
+    gemv_kernel<<<(N * 32 + 255) / 256, 256, 0, st>>>(W, x, b, N, K, silu_act ? 1 : 0, y);
+    return cudaGetLastError();
+}
+cudaError_t fmt_cond_silu(bool f16, const float *clin, const float *bc, const float *te, int M, int H, void *sc,
+                          cudaStream_t st) {
+    if (f16)
+        cond_silu_kernel<__half><<<grid_for((int64_t) M * H), 256, 0, st>>>(clin, bc, te, M, H, (__half *) sc);
+    else
+        cond_silu_kernel<float><<<grid_for((int64_t) M * H), 256, 0, st>>>(clin, bc, te, M, H, (float *) sc);
+    return cudaGetLastError();
+}
+cudaError_t fmt_embed_x(const float *x1, const float *bx, const float *pos, int T, int H, float *x, cudaStream_t st) {
+    embed_x_kernel<<<grid_for((int64_t) T * H), 256, 0, st>>>(x1, bx, pos, T, H, x);
+    return cudaGetLastError();
+}
+cudaError_t fmt_norm_mod(bool f16, const float *x, int M, int H, float eps, const float *mod, const float *bmod,
+                         int mod_stride, int shift_off, int scale_off, void *h, cudaStream_t st) {
+    if (f16)
+        norm_mod_kernel<__half><<<M, 256, 0, st>>>(x, H, eps, mod, bmod, mod_stride, shift_off, scale_off,
+                                                   (__half *) h);
+    else
+        norm_mod_kernel<float><<<M, 256, 0, st>>>(x, H, eps, mod, bmod, mod_stride, shift_off, scale_off,
+                                                  (float *) h);
+    return cudaGetLastError();
+}
+cudaError_t fmt_attn(bool f16, const float *qkv, const float *bqkv, int T, int H, int nh, int window, void *out,
+                     cudaStream_t st) {
+    if (2 * window + 1 > 16 || H % nh) return cudaErrorInvalidValue;
+    const int warps = 3 * nh * T;
+    if (f16)
+        attn_kernel<__half><<<(warps * 32 + 255) / 256, 256, 0, st>>>(qkv, bqkv, T, H, nh, window, (__half *) out);
+    else
+        attn_kernel<float><<<(warps * 32 + 255) / 256, 256, 0, st>>>(qkv, bqkv, T, H, nh, window, (float *) out);
+    return cudaGetLastError();
+}
+cudaError_t fmt_gate_residual(float *x, const float *o, const float *bo, const float *mod, const float *bmod,
+                              int mod_stride, int gate_off, int M, int H, cudaStream_t st) {
+    gate_residual_kernel<<<grid_for((int64_t) M * H), 256, 0, st>>>(x, o, bo, mod, bmod, mod_stride, gate_off, M, H);
+    return cudaGetLastError();
+}
+cudaError_t fmt_gelu(bool f16, const float *a, const float *b, int M, int N, void *y, cudaStream_t st) {
+    if (f16)
+        gelu_kernel<__half><<<grid_for((int64_t) M * N), 256, 0, st>>>(a, b, M, N, (__half *) y);
+    else
+        gelu_kernel<float><<<grid_for((int64_t) M * N), 256, 0, st>>>(a, b, M, N, (float *) y);
+    return cudaGetLastError();
+}
+cudaError_t fmt_cfg_euler(const float *vout, const float *bv, int T, int P, int D, float a_cfg, float e_cfg,
+                          float dt, float *x, float *x60, cudaStream_t st) {
+    cfg_euler_kernel<<<grid_for((int64_t) (T - P) * D), 256, 0, st>>>(vout, bv, T, P, D, a_cfg, e_cfg, dt, x, x60);
+    return cudaGetLastError();
+}
+cudaError_t fmt_add_bias(const float *a, const float *b, int M, int N, float *y, cudaStream_t st) {
+    add_bias_kernel<<<grid_for((int64_t) M * N), 256, 0, st>>>(a, b, M, N, y);
+    return cudaGetLastError();
+}
+cudaError_t fmt_to_half(const float *a, int64_t n, __half *y, cudaStream_t st) {
+    to_half_kernel<<<grid_for(n), 256, 0, st>>>(a, n, y);
+    return cudaGetLastError();
+}
+
+}  // namespace tpmd

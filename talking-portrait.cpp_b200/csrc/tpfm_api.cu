@@ -1,0 +1,489 @@
+// Flow-matching sampler C ABI (include/tpfm.h): fmt_model::forward
+// (src/fmt.cpp:64-211) and sample_chunk_ex (src/pipeline.cpp:15-91). The
+// plain linears are cuBLAS GEMMs (row-major Y[M][N] = X[M][K] W[N][K]^T, no
+// bias); norms, banded attention, activations, gated residuals and the
+// CFG/Euler update are the kernels of kernels_fmt.cu. A chunk's nine
+// forwards run as one captured CUDA graph.
+#include <cublas_v2.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "../../include/tpfm.h"
+#include "tpmd_internal.h"
+
+namespace tpmd {
+cudaError_t fmt_gemv(const float *W, const float *x, const float *b, int N, int K, bool silu_act, float *y,
+                     cudaStream_t st);
+cudaError_t fmt_cond_silu(bool f16, const float *clin, const float *bc, const float *te, int M, int H, void *sc,
+                          cudaStream_t st);
+cudaError_t fmt_embed_x(const float *x1, const float *bx, const float *pos, int T, int H, float *x, cudaStream_t st);
+cudaError_t fmt_norm_mod(bool f16, const float *x, int M, int H, float eps, const float *mod, const float *bmod,
+                         int mod_stride, int shift_off, int scale_off, void *h, cudaStream_t st);
+cudaError_t fmt_attn(bool f16, const float *qkv, const float *bqkv, int T, int H, int nh, int window, void *out,
+                     cudaStream_t st);
+cudaError_t fmt_gate_residual(float *x, const float *o, const float *bo, const float *mod, const float *bmod,
+                              int mod_stride, int gate_off, int M, int H, cudaStream_t st);
+cudaError_t fmt_gelu(bool f16, const float *a, const float *b, int M, int N, void *y, cudaStream_t st);
+cudaError_t fmt_cfg_euler(const float *vout, const float *bv, int T, int P, int D, float a_cfg, float e_cfg,
+                          float dt, float *x, float *x60, cudaStream_t st);
+cudaError_t fmt_add_bias(const float *a, const float *b, int M, int N, float *y, cudaStream_t st);
+cudaError_t fmt_to_half(const float *a, int64_t n, __half *y, cudaStream_t st);
+}  // namespace tpmd
+
+using namespace tpmd;
+
+namespace {
+thread_local std::string g_create_err;
+
+// torch linspace(0,1,nfe) in f32, as src/pipeline.cpp:13 computes it
+float ode_t(int i, int nfe) { return (float) ((double) i / (double) (nfe - 1)); }
+}  // namespace
+
+struct tpfm_ctx {
+    int device = 0;
+    bool f16 = false;
+    tpfm_config c{};
+    int T = 0, M = 0, CD = 0, FF = 0, H = 0;
+    std::string err;
+    std::map<std::string, int64_t> spec;
+    std::map<std::string, std::vector<float>> host;
+    std::map<std::string, size_t> off32, off16;
+    float *w32 = nullptr;
+    __half *w16 = nullptr;
+    bool wready = false;
+    cudaStream_t stream = nullptr;
+    cublasHandle_t blas = nullptr;
+    void *blas_ws = nullptr;
+    void *act = nullptr;
+    float *x60 = nullptr, *cond = nullptr, *clin = nullptr, *te0 = nullptr, *te = nullptr, *x1 = nullptr,
+          *x = nullptr, *mod = nullptr, *qkv = nullptr, *o = nullptr, *m1raw = nullptr, *fm = nullptr,
+          *vout = nullptr, *v = nullptr, *xc = nullptr, *tf = nullptr;
+    void *sc = nullptr, *h = nullptr, *att = nullptr, *m1 = nullptr, *cond_in = nullptr, *x60_in = nullptr;
+    cudaGraphExec_t graph = nullptr;
+
+    bool fail(const std::string &m) {
+        err = m;
+        return false;
+    }
+    bool ck(cudaError_t e, const char *what) {
+        if (e == cudaSuccess) return true;
+        err = std::string(what) + ": " + cudaGetErrorString(e);
+        cudaGetLastError();
+        return false;
+    }
+    bool bk(cublasStatus_t s, const char *what) {
+        if (s == CUBLAS_STATUS_SUCCESS) return true;
+        err = std::string(what) + ": cuBLAS status " + std::to_string((int) s);
+        return false;
+    }
+    const float *F(const std::string &n) const { return w32 + off32.at(n); }
+    // Y[M][N] (f32) = X[M][K] (GEMM input type) W[N][K]^T
+    bool gemm(const void *X, int Mr, int K, const std::string &wname, int N, float *Y) {
+        const float one = 1.0f, zero = 0.0f;
+        const void *W = f16 ? (const void *) (w16 + off16.at(wname)) : (const void *) F(wname);
+        const cudaDataType_t t = f16 ? CUDA_R_16F : CUDA_R_32F;
+        return bk(cublasGemmEx(blas, CUBLAS_OP_T, CUBLAS_OP_N, N, Mr, K, &one, W, t, K, X, t, K, &zero, Y,
+                               CUDA_R_32F, N, f16 ? CUBLAS_COMPUTE_32F : CUBLAS_COMPUTE_32F_PEDANTIC,
+                               CUBLAS_GEMM_DEFAULT),
+                  wname.c_str());
+    }
+    ~tpfm_ctx() {
+        if (device >= 0) cudaSetDevice(device);
+        if (graph) cudaGraphExecDestroy(graph);
+        if (blas) cublasDestroy(blas);
+        if (blas_ws) cudaFree(blas_ws);
+        if (act) cudaFree(act);
+        if (w32) cudaFree(w32);
+        if (w16) cudaFree(w16);
+        if (stream) cudaStreamDestroy(stream);
+    }
+};
+
+namespace {
+
+void build_spec(tpfm_ctx *c) {
+    const int H = c->H;
+    auto lin = [&](const std::string &n, int64_t out, int64_t in) {
+        c->spec[n + ".weight"] = out * in;
+        c->spec[n + ".bias"] = out;
+    };
+    lin("t_embedder.mlp.0", H, c->c.t_freq_dim);
+    lin("t_embedder.mlp.2", H, H);
+    lin("c_embedder", H, c->CD);
+    lin("x_embedder.proj", H, c->c.dim_w);
+    c->spec["pos_embed"] = (int64_t) c->T * H;
+    for (int i = 0; i < c->c.depth; i++) {
+        const std::string b = "blocks." + std::to_string(i) + ".";
+        lin(b + "adaLN_modulation.1", 6 * H, H);
+        lin(b + "attn.qkv", 3 * H, H);
+        lin(b + "attn.proj", H, H);
+        lin(b + "mlp.fc1", c->FF, H);
+        lin(b + "mlp.fc2", H, c->FF);
+    }
+    lin("decoder.adaLN_modulation.1", 2 * H, H);
+    lin("decoder.linear", c->c.dim_w, H);
+}
+
+// the weights that go through cuBLAS (kept f16 in f16 mode)
+bool is_gemm_weight(const std::string &n) {
+    const size_t k = n.size();
+    return k > 7 && n.compare(k - 7, 7, ".weight") == 0 && n.rfind("t_embedder.", 0) != 0;
+}
+
+// one forward on the device buffers: x60 (f32) and the chunk's clin are set;
+// tf row `s`; output in vout (no bias)
+bool forward_device(tpfm_ctx *c, int s) {
+    cudaStream_t st = c->stream;
+    const int H = c->H, T = c->T, M = c->M, FF = c->FF;
+    const bool h16 = c->f16;
+    auto K = [&](cudaError_t e, const char *w) { return c->ck(e, w); };
+    const float *tf = c->tf + (size_t) s * c->c.t_freq_dim;
+    if (!K(fmt_gemv(c->F("t_embedder.mlp.0.weight"), tf, c->F("t_embedder.mlp.0.bias"), H, c->c.t_freq_dim, true,
+                    c->te0, st),
+           "t embed") ||
+        !K(fmt_gemv(c->F("t_embedder.mlp.2.weight"), c->te0, c->F("t_embedder.mlp.2.bias"), H, H, false, c->te, st),
+           "t embed") ||
+        !K(fmt_cond_silu(h16, c->clin, c->F("c_embedder.bias"), c->te, M, H, c->sc, st), "cond silu"))
+        return false;
+    const void *x60_in = c->x60;
+    if (h16) {
+        if (!K(fmt_to_half(c->x60, (int64_t) T * c->c.dim_w, (__half *) c->x60_in, st), "x60 f16")) return false;
+        x60_in = c->x60_in;
+    }
+    if (!c->gemm(x60_in, T, c->c.dim_w, "x_embedder.proj.weight", H, c->x1) ||
+        !K(fmt_embed_x(c->x1, c->F("x_embedder.proj.bias"), c->F("pos_embed"), T, H, c->x, st), "x embed"))
+        return false;
+    for (int l = 0; l < c->c.depth; l++) {
+        const std::string b = "blocks." + std::to_string(l) + ".";
+        const float *bmod = c->F(b + "adaLN_modulation.1.bias");
+        if (!c->gemm(c->sc, M, H, b + "adaLN_modulation.1.weight", 6 * H, c->mod) ||
+            !K(fmt_norm_mod(h16, c->x, M, H, c->c.ln_eps, c->mod, bmod, 6 * H, 0, H, c->h, st), "norm") ||
+            !c->gemm(c->h, M, H, b + "attn.qkv.weight", 3 * H, c->qkv) ||
+            !K(fmt_attn(h16, c->qkv, c->F(b + "attn.qkv.bias"), T, H, c->c.n_heads, c->c.attn_window, c->att, st),
+               "attention") ||
+            !c->gemm(c->att, M, H, b + "attn.proj.weight", H, c->o) ||
+            !K(fmt_gate_residual(c->x, c->o, c->F(b + "attn.proj.bias"), c->mod, bmod, 6 * H, 2 * H, M, H, st),
+               "residual") ||
+            !K(fmt_norm_mod(h16, c->x, M, H, c->c.ln_eps, c->mod, bmod, 6 * H, 3 * H, 4 * H, c->h, st), "norm") ||
+            !c->gemm(c->h, M, H, b + "mlp.fc1.weight", FF, c->m1raw) ||
+            !K(fmt_gelu(h16, c->m1raw, c->F(b + "mlp.fc1.bias"), M, FF, c->m1, st), "gelu") ||
+            !c->gemm(c->m1, M, FF, b + "mlp.fc2.weight", H, c->o) ||
+            !K(fmt_gate_residual(c->x, c->o, c->F(b + "mlp.fc2.bias"), c->mod, bmod, 6 * H, 5 * H, M, H, st),
+               "residual"))
+            return false;
+    }
+    return c->gemm(c->sc, M, H, "decoder.adaLN_modulation.1.weight", 2 * H, c->fm) &&
+           K(fmt_norm_mod(h16, c->x, M, H, c->c.ln_eps, c->fm, c->F("decoder.adaLN_modulation.1.bias"), 2 * H, 0, H,
+                          c->h, st),
+             "norm") &&
+           c->gemm(c->h, M, H, "decoder.linear.weight", c->c.dim_w, c->vout);
+}
+
+// clin = cond . c_embedder^T (the conditioning rows, fixed for a chunk)
+bool embed_cond(tpfm_ctx *c) {
+    const void *in = c->cond;
+    if (c->f16) {
+        if (!c->ck(fmt_to_half(c->cond, (int64_t) c->M * c->CD, (__half *) c->cond_in, c->stream), "cond f16"))
+            return false;
+        in = c->cond_in;
+    }
+    return c->gemm(in, c->M, c->CD, "c_embedder.weight", c->H, c->clin);
+}
+
+bool ready(tpfm_ctx *c) {
+    if (!c->wready) return c->fail("weights not prepared (tpfm_prepare)");
+    return c->ck(cudaSetDevice(c->device), "cudaSetDevice");
+}
+
+}  // namespace
+
+extern "C" {
+
+void tpfm_default_config(tpfm_config *cfg) {
+    if (!cfg) return;
+    *cfg = tpfm_config{1024, 8, 8, 512, 512, 7, 50, 10, 2, 256, 10, 4.0f, 1e-6f, 2.0f, 1.0f};
+}
+
+tpfm_ctx *tpfm_create(int device, int dtype, const tpfm_config *cfg) {
+    int n = 0;
+    if (!cfg || (dtype != TPMD_DTYPE_F32 && dtype != TPMD_DTYPE_F16)) {
+        g_create_err = "tpfm_create: bad argument";
+        return nullptr;
+    }
+    if (cfg->dim_h <= 0 || cfg->n_heads <= 0 || cfg->dim_h % cfg->n_heads || cfg->depth <= 0 || cfg->nfe < 2 ||
+        cfg->chunk_frames <= 0 || cfg->prev_frames < 0 || cfg->attn_window < 0 || 2 * cfg->attn_window + 1 > 16 ||
+        cfg->t_freq_dim < 2 || cfg->t_freq_dim % 2 || cfg->dim_w <= 0 || cfg->dim_a < 0 || cfg->dim_e < 0 ||
+        cfg->mlp_ratio <= 0.0f) {
+        g_create_err = "tpfm_create: invalid config";
+        return nullptr;
+    }
+    if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) {
+        cudaGetLastError();
+        g_create_err = "tpfm_create: no such CUDA device";
+        return nullptr;
+    }
+    cudaDeviceProp pr{};
+    if (cudaGetDeviceProperties(&pr, device) != cudaSuccess || pr.major != 10) {
+        cudaGetLastError();
+        g_create_err = "tpfm_create: needs an sm_100 (B200) GPU";
+        return nullptr;
+    }
+    tpfm_ctx *c = new tpfm_ctx();
+    c->device = device;
+    c->f16 = dtype == TPMD_DTYPE_F16;
+    c->c = *cfg;
+    c->H = cfg->dim_h;
+    c->T = cfg->chunk_frames + cfg->prev_frames;
+    c->M = 3 * c->T;
+    c->CD = cfg->dim_w + cfg->dim_a + cfg->dim_e;
+    c->FF = (int) (cfg->dim_h * cfg->mlp_ratio);
+    build_spec(c);
+    // activations
+    const size_t H = c->H, T = c->T, M = c->M, D = cfg->dim_w, FF = c->FF, CD = c->CD;
+    const size_t es = c->f16 ? 2 : 4;
+    size_t sizes[] = {T * D * 4, M * CD * 4, M * H * 4, H * 4, H * 4, T * H * 4, M * H * 4, M * 6 * H * 4,
+                      M * 3 * H * 4, M * H * 4, M * FF * 4, M * 2 * H * 4, M * D * 4, M * D * 4,
+                      (size_t) cfg->chunk_frames * D * 4, (size_t) (cfg->nfe) * cfg->t_freq_dim * 4,
+                      M * H * es, M * H * es, M * H * es, M * FF * es, M * CD * es, T * D * es};
+    const int ns = sizeof(sizes) / sizeof(sizes[0]);
+    size_t offs[32], total = 0;
+    for (int i = 0; i < ns; i++) {
+        offs[i] = total;
+        total += (sizes[i] + 255) & ~(size_t) 255;
+    }
+    bool ok = c->ck(cudaSetDevice(device), "cudaSetDevice") &&
+              c->ck(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking), "stream") &&
+              c->ck(cudaMalloc(&c->act, total), "cudaMalloc(fmt activations)") &&
+              c->ck(cudaMalloc(&c->blas_ws, (size_t) 32 << 20), "cudaMalloc(cuBLAS workspace)") &&
+              c->bk(cublasCreate(&c->blas), "cublasCreate") && c->bk(cublasSetStream(c->blas, c->stream), "stream") &&
+              c->bk(cublasSetWorkspace(c->blas, c->blas_ws, (size_t) 32 << 20), "workspace") &&
+              c->bk(cublasSetMathMode(c->blas, c->f16 ? CUBLAS_DEFAULT_MATH : CUBLAS_PEDANTIC_MATH), "math mode");
+    if (!ok) {
+        g_create_err = c->err;
+        delete c;
+        return nullptr;
+    }
+    char *b = (char *) c->act;
+    int i = 0;
+    float **fl[] = {&c->x60, &c->cond, &c->clin, &c->te0, &c->te, &c->x1, &c->x, &c->mod, &c->qkv, &c->o,
+                    &c->m1raw, &c->fm, &c->vout, &c->v, &c->xc, &c->tf};
+    for (float **p : fl) *p = (float *) (b + offs[i++]);
+    void **vp[] = {&c->sc, &c->h, &c->att, &c->m1, &c->cond_in, &c->x60_in};
+    for (void **p : vp) *p = b + offs[i++];
+    // the t-embedding frequencies of every Euler step (host, as the reference)
+    const int half = cfg->t_freq_dim / 2;
+    std::vector<float> tf((size_t) cfg->nfe * cfg->t_freq_dim);
+    for (int s = 0; s < cfg->nfe; s++) {
+        const float t = ode_t(s, cfg->nfe);
+        for (int k = 0; k < half; k++) {
+            const float fr = (float) exp(-log(10000.0) * (double) k / (double) half);
+            tf[(size_t) s * cfg->t_freq_dim + k] = cosf(t * fr);
+            tf[(size_t) s * cfg->t_freq_dim + half + k] = sinf(t * fr);
+        }
+    }
+    if (!c->ck(cudaMemcpy(c->tf, tf.data(), tf.size() * 4, cudaMemcpyHostToDevice), "t freqs")) {
+        g_create_err = c->err;
+        delete c;
+        return nullptr;
+    }
+    return c;
+}
+
+const char *tpfm_create_error(void) { return g_create_err.c_str(); }
+void tpfm_destroy(tpfm_ctx *c) { delete c; }
+const char *tpfm_last_error(const tpfm_ctx *c) { return c ? c->err.c_str() : "no context"; }
+
+int tpfm_set_tensor(tpfm_ctx *c, const char *name, const float *data, int64_t n) {
+    if (!c) return -1;
+    if (!name || !data) return c->fail("tpfm_set_tensor: null argument"), -1;
+    auto it = c->spec.find(name);
+    if (it == c->spec.end()) return c->fail(std::string("tpfm_set_tensor: unknown tensor ") + name), -1;
+    if (it->second != n)
+        return c->fail(std::string("tpfm_set_tensor: size mismatch for ") + name + " (want " +
+                       std::to_string(it->second) + ", got " + std::to_string(n) + ")"),
+               -1;
+    c->host[name].assign(data, data + n);
+    c->wready = false;
+    return 0;
+}
+
+}  // extern "C"
+
+namespace {
+struct kv_check {
+    tpfm_ctx *c;
+    std::string bad;
+};
+// float.fmt.* keys (src/fmt.cpp:10-26) against the handle's config
+int check_kv(void *user, const char *key, int, double num, const char *) {
+    kv_check *k = (kv_check *) user;
+    const tpfm_config &g = k->c->c;
+    const std::string s = key;
+    if (s.rfind("float.fmt.", 0) != 0) return 0;
+    const std::string n = s.substr(10);
+    const std::map<std::string, double> want = {
+        {"dim_h", g.dim_h}, {"depth", g.depth}, {"n_heads", g.n_heads}, {"dim_w", g.dim_w}, {"dim_a", g.dim_a},
+        {"dim_e", g.dim_e}, {"chunk_frames", g.chunk_frames}, {"prev_frames", g.prev_frames},
+        {"num_total_frames", g.chunk_frames + g.prev_frames}, {"attn_window", g.attn_window},
+        {"t_freq_dim", g.t_freq_dim}, {"nfe", g.nfe}, {"a_cfg_scale", g.a_cfg}, {"e_cfg_scale", g.e_cfg},
+        {"ln_eps", g.ln_eps}, {"mlp_ratio", g.mlp_ratio}};
+    auto it = want.find(n);
+    if (it == want.end()) return 0;
+    if (std::fabs(num - it->second) > 1e-6 * std::max(1.0, std::fabs(it->second))) {
+        k->bad = s + " = " + std::to_string(num) + " differs from the handle's " + std::to_string(it->second);
+        return 1;
+    }
+    return 0;
+}
+int take_fmt_tensor(void *user, const char *name, const int64_t *, const float *data, int64_t n) {
+    tpfm_ctx *c = (tpfm_ctx *) user;
+    if (!c->spec.count(name)) return 0;  // not part of the model
+    return tpfm_set_tensor(c, name, data, n);
+}
+}  // namespace
+
+extern "C" {
+
+int tpfm_load_gguf(tpfm_ctx *c, const char *path) {
+    if (!c) return -1;
+    char e[1024] = {0};
+    kv_check k{c, ""};
+    if (tpmd_gguf_read_kv(path, "float-fmt", check_kv, &k, e, sizeof e) != 0) {
+        c->fail(k.bad.empty() ? std::string(e) : std::string(path) + ": " + k.bad);
+        return -1;
+    }
+    if (tpmd_gguf_read(path, "float-fmt", 0, take_fmt_tensor, c, e, sizeof e) != 0) {
+        if (std::string(e).find("rejected by the consumer") == std::string::npos) c->fail(e);
+        return -1;
+    }
+    return 0;
+}
+
+int tpfm_prepare(tpfm_ctx *c) {
+    if (!c) return -1;
+    for (auto &kv : c->spec)
+        if (!c->host.count(kv.first)) return c->fail("tpfm_prepare: missing tensor " + kv.first), -1;
+    size_t n32 = 0, n16 = 0;
+    c->off32.clear();
+    c->off16.clear();
+    for (auto &kv : c->spec) {
+        c->off32[kv.first] = n32;
+        n32 += ((size_t) kv.second + 63) & ~(size_t) 63;
+        if (c->f16 && is_gemm_weight(kv.first)) {
+            c->off16[kv.first] = n16;
+            n16 += ((size_t) kv.second + 127) & ~(size_t) 127;
+        }
+    }
+    std::vector<float> img(n32, 0.0f);
+    for (auto &kv : c->spec) memcpy(img.data() + c->off32[kv.first], c->host[kv.first].data(), kv.second * 4);
+    if (!c->ck(cudaSetDevice(c->device), "cudaSetDevice")) return -1;
+    if (c->w32) cudaFree(c->w32);
+    if (c->w16) cudaFree(c->w16);
+    c->w32 = nullptr;
+    c->w16 = nullptr;
+    if (c->graph) {
+        cudaGraphExecDestroy(c->graph);
+        c->graph = nullptr;
+    }
+    if (!c->ck(cudaMalloc(&c->w32, n32 * 4), "cudaMalloc(fmt weights)") ||
+        !c->ck(cudaMemcpy(c->w32, img.data(), n32 * 4, cudaMemcpyHostToDevice), "upload fmt weights"))
+        return -1;
+    if (c->f16) {
+        if (!c->ck(cudaMalloc(&c->w16, n16 * 2), "cudaMalloc(fmt f16 weights)")) return -1;
+        for (auto &kv : c->off16)
+            if (!c->ck(fmt_to_half(c->w32 + c->off32[kv.first], c->spec[kv.first], c->w16 + kv.second, c->stream),
+                       "f16 weights"))
+                return -1;
+        if (!c->ck(cudaStreamSynchronize(c->stream), "f16 weights")) return -1;
+    }
+    c->wready = true;
+    return 0;
+}
+
+int tpfm_forward(tpfm_ctx *c, const float *x60, const float *cond, float t, float *v) {
+    if (!c) return -1;
+    if (!x60 || !cond || !v) return c->fail("tpfm_forward: null argument"), -1;
+    if (!ready(c)) return -1;
+    // the t-embedding row for this t
+    const int half = c->c.t_freq_dim / 2;
+    std::vector<float> tf((size_t) c->c.t_freq_dim);
+    for (int k = 0; k < half; k++) {
+        const float fr = (float) exp(-log(10000.0) * (double) k / (double) half);
+        tf[(size_t) k] = cosf(t * fr);
+        tf[(size_t) half + k] = sinf(t * fr);
+    }
+    // a spare row past the sampler's steps holds it
+    float *row = c->tf + (size_t) (c->c.nfe - 1) * c->c.t_freq_dim;
+    cudaStream_t st = c->stream;
+    const size_t D = c->c.dim_w;
+    if (!c->ck(cudaMemcpyAsync(row, tf.data(), tf.size() * 4, cudaMemcpyHostToDevice, st), "t freq") ||
+        !c->ck(cudaMemcpyAsync(c->x60, x60, (size_t) c->T * D * 4, cudaMemcpyHostToDevice, st), "x60") ||
+        !c->ck(cudaMemcpyAsync(c->cond, cond, (size_t) c->M * c->CD * 4, cudaMemcpyHostToDevice, st), "cond") ||
+        !embed_cond(c) || !forward_device(c, c->c.nfe - 1) ||
+        !c->ck(fmt_add_bias(c->vout, c->F("decoder.linear.bias"), c->M, (int) D, c->v, st), "bias") ||
+        !c->ck(cudaMemcpyAsync(v, c->v, (size_t) c->M * D * 4, cudaMemcpyDeviceToHost, st), "v D2H") ||
+        !c->ck(cudaStreamSynchronize(st), "forward"))
+        return -1;
+    return 0;
+}
+
+int tpfm_sample_chunk(tpfm_ctx *c, const float *wr, const float *prev_wa, const float *cond_audio,
+                      const float *prev_x, const float *x0, int emotion, float *motion) {
+    if (!c) return -1;
+    if (!wr || !cond_audio || !x0 || !motion || (c->c.prev_frames > 0 && (!prev_wa || !prev_x)))
+        return c->fail("tpfm_sample_chunk: null argument"), -1;
+    if (!ready(c)) return -1;
+    const int T = c->T, P = c->c.prev_frames, CF = c->c.chunk_frames, D = c->c.dim_w, CD = c->CD;
+    // condition rows [wr | wa | we] per branch: uncond nulls the current
+    // frames' wa and we, audio-only nulls we; prev_wa rows stay in all
+    std::vector<float> cond((size_t) 3 * T * CD, 0.0f);
+    for (int b = 0; b < 3; b++)
+        for (int f = 0; f < T; f++) {
+            float *row = cond.data() + ((size_t) b * T + f) * CD;
+            memcpy(row, wr, (size_t) D * 4);
+            const float *wa = f < P ? prev_wa + (size_t) f * D : cond_audio + (size_t) (f - P) * D;
+            if (!(b == 0 && f >= P)) memcpy(row + D, wa, (size_t) D * 4);
+            if (b == 1 && emotion >= 0 && emotion < c->c.dim_e) row[D + c->c.dim_a + emotion] = 1.0f;
+        }
+    cudaStream_t st = c->stream;
+    if ((P > 0 && !c->ck(cudaMemcpyAsync(c->x60, prev_x, (size_t) P * D * 4, cudaMemcpyHostToDevice, st), "prev_x")) ||
+        !c->ck(cudaMemcpyAsync(c->x60 + (size_t) P * D, x0, (size_t) CF * D * 4, cudaMemcpyHostToDevice, st), "x0") ||
+        !c->ck(cudaMemcpyAsync(c->xc, x0, (size_t) CF * D * 4, cudaMemcpyHostToDevice, st), "x0") ||
+        !c->ck(cudaMemcpyAsync(c->cond, cond.data(), cond.size() * 4, cudaMemcpyHostToDevice, st), "cond"))
+        return -1;
+    if (!c->graph) {
+        // capture the chunk's device work once; buffers are fixed per handle
+        cudaGraph_t g = nullptr;
+        if (!c->ck(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal), "begin capture")) return -1;
+        bool ok = embed_cond(c);
+        for (int s = 0; ok && s < c->c.nfe - 1; s++) {
+            const float dt = ode_t(s + 1, c->c.nfe) - ode_t(s, c->c.nfe);
+            ok = forward_device(c, s) &&
+                 c->ck(fmt_cfg_euler(c->vout, c->F("decoder.linear.bias"), T, P, D, c->c.a_cfg, c->c.e_cfg, dt, c->xc,
+                                     c->x60, st),
+                       "cfg euler");
+        }
+        const cudaError_t e = cudaStreamEndCapture(st, &g);
+        if (!ok) {
+            if (g) cudaGraphDestroy(g);
+            return -1;
+        }
+        if (!c->ck(e, "end capture")) return -1;
+        const cudaError_t ie = cudaGraphInstantiate(&c->graph, g, 0);
+        cudaGraphDestroy(g);
+        if (!c->ck(ie, "instantiate")) return -1;
+    }
+    if (!c->ck(cudaGraphLaunch(c->graph, st), "graph launch") ||
+        !c->ck(cudaMemcpyAsync(motion, c->xc, (size_t) CF * D * 4, cudaMemcpyDeviceToHost, st), "motion D2H") ||
+        !c->ck(cudaStreamSynchronize(st), "sample chunk"))
+        return -1;
+    return 0;
+}
+
+}  // extern "C"

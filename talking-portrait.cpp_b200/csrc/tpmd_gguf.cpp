@@ -110,8 +110,8 @@ void put_err(char *buf, size_t len, const std::string &msg) {
 }
 
 int read_gguf(const char *path, const char *expect_arch, int fold, tpmd_gguf_tensor_fn cb, void *user,
-              std::string &err) {
-    if (!path || !cb) {
+              std::string &err, tpmd_gguf_kv_fn kv_cb = nullptr) {
+    if (!path || (!cb && !kv_cb)) {
         err = "tpmd_gguf_read: null argument";
         return -1;
     }
@@ -139,15 +139,17 @@ int read_gguf(const char *path, const char *expect_arch, int fold, tpmd_gguf_ten
     for (uint64_t i = 0; i < n_kv && c.ok; i++) {
         const std::string key = c.str();
         const uint32_t vt = c.get<uint32_t>();
+        double num = 0.0;
+        std::string sv;
         switch (vt) {
-            case 4: (void) c.get<uint32_t>(); break;
-            case 5: (void) c.get<int32_t>(); break;
-            case 6: (void) c.get<float>(); break;
-            case 7: (void) c.get<uint8_t>(); break;
+            case 4: num = c.get<uint32_t>(); break;
+            case 5: num = c.get<int32_t>(); break;
+            case 6: num = c.get<float>(); break;
+            case 7: num = c.get<uint8_t>() ? 1 : 0; break;
             case 8: {
-                std::string v = c.str();
+                sv = c.str();
                 if (key == "general.architecture") {
-                    arch = v;
+                    arch = sv;
                     have_arch = true;
                 }
                 break;
@@ -155,6 +157,10 @@ int read_gguf(const char *path, const char *expect_arch, int fold, tpmd_gguf_ten
             default:
                 err = P + ": unsupported KV type " + std::to_string(vt) + " for " + key;
                 return -1;
+        }
+        if (kv_cb && c.ok && kv_cb(user, key.c_str(), vt, num, vt == 8 ? sv.c_str() : nullptr) != 0) {
+            err = P + ": key " + key + " rejected by the consumer";
+            return -1;
         }
     }
     if (!c.ok) {
@@ -166,6 +172,7 @@ int read_gguf(const char *path, const char *expect_arch, int fold, tpmd_gguf_ten
               "', want " + expect_arch;
         return -1;
     }
+    if (!cb) return 0;  // key/value pairs only
     std::vector<tensor_info> infos((size_t) n_tensors);
     for (tensor_info &t : infos) {
         t.name = c.str();
@@ -265,6 +272,18 @@ int tpmd_gguf_read(const char *path, const char *expect_arch, int fold_scales, t
                    void *user, char *err, size_t err_len) {
     std::string e;
     const int rc = read_gguf(path, expect_arch, fold_scales, cb, user, e);
+    if (rc != 0) put_err(err, err_len, e);
+    return rc;
+}
+
+int tpmd_gguf_read_kv(const char *path, const char *expect_arch, tpmd_gguf_kv_fn cb, void *user, char *err,
+                      size_t err_len) {
+    std::string e;
+    if (!cb) {
+        put_err(err, err_len, "tpmd_gguf_read_kv: null argument");
+        return -1;
+    }
+    const int rc = read_gguf(path, expect_arch, 0, nullptr, user, e, cb);
     if (rc != 0) put_err(err, err_len, e);
     return rc;
 }

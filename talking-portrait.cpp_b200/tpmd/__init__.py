@@ -37,6 +37,9 @@ EXPORTS = ("tpmd_abi_version", "tpmd_create", "tpmd_create_error", "tpmd_destroy
            "tpmd_kernel_launches", "tpmd_decode_noalloc", "tpmd_gguf_read", "tpmd_load_gguf",
            "tpmd_set_feats_device", "tpme_create", "tpme_create_error", "tpme_destroy", "tpme_last_error",
            "tpme_set_tensor", "tpme_load_gguf", "tpme_prepare", "tpme_run", "tpme_feat_device",
+           "tpmd_gguf_read_kv", "tpfm_default_config", "tpfm_create", "tpfm_create_error", "tpfm_destroy",
+           "tpfm_last_error", "tpfm_set_tensor", "tpfm_load_gguf", "tpfm_prepare", "tpfm_forward",
+           "tpfm_sample_chunk",
            "tpk_bilinear_gather", "tpk_im2col_cf", "tpk_last_error")
 
 _lib = None
@@ -93,6 +96,19 @@ def load_library(path: str = LIB_PATH):
     L.tpme_prepare.argtypes = [v]
     L.tpme_run.argtypes = [v, v, v, v, v, C.POINTER(v)]
     L.tpme_feat_device.argtypes = [v, C.c_int, C.POINTER(v), C.POINTER(i64)]
+    L.tpmd_gguf_read_kv.argtypes = [cp, cp, GGUF_KV_FN, v, C.c_char_p, C.c_size_t]
+    L.tpfm_default_config.argtypes = [C.POINTER(FmtConfig)]
+    L.tpfm_create.argtypes = [C.c_int, C.c_int, C.POINTER(FmtConfig)]
+    L.tpfm_create.restype = v
+    L.tpfm_create_error.restype = cp
+    L.tpfm_destroy.argtypes = [v]
+    L.tpfm_last_error.argtypes = [v]
+    L.tpfm_last_error.restype = cp
+    L.tpfm_set_tensor.argtypes = [v, cp, v, i64]
+    L.tpfm_load_gguf.argtypes = [v, cp]
+    L.tpfm_prepare.argtypes = [v]
+    L.tpfm_forward.argtypes = [v, v, v, C.c_float, v]
+    L.tpfm_sample_chunk.argtypes = [v, v, v, v, v, v, C.c_int, v]
     L.tpk_bilinear_gather.argtypes = [v, C.c_int, C.c_int, C.c_int, C.c_int, v, i64, C.c_int,
                                       C.c_int, v, v]
     L.tpk_im2col_cf.argtypes = [v] + [C.c_int] * 12 + [v, C.c_int, v]
@@ -103,6 +119,34 @@ def load_library(path: str = LIB_PATH):
 
 GGUF_TENSOR_FN = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_char_p, C.POINTER(C.c_int64),
                              C.POINTER(C.c_float), C.c_int64)
+
+
+GGUF_KV_FN = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_char_p, C.c_int, C.c_double, C.c_char_p)
+
+
+class FmtConfig(C.Structure):
+    """tpfm_config: the FMT's float.fmt.* hyper-parameters."""
+    _fields_ = [(n, C.c_int) for n in ("dim_h", "depth", "n_heads", "dim_w", "dim_a", "dim_e",
+                                       "chunk_frames", "prev_frames", "attn_window", "t_freq_dim", "nfe")] + \
+               [(n, C.c_float) for n in ("mlp_ratio", "ln_eps", "a_cfg", "e_cfg")]
+
+
+def gguf_kv(path: str, expect_arch: str | None = None) -> dict:
+    """The key/value section of a GGUF v3 file through tpmd_gguf_read_kv:
+    {key: number or string}."""
+    L = load_library()
+    out: dict = {}
+
+    def cb(_user, key, vt, num, sv):
+        out[key.decode()] = sv.decode() if vt == 8 else num
+        return 0
+
+    fn = GGUF_KV_FN(cb)
+    err = C.create_string_buffer(1024)
+    if L.tpmd_gguf_read_kv(path.encode(), expect_arch.encode() if expect_arch else None, fn, None, err,
+                           len(err)) != 0:
+        raise TpmdError(err.value.decode())
+    return out
 
 
 def gguf_read(path: str, expect_arch: str | None = None, fold: bool = True) -> dict:
@@ -321,4 +365,64 @@ class MotionEncoder:
             self.close()
         except Exception:
             pass
+
+
+class FmtSampler:
+    """The flow-matching sampler on one GPU (fmt_model + sample_chunk_ex,
+    src/fmt.cpp:9-211, src/pipeline.cpp:15-91)."""
+
+    def __init__(self, cfg: dict, device: int = 0, dtype: int = DTYPE_F32):
+        self._L = load_library()
+        self.cfg = dict(cfg)
+        self._c = FmtConfig(**cfg)
+        self._h = self._L.tpfm_create(device, dtype, C.byref(self._c))
+        if not self._h:
+            raise TpmdError(self._L.tpfm_create_error().decode())
+
+    def _check(self, rc: int):
+        if rc != 0:
+            raise TpmdError(self._L.tpfm_last_error(self._h).decode())
+
+    def set_tensors(self, tensors: dict):
+        for name, arr in tensors.items():
+            a = np.ascontiguousarray(arr, np.float32)
+            self._check(self._L.tpfm_set_tensor(self._h, name.encode(), _np_ptr(a), a.size))
+
+    def load_gguf(self, path: str):
+        self._check(self._L.tpfm_load_gguf(self._h, path.encode()))
+
+    def prepare(self):
+        self._check(self._L.tpfm_prepare(self._h))
+
+    def forward(self, x60, cond, t: float) -> np.ndarray:
+        c = self.cfg
+        T = c["chunk_frames"] + c["prev_frames"]
+        x60 = np.ascontiguousarray(x60, np.float32)
+        cond = np.ascontiguousarray(cond, np.float32)
+        v = np.empty((3, T, c["dim_w"]), np.float32)
+        self._check(self._L.tpfm_forward(self._h, _np_ptr(x60), _np_ptr(cond), float(t), _np_ptr(v)))
+        return v
+
+    def sample(self, wr, prev_wa, cond_audio, prev_x, x0, emotion: int) -> np.ndarray:
+        a = [np.ascontiguousarray(z, np.float32) for z in (wr, prev_wa, cond_audio, prev_x, x0)]
+        out = np.empty((self.cfg["chunk_frames"], self.cfg["dim_w"]), np.float32)
+        self._check(self._L.tpfm_sample_chunk(self._h, *[_np_ptr(z) for z in a], int(emotion), _np_ptr(out)))
+        return out
+
+    def close(self):
+        if getattr(self, "_h", None):
+            self._L.tpfm_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def default_fmt_config() -> dict:
+    c = FmtConfig()
+    load_library().tpfm_default_config(C.byref(c))
+    return {n: getattr(c, n) for n, _ in FmtConfig._fields_}
 

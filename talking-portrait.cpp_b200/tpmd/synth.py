@@ -236,3 +236,65 @@ def make_image(seed: int = 0) -> np.ndarray:
         img[c] += 0.05 * rng.standard_normal((512, 512))
     return np.clip(img, -1.0, 1.0).astype(np.float32)
 
+
+# The flow-matching transformer of config 4 (8 blocks, d = 1024, 16 heads,
+# banded attention, 9 Euler steps, 3-way CFG, 50-frame chunks with 10-frame
+# context); keys as the GGUF's float.fmt.* hyper-parameters.
+FMT_CONFIG = dict(dim_h=1024, depth=8, n_heads=16, dim_w=512, dim_a=512, dim_e=7, chunk_frames=50,
+                  prev_frames=10, attn_window=2, t_freq_dim=256, nfe=10, mlp_ratio=4.0, ln_eps=1e-6,
+                  a_cfg=2.0, e_cfg=1.0)
+# a small instance of the same architecture for fast parity tests
+FMT_SMALL = dict(FMT_CONFIG, dim_h=256, depth=2, n_heads=4)
+
+
+def fmt_shapes(cfg: dict) -> dict[str, tuple[int, ...]]:
+    """name -> torch shape of the FMT tensors (src/fmt.cpp:64-170)."""
+    H, T = cfg["dim_h"], cfg["chunk_frames"] + cfg["prev_frames"]
+    CD, FF = cfg["dim_w"] + cfg["dim_a"] + cfg["dim_e"], int(cfg["dim_h"] * cfg["mlp_ratio"])
+    s: dict[str, tuple[int, ...]] = {}
+
+    def lin(n, out, inp):
+        s[n + ".weight"] = (out, inp)
+        s[n + ".bias"] = (out,)
+    lin("t_embedder.mlp.0", H, cfg["t_freq_dim"])
+    lin("t_embedder.mlp.2", H, H)
+    lin("c_embedder", H, CD)
+    lin("x_embedder.proj", H, cfg["dim_w"])
+    s["pos_embed"] = (1, T, H)
+    for i in range(cfg["depth"]):
+        b = f"blocks.{i}."
+        lin(b + "adaLN_modulation.1", 6 * H, H)
+        lin(b + "attn.qkv", 3 * H, H)
+        lin(b + "attn.proj", H, H)
+        lin(b + "mlp.fc1", FF, H)
+        lin(b + "mlp.fc2", H, FF)
+    lin("decoder.adaLN_modulation.1", 2 * H, H)
+    lin("decoder.linear", cfg["dim_w"], H)
+    return s
+
+
+def make_fmt_weights(cfg: dict, seed: int = 0) -> dict[str, np.ndarray]:
+    """Random-init FMT weights: Linear weights N(0, 1/fan_in) (activations
+    stay O(1); the adaLN layers are not zero-initialised, so every block
+    contributes), biases N(0, 0.02), pos_embed N(0, 0.1)."""
+    rng = np.random.default_rng([seed, 11])
+    out: dict[str, np.ndarray] = {}
+    for n, sh in fmt_shapes(cfg).items():
+        if n == "pos_embed":
+            out[n] = (rng.standard_normal(sh) * 0.1).astype(np.float32)
+        elif n.endswith(".bias"):
+            out[n] = (rng.standard_normal(sh) * 0.02).astype(np.float32)
+        else:
+            out[n] = (rng.standard_normal(sh) / np.sqrt(sh[1])).astype(np.float32)
+    return out
+
+
+def make_fmt_chunk(cfg: dict, seed: int = 0) -> dict[str, np.ndarray]:
+    """Inputs of one sampler chunk (chunk_io, src/pipeline.cpp:15-33):
+    reference latent wr, previous-context audio features and motion, the
+    chunk's audio features, the initial noise x0; emotion 'happy' (index 3)."""
+    rng = np.random.default_rng([seed, 12])
+    D, P, CF = cfg["dim_w"], cfg["prev_frames"], cfg["chunk_frames"]
+    f = lambda *sh: rng.standard_normal(sh).astype(np.float32)
+    return dict(wr=f(D), prev_wa=f(P, D), cond_audio=f(CF, D), prev_x=f(P, D), x0=f(CF, D), emotion=3)
+

@@ -155,3 +155,44 @@ class TorchEncoder:
             f = pyr[6 - j][0]
             feats.append(f.reshape(f.shape[0], -1).T.numpy())
         return dict(appearance=app.numpy(), lam=h.numpy(), motion=motion.numpy(), feats=feats)
+
+
+class TorchFmt:
+    """The flow-matching DiT forward in float64 torch, written from the
+    module definitions (DiT blocks with adaLN modulation h*(1+scale)+shift,
+    LayerNorm without affine, tanh GELU, banded attention |i-j| <= window via
+    an additive -inf mask, SiLU conditioning), independent of the oracle."""
+
+    def __init__(self, cfg: dict, raw: dict):
+        self.c = cfg
+        self.w = {k: _t(v) for k, v in raw.items()}
+
+    def _lin(self, n, x):
+        return x @ self.w[n + ".weight"].T + self.w[n + ".bias"]
+
+    def forward(self, x60, cond, t: float) -> np.ndarray:
+        c = self.c
+        H, T, nh = c["dim_h"], c["chunk_frames"] + c["prev_frames"], c["n_heads"]
+        hd = H // nh
+        half = c["t_freq_dim"] // 2
+        fr = torch.exp(-math.log(10000.0) * torch.arange(half, dtype=torch.float64) / half)
+        tf = torch.cat([torch.cos(t * fr), torch.sin(t * fr)])
+        te = self._lin("t_embedder.mlp.2", F.silu(self._lin("t_embedder.mlp.0", tf)))
+        sc = F.silu(self._lin("c_embedder", _t(cond)) + te)          # [3, T, H]
+        x = (self._lin("x_embedder.proj", _t(x60)) + self.w["pos_embed"][0])[None].repeat(3, 1, 1)
+        i = torch.arange(T)
+        mask = torch.where((i[:, None] - i[None, :]).abs() <= c["attn_window"], 0.0, -math.inf)
+        ln = lambda z: F.layer_norm(z, (H,), eps=c["ln_eps"])
+        for l in range(c["depth"]):
+            b = f"blocks.{l}."
+            sh1, sc1, g1, sh2, sc2, g2 = self._lin(b + "adaLN_modulation.1", sc).chunk(6, -1)
+            h = ln(x) * (1 + sc1) + sh1
+            q, k, v = self._lin(b + "attn.qkv", h).chunk(3, -1)
+            q, k, v = [z.reshape(3, T, nh, hd).transpose(1, 2) for z in (q, k, v)]
+            a = torch.softmax(q @ k.transpose(-1, -2) / math.sqrt(hd) + mask, -1) @ v
+            a = a.transpose(1, 2).reshape(3, T, H)
+            x = x + g1 * self._lin(b + "attn.proj", a)
+            h = ln(x) * (1 + sc2) + sh2
+            x = x + g2 * self._lin(b + "mlp.fc2", F.gelu(self._lin(b + "mlp.fc1", h), approximate="tanh"))
+        shf, scf = self._lin("decoder.adaLN_modulation.1", sc).chunk(2, -1)
+        return self._lin("decoder.linear", ln(x) * (1 + scf) + shf).numpy()
