@@ -295,6 +295,58 @@ def run_encoder(args):
     print(json.dumps(line), flush=True)
 
 
+def run_fmt(args):
+    """The flow-matching sampler of config 4 (8 DiT blocks, d = 1024, 16
+    heads, 9 Euler steps with 3-way CFG) on cuda:0: one 50-frame chunk per
+    step through tpfm_sample_chunk (host inputs in, motion out), wall clock
+    around the blocking call. The CPU baseline is the oracle's restatement
+    (one chunk) on the host cores."""
+    import tpmd
+    import oracle as O
+    from tpmd import synth
+    cfg = synth.FMT_CONFIG
+    w = synth.make_fmt_weights(cfg, 0)
+    io = synth.make_fmt_chunk(cfg, 0)
+    a = (io["wr"], io["prev_wa"], io["cond_audio"], io["prev_x"], io["x0"], io["emotion"])
+    dtype = tpmd.DTYPE_F16 if args.dtype == "f16" else tpmd.DTYPE_F32
+    s = tpmd.FmtSampler(cfg, 0, dtype)
+    s.set_tensors(w)
+    s.prepare()
+    for _ in range(args.warmup):
+        s.sample(*a)
+    with ClockSampler(0) as clk:
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            s.sample(*a)
+            clk.sample()
+        ms = (time.perf_counter() - t0) / args.steps * 1e3
+    H, T, FF, D = cfg["dim_h"], 60, 4 * cfg["dim_h"], cfg["dim_w"]
+    M = 3 * T
+    per_block = 2.0 * M * H * (6 * H + 3 * H + H + 2 * FF)
+    flop = (cfg["nfe"] - 1) * (cfg["depth"] * per_block + 2.0 * M * H * (2 * H + D) + 2.0 * T * D * H) + \
+        2.0 * M * (D + cfg["dim_a"] + cfg["dim_e"]) * H
+    cpu = None
+    if not args.no_cpu_baseline:
+        O.set_threads(os.cpu_count() or 1)
+        f = O.Fmt(cfg, w)
+        t0 = time.perf_counter()
+        f.sample(*a)
+        cpu = (time.perf_counter() - t0) * 1e3
+    line = {"metric": "fmt ms/chunk (50 frames, 9 steps, 3-way CFG)", "value": ms, "unit": "ms",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": False,
+            "dtype": args.dtype, "data": "synthetic (random-init DiT, random chunk inputs)",
+            "config": {"workload": "config 4 FMT: 8 blocks, d=1024, 16 heads, 60-frame window",
+                       "global_batch": 1},
+            "achieved_tflops": flop / (ms * 1e-3) / 1e12,
+            "e2e": {"value": ms, "unit": "ms", "h2d_bytes_per_step": 4 * D * (1 + 10 + 50 + 10 + 50),
+                    "d2h_bytes_per_step": 4 * 50 * D},
+            "reference_published_ms": 23.7,
+            "clocks": clk.summary(),
+            "cpu_baseline": None if cpu is None else {"value": cpu, "unit": "ms", "cores": O.threads(),
+                                                      "kind": "port", "sample": "1 chunk"}}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -306,12 +358,15 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--clip", type=int, default=0,
                     help="config 3: decode a clip of this many frames sharded across ranks per step")
-    ap.add_argument("--path", default="decoder", choices=["decoder", "encoder"],
-                    help="encoder: time the motion encoder (once-per-portrait step before the "
-                         "decoder) instead of the decoder; one GPU")
+    ap.add_argument("--path", default="decoder", choices=["decoder", "encoder", "fmt"],
+                    help="encoder: time the motion encoder (once per portrait); fmt: time the "
+                         "flow-matching sampler (one 50-frame chunk per step); one GPU")
     args = ap.parse_args()
     if args.path == "encoder":
         run_encoder(args)
+        return
+    if args.path == "fmt":
+        run_fmt(args)
         return
 
     rank = int(os.environ.get("RANK", "0"))
