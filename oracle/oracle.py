@@ -90,6 +90,13 @@ def lib():
         L.orc_fmt_sample.argtypes = [v, v, v, v, v, v, C.c_int, v]
         L.orc_fmt_error.argtypes = [v]
         L.orc_fmt_error.restype = C.c_char_p
+        L.orc_aud_create.argtypes = [v]
+        L.orc_aud_create.restype = v
+        L.orc_aud_destroy.argtypes = [v]
+        L.orc_aud_set.argtypes = [v, C.c_char_p, v, C.c_int64]
+        L.orc_aud_encode.argtypes = [v, v, C.c_int64, C.c_int64, v]
+        L.orc_aud_error.argtypes = [v]
+        L.orc_aud_error.restype = C.c_char_p
         L.orc_set_threads.argtypes = [C.c_int]
         L.orc_get_threads.restype = C.c_int
         _lib = L
@@ -351,6 +358,50 @@ class Fmt:
     def __del__(self):
         if getattr(self, "_h", None):
             self._L.orc_fmt_destroy(self._h)
+            self._h = None
+
+
+class AudConfig(C.Structure):
+    """orc_aud_config: the audio encoder's float.audio.* hyper-parameters."""
+    _fields_ = [("n_layers", C.c_int), ("n_heads", C.c_int), ("hidden", C.c_int), ("ffn", C.c_int),
+                ("dim_w", C.c_int), ("ln_eps", C.c_float), ("conv_dim", C.c_int * 7),
+                ("conv_kernel", C.c_int * 7), ("conv_stride", C.c_int * 7), ("pos_kernel", C.c_int),
+                ("pos_groups", C.c_int), ("sample_rate", C.c_int), ("fps", C.c_int)]
+
+
+def aud_config(cfg: dict) -> AudConfig:
+    c = AudConfig()
+    for k, val in cfg.items():
+        if k.startswith("conv_"):
+            getattr(c, k)[:] = list(val)
+        else:
+            setattr(c, k, val)
+    return c
+
+
+class Aud:
+    """The audio encoder restatement (audio_model::encode, src/audio_enc.cpp:55-236), f32."""
+
+    def __init__(self, cfg: dict, tensors: dict):
+        self._L = lib()
+        self.cfg = dict(cfg)
+        self._c = aud_config(cfg)
+        self._h = self._L.orc_aud_create(C.byref(self._c))
+        for n, a in tensors.items():
+            a = np.ascontiguousarray(a, np.float32)
+            if self._L.orc_aud_set(self._h, n.encode(), _p(a), a.size) != 0:
+                raise RuntimeError(self._L.orc_aud_error(self._h).decode())
+
+    def encode(self, audio, seq_len: int) -> np.ndarray:
+        a = np.ascontiguousarray(audio, np.float32)
+        out = np.empty((seq_len, self.cfg["dim_w"]), np.float32)
+        if self._L.orc_aud_encode(self._h, _p(a), a.size, seq_len, _p(out)) != 0:
+            raise RuntimeError(self._L.orc_aud_error(self._h).decode())
+        return out
+
+    def __del__(self):
+        if getattr(self, "_h", None):
+            self._L.orc_aud_destroy(self._h)
             self._h = None
 
 

@@ -1207,3 +1207,282 @@ int orc_fmt_sample(orc_fmt *f, const float *wr, const float *prev_wa, const floa
 
 }  // extern "C"
 
+// ---------------------------------------------------------------------------
+// audio encoder (src/audio_enc.cpp:55-236)
+// ---------------------------------------------------------------------------
+namespace {
+
+inline float gelu_erf(float v) { return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f)); }
+
+// per row of [M][N]: (x - mean)/sqrt(var + eps) * w + b (ggml_norm then affine)
+void layer_norm_rows(float *x, int64_t M, int N, const float *w, const float *b, float eps) {
+#pragma omp parallel for schedule(static)
+    for (int64_t m = 0; m < M; m++) {
+        float *r = x + m * N;
+        double mean = 0;
+        for (int i = 0; i < N; i++) mean += r[i];
+        mean /= N;
+        double var = 0;
+        for (int i = 0; i < N; i++) var += (r[i] - mean) * (r[i] - mean);
+        var /= N;
+        const float inv = (float) (1.0 / sqrt(var + eps));
+        for (int i = 0; i < N; i++) r[i] = (float) (r[i] - mean) * inv * (w ? w[i] : 1.0f) + (b ? b[i] : 0.0f);
+    }
+}
+
+// y[t][o] = sum_{k,c} W[o][c][k] x[t*s + k - p][c] (zero outside), x [T][C]
+// time-major channel-last, W torch [O][C][K]
+void conv1d_tc(const float *x, int64_t T, int C, const float *W, int O, int K, int s, int p, int64_t OT,
+               float *y) {
+#pragma omp parallel for schedule(static)
+    for (int64_t t = 0; t < OT; t++)
+        for (int o = 0; o < O; o++) {
+            float a = 0.0f;
+            for (int k = 0; k < K; k++) {
+                const int64_t ti = t * s + k - p;
+                if (ti < 0 || ti >= T) continue;
+                const float *xr = x + ti * C;
+                const float *wr = W + (size_t) o * C * K + k;
+                for (int c = 0; c < C; c++) a += wr[(size_t) c * K] * xr[c];
+            }
+            y[t * O + o] = a;
+        }
+}
+
+}  // namespace
+
+struct orc_aud {
+    orc_aud_config c{};
+    std::map<std::string, int64_t> spec;
+    std::map<std::string, std::vector<float>> t;
+    std::string err;
+    const std::vector<float> &get(const std::string &n) const { return t.at(n); }
+};
+
+extern "C" {
+
+orc_aud *orc_aud_create(const orc_aud_config *cfg) {
+    orc_aud *a = new orc_aud();
+    a->c = *cfg;
+    const int Hd = cfg->hidden, F = cfg->ffn;
+    int ic = 1;
+    for (int i = 0; i < 7; i++) {
+        a->spec["feature_extractor.conv_layers." + std::to_string(i) + ".conv.weight"] =
+            (int64_t) cfg->conv_dim[i] * ic * cfg->conv_kernel[i];
+        ic = cfg->conv_dim[i];
+    }
+    a->spec["feature_extractor.conv_layers.0.layer_norm.weight"] = cfg->conv_dim[0];
+    a->spec["feature_extractor.conv_layers.0.layer_norm.bias"] = cfg->conv_dim[0];
+    const int C = cfg->conv_dim[6];
+    a->spec["feature_projection.layer_norm.weight"] = C;
+    a->spec["feature_projection.layer_norm.bias"] = C;
+    a->spec["feature_projection.projection.weight"] = (int64_t) Hd * C;
+    a->spec["feature_projection.projection.bias"] = Hd;
+    a->spec["encoder.pos_conv_embed.conv.weight"] = (int64_t) Hd * (Hd / cfg->pos_groups) * cfg->pos_kernel;
+    a->spec["encoder.pos_conv_embed.conv.bias"] = Hd;
+    a->spec["encoder.layer_norm.weight"] = Hd;
+    a->spec["encoder.layer_norm.bias"] = Hd;
+    for (int i = 0; i < cfg->n_layers; i++) {
+        const std::string b = "encoder.layers." + std::to_string(i) + ".";
+        for (const char *pj : {"q_proj", "k_proj", "v_proj", "out_proj"}) {
+            a->spec[b + "attention." + pj + ".weight"] = (int64_t) Hd * Hd;
+            a->spec[b + "attention." + pj + ".bias"] = Hd;
+        }
+        a->spec[b + "layer_norm.weight"] = Hd;
+        a->spec[b + "layer_norm.bias"] = Hd;
+        a->spec[b + "feed_forward.intermediate_dense.weight"] = (int64_t) F * Hd;
+        a->spec[b + "feed_forward.intermediate_dense.bias"] = F;
+        a->spec[b + "feed_forward.output_dense.weight"] = (int64_t) Hd * F;
+        a->spec[b + "feed_forward.output_dense.bias"] = Hd;
+        a->spec[b + "final_layer_norm.weight"] = Hd;
+        a->spec[b + "final_layer_norm.bias"] = Hd;
+    }
+    a->spec["audio_projection.0.weight"] = (int64_t) cfg->dim_w * Hd * cfg->n_layers;
+    a->spec["audio_projection.0.bias"] = cfg->dim_w;
+    a->spec["audio_projection.1.weight"] = cfg->dim_w;
+    a->spec["audio_projection.1.bias"] = cfg->dim_w;
+    return a;
+}
+void orc_aud_destroy(orc_aud *a) { delete a; }
+const char *orc_aud_error(const orc_aud *a) { return a ? a->err.c_str() : "null audio encoder"; }
+
+int orc_aud_set(orc_aud *a, const char *name, const float *data, int64_t n) {
+    auto it = a->spec.find(name);
+    if (it == a->spec.end() || it->second != n) {
+        a->err = std::string("orc_aud_set: unknown tensor or size mismatch: ") + name;
+        return -1;
+    }
+    a->t[name].assign(data, data + n);
+    return 0;
+}
+
+int orc_aud_encode(orc_aud *a, const float *audio, int64_t n_in, int64_t seq_len, float *wa) {
+    for (auto &kv : a->spec)
+        if (!a->t.count(kv.first)) {
+            a->err = "orc_aud_encode: missing tensor " + kv.first;
+            return -1;
+        }
+    const orc_aud_config &c = a->c;
+    // replicate-pad (or crop) to exactly seq_len * sample_rate / fps samples
+    // unless already a multiple of it (src/audio_enc.cpp:60-70)
+    const int64_t unit = (int64_t) (seq_len * c.sample_rate / c.fps);
+    int64_t n = n_in;
+    std::vector<float> x;
+    if (unit > 0 && n % unit != 0) {
+        n = unit;
+        x.assign((size_t) n, n_in > 0 ? audio[n_in - 1] : 0.0f);
+        memcpy(x.data(), audio, (size_t) std::min(n, n_in) * 4);
+    } else {
+        x.assign(audio, audio + n);
+    }
+    // conv stack, time-major [T][C]
+    int64_t T = n;
+    int C = 1;
+    for (int i = 0; i < 7; i++) {
+        const int K = c.conv_kernel[i], s = c.conv_stride[i], O = c.conv_dim[i];
+        const int64_t OT = (T - K) / s + 1;
+        if (OT < 1) {
+            a->err = "audio too short";
+            return -1;
+        }
+        std::vector<float> y((size_t) OT * O);
+        conv1d_tc(x.data(), T, C, a->get("feature_extractor.conv_layers." + std::to_string(i) + ".conv.weight").data(),
+                  O, K, s, 0, OT, y.data());
+        if (i == 0) {
+            // GroupNorm with one group per channel: norm over time + affine
+            const std::vector<float> &gw = a->get("feature_extractor.conv_layers.0.layer_norm.weight");
+            const std::vector<float> &gb = a->get("feature_extractor.conv_layers.0.layer_norm.bias");
+#pragma omp parallel for schedule(static)
+            for (int o = 0; o < O; o++) {
+                double mean = 0;
+                for (int64_t t = 0; t < OT; t++) mean += y[(size_t) t * O + o];
+                mean /= (double) OT;
+                double var = 0;
+                for (int64_t t = 0; t < OT; t++) {
+                    const double d = y[(size_t) t * O + o] - mean;
+                    var += d * d;
+                }
+                var /= (double) OT;
+                const float inv = (float) (1.0 / sqrt(var + c.ln_eps));
+                for (int64_t t = 0; t < OT; t++)
+                    y[(size_t) t * O + o] = (float) (y[(size_t) t * O + o] - mean) * inv * gw[(size_t) o] + gb[(size_t) o];
+            }
+        }
+        for (float &v : y) v = gelu_erf(v);
+        x.swap(y);
+        T = OT;
+        C = O;
+    }
+    if (T < 2 || seq_len < 1) {
+        a->err = "audio too short";
+        return -1;
+    }
+    // linear interpolation, align_corners=True, to seq_len frames
+    const int64_t S = seq_len;
+    std::vector<float> h((size_t) S * C, 0.0f);
+    for (int64_t s = 0; s < S; s++) {
+        const double pos = S == 1 ? 0.0 : (double) s * (double) (T - 1) / (double) (S - 1);
+        int64_t i0 = (int64_t) pos;
+        if (i0 > T - 1) i0 = T - 1;
+        const double frac = pos - (double) i0;
+        const float w0 = (float) (1.0 - frac), w1 = (float) frac;
+        for (int ch = 0; ch < C; ch++) {
+            float v = w0 * x[(size_t) i0 * C + ch];
+            if (i0 + 1 < T && frac > 0) v += w1 * x[(size_t) (i0 + 1) * C + ch];
+            h[(size_t) s * C + ch] = v;
+        }
+    }
+    // feature projection: LayerNorm + Linear(C -> hidden)
+    const int Hd = c.hidden;
+    layer_norm_rows(h.data(), S, C, a->get("feature_projection.layer_norm.weight").data(),
+                    a->get("feature_projection.layer_norm.bias").data(), c.ln_eps);
+    std::vector<float> e((size_t) S * Hd);
+    linear_rows(h.data(), (int) S, C, a->get("feature_projection.projection.weight").data(),
+                a->get("feature_projection.projection.bias").data(), Hd, e.data());
+    // positional conv: grouped conv1d (K taps, pad K/2), drop the last step, GELU, add
+    {
+        const int G = c.pos_groups, cg = Hd / G, K = c.pos_kernel, pad = K / 2;
+        const std::vector<float> &pw = a->get("encoder.pos_conv_embed.conv.weight");
+        const std::vector<float> &pb = a->get("encoder.pos_conv_embed.conv.bias");
+        std::vector<float> pos((size_t) S * Hd);
+#pragma omp parallel for collapse(2) schedule(static)
+        for (int64_t t = 0; t < S; t++)
+            for (int o = 0; o < Hd; o++) {
+                const int g = o / cg;
+                float acc = 0.0f;
+                for (int k = 0; k < K; k++) {
+                    const int64_t ti = t + k - pad;
+                    if (ti < 0 || ti >= S) continue;
+                    const float *xr = e.data() + (size_t) ti * Hd + (size_t) g * cg;
+                    const float *wr = pw.data() + ((size_t) o * cg) * K + k;
+                    for (int ci = 0; ci < cg; ci++) acc += wr[(size_t) ci * K] * xr[ci];
+                }
+                pos[(size_t) t * Hd + o] = gelu_erf(acc + pb[(size_t) o]);
+            }
+        for (size_t q = 0; q < e.size(); q++) e[q] += pos[q];
+    }
+    layer_norm_rows(e.data(), S, Hd, a->get("encoder.layer_norm.weight").data(),
+                    a->get("encoder.layer_norm.bias").data(), c.ln_eps);
+    // post-norm transformer; all layer outputs stacked per frame
+    const int nh = c.n_heads, hd = Hd / nh, F = c.ffn, L = c.n_layers;
+    const float scaling = 1.0f / sqrtf((float) hd);
+    std::vector<float> stacked((size_t) S * Hd * L), q((size_t) S * Hd), k((size_t) S * Hd),
+        v((size_t) S * Hd), att((size_t) S * Hd), o((size_t) S * Hd), f1((size_t) S * F);
+    for (int l = 0; l < L; l++) {
+        const std::string b = "encoder.layers." + std::to_string(l) + ".";
+        auto W = [&](const std::string &n) { return a->get(b + n + ".weight").data(); };
+        auto B = [&](const std::string &n) { return a->get(b + n + ".bias").data(); };
+        linear_rows(e.data(), (int) S, Hd, W("attention.q_proj"), B("attention.q_proj"), Hd, q.data());
+        for (float &z : q) z *= scaling;
+        linear_rows(e.data(), (int) S, Hd, W("attention.k_proj"), B("attention.k_proj"), Hd, k.data());
+        linear_rows(e.data(), (int) S, Hd, W("attention.v_proj"), B("attention.v_proj"), Hd, v.data());
+#pragma omp parallel
+        {
+            std::vector<float> sc((size_t) S);
+#pragma omp for collapse(2) schedule(static)
+            for (int hh = 0; hh < nh; hh++)
+                for (int64_t i = 0; i < S; i++) {
+                    const float *qi = q.data() + (size_t) i * Hd + hh * hd;
+                    float mx = -INFINITY;
+                    for (int64_t j = 0; j < S; j++) {
+                        const float *kj = k.data() + (size_t) j * Hd + hh * hd;
+                        float d = 0.0f;
+                        for (int z = 0; z < hd; z++) d += qi[z] * kj[z];
+                        sc[(size_t) j] = d;
+                        mx = std::max(mx, d);
+                    }
+                    float sum = 0.0f;
+                    for (int64_t j = 0; j < S; j++) sum += (sc[(size_t) j] = expf(sc[(size_t) j] - mx));
+                    float *out = att.data() + (size_t) i * Hd + hh * hd;
+                    for (int z = 0; z < hd; z++) out[z] = 0.0f;
+                    for (int64_t j = 0; j < S; j++) {
+                        const float pj = sc[(size_t) j] / sum;
+                        const float *vj = v.data() + (size_t) j * Hd + hh * hd;
+                        for (int z = 0; z < hd; z++) out[z] += pj * vj[z];
+                    }
+                }
+        }
+        linear_rows(att.data(), (int) S, Hd, W("attention.out_proj"), B("attention.out_proj"), Hd, o.data());
+        for (size_t z = 0; z < e.size(); z++) e[z] += o[z];
+        layer_norm_rows(e.data(), S, Hd, W("layer_norm"), B("layer_norm"), c.ln_eps);
+        linear_rows(e.data(), (int) S, Hd, W("feed_forward.intermediate_dense"), B("feed_forward.intermediate_dense"),
+                    F, f1.data());
+        for (float &z : f1) z = gelu_erf(z);
+        linear_rows(f1.data(), (int) S, F, W("feed_forward.output_dense"), B("feed_forward.output_dense"), Hd,
+                    o.data());
+        for (size_t z = 0; z < e.size(); z++) e[z] += o[z];
+        layer_norm_rows(e.data(), S, Hd, W("final_layer_norm"), B("final_layer_norm"), c.ln_eps);
+        for (int64_t s = 0; s < S; s++)
+            memcpy(stacked.data() + ((size_t) s * L + l) * Hd, e.data() + (size_t) s * Hd, (size_t) Hd * 4);
+    }
+    // audio projection: Linear(L*hidden -> dim_w) + LayerNorm(eps 1e-5) + SiLU
+    linear_rows(stacked.data(), (int) S, Hd * L, a->get("audio_projection.0.weight").data(),
+                a->get("audio_projection.0.bias").data(), c.dim_w, wa);
+    layer_norm_rows(wa, S, c.dim_w, a->get("audio_projection.1.weight").data(),
+                    a->get("audio_projection.1.bias").data(), 1e-5f);
+    for (int64_t z = 0; z < S * c.dim_w; z++) wa[z] = silu(wa[z]);
+    return 0;
+}
+
+}  // extern "C"
+

@@ -141,6 +141,25 @@ int orc_fmt_sample(orc_fmt *f, const float *wr, const float *prev_wa, const floa
                    const float *prev_x, const float *x0, int emotion, float *motion);
 const char *orc_fmt_error(const orc_fmt *f);
 
+/* ---- audio encoder (audio_model::encode, src/audio_enc.cpp:55-236) -----
+ * Modified wav2vec2-base: 7 conv1d layers (+ GroupNorm on the first, GELU),
+ * linear interpolation (align_corners) to seq_len frames, feature
+ * projection, grouped positional conv, 12 post-norm transformer layers,
+ * Linear(12*hidden -> dim_w) + LayerNorm + SiLU over all layer outputs. */
+typedef struct {
+    int n_layers, n_heads, hidden, ffn, dim_w;
+    float ln_eps;
+    int conv_dim[7], conv_kernel[7], conv_stride[7];
+    int pos_kernel, pos_groups, sample_rate, fps;
+} orc_aud_config;
+typedef struct orc_aud orc_aud;
+orc_aud *orc_aud_create(const orc_aud_config *cfg);
+void orc_aud_destroy(orc_aud *a);
+int orc_aud_set(orc_aud *a, const char *name, const float *data, int64_t n);
+/* audio [n_in] -> wa [seq_len][dim_w] */
+int orc_aud_encode(orc_aud *a, const float *audio, int64_t n_in, int64_t seq_len, float *wa);
+const char *orc_aud_error(const orc_aud *a);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,241 @@
+// Kernels of the audio encoder (audio_model::encode, src/audio_enc.cpp:55-236),
+// float32, around cuBLAS GEMMs (tpae_api.cu). Activations are time-major
+// [T][C] (the conv stack) and token-major [S][H] (the transformer).
+#include "tpmd_internal.h"
+
+#include <algorithm>
+
+namespace tpmd {
+namespace {
+
+__device__ __forceinline__ float gelu_erf(float v) { return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f)); }
+__device__ __forceinline__ float silu(float v) { return v / (1.0f + expf(-v)); }
+inline int grid_for(int64_t n) { return (int) std::min<int64_t>((n + 255) / 256, 148 * 16); }
+
+// out[g][t][c*K + k] = x[t*s + k - p][c_off + g*C + c] (zero outside), the
+// column order of a torch conv1d weight row [C][K]
+__global__ void im2col1d_kernel(const float *__restrict__ x, int64_t T, int ld, int C, int K, int s, int p,
+                                int64_t OT, float *__restrict__ out) {
+    const int g = blockIdx.y;
+    const int64_t n = OT * C * K;
+    float *o = out + (int64_t) g * n;
+    for (int64_t e = (int64_t) blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t) gridDim.x * blockDim.x) {
+        const int k = (int) (e % K);
+        const int c = (int) ((e / K) % C);
+        const int64_t t = e / ((int64_t) K * C);
+        const int64_t ti = t * s + k - p;
+        o[e] = (ti >= 0 && ti < T) ? x[ti * ld + (int64_t) g * C + c] : 0.0f;
+    }
+}
+
+// per channel of x [T][C]: mean and 1/sqrt(var + eps) over time (double
+// accumulation); one block per channel
+__global__ void __launch_bounds__(256) chan_stats_kernel(const float *__restrict__ x, int64_t T, int C, float eps,
+                                                         float *__restrict__ mean, float *__restrict__ inv) {
+    __shared__ double red[8];
+    const int c = blockIdx.x;
+    double s = 0.0;
+    for (int64_t t = threadIdx.x; t < T; t += blockDim.x) s += x[t * C + c];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+    __syncthreads();
+    double m = 0.0;
+    for (int i = 0; i < 8; i++) m += red[i];
+    m /= (double) T;
+    __syncthreads();
+    double q = 0.0;
+    for (int64_t t = threadIdx.x; t < T; t += blockDim.x) {
+        const double d = x[t * C + c] - m;
+        q += d * d;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = q;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double v = 0.0;
+        for (int i = 0; i < 8; i++) v += red[i];
+        v /= (double) T;
+        mean[c] = (float) m;
+        inv[c] = (float) (1.0 / sqrt(v + (double) eps));
+    }
+}
+
+// x = gelu((x - mean[c]) * inv[c] * w[c] + b[c])  (GroupNorm, one group per channel)
+__global__ void chan_norm_gelu_kernel(float *__restrict__ x, int64_t T, int C, const float *__restrict__ mean,
+                                      const float *__restrict__ inv, const float *__restrict__ w,
+                                      const float *__restrict__ b) {
+    const int64_t n = T * C;
+    for (int64_t e = (int64_t) blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t) gridDim.x * blockDim.x) {
+        const int c = (int) (e % C);
+        x[e] = gelu_erf((x[e] - mean[c]) * inv[c] * __ldg(w + c) + __ldg(b + c));
+    }
+}
+
+__global__ void gelu_kernel(float *__restrict__ x, int64_t n) {
+    for (int64_t e = (int64_t) blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t) gridDim.x * blockDim.x)
+        x[e] = gelu_erf(x[e]);
+}
+
+// linear interpolation with align_corners=True from T to S rows of C
+__global__ void interp_kernel(const float *__restrict__ x, int64_t T, int C, int64_t S, float *__restrict__ y) {
+    const int64_t n = S * C;
+    for (int64_t e = (int64_t) blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t) gridDim.x * blockDim.x) {
+        const int c = (int) (e % C);
+        const int64_t s = e / C;
+        const double pos = S == 1 ? 0.0 : (double) s * (double) (T - 1) / (double) (S - 1);
+        int64_t i0 = (int64_t) pos;
+        if (i0 > T - 1) i0 = T - 1;
+        const double frac = pos - (double) i0;
+        float v = (float) (1.0 - frac) * x[i0 * C + c];
+        if (i0 + 1 < T && frac > 0) v += (float) frac * x[(i0 + 1) * C + c];
+        y[e] = v;
+    }
+}
+
+// row-wise layer norm with affine over N, optionally of (x + r + rb):
+//   y = LN(x + r + rb) * w + b, act: 0 none, 1 SiLU; y may alias x
+__global__ void __launch_bounds__(256) layer_norm_kernel(const float *x, const float *__restrict__ r,
+                                                         const float *__restrict__ rb, int N, float eps,
+                                                         const float *__restrict__ w, const float *__restrict__ b,
+                                                         int act, float *y) {
+    __shared__ float red[8];
+    extern __shared__ float row[];
+    const int64_t m = blockIdx.x;
+    float s = 0.0f;
+    for (int i = threadIdx.x; i < N; i += blockDim.x) {
+        float v = x[m * N + i];
+        if (r) v += r[m * N + i] + (rb ? __ldg(rb + i) : 0.0f);
+        row[i] = v;
+        s += v;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+    __syncthreads();
+    float mean = 0.0f;
+    for (int i = 0; i < 8; i++) mean += red[i];
+    mean /= (float) N;
+    __syncthreads();
+    float q = 0.0f;
+    for (int i = threadIdx.x; i < N; i += blockDim.x) {
+        const float d = row[i] - mean;
+        q = fmaf(d, d, q);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = q;
+    __syncthreads();
+    float var = 0.0f;
+    for (int i = 0; i < 8; i++) var += red[i];
+    var /= (float) N;
+    const float inv = 1.0f / sqrtf(var + eps);
+    for (int i = threadIdx.x; i < N; i += blockDim.x) {
+        float v = (row[i] - mean) * inv * __ldg(w + i) + __ldg(b + i);
+        if (act == 1) v = silu(v);
+        y[m * N + i] = v;
+    }
+}
+
+// y[m][n] = (y[m][n] + b[n]) * scale, act: 0 none, 1 GELU
+__global__ void bias_act_kernel(float *__restrict__ y, const float *__restrict__ b, int64_t M, int N, float scale,
+                                int act) {
+    const int64_t n = M * N;
+    for (int64_t e = (int64_t) blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t) gridDim.x * blockDim.x) {
+        float v = (y[e] + __ldg(b + e % N)) * scale;
+        if (act == 1) v = gelu_erf(v);
+        y[e] = v;
+    }
+}
+
+// e[s][i] += gelu(pos[s][i] + b[i])
+__global__ void pos_add_kernel(float *__restrict__ e, const float *__restrict__ pos, const float *__restrict__ b,
+                               int64_t S, int H) {
+    const int64_t n = S * H;
+    for (int64_t q = (int64_t) blockIdx.x * blockDim.x + threadIdx.x; q < n; q += (int64_t) gridDim.x * blockDim.x)
+        e[q] += gelu_erf(pos[q] + __ldg(b + q % H));
+}
+
+// softmax over the last dim of [rows][N] in place; one block per row
+__global__ void __launch_bounds__(256) softmax_kernel(float *__restrict__ x, int N) {
+    __shared__ float red[8];
+    float *r = x + (int64_t) blockIdx.x * N;
+    float mx = -INFINITY;
+    for (int i = threadIdx.x; i < N; i += blockDim.x) mx = fmaxf(mx, r[i]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    mx = red[0];
+    for (int i = 1; i < 8; i++) mx = fmaxf(mx, red[i]);
+    __syncthreads();
+    float s = 0.0f;
+    for (int i = threadIdx.x; i < N; i += blockDim.x) {
+        const float v = expf(r[i] - mx);
+        r[i] = v;
+        s += v;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+    __syncthreads();
+    float sum = 0.0f;
+    for (int i = 0; i < 8; i++) sum += red[i];
+    const float inv = 1.0f / sum;
+    for (int i = threadIdx.x; i < N; i += blockDim.x) r[i] *= inv;
+}
+
+// dst[s][off + i] = src[s][i] (stacking layer outputs per frame)
+__global__ void copy_cols_kernel(const float *__restrict__ src, int64_t S, int H, float *__restrict__ dst, int ld,
+                                 int off) {
+    const int64_t n = S * H;
+    for (int64_t e = (int64_t) blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t) gridDim.x * blockDim.x)
+        dst[(e / H) * ld + off + e % H] = src[e];
+}
+
+}  // namespace
+
+cudaError_t aud_im2col(const float *x, int64_t T, int ld, int C, int K, int s, int p, int64_t OT, int groups,
+                       float *out, cudaStream_t st) {
+    const dim3 grid(grid_for(OT * C * K), groups);
+    im2col1d_kernel<<<grid, 256, 0, st>>>(x, T, ld, C, K, s, p, OT, out);
+    return cudaGetLastError();
+}
+cudaError_t aud_group_norm_gelu(float *x, int64_t T, int C, float eps, const float *w, const float *b, float *stats,
+                                cudaStream_t st) {
+    chan_stats_kernel<<<C, 256, 0, st>>>(x, T, C, eps, stats, stats + C);
+    chan_norm_gelu_kernel<<<grid_for(T * C), 256, 0, st>>>(x, T, C, stats, stats + C, w, b);
+    return cudaGetLastError();
+}
+cudaError_t aud_gelu(float *x, int64_t n, cudaStream_t st) {
+    gelu_kernel<<<grid_for(n), 256, 0, st>>>(x, n);
+    return cudaGetLastError();
+}
+cudaError_t aud_interp(const float *x, int64_t T, int C, int64_t S, float *y, cudaStream_t st) {
+    interp_kernel<<<grid_for(S * C), 256, 0, st>>>(x, T, C, S, y);
+    return cudaGetLastError();
+}
+cudaError_t aud_layer_norm(const float *x, const float *r, const float *rb, int64_t M, int N, float eps,
+                           const float *w, const float *b, bool silu_act, float *y, cudaStream_t st) {
+    layer_norm_kernel<<<(unsigned) M, 256, N * sizeof(float), st>>>(x, r, rb, N, eps, w, b, silu_act ? 1 : 0, y);
+    return cudaGetLastError();
+}
+cudaError_t aud_bias_act(float *y, const float *b, int64_t M, int N, float scale, bool gelu, cudaStream_t st) {
+    bias_act_kernel<<<grid_for(M * N), 256, 0, st>>>(y, b, M, N, scale, gelu ? 1 : 0);
+    return cudaGetLastError();
+}
+cudaError_t aud_pos_add(float *e, const float *pos, const float *b, int64_t S, int H, cudaStream_t st) {
+    pos_add_kernel<<<grid_for(S * H), 256, 0, st>>>(e, pos, b, S, H);
+    return cudaGetLastError();
+}
+cudaError_t aud_softmax(float *x, int64_t rows, int N, cudaStream_t st) {
+    softmax_kernel<<<(unsigned) rows, 256, 0, st>>>(x, N);
+    return cudaGetLastError();
+}
+cudaError_t aud_copy_cols(const float *src, int64_t S, int H, float *dst, int ld, int off, cudaStream_t st) {
+    copy_cols_kernel<<<grid_for(S * H), 256, 0, st>>>(src, S, H, dst, ld, off);
+    return cudaGetLastError();
+}
+
+}  // namespace tpmd

@@ -39,7 +39,8 @@ EXPORTS = ("tpmd_abi_version", "tpmd_create", "tpmd_create_error", "tpmd_destroy
            "tpme_set_tensor", "tpme_load_gguf", "tpme_prepare", "tpme_run", "tpme_feat_device",
            "tpmd_gguf_read_kv", "tpfm_default_config", "tpfm_create", "tpfm_create_error", "tpfm_destroy",
            "tpfm_last_error", "tpfm_set_tensor", "tpfm_load_gguf", "tpfm_prepare", "tpfm_forward",
-           "tpfm_sample_chunk",
+           "tpfm_sample_chunk", "tpae_default_config", "tpae_create", "tpae_create_error", "tpae_destroy",
+           "tpae_last_error", "tpae_set_tensor", "tpae_load_gguf", "tpae_prepare", "tpae_encode",
            "tpk_bilinear_gather", "tpk_im2col_cf", "tpk_last_error")
 
 _lib = None
@@ -109,6 +110,17 @@ def load_library(path: str = LIB_PATH):
     L.tpfm_prepare.argtypes = [v]
     L.tpfm_forward.argtypes = [v, v, v, C.c_float, v]
     L.tpfm_sample_chunk.argtypes = [v, v, v, v, v, v, C.c_int, v]
+    L.tpae_default_config.argtypes = [C.POINTER(AudConfig)]
+    L.tpae_create.argtypes = [C.c_int, C.POINTER(AudConfig)]
+    L.tpae_create.restype = v
+    L.tpae_create_error.restype = cp
+    L.tpae_destroy.argtypes = [v]
+    L.tpae_last_error.argtypes = [v]
+    L.tpae_last_error.restype = cp
+    L.tpae_set_tensor.argtypes = [v, cp, v, i64]
+    L.tpae_load_gguf.argtypes = [v, cp]
+    L.tpae_prepare.argtypes = [v]
+    L.tpae_encode.argtypes = [v, v, i64, i64, v]
     L.tpk_bilinear_gather.argtypes = [v, C.c_int, C.c_int, C.c_int, C.c_int, v, i64, C.c_int,
                                       C.c_int, v, v]
     L.tpk_im2col_cf.argtypes = [v] + [C.c_int] * 12 + [v, C.c_int, v]
@@ -129,6 +141,24 @@ class FmtConfig(C.Structure):
     _fields_ = [(n, C.c_int) for n in ("dim_h", "depth", "n_heads", "dim_w", "dim_a", "dim_e",
                                        "chunk_frames", "prev_frames", "attn_window", "t_freq_dim", "nfe")] + \
                [(n, C.c_float) for n in ("mlp_ratio", "ln_eps", "a_cfg", "e_cfg")]
+
+
+class AudConfig(C.Structure):
+    """tpae_config: the audio encoder's float.audio.* hyper-parameters."""
+    _fields_ = [("n_layers", C.c_int), ("n_heads", C.c_int), ("hidden", C.c_int), ("ffn", C.c_int),
+                ("dim_w", C.c_int), ("ln_eps", C.c_float), ("conv_dim", C.c_int * 7),
+                ("conv_kernel", C.c_int * 7), ("conv_stride", C.c_int * 7), ("pos_kernel", C.c_int),
+                ("pos_groups", C.c_int), ("sample_rate", C.c_int), ("fps", C.c_int)]
+
+
+def _aud_config(cfg: dict) -> AudConfig:
+    c = AudConfig()
+    for k, val in cfg.items():
+        if k.startswith("conv_"):
+            getattr(c, k)[:] = list(val)
+        else:
+            setattr(c, k, val)
+    return c
 
 
 def gguf_kv(path: str, expect_arch: str | None = None) -> dict:
@@ -425,4 +455,59 @@ def default_fmt_config() -> dict:
     c = FmtConfig()
     load_library().tpfm_default_config(C.byref(c))
     return {n: getattr(c, n) for n, _ in FmtConfig._fields_}
+
+
+class AudioEncoder:
+    """The audio encoder on one GPU (audio_model::encode,
+    src/audio_enc.cpp:55-236): audio -> wa [seq_len, dim_w]."""
+
+    def __init__(self, cfg: dict, device: int = 0):
+        self._L = load_library()
+        self.cfg = dict(cfg)
+        self._c = _aud_config(cfg)
+        self._h = self._L.tpae_create(device, C.byref(self._c))
+        if not self._h:
+            raise TpmdError(self._L.tpae_create_error().decode())
+
+    def _check(self, rc: int):
+        if rc != 0:
+            raise TpmdError(self._L.tpae_last_error(self._h).decode())
+
+    def set_tensors(self, tensors: dict):
+        for name, arr in tensors.items():
+            a = np.ascontiguousarray(arr, np.float32)
+            self._check(self._L.tpae_set_tensor(self._h, name.encode(), _np_ptr(a), a.size))
+
+    def load_gguf(self, path: str):
+        self._check(self._L.tpae_load_gguf(self._h, path.encode()))
+
+    def prepare(self):
+        self._check(self._L.tpae_prepare(self._h))
+
+    def encode(self, audio: np.ndarray, seq_len: int) -> np.ndarray:
+        a = np.ascontiguousarray(audio, np.float32)
+        out = np.empty((seq_len, self.cfg["dim_w"]), np.float32)
+        self._check(self._L.tpae_encode(self._h, _np_ptr(a), a.size, seq_len, _np_ptr(out)))
+        return out
+
+    def close(self):
+        if getattr(self, "_h", None):
+            self._L.tpae_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def default_audio_config() -> dict:
+    c = AudConfig()
+    load_library().tpae_default_config(C.byref(c))
+    out = {}
+    for n, _ in AudConfig._fields_:
+        v = getattr(c, n)
+        out[n] = tuple(v) if n.startswith("conv_") else v
+    return out
 

@@ -298,3 +298,85 @@ def make_fmt_chunk(cfg: dict, seed: int = 0) -> dict[str, np.ndarray]:
     f = lambda *sh: rng.standard_normal(sh).astype(np.float32)
     return dict(wr=f(D), prev_wa=f(P, D), cond_audio=f(CF, D), prev_x=f(P, D), x0=f(CF, D), emotion=3)
 
+
+# wav2vec2-base as config 4 names it (7-conv group-norm stem, 12 layers,
+# d = 768, 12 heads, FFN 3072) with the projection to the 512-d motion space;
+# keys as the GGUF's float.audio.* hyper-parameters (src/audio_enc.cpp:25-45)
+AUDIO_CONFIG = dict(n_layers=12, n_heads=12, hidden=768, ffn=3072, dim_w=512, ln_eps=1e-5,
+                    conv_dim=(512,) * 7, conv_kernel=(10, 3, 3, 3, 3, 2, 2), conv_stride=(5, 2, 2, 2, 2, 2, 2),
+                    pos_kernel=128, pos_groups=16, sample_rate=16000, fps=25)
+AUDIO_SMALL = dict(AUDIO_CONFIG, n_layers=2, n_heads=4, hidden=128, ffn=256, dim_w=64, conv_dim=(32,) * 7,
+                   pos_kernel=16, pos_groups=4)
+
+
+def audio_shapes(cfg: dict) -> dict[str, tuple[int, ...]]:
+    """name -> torch shape of the audio encoder's tensors."""
+    s: dict[str, tuple[int, ...]] = {}
+    ic = 1
+    for i in range(7):
+        s[f"feature_extractor.conv_layers.{i}.conv.weight"] = (cfg["conv_dim"][i], ic, cfg["conv_kernel"][i])
+        ic = cfg["conv_dim"][i]
+    s["feature_extractor.conv_layers.0.layer_norm.weight"] = (cfg["conv_dim"][0],)
+    s["feature_extractor.conv_layers.0.layer_norm.bias"] = (cfg["conv_dim"][0],)
+    C, H, F, L = cfg["conv_dim"][6], cfg["hidden"], cfg["ffn"], cfg["n_layers"]
+    s["feature_projection.layer_norm.weight"] = (C,)
+    s["feature_projection.layer_norm.bias"] = (C,)
+    s["feature_projection.projection.weight"] = (H, C)
+    s["feature_projection.projection.bias"] = (H,)
+    s["encoder.pos_conv_embed.conv.weight"] = (H, H // cfg["pos_groups"], cfg["pos_kernel"])
+    s["encoder.pos_conv_embed.conv.bias"] = (H,)
+    s["encoder.layer_norm.weight"] = (H,)
+    s["encoder.layer_norm.bias"] = (H,)
+    for i in range(L):
+        b = f"encoder.layers.{i}."
+        for pj in ("q_proj", "k_proj", "v_proj", "out_proj"):
+            s[b + f"attention.{pj}.weight"] = (H, H)
+            s[b + f"attention.{pj}.bias"] = (H,)
+        s[b + "layer_norm.weight"] = (H,)
+        s[b + "layer_norm.bias"] = (H,)
+        s[b + "feed_forward.intermediate_dense.weight"] = (F, H)
+        s[b + "feed_forward.intermediate_dense.bias"] = (F,)
+        s[b + "feed_forward.output_dense.weight"] = (H, F)
+        s[b + "feed_forward.output_dense.bias"] = (H,)
+        s[b + "final_layer_norm.weight"] = (H,)
+        s[b + "final_layer_norm.bias"] = (H,)
+    s["audio_projection.0.weight"] = (cfg["dim_w"], H * L)
+    s["audio_projection.0.bias"] = (cfg["dim_w"],)
+    s["audio_projection.1.weight"] = (cfg["dim_w"],)
+    s["audio_projection.1.bias"] = (cfg["dim_w"],)
+    return s
+
+
+def make_audio_weights(cfg: dict, seed: int = 0) -> dict[str, np.ndarray]:
+    """Random-init audio encoder: conv and linear weights N(0, 1/fan_in),
+    biases N(0, 0.02), layer-norm gains 1 + N(0, 0.1) and shifts N(0, 0.1)."""
+    rng = np.random.default_rng([seed, 13])
+    out: dict[str, np.ndarray] = {}
+    for n, sh in audio_shapes(cfg).items():
+        if "norm" in n:
+            base = 1.0 if n.endswith(".weight") else 0.0
+            out[n] = (base + rng.standard_normal(sh) * 0.1).astype(np.float32)
+        elif n.endswith(".bias"):
+            out[n] = (rng.standard_normal(sh) * 0.02).astype(np.float32)
+        else:
+            fan = int(np.prod(sh[1:]))
+            out[n] = (rng.standard_normal(sh) / np.sqrt(fan)).astype(np.float32)
+    return out
+
+
+def make_audio(seconds: float, seed: int = 0, sr: int = 16000) -> np.ndarray:
+    """Config-4 style synthetic speech-like audio: band-limited noise
+    (80-4000 Hz) under a 2-8 Hz syllabic envelope, peak 0.5, then the
+    feature extractor's zero-mean unit-variance normalisation."""
+    rng = np.random.default_rng([seed, 14])
+    n = int(seconds * sr)
+    spec = np.fft.rfft(rng.standard_normal(n))
+    f = np.fft.rfftfreq(n, 1.0 / sr)
+    spec[(f < 80) | (f > 4000)] = 0
+    x = np.fft.irfft(spec, n)
+    t = np.arange(n) / sr
+    env = 0.5 + 0.5 * np.sin(2 * np.pi * rng.uniform(2, 8) * t + rng.uniform(0, 2 * np.pi))
+    x = x * env
+    x = 0.5 * x / np.abs(x).max()
+    return ((x - x.mean()) / (x.std() + 1e-7)).astype(np.float32)
+

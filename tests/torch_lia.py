@@ -196,3 +196,58 @@ class TorchFmt:
             x = x + g2 * self._lin(b + "mlp.fc2", F.gelu(self._lin(b + "mlp.fc1", h), approximate="tanh"))
         shf, scf = self._lin("decoder.adaLN_modulation.1", sc).chunk(2, -1)
         return self._lin("decoder.linear", ln(x) * (1 + scf) + shf).numpy()
+
+
+class TorchAudio:
+    """The modified wav2vec2 audio encoder in float64 torch (conv1d stem with
+    a per-channel GroupNorm, exact-erf GELU, align_corners linear
+    interpolation, grouped positional conv, post-norm transformer layers,
+    projection of all layer outputs), independent of the oracle."""
+
+    def __init__(self, cfg: dict, raw: dict):
+        self.c = cfg
+        self.w = {k: _t(v) for k, v in raw.items()}
+
+    def encode(self, audio: np.ndarray, seq_len: int) -> np.ndarray:
+        c, w = self.c, self.w
+        x = _t(audio)
+        unit = seq_len * c["sample_rate"] // c["fps"]
+        if unit > 0 and x.numel() % unit != 0:
+            pad = torch.full((unit,), float(x[-1]), dtype=torch.float64)
+            m = min(unit, x.numel())
+            pad[:m] = x[:m]
+            x = pad
+        h = x[None, None]
+        for i in range(7):
+            h = F.conv1d(h, w[f"feature_extractor.conv_layers.{i}.conv.weight"], stride=c["conv_stride"][i])
+            if i == 0:
+                h = F.group_norm(h, h.shape[1], w["feature_extractor.conv_layers.0.layer_norm.weight"],
+                                 w["feature_extractor.conv_layers.0.layer_norm.bias"], eps=c["ln_eps"])
+            h = F.gelu(h)
+        h = F.interpolate(h, size=seq_len, mode="linear", align_corners=True)[0].T   # [S, C]
+        h = F.layer_norm(h, (h.shape[1],), w["feature_projection.layer_norm.weight"],
+                         w["feature_projection.layer_norm.bias"], eps=c["ln_eps"])
+        h = h @ w["feature_projection.projection.weight"].T + w["feature_projection.projection.bias"]
+        K = c["pos_kernel"]
+        pos = F.conv1d(h.T[None], w["encoder.pos_conv_embed.conv.weight"], w["encoder.pos_conv_embed.conv.bias"],
+                       padding=K // 2, groups=c["pos_groups"])[0, :, :seq_len]
+        h = h + F.gelu(pos).T
+        Hd, nh = c["hidden"], c["n_heads"]
+        ln = lambda z, n: F.layer_norm(z, (Hd,), w[n + ".weight"], w[n + ".bias"], eps=c["ln_eps"])
+        h = ln(h, "encoder.layer_norm")
+        outs = []
+        for l in range(c["n_layers"]):
+            b = f"encoder.layers.{l}."
+            lin = lambda z, n: z @ w[b + n + ".weight"].T + w[b + n + ".bias"]
+            q = lin(h, "attention.q_proj") / math.sqrt(Hd // nh)
+            k, v = lin(h, "attention.k_proj"), lin(h, "attention.v_proj")
+            q, k, v = [z.reshape(seq_len, nh, -1).transpose(0, 1) for z in (q, k, v)]
+            a = (torch.softmax(q @ k.transpose(-1, -2), -1) @ v).transpose(0, 1).reshape(seq_len, Hd)
+            h = ln(h + lin(a, "attention.out_proj"), b + "layer_norm")
+            f = lin(F.gelu(lin(h, "feed_forward.intermediate_dense")), "feed_forward.output_dense")
+            h = ln(h + f, b + "final_layer_norm")
+            outs.append(h)
+        st = torch.cat(outs, -1)
+        o = st @ w["audio_projection.0.weight"].T + w["audio_projection.0.bias"]
+        o = F.layer_norm(o, (c["dim_w"],), w["audio_projection.1.weight"], w["audio_projection.1.bias"], eps=1e-5)
+        return F.silu(o).numpy()
