@@ -41,6 +41,9 @@ EXPORTS = ("tpmd_abi_version", "tpmd_create", "tpmd_create_error", "tpmd_destroy
            "tpfm_last_error", "tpfm_set_tensor", "tpfm_load_gguf", "tpfm_prepare", "tpfm_forward",
            "tpfm_sample_chunk", "tpae_default_config", "tpae_create", "tpae_create_error", "tpae_destroy",
            "tpae_last_error", "tpae_set_tensor", "tpae_load_gguf", "tpae_prepare", "tpae_encode",
+           "tppl_create", "tppl_create_error", "tppl_destroy", "tppl_last_error", "tppl_load",
+           "tppl_motion_encoder", "tppl_audio_encoder", "tppl_sampler", "tppl_decoder", "tppl_prepare",
+           "tppl_n_frames", "tppl_n_chunks", "tppl_generate", "tppl_generate_cb", "tppl_styles",
            "tpk_bilinear_gather", "tpk_im2col_cf", "tpk_last_error")
 
 _lib = None
@@ -121,6 +124,24 @@ def load_library(path: str = LIB_PATH):
     L.tpae_load_gguf.argtypes = [v, cp]
     L.tpae_prepare.argtypes = [v]
     L.tpae_encode.argtypes = [v, v, i64, i64, v]
+    L.tppl_create.argtypes = [C.c_int, cp, C.POINTER(FmtConfig), C.POINTER(AudConfig), C.c_int]
+    L.tppl_create.restype = v
+    L.tppl_create_error.restype = cp
+    L.tppl_destroy.argtypes = [v]
+    L.tppl_last_error.argtypes = [v]
+    L.tppl_last_error.restype = cp
+    L.tppl_load.argtypes = [v, cp]
+    for fn in ("tppl_motion_encoder", "tppl_audio_encoder", "tppl_sampler", "tppl_decoder"):
+        getattr(L, fn).argtypes = [v]
+        getattr(L, fn).restype = v
+    L.tppl_prepare.argtypes = [v]
+    L.tppl_n_frames.argtypes = [i64]
+    L.tppl_n_frames.restype = i64
+    L.tppl_n_chunks.argtypes = [i64]
+    L.tppl_n_chunks.restype = i64
+    L.tppl_generate.argtypes = [v, v, v, i64, C.c_int, v, C.c_uint64, v]
+    L.tppl_generate_cb.argtypes = [v, v, v, i64, C.c_int, v, C.c_uint64, FRAME_FN, v]
+    L.tppl_styles.argtypes = [v, v, v, i64, C.c_int, v, C.c_uint64, v]
     L.tpk_bilinear_gather.argtypes = [v, C.c_int, C.c_int, C.c_int, C.c_int, v, i64, C.c_int,
                                       C.c_int, v, v]
     L.tpk_im2col_cf.argtypes = [v] + [C.c_int] * 12 + [v, C.c_int, v]
@@ -141,6 +162,9 @@ class FmtConfig(C.Structure):
     _fields_ = [(n, C.c_int) for n in ("dim_h", "depth", "n_heads", "dim_w", "dim_a", "dim_e",
                                        "chunk_frames", "prev_frames", "attn_window", "t_freq_dim", "nfe")] + \
                [(n, C.c_float) for n in ("mlp_ratio", "ln_eps", "a_cfg", "e_cfg")]
+
+
+FRAME_FN = C.CFUNCTYPE(C.c_int, C.c_int64, C.POINTER(C.c_float), C.c_void_p)
 
 
 class AudConfig(C.Structure):
@@ -510,4 +534,82 @@ def default_audio_config() -> dict:
         v = getattr(c, n)
         out[n] = tuple(v) if n.startswith("conv_") else v
     return out
+
+
+class Pipeline:
+    """The end-to-end generator (tppl_*, the reference's generate_impl,
+    src/pipeline.cpp:99-186): portrait + audio -> 25 fps frames."""
+
+    def __init__(self, device: int = 0, ftype: str = "f32", fmt_cfg: dict | None = None,
+                 audio_cfg: dict | None = None, max_batch: int = 50):
+        self._L = load_library()
+        fc = C.byref(FmtConfig(**fmt_cfg)) if fmt_cfg else None
+        ac = C.byref(_aud_config(audio_cfg)) if audio_cfg else None
+        self._h = self._L.tppl_create(device, ftype.encode(), fc, ac, max_batch)
+        if not self._h:
+            raise TpmdError(self._L.tppl_create_error().decode())
+
+    def _check(self, rc: int):
+        if rc < 0:
+            raise TpmdError(self._L.tppl_last_error(self._h).decode())
+        return rc
+
+    def _set(self, fn_stage, fn_set, tensors):
+        h = getattr(self._L, fn_stage)(self._h)
+        for name, arr in tensors.items():
+            a = np.ascontiguousarray(arr, np.float32)
+            if getattr(self._L, fn_set)(h, name.encode(), _np_ptr(a), a.size) != 0:
+                raise TpmdError(f"{fn_set}: {name}")
+
+    def set_weights(self, encoder: dict, audio: dict, fmt: dict, decoder: dict):
+        self._set("tppl_motion_encoder", "tpme_set_tensor", encoder)
+        self._set("tppl_audio_encoder", "tpae_set_tensor", audio)
+        self._set("tppl_sampler", "tpfm_set_tensor", fmt)
+        self._set("tppl_decoder", "tpmd_set_tensor", decoder)
+        self._check(self._L.tppl_prepare(self._h))
+
+    def load(self, gguf_dir: str):
+        self._check(self._L.tppl_load(self._h, gguf_dir.encode()))
+
+    def n_frames(self, n_samples: int) -> int:
+        return self._L.tppl_n_frames(n_samples)
+
+    def generate(self, image, audio, emotion: int, noise=None, seed: int = 0, out=None) -> np.ndarray:
+        img = np.ascontiguousarray(image, np.float32)
+        au = np.ascontiguousarray(audio, np.float32)
+        n = self.n_frames(au.size)
+        if out is None:
+            out = np.empty((n, 3, 512, 512), np.float32)
+        nz = None if noise is None else np.ascontiguousarray(noise, np.float32)
+        self._check(self._L.tppl_generate(self._h, _np_ptr(img), _np_ptr(au), au.size, emotion,
+                                          _np_ptr(nz) if nz is not None else None, seed, _np_ptr(out)))
+        return out
+
+    def styles(self, image, audio, emotion: int, noise=None, seed: int = 0) -> np.ndarray:
+        img = np.ascontiguousarray(image, np.float32)
+        au = np.ascontiguousarray(audio, np.float32)
+        st = np.empty((self.n_frames(au.size), 512), np.float32)
+        nz = None if noise is None else np.ascontiguousarray(noise, np.float32)
+        self._check(self._L.tppl_styles(self._h, _np_ptr(img), _np_ptr(au), au.size, emotion,
+                                        _np_ptr(nz) if nz is not None else None, seed, _np_ptr(st)))
+        return st
+
+    def generate_cb(self, image, audio, emotion: int, cb, noise=None, seed: int = 0) -> int:
+        img = np.ascontiguousarray(image, np.float32)
+        au = np.ascontiguousarray(audio, np.float32)
+        nz = None if noise is None else np.ascontiguousarray(noise, np.float32)
+        fn = FRAME_FN(lambda i, p, _u: cb(i, np.ctypeslib.as_array(p, shape=(3, 512, 512))))
+        return self._check(self._L.tppl_generate_cb(self._h, _np_ptr(img), _np_ptr(au), au.size, emotion,
+                                                    _np_ptr(nz) if nz is not None else None, seed, fn, None))
+
+    def close(self):
+        if getattr(self, "_h", None):
+            self._L.tppl_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 

@@ -379,4 +379,6 @@ def make_audio(seconds: float, seed: int = 0, sr: int = 16000) -> np.ndarray:
     x = x * env
     x = 0.5 * x / np.abs(x).max()
     return ((x - x.mean()) / (x.std() + 1e-7)).astype(np.float32)
+# the small audio encoder with the 512-d output the sampler's audio condition takes
+AUDIO_SMALL512 = dict(AUDIO_SMALL, dim_w=512)
 

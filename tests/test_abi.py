@@ -18,8 +18,8 @@ from tpmd import synth
 
 def declared_symbols():
     src = "".join(open(os.path.join(ROOT, "include", h)).read()
-                  for h in ("tpmd.h", "tpme.h", "tpfm.h", "tpae.h"))
-    return sorted(set(re.findall(r"\b((?:tpmd|tpme|tpfm|tpae|tpk)_[a-z0-9_]+)\s*\(", src)))
+                  for h in ("tpmd.h", "tpme.h", "tpfm.h", "tpae.h", "tppl.h"))
+    return sorted(set(re.findall(r"\b((?:tpmd|tpme|tpfm|tpae|tppl|tpk)_[a-z0-9_]+)\s*\(", src)))
 
 
 def test_exports_every_declared_symbol():
