@@ -239,9 +239,10 @@ class MotionDecoder:
     """One decoder on one GPU (mirrors the reference's motion_dec:
     prepare / set_feats / decode_batch, src/motion_dec.h:10-49)."""
 
-    def __init__(self, device: int = 0, dtype: int = DTYPE_F16, max_batch: int = 64):
+    def __init__(self, device: int = 0, dtype: int = DTYPE_F16, max_batch: int = 64, _handle=None):
         self._L = load_library()
-        self._h = self._L.tpmd_create(device, dtype, max_batch)
+        self._owned = _handle is None
+        self._h = self._L.tpmd_create(device, dtype, max_batch) if _handle is None else _handle
         if not self._h:
             raise TpmdError(self._L.tpmd_create_error().decode())
         self.dtype = dtype
@@ -331,7 +332,8 @@ class MotionDecoder:
 
     def close(self):
         if getattr(self, "_h", None):
-            self._L.tpmd_destroy(self._h)
+            if getattr(self, "_owned", True):
+                self._L.tpmd_destroy(self._h)
             self._h = None
 
     def __del__(self):
@@ -570,6 +572,10 @@ class Pipeline:
 
     def load(self, gguf_dir: str):
         self._check(self._L.tppl_load(self._h, gguf_dir.encode()))
+
+    def decoder(self) -> "MotionDecoder":
+        """The pipeline's own decoder (not owned by the returned object)."""
+        return MotionDecoder(0, DTYPE_F16, 1, _handle=self._L.tppl_decoder(self._h))
 
     def n_frames(self, n_samples: int) -> int:
         return self._L.tppl_n_frames(n_samples)
