@@ -71,6 +71,18 @@ int tppl_generate_cb(tppl_ctx *ctx, const float *image, const float *audio, int6
 int tppl_styles(tppl_ctx *ctx, const float *image, const float *audio, int64_t n_samples, int emotion,
                 const float *noise, uint64_t seed, float *styles);
 
+/* The same styles chunk by chunk, as the sampler produces them: after each
+ * 50-frame chunk, cb(frame0, n, styles, ud) with the decoder styles
+ * [n][512] of frames frame0 .. frame0 + n - 1 (valid during the call; the
+ * clip's padded tail frames are not passed). The decoder's feats are set
+ * before the first call. A nonzero return stops the generation. Returns
+ * n_frames or -1. Lets a caller decode on other GPUs while the sampler
+ * runs (the reference samples every chunk before decoding,
+ * src/pipeline.cpp:134-184; frames depend only on their styles). */
+typedef int (*tppl_styles_fn)(int64_t frame0, int64_t n, const float *styles, void *ud);
+int tppl_styles_cb(tppl_ctx *ctx, const float *image, const float *audio, int64_t n_samples, int emotion,
+                   const float *noise, uint64_t seed, tppl_styles_fn cb, void *ud);
+
 #ifdef __cplusplus
 }
 #endif

@@ -144,16 +144,59 @@ __global__ void __launch_bounds__(256) attn_kernel(const float *__restrict__ qkv
     }
 }
 
-// x += (mod[m][gate] + bmod[gate]) * (o + bo)
-__global__ void gate_residual_kernel(float *__restrict__ x, const float *__restrict__ o,
-                                     const float *__restrict__ bo, const float *__restrict__ mod,
-                                     const float *__restrict__ bmod, int mod_stride, int gate_off, int M, int H) {
-    const int64_t n = (int64_t) M * H;
-    for (int64_t e = (int64_t) blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t) gridDim.x * blockDim.x) {
-        const int64_t m = e / H;
-        const int i = (int) (e % H);
-        const float g = mod[m * mod_stride + gate_off + i] + __ldg(bmod + gate_off + i);
-        x[e] += g * (o[e] + __ldg(bo + i));
+// the gated residual of one sub-block followed by the next layer norm, per
+// row: x += (mod[gate] + bmod[gate]) * (o + bo), then h = LN(x) * (1 + scale)
+// + shift with the next norm's modulation (mod2, bmod2). Each element and
+// each sum is formed in the same order as a separate residual update then
+// norm_mod_kernel would form them.
+constexpr int RN_PER_THREAD = 16;  // H <= 16 x blockDim
+template <typename TIN>
+__global__ void __launch_bounds__(256) res_norm_kernel(float *__restrict__ x, const float *__restrict__ o,
+                                                       const float *__restrict__ bo, const float *__restrict__ mod,
+                                                       const float *__restrict__ bmod, int mod_stride, int gate_off,
+                                                       int H, float eps, const float *__restrict__ mod2,
+                                                       const float *__restrict__ bmod2, int shift_off, int scale_off,
+                                                       TIN *__restrict__ h) {
+    __shared__ float red[32];
+    const int m = blockIdx.x;
+    float *r = x + (int64_t) m * H;
+    const float *orow = o + (int64_t) m * H;
+    const float *md = mod + (int64_t) m * mod_stride;
+    float xv[RN_PER_THREAD];
+    float s = 0.0f;
+#pragma unroll
+    for (int k = 0; k < RN_PER_THREAD; k++) {
+        const int i = threadIdx.x + k * blockDim.x;
+        if (i < H) {
+            const float g = md[gate_off + i] + __ldg(bmod + gate_off + i);
+            const float v = r[i] + g * (orow[i] + __ldg(bo + i));
+            r[i] = v;
+            xv[k] = v;
+            s += v;
+        }
+    }
+    const float mean = block_sum(s, red) / (float) H;
+    float q = 0.0f;
+#pragma unroll
+    for (int k = 0; k < RN_PER_THREAD; k++) {
+        const int i = threadIdx.x + k * blockDim.x;
+        if (i < H) {
+            const float d = xv[k] - mean;
+            q = fmaf(d, d, q);
+        }
+    }
+    const float var = block_sum(q, red) / (float) H;
+    const float inv = 1.0f / sqrtf(var + eps);
+    const float *md2 = mod2 + (int64_t) m * mod_stride;
+#pragma unroll
+    for (int k = 0; k < RN_PER_THREAD; k++) {
+        const int i = threadIdx.x + k * blockDim.x;
+        if (i < H) {
+            const float v = (xv[k] - mean) * inv;
+            const float sc = md2[scale_off + i] + __ldg(bmod2 + scale_off + i);
+            const float sh = md2[shift_off + i] + __ldg(bmod2 + shift_off + i);
+            h[(int64_t) m * H + i] = cvt<TIN>(v * sc + v + sh);
+        }
     }
 }
 
@@ -240,9 +283,16 @@ cudaError_t fmt_attn(bool f16, const float *qkv, const float *bqkv, int T, int H
         attn_kernel<float><<<(warps * 32 + 255) / 256, 256, 0, st>>>(qkv, bqkv, T, H, nh, window, (float *) out);
     return cudaGetLastError();
 }
-cudaError_t fmt_gate_residual(float *x, const float *o, const float *bo, const float *mod, const float *bmod,
-                              int mod_stride, int gate_off, int M, int H, cudaStream_t st) {
-    gate_residual_kernel<<<grid_for((int64_t) M * H), 256, 0, st>>>(x, o, bo, mod, bmod, mod_stride, gate_off, M, H);
+cudaError_t fmt_res_norm(bool f16, float *x, const float *o, const float *bo, const float *mod, const float *bmod,
+                         int mod_stride, int gate_off, int M, int H, float eps, const float *mod2, const float *bmod2,
+                         int shift_off, int scale_off, void *h, cudaStream_t st) {
+    if (H > RN_PER_THREAD * 256) return cudaErrorInvalidValue;
+    if (f16)
+        res_norm_kernel<__half><<<M, 256, 0, st>>>(x, o, bo, mod, bmod, mod_stride, gate_off, H, eps, mod2, bmod2,
+                                                   shift_off, scale_off, (__half *) h);
+    else
+        res_norm_kernel<float><<<M, 256, 0, st>>>(x, o, bo, mod, bmod, mod_stride, gate_off, H, eps, mod2, bmod2,
+                                                  shift_off, scale_off, (float *) h);
     return cudaGetLastError();
 }
 cudaError_t fmt_gelu(bool f16, const float *a, const float *b, int M, int N, void *y, cudaStream_t st) {

@@ -1,9 +1,11 @@
 // Flow-matching sampler C ABI (include/tpfm.h): fmt_model::forward
 // (src/fmt.cpp:64-211) and sample_chunk_ex (src/pipeline.cpp:15-91). The
 // plain linears are cuBLAS GEMMs (row-major Y[M][N] = X[M][K] W[N][K]^T, no
-// bias); norms, banded attention, activations, gated residuals and the
-// CFG/Euler update are the kernels of kernels_fmt.cu. A chunk's nine
-// forwards run as one captured CUDA graph.
+// bias). The adaLN modulations of all blocks and of the final layer depend
+// only on the conditioning, so one GEMM per forward computes them together
+// (their weights are contiguous in the arena). Norms, banded attention,
+// activations, gated residuals and the CFG/Euler update are the kernels of
+// kernels_fmt.cu. A chunk's nine forwards run as one captured CUDA graph.
 #include <cublas_v2.h>
 #include <cuda_runtime.h>
 
@@ -27,9 +29,10 @@ cudaError_t fmt_norm_mod(bool f16, const float *x, int M, int H, float eps, cons
                          int mod_stride, int shift_off, int scale_off, void *h, cudaStream_t st);
 cudaError_t fmt_attn(bool f16, const float *qkv, const float *bqkv, int T, int H, int nh, int window, void *out,
                      cudaStream_t st);
-cudaError_t fmt_gate_residual(float *x, const float *o, const float *bo, const float *mod, const float *bmod,
-                              int mod_stride, int gate_off, int M, int H, cudaStream_t st);
 cudaError_t fmt_gelu(bool f16, const float *a, const float *b, int M, int N, void *y, cudaStream_t st);
+cudaError_t fmt_res_norm(bool f16, float *x, const float *o, const float *bo, const float *mod, const float *bmod,
+                         int mod_stride, int gate_off, int M, int H, float eps, const float *mod2, const float *bmod2,
+                         int shift_off, int scale_off, void *h, cudaStream_t st);
 cudaError_t fmt_cfg_euler(const float *vout, const float *bv, int T, int P, int D, float a_cfg, float e_cfg,
                           float dt, float *x, float *x60, cudaStream_t st);
 cudaError_t fmt_add_bias(const float *a, const float *b, int M, int N, float *y, cudaStream_t st);
@@ -50,6 +53,7 @@ struct tpfm_ctx {
     bool f16 = false;
     tpfm_config c{};
     int T = 0, M = 0, CD = 0, FF = 0, H = 0;
+    int nmod = 0;  // adaLN columns of all blocks + the final layer
     std::string err;
     std::map<std::string, int64_t> spec;
     std::map<std::string, std::vector<float>> host;
@@ -62,7 +66,7 @@ struct tpfm_ctx {
     void *blas_ws = nullptr;
     void *act = nullptr;
     float *x60 = nullptr, *cond = nullptr, *clin = nullptr, *te0 = nullptr, *te = nullptr, *x1 = nullptr,
-          *x = nullptr, *mod = nullptr, *qkv = nullptr, *o = nullptr, *m1raw = nullptr, *fm = nullptr,
+          *x = nullptr, *mod = nullptr, *qkv = nullptr, *o = nullptr, *m1raw = nullptr,
           *vout = nullptr, *v = nullptr, *xc = nullptr, *tf = nullptr;
     void *sc = nullptr, *h = nullptr, *att = nullptr, *m1 = nullptr, *cond_in = nullptr, *x60_in = nullptr;
     cudaGraphExec_t graph = nullptr;
@@ -83,16 +87,23 @@ struct tpfm_ctx {
         return false;
     }
     const float *F(const std::string &n) const { return w32 + off32.at(n); }
+    const void *Wt(const std::string &n) const {
+        return f16 ? (const void *) (w16 + off16.at(n)) : (const void *) F(n);
+    }
     // Y[M][N] (f32) = X[M][K] (GEMM input type) W[N][K]^T
-    bool gemm(const void *X, int Mr, int K, const std::string &wname, int N, float *Y) {
+    bool gemm_w(const void *X, int Mr, int K, const void *W, int N, float *Y, const char *what) {
         const float one = 1.0f, zero = 0.0f;
-        const void *W = f16 ? (const void *) (w16 + off16.at(wname)) : (const void *) F(wname);
         const cudaDataType_t t = f16 ? CUDA_R_16F : CUDA_R_32F;
         return bk(cublasGemmEx(blas, CUBLAS_OP_T, CUBLAS_OP_N, N, Mr, K, &one, W, t, K, X, t, K, &zero, Y,
                                CUDA_R_32F, N, f16 ? CUBLAS_COMPUTE_32F : CUBLAS_COMPUTE_32F_PEDANTIC,
                                CUBLAS_GEMM_DEFAULT),
-                  wname.c_str());
+                  what);
     }
+    bool gemm(const void *X, int Mr, int K, const std::string &wname, int N, float *Y) {
+        return gemm_w(X, Mr, K, Wt(wname), N, Y, wname.c_str());
+    }
+    // the first adaLN weight: all depth + 1 of them are contiguous from here
+    const void *adaln_w() const { return Wt("blocks.0.adaLN_modulation.1.weight"); }
     ~tpfm_ctx() {
         if (device >= 0) cudaSetDevice(device);
         if (graph) cudaGraphExecDestroy(graph);
@@ -156,33 +167,42 @@ bool forward_device(tpfm_ctx *c, int s) {
         if (!K(fmt_to_half(c->x60, (int64_t) T * c->c.dim_w, (__half *) c->x60_in, st), "x60 f16")) return false;
         x60_in = c->x60_in;
     }
+    const int NM = c->nmod;
     if (!c->gemm(x60_in, T, c->c.dim_w, "x_embedder.proj.weight", H, c->x1) ||
-        !K(fmt_embed_x(c->x1, c->F("x_embedder.proj.bias"), c->F("pos_embed"), T, H, c->x, st), "x embed"))
+        !K(fmt_embed_x(c->x1, c->F("x_embedder.proj.bias"), c->F("pos_embed"), T, H, c->x, st), "x embed") ||
+        !c->gemm_w(c->sc, M, H, c->adaln_w(), NM, c->mod, "adaLN modulation"))
+        return false;
+    // each gated residual runs fused with the layer norm after it; only the
+    // first block's attention norm stands alone
+    const float eps = c->c.ln_eps;
+    if (!K(fmt_norm_mod(h16, c->x, M, H, eps, c->mod, c->F("blocks.0.adaLN_modulation.1.bias"), NM, 0, H, c->h, st),
+           "norm"))
         return false;
     for (int l = 0; l < c->c.depth; l++) {
         const std::string b = "blocks." + std::to_string(l) + ".";
         const float *bmod = c->F(b + "adaLN_modulation.1.bias");
-        if (!c->gemm(c->sc, M, H, b + "adaLN_modulation.1.weight", 6 * H, c->mod) ||
-            !K(fmt_norm_mod(h16, c->x, M, H, c->c.ln_eps, c->mod, bmod, 6 * H, 0, H, c->h, st), "norm") ||
-            !c->gemm(c->h, M, H, b + "attn.qkv.weight", 3 * H, c->qkv) ||
+        const float *md = c->mod + (size_t) l * 6 * H;  // this block's six modulation vectors
+        // the norm after the MLP residual: the next block's attention norm, or the final layer's
+        const bool last = l + 1 == c->c.depth;
+        const float *md2 = c->mod + (size_t) (l + 1) * 6 * H;
+        const float *bmod2 = last ? c->F("decoder.adaLN_modulation.1.bias")
+                                  : c->F("blocks." + std::to_string(l + 1) + ".adaLN_modulation.1.bias");
+        if (!c->gemm(c->h, M, H, b + "attn.qkv.weight", 3 * H, c->qkv) ||
             !K(fmt_attn(h16, c->qkv, c->F(b + "attn.qkv.bias"), T, H, c->c.n_heads, c->c.attn_window, c->att, st),
                "attention") ||
             !c->gemm(c->att, M, H, b + "attn.proj.weight", H, c->o) ||
-            !K(fmt_gate_residual(c->x, c->o, c->F(b + "attn.proj.bias"), c->mod, bmod, 6 * H, 2 * H, M, H, st),
-               "residual") ||
-            !K(fmt_norm_mod(h16, c->x, M, H, c->c.ln_eps, c->mod, bmod, 6 * H, 3 * H, 4 * H, c->h, st), "norm") ||
+            !K(fmt_res_norm(h16, c->x, c->o, c->F(b + "attn.proj.bias"), md, bmod, NM, 2 * H, M, H, eps, md, bmod,
+                            3 * H, 4 * H, c->h, st),
+               "residual + norm") ||
             !c->gemm(c->h, M, H, b + "mlp.fc1.weight", FF, c->m1raw) ||
             !K(fmt_gelu(h16, c->m1raw, c->F(b + "mlp.fc1.bias"), M, FF, c->m1, st), "gelu") ||
             !c->gemm(c->m1, M, FF, b + "mlp.fc2.weight", H, c->o) ||
-            !K(fmt_gate_residual(c->x, c->o, c->F(b + "mlp.fc2.bias"), c->mod, bmod, 6 * H, 5 * H, M, H, st),
-               "residual"))
+            !K(fmt_res_norm(h16, c->x, c->o, c->F(b + "mlp.fc2.bias"), md, bmod, NM, 5 * H, M, H, eps, md2, bmod2, 0,
+                            H, c->h, st),
+               "residual + norm"))
             return false;
     }
-    return c->gemm(c->sc, M, H, "decoder.adaLN_modulation.1.weight", 2 * H, c->fm) &&
-           K(fmt_norm_mod(h16, c->x, M, H, c->c.ln_eps, c->fm, c->F("decoder.adaLN_modulation.1.bias"), 2 * H, 0, H,
-                          c->h, st),
-             "norm") &&
-           c->gemm(c->h, M, H, "decoder.linear.weight", c->c.dim_w, c->vout);
+    return c->gemm(c->h, M, H, "decoder.linear.weight", c->c.dim_w, c->vout);
 }
 
 // clin = cond . c_embedder^T (the conditioning rows, fixed for a chunk)
@@ -243,12 +263,13 @@ tpfm_ctx *tpfm_create(int device, int dtype, const tpfm_config *cfg) {
     c->M = 3 * c->T;
     c->CD = cfg->dim_w + cfg->dim_a + cfg->dim_e;
     c->FF = (int) (cfg->dim_h * cfg->mlp_ratio);
+    c->nmod = cfg->depth * 6 * cfg->dim_h + 2 * cfg->dim_h;
     build_spec(c);
     // activations
     const size_t H = c->H, T = c->T, M = c->M, D = cfg->dim_w, FF = c->FF, CD = c->CD;
     const size_t es = c->f16 ? 2 : 4;
-    size_t sizes[] = {T * D * 4, M * CD * 4, M * H * 4, H * 4, H * 4, T * H * 4, M * H * 4, M * 6 * H * 4,
-                      M * 3 * H * 4, M * H * 4, M * FF * 4, M * 2 * H * 4, M * D * 4, M * D * 4,
+    size_t sizes[] = {T * D * 4, M * CD * 4, M * H * 4, H * 4, H * 4, T * H * 4, M * H * 4, M * (size_t) c->nmod * 4,
+                      M * 3 * H * 4, M * H * 4, M * FF * 4, M * D * 4, M * D * 4,
                       (size_t) cfg->chunk_frames * D * 4, (size_t) (cfg->nfe) * cfg->t_freq_dim * 4,
                       M * H * es, M * H * es, M * H * es, M * FF * es, M * CD * es, T * D * es};
     const int ns = sizeof(sizes) / sizeof(sizes[0]);
@@ -272,7 +293,7 @@ tpfm_ctx *tpfm_create(int device, int dtype, const tpfm_config *cfg) {
     char *b = (char *) c->act;
     int i = 0;
     float **fl[] = {&c->x60, &c->cond, &c->clin, &c->te0, &c->te, &c->x1, &c->x, &c->mod, &c->qkv, &c->o,
-                    &c->m1raw, &c->fm, &c->vout, &c->v, &c->xc, &c->tf};
+                    &c->m1raw, &c->vout, &c->v, &c->xc, &c->tf};
     for (float **p : fl) *p = (float *) (b + offs[i++]);
     void **vp[] = {&c->sc, &c->h, &c->att, &c->m1, &c->cond_in, &c->x60_in};
     for (void **p : vp) *p = b + offs[i++];
@@ -372,12 +393,26 @@ int tpfm_prepare(tpfm_ctx *c) {
     size_t n32 = 0, n16 = 0;
     c->off32.clear();
     c->off16.clear();
-    for (auto &kv : c->spec) {
-        c->off32[kv.first] = n32;
-        n32 += ((size_t) kv.second + 63) & ~(size_t) 63;
-        if (c->f16 && is_gemm_weight(kv.first)) {
-            c->off16[kv.first] = n16;
-            n16 += ((size_t) kv.second + 127) & ~(size_t) 127;
+    // the adaLN weights of every block and of the final layer first, back to
+    // back in that order: one GEMM computes all the modulations
+    std::vector<std::string> order;
+    for (int l = 0; l < c->c.depth; l++) order.push_back("blocks." + std::to_string(l) + ".adaLN_modulation.1.weight");
+    order.push_back("decoder.adaLN_modulation.1.weight");
+    for (auto &kv : c->spec)
+        if (std::find(order.begin(), order.end(), kv.first) == order.end()) order.push_back(kv.first);
+    const size_t n_adaln = (size_t) c->c.depth + 1;
+    for (size_t i = 0; i < order.size(); i++) {
+        const std::string &n = order[i];
+        const size_t sz = (size_t) c->spec.at(n);
+        c->off32[n] = n32;
+        n32 += sz;
+        if (c->f16 && is_gemm_weight(n)) {
+            c->off16[n] = n16;
+            n16 += sz;
+        }
+        if (i + 1 >= n_adaln) {  // 256-byte aligned starts after the adaLN group
+            n32 = (n32 + 63) & ~(size_t) 63;
+            n16 = (n16 + 127) & ~(size_t) 127;
         }
     }
     std::vector<float> img(n32, 0.0f);

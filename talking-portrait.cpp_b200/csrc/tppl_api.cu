@@ -39,9 +39,11 @@ struct tppl_ctx {
 namespace {
 
 // stages 1-3 of generate_impl: encoder (feats to the decoder on the GPU),
-// audio features, chunked sampling -> styles[t] = appearance + r_d[t]
+// audio features, chunked sampling -> styles[t] = appearance + r_d[t];
+// each chunk's styles go to `cb` (when given) as soon as they exist
 int make_styles(tppl_ctx *c, const float *image, const float *audio, int64_t n_samples, int emotion,
-                const float *noise, uint64_t seed, std::vector<float> &styles) {
+                const float *noise, uint64_t seed, std::vector<float> &styles, tppl_styles_fn cb = nullptr,
+                void *ud = nullptr) {
     const int64_t n_frames = tppl_n_frames(n_samples), n_chunks = tppl_n_chunks(n_frames);
     if (!image || !audio) return c->fail("tppl: null argument");
     if (n_frames <= 0) return c->fail("audio too short");
@@ -68,6 +70,7 @@ int make_styles(tppl_ctx *c, const float *image, const float *audio, int64_t n_s
     }
     std::vector<float> r_d((size_t) n_chunks * CF * D), prev_x((size_t) P * D, 0.0f), prev_wa((size_t) P * D, 0.0f),
         wa_t((size_t) CF * D);
+    styles.assign((size_t) n_frames * STYLE, 0.0f);
     for (int64_t ck = 0; ck < n_chunks; ck++) {
         const int64_t f0 = ck * CF;
         for (int64_t f = 0; f < CF; f++) {  // replicate-padded at the clip's end
@@ -80,10 +83,12 @@ int make_styles(tppl_ctx *c, const float *image, const float *audio, int64_t n_s
             return c->fail(tpfm_last_error(c->fm));
         memcpy(prev_x.data(), out + (size_t) (CF - P) * D, (size_t) P * D * 4);
         memcpy(prev_wa.data(), wa_t.data() + (size_t) (CF - P) * D, (size_t) P * D * 4);
+        const int64_t f1 = std::min<int64_t>(f0 + CF, n_frames);
+        for (int64_t t = f0; t < f1; t++)
+            for (int i = 0; i < STYLE; i++)
+                styles[(size_t) t * STYLE + i] = app[(size_t) i] + r_d[(size_t) t * D + i];
+        if (cb && cb(f0, f1 - f0, styles.data() + (size_t) f0 * STYLE, ud) != 0) break;
     }
-    styles.resize((size_t) n_frames * STYLE);
-    for (int64_t t = 0; t < n_frames; t++)
-        for (int i = 0; i < STYLE; i++) styles[(size_t) t * STYLE + i] = app[(size_t) i] + r_d[(size_t) t * D + i];
     return (int) n_frames;
 }
 
@@ -174,6 +179,14 @@ int tppl_styles(tppl_ctx *c, const float *image, const float *audio, int64_t n_s
     if (n < 0) return -1;
     memcpy(styles, st.data(), st.size() * 4);
     return n;
+}
+
+int tppl_styles_cb(tppl_ctx *c, const float *image, const float *audio, int64_t n_samples, int emotion,
+                   const float *noise, uint64_t seed, tppl_styles_fn cb, void *ud) {
+    if (!c) return -1;
+    if (!cb) return c->fail("tppl_styles_cb: null callback");
+    std::vector<float> st;
+    return make_styles(c, image, audio, n_samples, emotion, noise, seed, st, cb, ud);
 }
 
 int tppl_generate(tppl_ctx *c, const float *image, const float *audio, int64_t n_samples, int emotion,

@@ -43,7 +43,7 @@ EXPORTS = ("tpmd_abi_version", "tpmd_create", "tpmd_create_error", "tpmd_destroy
            "tpae_last_error", "tpae_set_tensor", "tpae_load_gguf", "tpae_prepare", "tpae_encode",
            "tppl_create", "tppl_create_error", "tppl_destroy", "tppl_last_error", "tppl_load",
            "tppl_motion_encoder", "tppl_audio_encoder", "tppl_sampler", "tppl_decoder", "tppl_prepare",
-           "tppl_n_frames", "tppl_n_chunks", "tppl_generate", "tppl_generate_cb", "tppl_styles",
+           "tppl_n_frames", "tppl_n_chunks", "tppl_generate", "tppl_generate_cb", "tppl_styles", "tppl_styles_cb",
            "tpk_bilinear_gather", "tpk_im2col_cf", "tpk_last_error")
 
 _lib = None
@@ -142,6 +142,7 @@ def load_library(path: str = LIB_PATH):
     L.tppl_generate.argtypes = [v, v, v, i64, C.c_int, v, C.c_uint64, v]
     L.tppl_generate_cb.argtypes = [v, v, v, i64, C.c_int, v, C.c_uint64, FRAME_FN, v]
     L.tppl_styles.argtypes = [v, v, v, i64, C.c_int, v, C.c_uint64, v]
+    L.tppl_styles_cb.argtypes = [v, v, v, i64, C.c_int, v, C.c_uint64, STYLES_FN, v]
     L.tpk_bilinear_gather.argtypes = [v, C.c_int, C.c_int, C.c_int, C.c_int, v, i64, C.c_int,
                                       C.c_int, v, v]
     L.tpk_im2col_cf.argtypes = [v] + [C.c_int] * 12 + [v, C.c_int, v]
@@ -165,6 +166,7 @@ class FmtConfig(C.Structure):
 
 
 FRAME_FN = C.CFUNCTYPE(C.c_int, C.c_int64, C.POINTER(C.c_float), C.c_void_p)
+STYLES_FN = C.CFUNCTYPE(C.c_int, C.c_int64, C.c_int64, C.POINTER(C.c_float), C.c_void_p)
 
 
 class AudConfig(C.Structure):
@@ -599,6 +601,16 @@ class Pipeline:
         self._check(self._L.tppl_styles(self._h, _np_ptr(img), _np_ptr(au), au.size, emotion,
                                         _np_ptr(nz) if nz is not None else None, seed, _np_ptr(st)))
         return st
+
+    def styles_cb(self, image, audio, emotion: int, cb, noise=None, seed: int = 0) -> int:
+        """tppl_styles_cb: cb(frame0, styles [n, 512] view valid during the
+        call) after each sampler chunk; a truthy return stops. Returns n_frames."""
+        img = np.ascontiguousarray(image, np.float32)
+        au = np.ascontiguousarray(audio, np.float32)
+        nz = None if noise is None else np.ascontiguousarray(noise, np.float32)
+        fn = STYLES_FN(lambda f0, n, p, _u: int(bool(cb(f0, np.ctypeslib.as_array(p, shape=(n, 512))))))
+        return self._check(self._L.tppl_styles_cb(self._h, _np_ptr(img), _np_ptr(au), au.size, emotion,
+                                                  _np_ptr(nz) if nz is not None else None, seed, fn, None))
 
     def generate_cb(self, image, audio, emotion: int, cb, noise=None, seed: int = 0) -> int:
         img = np.ascontiguousarray(image, np.float32)

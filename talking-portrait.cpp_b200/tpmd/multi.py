@@ -13,8 +13,15 @@ data-path collective:
   slice of the caller's frame buffer;
 * device time is reduced as the max over ranks.
 
+End to end (generate_pipelined) the serial stages (encoders, sampler) run on
+rank 0 and the decode overlaps them: the sampler hands over each chunk's
+styles as soon as they exist (tppl_styles_cb), rank 0 broadcasts them, and
+the other ranks decode their share of the chunk while the next one is
+sampled.
+
 The reference has no multi-GPU path (src/pipeline.cpp:153-184 decodes
-batches serially on one device); this module is new.
+batches serially on one device, after sampling every chunk); this module is
+new.
 """
 from __future__ import annotations
 
@@ -78,3 +85,103 @@ def max_over_ranks(value: float, device=None, group=None) -> float:
                      device=device if device is not None else "cpu")
     dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
     return float(t.item())
+
+
+FRAME_BYTES = 3 * 512 * 512 * 4  # one decoded frame, float32 CHW
+
+
+def pipeline_plan(n_frames: int, world: int, chunk: int = 50) -> list[list[tuple[int, int]]]:
+    """Per sampler chunk k, the [lo, hi) frames each rank decodes when rank 0
+    runs the serial stages and the decode overlaps them:
+
+    * one rank: rank 0 decodes everything (after the sampler);
+    * two ranks: rank 1 decodes the chunks as they come and rank 0 the last
+      n_chunks // 7 of them once its sampler is done (one decoding GPU alone
+      falls behind the sampler);
+    * more ranks: each chunk is split in contiguous ranges over ranks
+      1 .. world-1 whose sizes differ by at most one frame (the larger
+      ranges rotate from chunk to chunk); rank 0 only samples.
+    """
+    if n_frames < 0 or world < 1 or chunk < 1:
+        raise ValueError("bad plan arguments")
+    n_chunks = -(-n_frames // chunk)
+    tail = n_chunks // 7
+    plan = []
+    for k in range(n_chunks):
+        f0, f1 = k * chunk, min(n_frames, (k + 1) * chunk)
+        ranges = [(f0, f0)] * world
+        if world == 1:
+            ranges[0] = (f0, f1)
+        elif world == 2:
+            ranges[0 if k >= n_chunks - tail else 1] = (f0, f1)
+        else:
+            m, n = world - 1, f1 - f0
+            lo = f0
+            for i in range(m):
+                size = n // m + (1 if (i - k) % m < n % m else 0)
+                ranges[1 + i] = (lo, lo + size)
+                lo += size
+        plan.append(ranges)
+    return plan
+
+
+def frames_per_rank(plan: list[list[tuple[int, int]]], rank: int) -> int:
+    return sum(hi - lo for ranges in plan for lo, hi in (ranges[rank],))
+
+
+def generate_pipelined(rank: int, world: int, device, n_frames: int, dec, frames, pipe=None, image=None,
+                       audio=None, emotion: int = 0, seed: int = 0, noise=None, group=None,
+                       chunk: int = 50) -> int:
+    """Config-4 generation on `world` GPUs with the decode overlapping the
+    sampler (pipeline_plan). Rank 0 passes `pipe` (a tpmd.Pipeline whose
+    decoder is `dec`) and the inputs; the other ranks pass a MotionDecoder
+    that already holds rank 0's weight arena (share_decoder or
+    adopt_arena(0)). Every rank writes the frames it decodes, in frame order,
+    into `frames` (host float32 [m, 3, 512, 512], m >= its frame count;
+    pinned for full copy speed). Returns the number of frames this rank
+    decoded. Every rank takes the same collective steps: one feats broadcast
+    and one styles broadcast per chunk."""
+    import numpy as np
+    import torch
+
+    plan = pipeline_plan(n_frames, world, chunk)
+    n_chunks = len(plan)
+    fbytes = FRAME_BYTES
+    out = frames.data_ptr()
+    st_dev = torch.empty((max(n_chunks, 1), chunk, 512), dtype=torch.float32, device=device)
+    done = 0
+    if rank == 0:
+        own = []
+
+        def on_chunk(f0, styles):
+            k = f0 // chunk
+            if world > 1:
+                if k == 0:
+                    broadcast_bytes(arena_tensor(dec, 1, device), 0, group)
+                st_dev[k, :styles.shape[0]].copy_(torch.from_numpy(styles))
+                broadcast_bytes(st_dev[k], 0, group)
+            lo, hi = plan[k][0]
+            if hi > lo:
+                own.append(styles[lo - f0:hi - f0].copy())
+            return 0
+
+        pipe.styles_cb(image, audio, emotion, on_chunk, noise=noise, seed=seed)
+        if own:
+            st = np.ascontiguousarray(np.concatenate(own))
+            dec.decode_ptr(st.ctypes.data, st.shape[0], out)
+            done = st.shape[0]
+    else:
+        for k in range(n_chunks):
+            if k == 0:
+                broadcast_bytes(arena_tensor(dec, 1, device), 0, group)
+                if torch.device(device).type == "cuda":
+                    torch.cuda.synchronize(device)
+                dec.adopt_arena(1)
+            broadcast_bytes(st_dev[k], 0, group)
+            lo, hi = plan[k][rank]
+            if hi > lo:
+                f0 = k * chunk
+                s_h = st_dev[k, lo - f0:hi - f0].cpu()
+                dec.decode_ptr(s_h.data_ptr(), hi - lo, out + done * fbytes)
+                done += hi - lo
+    return done

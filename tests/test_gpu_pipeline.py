@@ -92,3 +92,19 @@ def test_seeded_noise_and_callback(pipe, case):
 def test_pipeline_rejects_mismatched_stages():
     with pytest.raises(tpmd.TpmdError, match="dim_a"):
         tpmd.Pipeline(0, "f32", FMT, synth.AUDIO_SMALL)
+
+
+def test_styles_cb_chunks_match_styles(pipe, case):
+    ref = pipe.styles(case["img"], case["audio"], 3, noise=case["noise"])
+    seen = []
+
+    def cb(f0, st):
+        seen.append((f0, st.copy()))
+        return 0
+
+    assert pipe.styles_cb(case["img"], case["audio"], 3, cb, noise=case["noise"]) == 75
+    assert [f for f, _ in seen] == [0, 50] and seen[1][1].shape == (25, 512)  # the padded tail is not passed
+    assert np.array_equal(np.concatenate([s for _, s in seen]), ref)
+    calls = []
+    pipe.styles_cb(case["img"], case["audio"], 3, lambda f0, st: calls.append(f0) or 1, noise=case["noise"])
+    assert calls == [0]  # a nonzero return stops the sampler

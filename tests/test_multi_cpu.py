@@ -1,7 +1,9 @@
-"""Host logic of the multi-GPU path on 2 gloo ranks (CPU): frame sharding
+"""Host logic of the multi-GPU path on gloo ranks (CPU): frame sharding
 covers a clip exactly once, arena bytes broadcast from rank 0, max-over-ranks
-timing, and a rank that fails before the broadcast is seen by the other
-through a short process-group timeout rather than a hang."""
+timing, the pipelined end-to-end schedule (every frame decoded once, by the
+planned rank, from the styles of its own chunk, with the same collective
+steps on every rank), and a rank that fails before the broadcast is seen by
+the other through a short process-group timeout rather than a hang."""
 from __future__ import annotations
 
 import os
@@ -30,6 +32,30 @@ def test_frame_ranges_cover_clip():
         multi.frame_range(10, 2, 2)
     with pytest.raises(ValueError):
         multi.sub_batches(0, 10, 0)
+
+
+def test_pipeline_plan_covers_each_chunk_once():
+    for n in (0, 1, 49, 50, 51, 750, 751):
+        for world in (1, 2, 3, 4, 8):
+            plan = multi.pipeline_plan(n, world)
+            assert len(plan) == -(-n // 50)
+            for k, ranges in enumerate(plan):
+                assert len(ranges) == world
+                got = sorted(r for r in ranges if r[1] > r[0])
+                f0, f1 = 50 * k, min(n, 50 * k + 50)
+                assert got[0][0] == f0 and got[-1][1] == f1
+                assert all(a[1] == b[0] for a, b in zip(got, got[1:]))
+                if world >= 3:
+                    assert ranges[0][1] == ranges[0][0]  # rank 0 only samples
+                    sizes = [hi - lo for lo, hi in ranges[1:]]
+                    assert max(sizes) - min(sizes) <= 1
+            total = sum(multi.frames_per_rank(plan, r) for r in range(world))
+            assert total == n
+    p2 = multi.pipeline_plan(750, 2)
+    assert multi.frames_per_rank(p2, 0) == 100 and multi.frames_per_rank(p2, 1) == 650
+    assert [multi.frames_per_rank(multi.pipeline_plan(750, 8), r) for r in range(8)] == [0, 108] + [107] * 6
+    with pytest.raises(ValueError):
+        multi.pipeline_plan(10, 0)
 
 
 def _free_port():
@@ -71,6 +97,86 @@ def _run(mode):
         if p.is_alive():
             p.kill()
     return sorted(out)
+
+
+class _FakeDecoder:
+    """decode_ptr writes each frame's style[0] into the first float of the
+    frame; the feats arena is a small byte tensor."""
+
+    def __init__(self, rank):
+        self.feats = torch.arange(64, dtype=torch.uint8) if rank == 0 else torch.zeros(64, dtype=torch.uint8)
+        self.adopted = False
+
+    def adopt_arena(self, which):
+        self.adopted = which == 1
+
+    def decode_ptr(self, sp, n, op):
+        import ctypes
+        import numpy as np
+        st = np.ctypeslib.as_array((ctypes.c_float * (n * 512)).from_address(sp)).reshape(n, 512)
+        for i in range(n):
+            ctypes.c_float.from_address(op + i * multi.FRAME_BYTES).value = float(st[i, 0])
+
+
+class _FakePipeline:
+    """styles_cb over `n` frames in chunks of `chunk`: style of frame t is t."""
+
+    def __init__(self, n, chunk):
+        self.n, self.chunk = n, chunk
+
+    def styles_cb(self, image, audio, emotion, cb, noise=None, seed=0):
+        import numpy as np
+        for f0 in range(0, self.n, self.chunk):
+            f1 = min(self.n, f0 + self.chunk)
+            st = np.repeat(np.arange(f0, f1, dtype=np.float32)[:, None], 512, axis=1)
+            if cb(f0, st):
+                break
+        return self.n
+
+
+def _pipe_worker(rank, world, port, n, chunk, q):
+    import datetime
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    try:
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=20))
+        multi.arena_tensor = lambda dec, which, device: dec.feats
+        multi.FRAME_BYTES = 16  # a 4-float frame keeps the buffers small
+        dec = _FakeDecoder(rank)
+        plan = multi.pipeline_plan(n, world, chunk)
+        m = max(multi.frames_per_rank(plan, rank), 1)
+        frames = torch.zeros((m, 4))
+        got = multi.generate_pipelined(rank, world, "cpu", n, dec, frames,
+                                       pipe=_FakePipeline(n, chunk) if rank == 0 else None, chunk=chunk)
+        marks = [float(frames[i, 0]) for i in range(got)]
+        feats_ok = bool(torch.equal(dec.feats, torch.arange(64, dtype=torch.uint8))) and (rank == 0 or dec.adopted)
+        q.put((rank, "ok", marks, feats_ok))
+        dist.destroy_process_group()
+    except Exception as e:
+        q.put((rank, "error", type(e).__name__ + ": " + str(e)[:300], None))
+
+
+@pytest.mark.parametrize("world,n", [(1, 23), (2, 71), (3, 23), (4, 95)])
+def test_pipelined_generation_gloo(world, n):
+    chunk = 10
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_pipe_worker, args=(r, world, port, n, chunk, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = sorted(q.get(timeout=180) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert all(o[1] == "ok" for o in out), out
+    plan = multi.pipeline_plan(n, world, chunk)
+    for rank, _, marks, feats_ok in out:
+        want = [float(t) for ranges in plan for lo, hi in (ranges[rank],) for t in range(lo, hi)]
+        assert marks == want, (rank, marks, want)
+        assert feats_ok
+    assert sorted(m for o in out for m in o[2]) == [float(t) for t in range(n)]
 
 
 def test_broadcast_and_max_over_ranks_gloo():
