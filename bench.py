@@ -586,7 +586,7 @@ def main():
     roof["traffic"] = traffic
     roof["algorithmic_bytes"] = byts
     kernels = {k: {"launches": v[0], "ms": round(v[1], 4), "share": round(v[1] / total, 4)}
-               for k, v in sorted(prof.items(), key=lambda kv: -kv[1][1])[:8]}
+               for k, v in sorted(prof.items(), key=lambda kv: -kv[1][1])}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

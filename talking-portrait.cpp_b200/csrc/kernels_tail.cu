@@ -15,7 +15,9 @@
 //
 // Mapping: a pixel is handled by G = OC/CPL lanes, each owning CPL
 // consecutive channels; 32/G pixels per warp. Channel sums (ToFlow, ToRGB)
-// reduce across the G lanes with xor shuffles.
+// reduce across the G lanes with xor shuffles. The ToFlow and ToRGB weights
+// sit in shared memory lane-interleaved, [k][c][lane of the group], so the
+// lanes of a warp read consecutive words (no bank conflicts).
 #include "tpmd_internal.h"
 
 #include <algorithm>
@@ -67,22 +69,35 @@ struct chans<__half, CPL> {
     }
 };
 
-// upfirdn2d(up=2, pad=(2,1)) of one h x h plane at output (x, y), in the
-// reference op's tap order (patch:559-569)
+// upfirdn2d(up=2, pad=(2,1)) of an h x h plane at output (x, y): of the
+// 4x4 kernel only the taps of (x, y)'s parity meet source pixels, so four
+// taps (source pixel, kernel index) serve every plane of the pixel, in the
+// reference op's tap order (patch:559-569). Taps outside the plane read
+// pixel 0 with weight 0.
+struct up_taps {
+    int off[4];  // source pixel sy * h + sx
+    int k[4];    // kernel index, -1 outside the plane
+};
+__device__ __forceinline__ up_taps up2x_taps(int x, int y, int h) {
+    up_taps t;
+    const int px = x & 1, py = y & 1, nx = x >> 1, ny = y >> 1;
+#pragma unroll
+    for (int a = 0; a < 2; a++)
+#pragma unroll
+        for (int bb = 0; bb < 2; bb++) {
+            const int sy = ny + py - 1 + a, sx = nx + px - 1 + bb;
+            const bool in = sy >= 0 && sy < h && sx >= 0 && sx < h;
+            t.off[2 * a + bb] = in ? sy * h + sx : 0;
+            t.k[2 * a + bb] = in ? (px + 2 * bb) + 4 * (py + 2 * a) : -1;
+        }
+    return t;
+}
 __device__ __forceinline__ float up2x(const float *__restrict__ src, const float *__restrict__ k4,
-                                      int x, int y, int h) {
+                                      const up_taps &t) {
     float acc = 0.0f;
 #pragma unroll
-    for (int j = 0; j < 4; j++) {
-        const int vy = y + j - 2;
-        if (vy < 0 || vy >= 2 * h || (vy & 1)) continue;
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const int vx = x + i - 2;
-            if (vx < 0 || vx >= 2 * h || (vx & 1)) continue;
-            acc = fmaf(__ldg(src + (vy >> 1) * h + (vx >> 1)), __ldg(k4 + i + 4 * j), acc);
-        }
-    }
+    for (int i = 0; i < 4; i++)
+        acc = fmaf(__ldg(src + t.off[i]), t.k[i] >= 0 ? __ldg(k4 + t.k[i]) : 0.0f, acc);
     return acc;
 }
 
@@ -96,12 +111,14 @@ __device__ __forceinline__ float group_sum(float v) {
 template <typename T, int CPL, int G>
 __global__ void __launch_bounds__(256) tail_kernel(tail_params p) {
     constexpr int PW = 32 / G;  // pixels per warp
-    __shared__ __align__(16) float s_fw[3][512];
-    __shared__ __align__(16) float s_rw[3][512];
+    __shared__ __align__(16) float s_fw[3 * 512];  // [k][c][g]: weight k of channel g*CPL + c
+    __shared__ __align__(16) float s_rw[3 * 512];
     const int OC = p.OC, r = p.r;
-    for (int i = threadIdx.x; i < 3 * OC; i += blockDim.x) {
-        s_fw[i / OC][i % OC] = p.fW[i];
-        s_rw[i / OC][i % OC] = p.rW[i];
+    for (int i = threadIdx.x; i < 3 * OC; i += blockDim.x) {  // i = (k * CPL + c) * G + g
+        const int g = i % G, c = (i / G) % CPL, k = i / (G * CPL);
+        const int src = k * OC + g * CPL + c;
+        s_fw[i] = __ldg(p.fW + src);
+        s_rw[i] = __ldg(p.rW + src);
     }
     __syncthreads();
 
@@ -111,6 +128,7 @@ __global__ void __launch_bounds__(256) tail_kernel(tail_params p) {
     const int64_t rr = (int64_t) r * r;
     const int64_t npix = (int64_t) p.B * rr;
     const int h = r / 2;
+    const int lg = __ffs(r) - 1;  // r is a power of two
     const int64_t warp0 = ((int64_t) blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int64_t nwarps = ((int64_t) gridDim.x * blockDim.x) >> 5;
     const T *outp = (const T *) p.out;
@@ -118,9 +136,10 @@ __global__ void __launch_bounds__(256) tail_kernel(tail_params p) {
 
     for (int64_t base = warp0 * PW; base < npix; base += nwarps * PW) {
         const int64_t pix = base + grp;  // npix is a multiple of PW
-        const int64_t b = pix / rr;
-        const int pr = (int) (pix - b * rr);
-        const int y = pr / r, x = pr - (pr / r) * r;
+        const int64_t b = pix >> (2 * lg);
+        const int pr = (int) (pix & (rr - 1));
+        const int y = pr >> lg, x = pr & (r - 1);
+        const up_taps ut = up2x_taps(x, y, h);
 
         float o[CPL], fs[CPL];
         chans<T, CPL>::load(outp + pix * OC + c0, o);
@@ -129,16 +148,16 @@ __global__ void __launch_bounds__(256) tail_kernel(tail_params p) {
 #pragma unroll
         for (int c = 0; c < CPL; c++) {
             const float xs = o[c] * fs[c];
-            f0 = fmaf(s_fw[0][c0 + c], xs, f0);
-            f1 = fmaf(s_fw[1][c0 + c], xs, f1);
-            f2 = fmaf(s_fw[2][c0 + c], xs, f2);
+            f0 = fmaf(s_fw[c * G + gl], xs, f0);
+            f1 = fmaf(s_fw[(CPL + c) * G + gl], xs, f1);
+            f2 = fmaf(s_fw[(2 * CPL + c) * G + gl], xs, f2);
         }
         float fl[3] = {group_sum<G>(f0), group_sum<G>(f1), group_sum<G>(f2)};
 #pragma unroll
         for (int k = 0; k < 3; k++) {
             fl[k] += __ldg(p.fb + k);
             if (p.skipf_prev)
-                fl[k] += up2x(p.skipf_prev + (b * 3 + k) * (int64_t) h * h, p.fup, x, y, h);
+                fl[k] += up2x(p.skipf_prev + (b * 3 + k) * (int64_t) h * h, p.fup, ut);
         }
         if (p.skipf_out && gl == 0) {
 #pragma unroll
@@ -174,9 +193,9 @@ __global__ void __launch_bounds__(256) tail_kernel(tail_params p) {
 #pragma unroll
         for (int c = 0; c < CPL; c++) {
             const float w = smp[c] * m;
-            g0 = fmaf(s_rw[0][c0 + c], w, g0);
-            g1 = fmaf(s_rw[1][c0 + c], w, g1);
-            g2 = fmaf(s_rw[2][c0 + c], w, g2);
+            g0 = fmaf(s_rw[c * G + gl], w, g0);
+            g1 = fmaf(s_rw[(CPL + c) * G + gl], w, g1);
+            g2 = fmaf(s_rw[(2 * CPL + c) * G + gl], w, g2);
             smp[c] = w + o[c] * om;  // trunk
         }
         float rg[3] = {group_sum<G>(g0), group_sum<G>(g1), group_sum<G>(g2)};
@@ -185,7 +204,7 @@ __global__ void __launch_bounds__(256) tail_kernel(tail_params p) {
             for (int k = 0; k < 3; k++) {
                 float v = rg[k] + __ldg(p.rlb + k);
                 v = (v > 0.0f ? v : 0.2f * v) + __ldg(p.rb + k);
-                if (p.skip_prev) v += up2x(p.skip_prev + (b * 3 + k) * (int64_t) h * h, p.rup, x, y, h);
+                if (p.skip_prev) v += up2x(p.skip_prev + (b * 3 + k) * (int64_t) h * h, p.rup, ut);
                 p.skip_out[(b * 3 + k) * rr + pr] = v;
             }
         }
@@ -203,8 +222,11 @@ template <typename T, int CPL, int G>
 cudaError_t run_tail(const tail_params &p, cudaStream_t st) {
     constexpr int PW = 32 / G;
     const int64_t npix = (int64_t) p.B * p.r * p.r;
+    if (p.r < 2 || (p.r & (p.r - 1))) return cudaErrorInvalidValue;
     const int64_t warps = (npix + PW - 1) / PW;
-    const int blocks = (int) std::min<int64_t>((warps + 7) / 8, 148 * 8);
+    // resident blocks only (3 per SM at this kernel's registers): each block
+    // stages the weights once and strides over the pixels
+    const int blocks = (int) std::min<int64_t>((warps + 7) / 8, 148 * 3);
     tail_kernel<T, CPL, G><<<blocks, 256, 0, st>>>(p);
     return cudaGetLastError();
 }
