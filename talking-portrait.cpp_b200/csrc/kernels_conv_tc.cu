@@ -41,6 +41,7 @@ struct tc_params {
     int lg_x, lg_y, lg_n;      // their log2
     int lg_oc;                 // log2 of OC (sub-pixel class of column n = n >> lg_oc)
     int num_tiles;
+    int yb, strips;            // KHS: output rows per work unit, units per column of the map
     __half *y;
     const float *inv_den;
     int den_stride;
@@ -62,7 +63,7 @@ struct tc_params {
     const float4 *proj;  // last level: ToRGB conv.0 applied to the feats per pixel
 };
 
-template <int BN, int KC, int NACC, bool TAIL, bool BRES, bool HALO = false, int RPS = 1>
+template <int BN, int KC, int NACC, bool TAIL, bool BRES, bool HALO = false, int RPS = 1, bool KHS = false>
 struct tc_cfg {
     static constexpr int A_TAP = BM * KC * 2;   // one tap's A tile
     static constexpr int B_TAP = BN * KC * 2;   // one tap's B tile
@@ -98,19 +99,34 @@ struct tc_cfg {
     // tcgen05.commit per two stages)
     static constexpr int STAGES = ((BUDGET / STAGE_BYTES) > 20 ? 20 : (BUDGET / STAGE_BYTES)) & ~1;
     static constexpr int B_REGION = BRES ? B_RES : STAGES * B_BYTES;
-    static constexpr uint32_t TMEM_COLS = NACC * BN;  // one accumulator per epilogue group
+    // KHS (kernel rows stacked in N): a work unit is a strip of output rows of
+    // one 128-pixel column segment; each input row is one halo box, multiplied
+    // by the three kernel rows' weights side by side (N = 3 BN). Block j of
+    // the product belongs to output row yi - 1 + j, so the accumulators of
+    // consecutive output rows live in a ring of R = 512 / BN TMEM slots and
+    // each output row is complete after the next input row. Slots are zeroed
+    // by the epilogue after use, so every MMA accumulates.
+    static constexpr int R = KHS ? 512 / BN : 0;
+    static constexpr int NSLOT = KHS ? R : NACC;  // accumulators with their own full/empty barriers
+    static constexpr uint32_t TMEM_COLS = KHS ? 512 : NACC * BN;  // one accumulator per epilogue group
     static constexpr int THREADS = 64 + 128 * NACC;
     static constexpr uint32_t LAYOUT = KC == 64 ? 2u : 4u;
     static constexpr uint32_t SBO = KC == 64 ? 1024u : 512u;
     // kind::f16 instruction descriptor: D f32, A/B f16, both K-major, N, M
     static constexpr uint32_t IDESC =
         (1u << 4) | ((uint32_t) (BN >> 3) << 17) | ((uint32_t) (BM >> 4) << 24);
-    static constexpr int NBARS = 2 * STAGES + 2 * NACC + 2;
+    // the same with N = nb * BN (KHS: nb stacked kernel rows)
+    static __device__ __forceinline__ uint32_t idesc_n(int nb) {
+        return (1u << 4) | ((uint32_t) ((nb * BN) >> 3) << 17) | ((uint32_t) (BM >> 4) << 24);
+    }
+    static constexpr int NBARS = 2 * STAGES + 2 * NSLOT + 2;
     static constexpr int SMEM = 1024 + STAGES * A_BYTES + B_REGION + EXTRA + NBARS * 8 + 16;
     static_assert((TMEM_COLS & (TMEM_COLS - 1)) == 0 && TMEM_COLS >= 32 && TMEM_COLS <= 512, "TMEM");
     static_assert(SMEM <= 232448, "shared memory");
     static_assert(STAGES >= 2, "pipeline depth");
     static_assert(RPS == 1 || (RPS == 3 && HALO && BRES), "rows per stage");
+    static_assert(!KHS || (TAIL && HALO && BRES && RPS == 1 && (BN == 32 || BN == 64) && R % NACC == 0),
+                  "stacked kernel rows");
 };
 
 struct tile_pos {
@@ -169,11 +185,19 @@ __device__ __forceinline__ void st_half16(__half *p, const float *v) {
     q[1] = pk[1];
 }
 
-template <int BN, int KC, bool UP, int NACC, bool TAIL, bool BRES, bool HALO, int RPS>
-__global__ void __launch_bounds__(tc_cfg<BN, KC, NACC, TAIL, BRES, HALO, RPS>::THREADS, 1)
+// KHS work unit t: (frame, strip of p.yb output rows, 128-pixel segment)
+__device__ __forceinline__ void unit_of(const tc_params &p, int t, int &b, int &y0, int &x0) {
+    const int xs = t % p.tiles_x, m = t / p.tiles_x;
+    x0 = xs * BM;
+    y0 = (m % p.strips) * p.yb;
+    b = m / p.strips;
+}
+
+template <int BN, int KC, bool UP, int NACC, bool TAIL, bool BRES, bool HALO, int RPS, bool KHS>
+__global__ void __launch_bounds__(tc_cfg<BN, KC, NACC, TAIL, BRES, HALO, RPS, KHS>::THREADS, 1)
 conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const tc_params p) {
-    using cfg = tc_cfg<BN, KC, NACC, TAIL, BRES, HALO, RPS>;
+    using cfg = tc_cfg<BN, KC, NACC, TAIL, BRES, HALO, RPS, KHS>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = (uint8_t *) (((uintptr_t) smem_raw + 1023) & ~(uintptr_t) 1023);
     uint8_t *sA = smem;
@@ -182,19 +206,20 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     uint64_t *bars = (uint64_t *) (sB + cfg::B_REGION + cfg::EXTRA);
     uint32_t *tmem_slot = (uint32_t *) (bars + cfg::NBARS);
     auto full = [&](int s) { return smem_u32(&bars[s]); };
-    auto empty = [&](int s) { return smem_u32(&bars[cfg::STAGES + (s >> 1)]); };  // per stage pair
+    // per stage pair (KHS: per stage)
+    auto empty = [&](int s) { return smem_u32(&bars[cfg::STAGES + (KHS ? s : (s >> 1))]); };
     auto tfull = [&](int a) { return smem_u32(&bars[2 * cfg::STAGES + a]); };
-    auto tempty = [&](int a) { return smem_u32(&bars[2 * cfg::STAGES + NACC + a]); };
-    const uint32_t drain = smem_u32(&bars[2 * cfg::STAGES + 2 * NACC]);
-    const uint32_t bres_bar = smem_u32(&bars[2 * cfg::STAGES + 2 * NACC + 1]);
+    auto tempty = [&](int a) { return smem_u32(&bars[2 * cfg::STAGES + cfg::NSLOT + a]); };
+    const uint32_t drain = smem_u32(&bars[2 * cfg::STAGES + 2 * cfg::NSLOT]);
+    const uint32_t bres_bar = smem_u32(&bars[2 * cfg::STAGES + 2 * cfg::NSLOT + 1]);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         for (int s = 0; s < cfg::STAGES; s++) {
             mbar_init(full(s), 1);
-            if (!(s & 1)) mbar_init(empty(s), 1);
+            if (KHS || !(s & 1)) mbar_init(empty(s), 1);
         }
-        for (int a = 0; a < NACC; a++) {
+        for (int a = 0; a < cfg::NSLOT; a++) {
             mbar_init(tfull(a), 1);
             mbar_init(tempty(a), 4);
         }
@@ -221,6 +246,18 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    if constexpr (KHS) {
+        // every ring slot starts at zero: the first epilogue group clears TMEM
+        if (warp >= 2 && warp < 6) {
+            const uint32_t lanes = (uint32_t) ((warp & 3) * 32) << 16;
+            const uint32_t z[16] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+            for (int c = 0; c < (int) cfg::TMEM_COLS; c += 16) tmem_st16(tmem_base + lanes + (uint32_t) c, z);
+            tmem_wait_st();
+        }
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+    }
 
     if (warp == 0) {
         if (lane == 0) {
@@ -231,9 +268,34 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             bool ok = true;
             const uint32_t sA0 = smem_u32(sA), sB0 = smem_u32(sB);
             if (BRES) {  // the nine weight taps, once
+                // (KHS: slot kw*3 + j holds kernel row 2 - j of column kw, so the
+                // three kernel rows of a column are one N = 3 BN operand)
                 mbar_expect_tx(bres_bar, cfg::B_RES);
-                for (int i = 0; i < 9; i++) tma_load_2d(sB0 + i * cfg::B_TAP, &tmB, bres_bar, i * p.IC, 0);
+                for (int i = 0; i < 9; i++) {
+                    const int tap = KHS ? (2 - i % 3) * 3 + i / 3 : i;
+                    tma_load_2d(sB0 + i * cfg::B_TAP, &tmB, bres_bar, tap * p.IC, 0);
+                }
             }
+            if constexpr (KHS) {  // one halo box per input row of each unit
+                for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+                    int b, y0, x0;
+                    unit_of(p, t, b, y0, x0);
+                    for (int yi = y0 - 1; yi <= y0 + p.yb; yi++) {
+                        if (yi < 0 || yi >= p.H) continue;  // zero padding rows: neither load nor MMA
+                        if (!mbar_wait(empty(s), ph ^ 1)) {
+                            ok = false;
+                            break;
+                        }
+                        mbar_expect_tx(full(s), cfg::STAGE_TX);
+                        tma_load_4d(sA0 + s * cfg::A_BYTES, &tmA, full(s), 0, x0 - 1, yi, b);
+                        it++;
+                        if (++s == cfg::STAGES) {
+                            s = 0;
+                            ph ^= 1;
+                        }
+                    }
+                }
+            } else
             for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
                 const tile_pos tp = tile_of(p, t, BN);
                 for (int kh = 0; kh < 3 && ok; kh += RPS) {
@@ -290,6 +352,59 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             const uint64_t ad0 = smem_desc(smem_u32(sA), cfg::SBO, cfg::LAYOUT);
             const uint64_t bd0 = smem_desc(smem_u32(sB), cfg::SBO, cfg::LAYOUT);
             if (BRES && !mbar_wait(bres_bar, 0)) ok = false;
+            if constexpr (KHS) {
+                // output row rc of this CTA (counted over its units) accumulates
+                // in slot rc % R, its (rc / R)-th use
+                uint32_t rc0 = 0;
+                for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+                    int b, y0, x0;
+                    unit_of(p, t, b, y0, x0);
+                    const int yend = y0 + p.yb;
+                    for (int yi = y0 - 1; yi <= yend; yi++) {
+                        if (yi + 1 < yend) {  // row yi + 1 is first touched here: its slot must be free
+                            const uint32_t rc = rc0 + (uint32_t) (yi + 1 - y0);
+                            if (rc >= (uint32_t) cfg::R &&
+                                !mbar_wait(tempty(rc % cfg::R), ((rc / cfg::R) - 1) & 1)) {
+                                ok = false;
+                                break;
+                            }
+                            tc_fence_after();  // the epilogue's clearing stores come first
+                        }
+                        if (yi >= 0 && yi < p.H) {
+                            if (!mbar_wait(full(s), ph)) {
+                                ok = false;
+                                break;
+                            }
+                            tc_fence_after();
+                            // blocks j = jlo..jhi: the output rows yi - 1 + j of this strip,
+                            // in consecutive slots except where the ring wraps
+                            const int jlo = max(0, y0 - (yi - 1)), jhi = min(2, yend - yi);
+                            const int nb = jhi - jlo + 1;
+                            const uint32_t sl = (rc0 + (uint32_t) (yi - 1 + jlo - y0)) % cfg::R;
+                            const int n1 = min(nb, cfg::R - (int) sl);
+                            const uint64_t ad = ad0 + (uint64_t) ((s * cfg::A_BYTES) >> 4);
+#pragma unroll
+                            for (int kw = 0; kw < 3; kw++)
+#pragma unroll
+                                for (int kx = 0; kx < KC / 16; kx++) {  // +32 bytes along K per step
+                                    const uint64_t a_d = ad + ((kw * KC * 2) >> 4) + 2 * kx;
+                                    const uint64_t b_d = bd0 + (((kw * 3 + jlo) * cfg::B_TAP) >> 4) + 2 * kx;
+                                    umma_f16(tmem_base + sl * BN, a_d, b_d, cfg::idesc_n(n1), 1);
+                                    if (n1 < nb)
+                                        umma_f16(tmem_base, a_d, b_d + ((n1 * cfg::B_TAP) >> 4), cfg::idesc_n(nb - n1), 1);
+                                }
+                            umma_commit(empty(s));
+                            if (++s == cfg::STAGES) {
+                                s = 0;
+                                ph ^= 1;
+                            }
+                        }
+                        if (yi - 1 >= y0)  // output row yi - 1 has all its contributions
+                            umma_commit(tfull((rc0 + (uint32_t) (yi - 1 - y0)) % cfg::R));
+                    }
+                    rc0 += (uint32_t) p.yb;
+                }
+            } else
             for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
                 if (!mbar_wait(tempty(a), aph ^ 1)) {
                     ok = false;
@@ -339,11 +454,11 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         const int q = warp & 3;
         const int row = q * 32 + lane;
         const int bx = row % p.bw, by = (row / p.bw) % p.bh, bz = row / (p.bw * p.bh);
-        const uint32_t taddr0 = tmem_base + ((uint32_t) (q * 32) << 16) + g * BN;
+        const uint32_t lanes = (uint32_t) (q * 32) << 16;
         const float *s_fw = sx, *s_up = sx + 3 * BN;
-        uint32_t k = g;
-        for (int t = blockIdx.x + g * gridDim.x; t < p.num_tiles; t += NACC * gridDim.x, k += NACC) {
-            const tile_pos tp = tile_of(p, t, BN);
+        // one tile's epilogue: its accumulator at taddr0 is complete once
+        // barrier `bar` finishes phase `par`; false if that wait timed out
+        auto tile_body = [&](const tile_pos &tp, uint32_t taddr0, uint32_t bar, uint32_t par) -> bool {
             const int b = tp.b0 + bz, y = tp.y0 + by, x = tp.x0 + bx;
             // TAIL: the up-sampled flow and rgb skips depend on the pixel only;
             // their loads are issued before the wait for the accumulator
@@ -385,10 +500,10 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     }
                 }
             }
-            const bool ok = __all_sync(0xffffffffu, mbar_wait(tfull(g), (k / NACC) & 1));
+            const bool ok = __all_sync(0xffffffffu, mbar_wait(bar, par));
             if (!ok) {
                 if (lane == 0) atomicExch(p.err, 1);
-                break;
+                return false;
             }
             tc_fence_after();
             if constexpr (!TAIL) {
@@ -556,9 +671,44 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     p.skip_out[((int64_t) b * 3 + kk) * rr2 + (int64_t) y * r + x] = v;
                 }
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(tempty(g));
+            return true;
+        };
+        if constexpr (KHS) {
+            // group g takes the output rows rc = g, g + NACC, ... of the CTA's units
+            // (p.yb is a multiple of NACC); after each row it clears the row's slot
+            const uint32_t z[16] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+            uint32_t rc0 = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+                tile_pos tp;
+                tp.n0 = 0;
+                unit_of(p, t, tp.b0, tp.y0, tp.x0);
+                const int y0 = tp.y0;
+                for (int i = g; i < p.yb; i += NACC) {
+                    const uint32_t rc = rc0 + (uint32_t) i, sl = rc % cfg::R;
+                    const uint32_t slot = tmem_base + lanes + sl * BN;
+                    tp.y0 = y0 + i;
+                    if (!tile_body(tp, slot, tfull(sl), (rc / cfg::R) & 1)) {
+                        ok = false;
+                        break;
+                    }
+#pragma unroll
+                    for (int c0 = 0; c0 < BN; c0 += 16) tmem_st16(slot + c0, z);
+                    tmem_wait_st();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(tempty(sl));
+                }
+                rc0 += (uint32_t) p.yb;
+            }
+        } else {
+            uint32_t k = g;
+            for (int t = blockIdx.x + g * gridDim.x; t < p.num_tiles; t += NACC * gridDim.x, k += NACC) {
+                if (!tile_body(tile_of(p, t, BN), tmem_base + lanes + g * BN, tfull(g), (k / NACC) & 1)) break;
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(tempty(g));
+            }
         }
     }
     tc_fence_before();
@@ -579,9 +729,10 @@ int ilog2(int v) {  // log2 of a power of two, else -1
 }
 
 
-template <int BN, int KC, bool UP, int NACC, bool TAIL, bool BRES = false, bool HALO = false, int RPS = 1>
+template <int BN, int KC, bool UP, int NACC, bool TAIL, bool BRES = false, bool HALO = false, int RPS = 1,
+          bool KHS = false>
 cudaError_t run_tc(const conv_params &cp, const tail_params *tl, cudaStream_t st) {
-    using cfg = tc_cfg<BN, KC, NACC, TAIL, BRES, HALO, RPS>;
+    using cfg = tc_cfg<BN, KC, NACC, TAIL, BRES, HALO, RPS, KHS>;
     auto enc = encode_fn();
     if (!enc) return cudaErrorNotSupported;
     tc_params p{};
@@ -606,7 +757,20 @@ cudaError_t run_tc(const conv_params &cp, const tail_params *tl, cudaStream_t st
     if (p.lg_x < 0 || p.lg_y < 0 || p.lg_n < 0 || p.lg_oc < 0 || p.N % BN) return cudaErrorInvalidValue;
     if (UP && (BN % 16 || (BN > cp.OC && BN % cp.OC))) return cudaErrorInvalidValue;
     const int tiles_b = (cp.B + p.bb - 1) / p.bb;
-    const int64_t nt = (int64_t) tiles_b * p.tiles_y * p.tiles_x * p.tiles_n;
+    int64_t nt = (int64_t) tiles_b * p.tiles_y * p.tiles_x * p.tiles_n;
+    if (KHS) {
+        // units of yb output rows: the longest strips that still give every SM
+        // at least 8 units (the row count per CTA then differs by a few percent)
+        if (p.bw != BM || cp.W % BM || cp.H % 8) return cudaErrorInvalidValue;
+        p.yb = 8;
+        for (int c = 32; c > 8; c >>= 1)
+            if (cp.H % c == 0 && (int64_t) cp.B * (cp.H / c) * p.tiles_x >= 8 * sm_count()) {
+                p.yb = c;
+                break;
+            }
+        p.strips = cp.H / p.yb;
+        nt = (int64_t) cp.B * p.strips * p.tiles_x;
+    }
     if (nt >= (1ll << 30)) return cudaErrorInvalidValue;
     p.num_tiles = (int) nt;
     if (BRES && (p.cpt != 1 || p.tiles_n != 1)) return cudaErrorInvalidValue;  // 9 taps x 1 chunk, 1 N tile
@@ -673,13 +837,13 @@ cudaError_t run_tc(const conv_params &cp, const tail_params *tl, cudaStream_t st
     int dev = 0;
     cudaGetDevice(&dev);
     if (!(attr_set >> (dev & 63) & 1)) {
-        const cudaError_t e = cudaFuncSetAttribute(conv_tc_kernel<BN, KC, UP, NACC, TAIL, BRES, HALO, RPS>,
+        const cudaError_t e = cudaFuncSetAttribute(conv_tc_kernel<BN, KC, UP, NACC, TAIL, BRES, HALO, RPS, KHS>,
                                                    cudaFuncAttributeMaxDynamicSharedMemorySize, cfg::SMEM);
         if (e != cudaSuccess) return e;
         attr_set |= 1ull << (dev & 63);
     }
     const int grid = (int) (p.num_tiles < sm_count() ? p.num_tiles : sm_count());
-    conv_tc_kernel<BN, KC, UP, NACC, TAIL, BRES, HALO, RPS><<<grid, cfg::THREADS, cfg::SMEM, st>>>(tmA, tmB, p);
+    conv_tc_kernel<BN, KC, UP, NACC, TAIL, BRES, HALO, RPS, KHS><<<grid, cfg::THREADS, cfg::SMEM, st>>>(tmA, tmB, p);
     return cudaGetLastError();
 }
 
@@ -717,10 +881,10 @@ cudaError_t launch_conv_tail_tc(const conv_params &p, const tail_params &t, cuda
     if (!conv_tail_tc_supported(p.IC, p.OC, p.W) || !p.err || p.H != p.W) return cudaErrorInvalidValue;
     const bool halo = p.W >= BM;  // one-row tiles: taps share a halo box
     switch (p.OC) {
-        case 32:
-            return halo ? run_tc<32, 32, false, 4, true, true, true, 3>(p, &t, st)
+        case 32:  // halo: kernel rows stacked in N, row accumulators in a TMEM ring
+            return halo ? run_tc<32, 32, false, 4, true, true, true, 1, true>(p, &t, st)
                         : run_tc<32, 32, false, 4, true, true>(p, &t, st);
-        case 64:
+        case 64:  // (stacked kernel rows measured slower here: 6 one-row stages)
             return halo ? run_tc<64, 64, false, 4, true, true, true, 3>(p, &t, st)
                         : run_tc<64, 64, false, 4, true>(p, &t, st);
         case 128:
