@@ -860,6 +860,14 @@ cudaError_t launch_conv_tc(bool up, const conv_params &p, cudaStream_t st) {
     const int N = up ? 4 * p.OC : p.OC;
     if (!conv_tc_supported(up, p.IC, p.OC) || !p.err) return cudaErrorInvalidValue;
     if (p.IC == 32) return run_tc<32, 32, false, 4, false>(p, nullptr, st);
+    // 128-pixel M tiles, as run_tc forms them
+    const int bw = p.W < BM ? p.W : BM, bh = p.H < BM / bw ? p.H : BM / bw, bb = BM / (bw * bh);
+    const int64_t m_tiles = (int64_t) ((p.B + bb - 1) / bb) * (p.H / bh) * (p.W / bw);
+    // the small early levels (4x4 .. 8x8 maps) leave most SMs idle with
+    // 256-wide N tiles; 128-wide ones double the tile count at the same K
+    if (N >= 256 && m_tiles * (N / 256) < sm_count())
+        return up ? run_tc<128, 64, true, 4, false>(p, nullptr, st)
+                  : run_tc<128, 64, false, 4, false>(p, nullptr, st);
     if (N >= 256)
         return up ? run_tc<256, 64, true, 2, false>(p, nullptr, st)
                   : run_tc<256, 64, false, 2, false>(p, nullptr, st);

@@ -9,85 +9,100 @@
 //          folds the FusedLeakyReLU sqrt(2));
 //  conv1:  x0[b][p][c] = input[p][c] * s_conv1[b][c] (src/motion_dec.cpp:375-384).
 //
-// Both reductions are one warp per output row: the row (512 or IC+1 floats)
-// sits in registers, read once, and is reused for every frame of the batch,
-// so the weight stream is read once per batch, coalesced.
+// Both reductions are small f32 GEMMs (rows x frames x K <= 512). One
+// register-tiled kernel serves both: a block owns 64 rows x 64 frames, K is
+// staged through shared memory 32 at a time, and each thread accumulates a
+// 4 x 4 outer product (rows o0 + tx + 16 i, frames b0 + 4 ty + j) in K order.
+// Shared reads are conflict-free or broadcast; stores are coalesced along
+// rows.
 #include "tpmd_internal.h"
 
 namespace tpmd {
 namespace {
 
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
-}
+constexpr int PT = 64, PK = 32;  // tile rows and frames, K per stage
 
+// DEN = false: s_all[b][o] = W[o] . lat[b] + bmod[o] (W [rows][512]).
+// DEN = true:  per conv (a tile never spans two), inv_den[b][d_off + o] =
+//              1 / sqrt(S_aug[o][:IC] . s[b]^2 + S_aug[o][IC]).
+template <bool DEN>
 __global__ void __launch_bounds__(256)
-style_kernel(const float *__restrict__ wmod, const float *__restrict__ bmod, int rows,
-             const float *__restrict__ lat, int B, float *__restrict__ s_all) {
-    const int lane = threadIdx.x & 31;
-    const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    if (row >= rows) return;
-    float w[STYLE_DIM / 32];
-#pragma unroll
-    for (int i = 0; i < STYLE_DIM / 32; i++) w[i] = __ldg(wmod + (int64_t) row * STYLE_DIM + lane + 32 * i);
-    const float bias = __ldg(bmod + row);
-    // four frames per pass: independent loads and reductions overlap
-    for (int b0 = 0; b0 < B; b0 += 4) {
-        float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-        for (int f = 0; f < 4; f++) {
-            if (b0 + f >= B) continue;
-            const float *l = lat + (int64_t) (b0 + f) * STYLE_DIM;
-#pragma unroll
-            for (int i = 0; i < STYLE_DIM / 32; i++) a[f] = fmaf(w[i], __ldg(l + lane + 32 * i), a[f]);
+prologue_gemm_kernel(const float *__restrict__ w, const float *__restrict__ bmod, int rows,
+                     const float *__restrict__ a, int a_stride, int B, den_table t, float *__restrict__ out,
+                     int out_stride) {
+    __shared__ float Ws[PT][PK + 1], As[PT][PK + 1];
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    const int b0 = blockIdx.y * PT;
+    // the tile's rows: [o0, o0 + nrow) of W (stride ldw), K columns
+    int o0, nrow, K, ldw, a_off = 0, d_off = 0;
+    const float *W;
+    if (DEN) {
+        int c = 0, tile = blockIdx.x;
+        while (c < t.n) {
+            const int nt = (t.row0[c + 1] - t.row0[c] + PT - 1) / PT;
+            if (tile < nt) break;
+            tile -= nt;
+            c++;
         }
-#pragma unroll
-        for (int f = 0; f < 4; f++) a[f] = warp_sum(a[f]);
-        if (lane < 4 && b0 + lane < B) {
-            const float v = lane == 0 ? a[0] : lane == 1 ? a[1] : lane == 2 ? a[2] : a[3];
-            s_all[(int64_t) (b0 + lane) * rows + row] = v + bias;
-        }
+        if (c >= t.n) return;
+        K = t.ic[c];
+        ldw = K + 1;
+        o0 = tile * PT;
+        nrow = min(PT, t.row0[c + 1] - t.row0[c] - o0);
+        W = w + t.saug_off[c];
+        a_off = t.s_off[c];
+        d_off = t.d_off[c];
+    } else {
+        K = 512;
+        ldw = 512;
+        o0 = blockIdx.x * PT;
+        nrow = min(PT, rows - o0);
+        W = w;
     }
-}
-
-__global__ void __launch_bounds__(256)
-den_kernel(const float *__restrict__ saug, den_table t, const float *__restrict__ s_all,
-           int s_stride, int B, float *__restrict__ inv_den, int d_stride) {
-    const int lane = threadIdx.x & 31;
-    const int g = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    if (g >= t.row0[t.n]) return;
-    int c = 0;
-    while (g >= t.row0[c + 1]) c++;
-    const int o = g - t.row0[c];
-    const int IC = t.ic[c];
-    const float *r = saug + t.saug_off[c] + (int64_t) o * (IC + 1);
-    constexpr int MAXPER = 512 / 32;
-    float w[MAXPER];
-    const int per = IC / 32;  // IC is a multiple of 32 (32..512)
+    float acc[4][4];
 #pragma unroll
-    for (int i = 0; i < MAXPER; i++) w[i] = i < per ? __ldg(r + lane + 32 * i) : 0.0f;
-    const float eps = __ldg(r + IC);
-    for (int b0 = 0; b0 < B; b0 += 4) {  // four frames per pass
-        float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    for (int i = 0; i < 4; i++)
 #pragma unroll
-        for (int f = 0; f < 4; f++) {
-            if (b0 + f >= B) continue;
-            const float *s = s_all + (int64_t) (b0 + f) * s_stride + t.s_off[c];
+        for (int j = 0; j < 4; j++) acc[i][j] = 0.0f;
+    const int lk = threadIdx.x & 31, lr = threadIdx.x >> 5;  // loader: column lk, rows lr + 8 m
+    for (int k0 = 0; k0 < K; k0 += PK) {
+        const bool kin = k0 + lk < K;
 #pragma unroll
-            for (int i = 0; i < MAXPER; i++) {
-                if (i < per) {
-                    const float v = __ldg(s + lane + 32 * i);
-                    a[f] = fmaf(w[i], v * v, a[f]);
-                }
-            }
+        for (int m = 0; m < PT / 8; m++) {
+            const int r = lr + 8 * m;
+            Ws[r][lk] = (kin && r < nrow) ? __ldg(W + (int64_t) (o0 + r) * ldw + k0 + lk) : 0.0f;
+            const int b = b0 + r;
+            float v = (kin && b < B) ? __ldg(a + (int64_t) b * a_stride + a_off + k0 + lk) : 0.0f;
+            As[r][lk] = DEN ? v * v : v;
         }
+        __syncthreads();
+#pragma unroll 8
+        for (int kk = 0; kk < PK; kk++) {
+            float wv[4], av[4];
 #pragma unroll
-        for (int f = 0; f < 4; f++) a[f] = warp_sum(a[f]) + eps;
-        if (lane < 4 && b0 + lane < B) {
-            const float v = lane == 0 ? a[0] : lane == 1 ? a[1] : lane == 2 ? a[2] : a[3];
-            inv_den[(int64_t) (b0 + lane) * d_stride + t.d_off[c] + o] = 1.0f / sqrtf(v);
+            for (int i = 0; i < 4; i++) wv[i] = Ws[tx + 16 * i][kk];
+#pragma unroll
+            for (int j = 0; j < 4; j++) av[j] = As[4 * ty + j][kk];
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) acc[i][j] = fmaf(wv[i], av[j], acc[i][j]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int r = tx + 16 * i;
+        if (r >= nrow) continue;
+        const float extra = DEN ? __ldg(W + (int64_t) (o0 + r) * ldw + K) : __ldg(bmod + o0 + r);
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int b = b0 + 4 * ty + j;
+            if (b >= B) continue;
+            if (DEN)
+                out[(int64_t) b * out_stride + d_off + o0 + r] = 1.0f / sqrtf(acc[i][j] + extra);
+            else
+                out[(int64_t) b * out_stride + o0 + r] = acc[i][j] + extra;
         }
     }
 }
@@ -116,16 +131,22 @@ __global__ void conv1_input_kernel(const float *__restrict__ input, const float 
 
 cudaError_t launch_style(const float *wmod, const float *bmod, int rows, const float *lat, int B,
                          float *s_all, cudaStream_t st) {
-    const int blocks = (rows * 32 + 255) / 256;
-    style_kernel<<<blocks, 256, 0, st>>>(wmod, bmod, rows, lat, B, s_all);
+    if (rows <= 0 || B <= 0) return cudaErrorInvalidValue;
+    const dim3 grid((rows + PT - 1) / PT, (B + PT - 1) / PT);
+    prologue_gemm_kernel<false><<<grid, 256, 0, st>>>(wmod, bmod, rows, lat, STYLE_DIM, B, den_table{}, s_all, rows);
     return cudaGetLastError();
 }
 
 cudaError_t launch_den(const float *saug, const den_table &t, const float *s_all, int s_stride,
                        int B, float *inv_den, int d_stride, cudaStream_t st) {
-    const int rows = t.row0[t.n];
-    const int blocks = (rows * 32 + 255) / 256;
-    den_kernel<<<blocks, 256, 0, st>>>(saug, t, s_all, s_stride, B, inv_den, d_stride);
+    if (t.n <= 0 || B <= 0) return cudaErrorInvalidValue;
+    int tiles = 0;
+    for (int c = 0; c < t.n; c++) {
+        if (t.ic[c] <= 0 || t.ic[c] > 512) return cudaErrorInvalidValue;
+        tiles += (t.row0[c + 1] - t.row0[c] + PT - 1) / PT;
+    }
+    const dim3 grid(tiles, (B + PT - 1) / PT);
+    prologue_gemm_kernel<true><<<grid, 256, 0, st>>>(saug, nullptr, 0, s_all, s_stride, B, t, inv_den, d_stride);
     return cudaGetLastError();
 }
 
