@@ -65,17 +65,27 @@ prologue_gemm_kernel(const float *__restrict__ w, const float *__restrict__ bmod
 #pragma unroll
         for (int j = 0; j < 4; j++) acc[i][j] = 0.0f;
     const int lk = threadIdx.x & 31, lr = threadIdx.x >> 5;  // loader: column lk, rows lr + 8 m
-    for (int k0 = 0; k0 < K; k0 += PK) {
+    // the next K chunk is fetched into registers while this one is multiplied
+    float wn[PT / 8], an[PT / 8];
+    auto fetch = [&](int k0) {
         const bool kin = k0 + lk < K;
 #pragma unroll
         for (int m = 0; m < PT / 8; m++) {
+            const int r = lr + 8 * m, b = b0 + r;
+            wn[m] = (kin && r < nrow) ? __ldg(W + (int64_t) (o0 + r) * ldw + k0 + lk) : 0.0f;
+            an[m] = (kin && b < B) ? __ldg(a + (int64_t) b * a_stride + a_off + k0 + lk) : 0.0f;
+        }
+    };
+    fetch(0);
+    for (int k0 = 0; k0 < K; k0 += PK) {
+#pragma unroll
+        for (int m = 0; m < PT / 8; m++) {
             const int r = lr + 8 * m;
-            Ws[r][lk] = (kin && r < nrow) ? __ldg(W + (int64_t) (o0 + r) * ldw + k0 + lk) : 0.0f;
-            const int b = b0 + r;
-            float v = (kin && b < B) ? __ldg(a + (int64_t) b * a_stride + a_off + k0 + lk) : 0.0f;
-            As[r][lk] = DEN ? v * v : v;
+            Ws[r][lk] = wn[m];
+            As[r][lk] = DEN ? an[m] * an[m] : an[m];
         }
         __syncthreads();
+        if (k0 + PK < K) fetch(k0 + PK);
 #pragma unroll 8
         for (int kk = 0; kk < PK; kk++) {
             float wv[4], av[4];
