@@ -181,3 +181,13 @@ def test_tcgen05_matches_simt_f16(model, level):
         c = cosine(a[k], b[k])
         print(f"level {level} {k}: tc vs simt cos {c:.9f} max-abs {max_abs(a[k], b[k]):.3e}")
         assert c >= 0.9999, (level, k, c)
+
+
+def test_strip_heights_agree(model):
+    """the r512 conv2 work units are strips of 8, 16 or 32 output rows,
+    chosen from the batch size; every output row sums the same kernel rows in
+    the same order, so the frames are bit-identical"""
+    st = np.concatenate([model["styles"]] * 24)[:24]
+    st = st + 0.01 * np.arange(24, dtype=np.float32)[:, None]  # 24 distinct frames
+    outs = [make_dec(model, tpmd.DTYPE_F16, max_batch=mb).decode(st) for mb in (24, 12, 8)]
+    assert np.array_equal(outs[0], outs[1]) and np.array_equal(outs[0], outs[2])
