@@ -2,10 +2,16 @@
 // generate_impl (src/pipeline.cpp:99-186) over the four stage handles. Host
 // orchestration only; every stage runs on the GPU.
 #include <algorithm>
+#include <condition_variable>
+#include <memory>
 #include <cstdio>
 #include <cstring>
+#include <deque>
+#include <mutex>
 #include <random>
 #include <string>
+#include <thread>
+#include <utility>
 #include <vector>
 
 #include "../../include/tppl.h"
@@ -189,14 +195,93 @@ int tppl_styles_cb(tppl_ctx *c, const float *image, const float *audio, int64_t 
     return make_styles(c, image, audio, n_samples, emotion, noise, seed, st, cb, ud);
 }
 
+namespace {
+// Decodes chunks of frames on its own thread (the decoder's stream) while the
+// calling thread samples the next chunk; the frames go straight to the
+// caller's buffer. The styles vector is sized before the first chunk and
+// never reallocated, so the worker reads it in place.
+struct chunk_decoder {
+    tpmd_ctx *md;
+    const float *styles;
+    float *out;
+    std::mutex mu;
+    std::condition_variable cv;
+    std::deque<std::pair<int64_t, int64_t>> todo;  // [frame0, n)
+    bool closed = false, failed = false;
+    std::string err;
+    std::thread th;
+    chunk_decoder(tpmd_ctx *m, const float *st, float *o) : md(m), styles(st), out(o) {
+        th = std::thread([this] { run(); });
+    }
+    void run() {
+        for (;;) {
+            std::pair<int64_t, int64_t> job;
+            {
+                std::unique_lock<std::mutex> lk(mu);
+                cv.wait(lk, [this] { return closed || !todo.empty(); });
+                if (todo.empty()) return;
+                job = todo.front();
+                todo.pop_front();
+            }
+            if (failed) continue;  // drain the queue after an error
+            if (tpmd_decode(md, styles + (size_t) job.first * STYLE, job.second,
+                            out + (size_t) job.first * IMG_PIX) != 0) {
+                std::lock_guard<std::mutex> lk(mu);
+                failed = true;
+                err = tpmd_last_error(md);
+            }
+        }
+    }
+    void push(int64_t f0, int64_t n) {
+        {
+            std::lock_guard<std::mutex> lk(mu);
+            todo.emplace_back(f0, n);
+        }
+        cv.notify_one();
+    }
+    bool has_failed() {
+        std::lock_guard<std::mutex> lk(mu);
+        return failed;
+    }
+    // waits for every queued chunk; false if one failed
+    bool finish() {
+        {
+            std::lock_guard<std::mutex> lk(mu);
+            closed = true;
+        }
+        cv.notify_one();
+        if (th.joinable()) th.join();
+        return !failed;
+    }
+    ~chunk_decoder() { finish(); }
+};
+}  // namespace
+
 int tppl_generate(tppl_ctx *c, const float *image, const float *audio, int64_t n_samples, int emotion,
                   const float *noise, uint64_t seed, float *out_frames) {
     if (!c) return -1;
     if (!out_frames) return c->fail("tppl_generate: null output");
+    // make_styles sizes the styles vector before its first callback; the
+    // decoder thread starts on the first chunk
     std::vector<float> st;
-    const int n = make_styles(c, image, audio, n_samples, emotion, noise, seed, st);
+    std::unique_ptr<chunk_decoder> dec;
+    struct ctx_t {
+        tppl_ctx *c;
+        std::vector<float> *st;
+        std::unique_ptr<chunk_decoder> *dec;
+        float *out;
+    } cx{c, &st, &dec, out_frames};
+    auto on_chunk = [](int64_t f0, int64_t n, const float *, void *ud) -> int {
+        ctx_t *x = (ctx_t *) ud;
+        if (!*x->dec) x->dec->reset(new chunk_decoder(x->c->md, x->st->data(), x->out));
+        if ((*x->dec)->has_failed()) return 1;
+        (*x->dec)->push(f0, n);
+        return 0;
+    };
+    const int n = make_styles(c, image, audio, n_samples, emotion, noise, seed, st, on_chunk, &cx);
+    const bool ok = !dec || dec->finish();
     if (n < 0) return -1;
-    if (tpmd_decode(c->md, st.data(), n, out_frames) != 0) return c->fail(tpmd_last_error(c->md));
+    if (!ok) return c->fail(dec->err);
     return n;
 }
 
