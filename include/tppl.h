@@ -54,7 +54,10 @@ int64_t tppl_n_chunks(int64_t n_frames);
  * normalised 16 kHz mono, emotion index, noise [n_chunks][50][512] or NULL
  * (then drawn from `seed`, the same draw for every chunk, as the
  * reference's fixed-seed generator does) -> out_frames
- * [n_frames][3][512][512]. Returns n_frames or -1. */
+ * [n_frames][3][512][512]. Returns n_frames or -1. Each sampler chunk's
+ * frames are decoded on an internal worker thread (the decoder's own
+ * stream) while the next chunk is sampled; the call returns when every
+ * frame is in out_frames. */
 int tppl_generate(tppl_ctx *ctx, const float *image, const float *audio, int64_t n_samples, int emotion,
                   const float *noise, uint64_t seed, float *out_frames);
 
