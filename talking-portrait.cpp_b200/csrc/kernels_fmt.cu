@@ -210,10 +210,11 @@ __global__ void gelu_kernel(const float *__restrict__ a, const float *__restrict
 }
 
 // v = out + b; per current frame f: vc = (u + a_cfg (a - u)) + e_cfg (fu - a);
-// x[f] += dt * vc; the next forward's x60 rows P.. are the new x
+// x[f] += dt * vc; the next forward's x60 rows P.. are the new x (and their
+// f16 copy, the next x_embedder GEMM's input, when x60h is given)
 __global__ void cfg_euler_kernel(const float *__restrict__ vout, const float *__restrict__ bv, int T, int P,
                                  int D, float a_cfg, float e_cfg, float dt, float *__restrict__ x,
-                                 float *__restrict__ x60) {
+                                 float *__restrict__ x60, __half *__restrict__ x60h) {
     const int CF = T - P;
     const int64_t n = (int64_t) CF * D;
     const int64_t br = (int64_t) T * D;
@@ -226,6 +227,7 @@ __global__ void cfg_euler_kernel(const float *__restrict__ vout, const float *__
         const float nx = x[e] + dt * vc;
         x[e] = nx;
         x60[q] = nx;
+        if (x60h) x60h[q] = __float2half_rn(nx);
     }
 }
 
@@ -303,8 +305,9 @@ cudaError_t fmt_gelu(bool f16, const float *a, const float *b, int M, int N, voi
     return cudaGetLastError();
 }
 cudaError_t fmt_cfg_euler(const float *vout, const float *bv, int T, int P, int D, float a_cfg, float e_cfg,
-                          float dt, float *x, float *x60, cudaStream_t st) {
-    cfg_euler_kernel<<<grid_for((int64_t) (T - P) * D), 256, 0, st>>>(vout, bv, T, P, D, a_cfg, e_cfg, dt, x, x60);
+                          float dt, float *x, float *x60, __half *x60h, cudaStream_t st) {
+    cfg_euler_kernel<<<grid_for((int64_t) (T - P) * D), 256, 0, st>>>(vout, bv, T, P, D, a_cfg, e_cfg, dt, x, x60,
+                                                                     x60h);
     return cudaGetLastError();
 }
 cudaError_t fmt_add_bias(const float *a, const float *b, int M, int N, float *y, cudaStream_t st) {

@@ -34,7 +34,7 @@ cudaError_t fmt_res_norm(bool f16, float *x, const float *o, const float *bo, co
                          int mod_stride, int gate_off, int M, int H, float eps, const float *mod2, const float *bmod2,
                          int shift_off, int scale_off, void *h, cudaStream_t st);
 cudaError_t fmt_cfg_euler(const float *vout, const float *bv, int T, int P, int D, float a_cfg, float e_cfg,
-                          float dt, float *x, float *x60, cudaStream_t st);
+                          float dt, float *x, float *x60, __half *x60h, cudaStream_t st);
 cudaError_t fmt_add_bias(const float *a, const float *b, int M, int N, float *y, cudaStream_t st);
 cudaError_t fmt_to_half(const float *a, int64_t n, __half *y, cudaStream_t st);
 }  // namespace tpmd
@@ -67,7 +67,8 @@ struct tpfm_ctx {
     void *act = nullptr;
     float *x60 = nullptr, *cond = nullptr, *clin = nullptr, *te0 = nullptr, *te = nullptr, *x1 = nullptr,
           *x = nullptr, *mod = nullptr, *qkv = nullptr, *o = nullptr, *m1raw = nullptr,
-          *vout = nullptr, *v = nullptr, *xc = nullptr, *tf = nullptr;
+          *vout = nullptr, *v = nullptr, *xc = nullptr, *tf = nullptr,
+          *te_all = nullptr;  // timestep embedding of every sampler step (prepare)
     void *sc = nullptr, *h = nullptr, *att = nullptr, *m1 = nullptr, *cond_in = nullptr, *x60_in = nullptr;
     cudaGraphExec_t graph = nullptr;
 
@@ -147,24 +148,36 @@ bool is_gemm_weight(const std::string &n) {
     return k > 7 && n.compare(k - 7, 7, ".weight") == 0 && n.rfind("t_embedder.", 0) != 0;
 }
 
+// the timestep MLP of tf row `s` into te (two GEMVs)
+bool t_embed(tpfm_ctx *c, int s, float *te) {
+    const int H = c->H;
+    const float *tf = c->tf + (size_t) s * c->c.t_freq_dim;
+    return c->ck(fmt_gemv(c->F("t_embedder.mlp.0.weight"), tf, c->F("t_embedder.mlp.0.bias"), H, c->c.t_freq_dim,
+                          true, c->te0, c->stream),
+                 "t embed") &&
+           c->ck(fmt_gemv(c->F("t_embedder.mlp.2.weight"), c->te0, c->F("t_embedder.mlp.2.bias"), H, H, false, te,
+                          c->stream),
+                 "t embed");
+}
+
 // one forward on the device buffers: x60 (f32) and the chunk's clin are set;
-// tf row `s`; output in vout (no bias)
-bool forward_device(tpfm_ctx *c, int s) {
+// tf row `s`; output in vout (no bias). in_chunk: a sampler step, whose
+// timestep embedding was computed at prepare and whose x60 f16 copy the
+// chunk keeps current; otherwise both are formed here.
+bool forward_device(tpfm_ctx *c, int s, bool in_chunk = false) {
     cudaStream_t st = c->stream;
     const int H = c->H, T = c->T, M = c->M, FF = c->FF;
     const bool h16 = c->f16;
     auto K = [&](cudaError_t e, const char *w) { return c->ck(e, w); };
-    const float *tf = c->tf + (size_t) s * c->c.t_freq_dim;
-    if (!K(fmt_gemv(c->F("t_embedder.mlp.0.weight"), tf, c->F("t_embedder.mlp.0.bias"), H, c->c.t_freq_dim, true,
-                    c->te0, st),
-           "t embed") ||
-        !K(fmt_gemv(c->F("t_embedder.mlp.2.weight"), c->te0, c->F("t_embedder.mlp.2.bias"), H, H, false, c->te, st),
-           "t embed") ||
-        !K(fmt_cond_silu(h16, c->clin, c->F("c_embedder.bias"), c->te, M, H, c->sc, st), "cond silu"))
+    const float *te = in_chunk ? c->te_all + (size_t) s * H : c->te;
+    if ((!in_chunk && !t_embed(c, s, c->te)) ||
+        !K(fmt_cond_silu(h16, c->clin, c->F("c_embedder.bias"), te, M, H, c->sc, st), "cond silu"))
         return false;
     const void *x60_in = c->x60;
     if (h16) {
-        if (!K(fmt_to_half(c->x60, (int64_t) T * c->c.dim_w, (__half *) c->x60_in, st), "x60 f16")) return false;
+        if (!in_chunk &&
+            !K(fmt_to_half(c->x60, (int64_t) T * c->c.dim_w, (__half *) c->x60_in, st), "x60 f16"))
+            return false;
         x60_in = c->x60_in;
     }
     const int NM = c->nmod;
@@ -271,6 +284,7 @@ tpfm_ctx *tpfm_create(int device, int dtype, const tpfm_config *cfg) {
     size_t sizes[] = {T * D * 4, M * CD * 4, M * H * 4, H * 4, H * 4, T * H * 4, M * H * 4, M * (size_t) c->nmod * 4,
                       M * 3 * H * 4, M * H * 4, M * FF * 4, M * D * 4, M * D * 4,
                       (size_t) cfg->chunk_frames * D * 4, (size_t) (cfg->nfe) * cfg->t_freq_dim * 4,
+                      (size_t) cfg->nfe * H * 4,
                       M * H * es, M * H * es, M * H * es, M * FF * es, M * CD * es, T * D * es};
     const int ns = sizeof(sizes) / sizeof(sizes[0]);
     size_t offs[32], total = 0;
@@ -293,7 +307,7 @@ tpfm_ctx *tpfm_create(int device, int dtype, const tpfm_config *cfg) {
     char *b = (char *) c->act;
     int i = 0;
     float **fl[] = {&c->x60, &c->cond, &c->clin, &c->te0, &c->te, &c->x1, &c->x, &c->mod, &c->qkv, &c->o,
-                    &c->m1raw, &c->vout, &c->v, &c->xc, &c->tf};
+                    &c->m1raw, &c->vout, &c->v, &c->xc, &c->tf, &c->te_all};
     for (float **p : fl) *p = (float *) (b + offs[i++]);
     void **vp[] = {&c->sc, &c->h, &c->att, &c->m1, &c->cond_in, &c->x60_in};
     for (void **p : vp) *p = b + offs[i++];
@@ -437,6 +451,10 @@ int tpfm_prepare(tpfm_ctx *c) {
                 return -1;
         if (!c->ck(cudaStreamSynchronize(c->stream), "f16 weights")) return -1;
     }
+    // the sampler's timestep embeddings depend only on the weights
+    for (int s = 0; s + 1 < c->c.nfe; s++)
+        if (!t_embed(c, s, c->te_all + (size_t) s * c->H)) return -1;
+    if (!c->ck(cudaStreamSynchronize(c->stream), "t embeddings")) return -1;
     c->wready = true;
     return 0;
 }
@@ -496,12 +514,14 @@ int tpfm_sample_chunk(tpfm_ctx *c, const float *wr, const float *prev_wa, const 
         // capture the chunk's device work once; buffers are fixed per handle
         cudaGraph_t g = nullptr;
         if (!c->ck(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal), "begin capture")) return -1;
-        bool ok = embed_cond(c);
+        // the f16 copy of x60 is made once here; each Euler step refreshes its rows
+        bool ok = embed_cond(c) &&
+                  (!c->f16 || c->ck(fmt_to_half(c->x60, (int64_t) T * D, (__half *) c->x60_in, st), "x60 f16"));
         for (int s = 0; ok && s < c->c.nfe - 1; s++) {
             const float dt = ode_t(s + 1, c->c.nfe) - ode_t(s, c->c.nfe);
-            ok = forward_device(c, s) &&
+            ok = forward_device(c, s, true) &&
                  c->ck(fmt_cfg_euler(c->vout, c->F("decoder.linear.bias"), T, P, D, c->c.a_cfg, c->c.e_cfg, dt, c->xc,
-                                     c->x60, st),
+                                     c->x60, c->f16 ? (__half *) c->x60_in : nullptr, st),
                        "cfg euler");
         }
         const cudaError_t e = cudaStreamEndCapture(st, &g);
