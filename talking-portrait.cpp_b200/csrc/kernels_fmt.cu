@@ -64,28 +64,25 @@ __global__ void cond_silu_kernel(const float *__restrict__ clin, const float *__
     }
 }
 
-// x[b][f][i] = x1[f][i] + bx[i] + pos[f][i] for the three branches
-__global__ void embed_x_kernel(const float *__restrict__ x1, const float *__restrict__ bx,
-                               const float *__restrict__ pos, int T, int H, float *__restrict__ x) {
-    const int64_t n = (int64_t) T * H;
-    for (int64_t e = (int64_t) blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t) gridDim.x * blockDim.x) {
-        const float v = x1[e] + __ldg(bx + e % H) + __ldg(pos + e);
-        x[e] = v;
-        x[n + e] = v;
-        x[2 * n + e] = v;
-    }
-}
-
 // h = LN(x) * (1 + scale) + shift per row (ggml_norm: no affine; mean and
-// variance in two passes), scale/shift = mod[m][off..] + bmod[off..]
+// variance in two passes), scale/shift = mod[m][off..] + bmod[off..]. With
+// x1 given, the row is first formed as x1[f] + bx + pos[f] (f = m mod T, the
+// x embedding of the three branches) and stored to x.
 template <typename TIN>
-__global__ void __launch_bounds__(256) norm_mod_kernel(const float *__restrict__ x, int H, float eps,
+__global__ void __launch_bounds__(256) norm_mod_kernel(float *__restrict__ x, int H, float eps,
                                                        const float *__restrict__ mod,
                                                        const float *__restrict__ bmod, int mod_stride,
-                                                       int shift_off, int scale_off, TIN *__restrict__ h) {
+                                                       int shift_off, int scale_off, TIN *__restrict__ h,
+                                                       const float *__restrict__ x1, const float *__restrict__ bx,
+                                                       const float *__restrict__ pos, int T) {
     __shared__ float red[32];
     const int m = blockIdx.x;
-    const float *r = x + (int64_t) m * H;
+    float *r = x + (int64_t) m * H;
+    if (x1) {
+        const int64_t f = m % T;
+        for (int i = threadIdx.x; i < H; i += blockDim.x)
+            r[i] = x1[f * H + i] + __ldg(bx + i) + __ldg(pos + f * H + i);
+    }
     float s = 0.0f;
     for (int i = threadIdx.x; i < H; i += blockDim.x) s += r[i];
     const float mean = block_sum(s, red) / (float) H;
@@ -261,18 +258,16 @@ cudaError_t fmt_cond_silu(bool f16, const float *clin, const float *bc, const fl
         cond_silu_kernel<float><<<grid_for((int64_t) M * H), 256, 0, st>>>(clin, bc, te, M, H, (float *) sc);
     return cudaGetLastError();
 }
-cudaError_t fmt_embed_x(const float *x1, const float *bx, const float *pos, int T, int H, float *x, cudaStream_t st) {
-    embed_x_kernel<<<grid_for((int64_t) T * H), 256, 0, st>>>(x1, bx, pos, T, H, x);
-    return cudaGetLastError();
-}
-cudaError_t fmt_norm_mod(bool f16, const float *x, int M, int H, float eps, const float *mod, const float *bmod,
-                         int mod_stride, int shift_off, int scale_off, void *h, cudaStream_t st) {
+cudaError_t fmt_norm_mod(bool f16, float *x, int M, int H, float eps, const float *mod, const float *bmod,
+                         int mod_stride, int shift_off, int scale_off, void *h, cudaStream_t st, const float *x1,
+                         const float *bx, const float *pos, int T) {
+    if (x1 && (!bx || !pos || T <= 0)) return cudaErrorInvalidValue;
     if (f16)
         norm_mod_kernel<__half><<<M, 256, 0, st>>>(x, H, eps, mod, bmod, mod_stride, shift_off, scale_off,
-                                                   (__half *) h);
+                                                   (__half *) h, x1, bx, pos, T);
     else
         norm_mod_kernel<float><<<M, 256, 0, st>>>(x, H, eps, mod, bmod, mod_stride, shift_off, scale_off,
-                                                  (float *) h);
+                                                  (float *) h, x1, bx, pos, T);
     return cudaGetLastError();
 }
 cudaError_t fmt_attn(bool f16, const float *qkv, const float *bqkv, int T, int H, int nh, int window, void *out,

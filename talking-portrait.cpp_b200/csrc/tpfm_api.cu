@@ -24,9 +24,11 @@ cudaError_t fmt_gemv(const float *W, const float *x, const float *b, int N, int 
                      cudaStream_t st);
 cudaError_t fmt_cond_silu(bool f16, const float *clin, const float *bc, const float *te, int M, int H, void *sc,
                           cudaStream_t st);
-cudaError_t fmt_embed_x(const float *x1, const float *bx, const float *pos, int T, int H, float *x, cudaStream_t st);
-cudaError_t fmt_norm_mod(bool f16, const float *x, int M, int H, float eps, const float *mod, const float *bmod,
-                         int mod_stride, int shift_off, int scale_off, void *h, cudaStream_t st);
+// with x1: x = x1[m mod T] + bx + pos[m mod T] first (stored), then the norm
+cudaError_t fmt_norm_mod(bool f16, float *x, int M, int H, float eps, const float *mod, const float *bmod,
+                         int mod_stride, int shift_off, int scale_off, void *h, cudaStream_t st,
+                         const float *x1 = nullptr, const float *bx = nullptr, const float *pos = nullptr,
+                         int T = 0);
 cudaError_t fmt_attn(bool f16, const float *qkv, const float *bqkv, int T, int H, int nh, int window, void *out,
                      cudaStream_t st);
 cudaError_t fmt_gelu(bool f16, const float *a, const float *b, int M, int N, void *y, cudaStream_t st);
@@ -182,14 +184,15 @@ bool forward_device(tpfm_ctx *c, int s, bool in_chunk = false) {
     }
     const int NM = c->nmod;
     if (!c->gemm(x60_in, T, c->c.dim_w, "x_embedder.proj.weight", H, c->x1) ||
-        !K(fmt_embed_x(c->x1, c->F("x_embedder.proj.bias"), c->F("pos_embed"), T, H, c->x, st), "x embed") ||
         !c->gemm_w(c->sc, M, H, c->adaln_w(), NM, c->mod, "adaLN modulation"))
         return false;
-    // each gated residual runs fused with the layer norm after it; only the
-    // first block's attention norm stands alone
+    // each gated residual runs fused with the layer norm after it; the first
+    // block's attention norm forms the embedded rows (x1 + bias + pos, three
+    // branches) itself
     const float eps = c->c.ln_eps;
-    if (!K(fmt_norm_mod(h16, c->x, M, H, eps, c->mod, c->F("blocks.0.adaLN_modulation.1.bias"), NM, 0, H, c->h, st),
-           "norm"))
+    if (!K(fmt_norm_mod(h16, c->x, M, H, eps, c->mod, c->F("blocks.0.adaLN_modulation.1.bias"), NM, 0, H, c->h, st,
+                        c->x1, c->F("x_embedder.proj.bias"), c->F("pos_embed"), T),
+           "embed + norm"))
         return false;
     for (int l = 0; l < c->c.depth; l++) {
         const std::string b = "blocks." + std::to_string(l) + ".";
