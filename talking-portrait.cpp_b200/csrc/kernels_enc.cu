@@ -47,7 +47,10 @@ __global__ void __launch_bounds__(256) enc_stem_kernel(const float *__restrict__
     }
 }
 
-__global__ void __launch_bounds__(256) enc_conv_kernel(enc_conv_params p) {
+// blockIdx.z = split: the block sums the k-steps (tap, 16-channel chunk)
+// [z * per, (z + 1) * per) of K; with several splits the raw sums go to
+// p.part[z][m][n] and enc_split_reduce_kernel applies the epilogue
+__global__ void __launch_bounds__(256) enc_conv_kernel(enc_conv_params p, int per) {
     __shared__ __align__(16) float As[EBK][EBM + 4];
     __shared__ __align__(16) float Bs[EBK][EBN + 4];
     const int M = p.OH * p.OW, N = p.OC, KT = p.K * p.K, Kall = KT * p.IC;
@@ -71,12 +74,15 @@ __global__ void __launch_bounds__(256) enc_conv_kernel(enc_conv_params p) {
 #pragma unroll
         for (int j = 0; j < 4; j++) acc[i][j] = 0.0f;
 
-    for (int tap = 0; tap < KT; tap++) {
+    const int CK = p.IC / EBK;  // 16-channel chunks per tap
+    const int ks0 = blockIdx.z * per, ks1 = min(KT * CK, ks0 + per);
+    for (int tap = ks0 / CK; tap < KT && tap * CK < ks1; tap++) {
         const int iy = oy * p.stride + tap / p.K - p.pad, ix = ox * p.stride + tap % p.K - p.pad;
         const bool in_b = a_valid && iy >= 0 && iy < p.IH && ix >= 0 && ix < p.IW;
         const float *xp = p.x + ((int64_t) iy * p.IW + ix) * p.IC + a_c;
         const float *wp = wrow + (int64_t) tap * p.IC + b_k;
-        for (int c0 = 0; c0 < p.IC; c0 += EBK) {
+        const int cb = max(ks0 - tap * CK, 0) * EBK, ce = min(ks1 - tap * CK, CK) * EBK;
+        for (int c0 = cb; c0 < ce; c0 += EBK) {
             float av[8], bv[4];
             if (in_b) {
                 const float4 u = __ldg(reinterpret_cast<const float4 *>(xp + c0));
@@ -124,12 +130,30 @@ __global__ void __launch_bounds__(256) enc_conv_kernel(enc_conv_params p) {
             const int n = n0 + tn * 4 + j;
             if (n >= N) continue;
             float v = acc[i][j];
+            if (gridDim.z > 1) {
+                p.part[((int64_t) blockIdx.z * M + m) * N + n] = v;
+                continue;
+            }
             if (p.bias) v += __ldg(p.bias + n);
             if (p.lrelu) v = fmaxf(v, 0.2f * v);
             const int64_t dst = (int64_t) m * N + n;
             if (p.res) v += p.res[dst];
             p.y[dst] = v;
         }
+    }
+}
+
+// the split-K sums in split order (deterministic), then the conv epilogue
+__global__ void __launch_bounds__(256) enc_split_reduce_kernel(enc_conv_params p, int S) {
+    const int64_t MN = (int64_t) p.OH * p.OW * p.OC;
+    for (int64_t e = (int64_t) blockIdx.x * blockDim.x + threadIdx.x; e < MN; e += (int64_t) gridDim.x * blockDim.x) {
+        float v = p.part[e];
+        for (int z = 1; z < S; z++) v += p.part[z * MN + e];
+        const int n = (int) (e % p.OC);
+        if (p.bias) v += __ldg(p.bias + n);
+        if (p.lrelu) v = fmaxf(v, 0.2f * v);
+        if (p.res) v += p.res[e];
+        p.y[e] = v;
     }
 }
 
@@ -220,8 +244,26 @@ cudaError_t launch_enc_stem(const float *img, const float *w, const float *b, fl
 
 cudaError_t launch_enc_conv(const enc_conv_params &p, cudaStream_t st) {
     if (p.IC % EBK || p.OH <= 0 || p.OW <= 0) return cudaErrorInvalidValue;
-    const dim3 grid((unsigned) ((p.OH * p.OW + EBM - 1) / EBM), (unsigned) ((p.OC + EBN - 1) / EBN));
-    enc_conv_kernel<<<grid, 256, 0, st>>>(p);
+    const int64_t M = (int64_t) p.OH * p.OW;
+    const int gx = (int) ((M + EBM - 1) / EBM), gy = (p.OC + EBN - 1) / EBN;
+    const int ksteps = p.K * p.K * (p.IC / EBK);
+    // the deep low-resolution convs launch a few blocks with long K loops:
+    // split K so that about two blocks per SM work on them
+    int S = 1;
+    if (p.part && gx * gy < 148) {
+        S = (2 * 148 + gx * gy - 1) / (gx * gy);
+        S = std::min(S, 16);
+        S = std::min(S, ksteps / 4);  // at least four k-steps per split
+        while (S > 1 && (int64_t) S * M * p.OC > p.part_floats) S--;
+        if (S < 1) S = 1;
+    }
+    const int per = (ksteps + S - 1) / S;
+    S = (ksteps + per - 1) / per;  // no empty split
+    enc_conv_kernel<<<dim3((unsigned) gx, (unsigned) gy, (unsigned) S), 256, 0, st>>>(p, per);
+    if (S > 1) {
+        const int64_t n = M * p.OC;
+        enc_split_reduce_kernel<<<(int) std::min<int64_t>((n + 255) / 256, 148 * 8), 256, 0, st>>>(p, S);
+    }
     return cudaGetLastError();
 }
 

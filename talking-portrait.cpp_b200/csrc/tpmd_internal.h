@@ -93,6 +93,8 @@ struct enc_conv_params {
     int lrelu;             // leaky relu 0.2 after the bias
     const float *res;      // [OH][OW][OC] added last, or nullptr (may alias y)
     float *y;              // [OH][OW][OC]
+    float *part;           // split-K partial sums (nullptr: no split)
+    int64_t part_floats;   // its capacity
 };
 struct enc_head_params {
     const float *W[5], *b[5];  // EqualLinears, [out][512]

@@ -64,6 +64,8 @@ void to_tap_major(const float *w, int OC, int IC, int K, float *out) {
 
 }  // namespace
 
+constexpr size_t PART_FLOATS = (size_t) 4 << 20;  // 16 MB
+
 struct tpme_ctx {
     int device = 0;
     std::string err;
@@ -77,6 +79,7 @@ struct tpme_ctx {
     void *ws = nullptr;
     float *img = nullptr, *pyr[8] = {nullptr}, *x1 = nullptr, *xb = nullptr, *sb = nullptr;
     float *app = nullptr, *lam = nullptr, *mot = nullptr;
+    float *part = nullptr;  // split-K partial sums (PART_FLOATS)
 
     bool fail(const std::string &m) {
         err = m;
@@ -126,6 +129,7 @@ tpme_ctx *tpme_create(int device) {
     sizes[k++] = 512;
     sizes[k++] = 32;
     sizes[k++] = 512;
+    sizes[k++] = PART_FLOATS;  // split-K partial sums of the deep convs
     size_t offs[16];
     for (int i = 0; i < k; i++) {
         offs[i] = total;
@@ -149,6 +153,7 @@ tpme_ctx *tpme_create(int device) {
     c->app = b + offs[i++];
     c->lam = b + offs[i++];
     c->mot = b + offs[i++];
+    c->part = b + offs[i++];
     return c;
 }
 
@@ -260,6 +265,7 @@ int tpme_run(tpme_ctx *c, const float *image, float *appearance, float *lambda, 
             return c->W(nm);
         };
         enc_conv_params p{};
+        p.part = c->part, p.part_floats = PART_FLOATS;
         // conv1: 3x3 pad 1 + FusedLeakyReLU -> x1
         p.x = c->pyr[i - 1], p.IH = H, p.IW = H, p.IC = C;
         p.w = T("conv1.0.weight"), p.OC = C, p.K = 3, p.stride = 1, p.pad = 1, p.OH = H, p.OW = H;
@@ -282,6 +288,7 @@ int tpme_run(tpme_ctx *c, const float *image, float *appearance, float *lambda, 
     }
     // 4x4 valid conv -> appearance; fc chain and motion
     enc_conv_params p{};
+    p.part = c->part, p.part_floats = PART_FLOATS;
     p.x = c->pyr[7], p.IH = 4, p.IW = 4, p.IC = 512;
     p.w = c->W("enc.net_app.convs.8.weight"), p.OC = 512, p.K = 4, p.stride = 1, p.pad = 0, p.OH = 1, p.OW = 1;
     p.y = c->app;
