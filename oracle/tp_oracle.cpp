@@ -62,6 +62,41 @@ void conv_row(const float *x, int IC, int IH, int IW, const float *w, int KH,
     }
 }
 
+// Register-blocked form of conv_row for 8 output channels and 16 output
+// columns: the 8 x 16 sums stay in eight vector registers while (ic, ky, kx) runs, and the
+// input comes from a copy padded by pl columns on the left and enough on the
+// right (xpad rows of width PW), so no column test sits in the inner loop.
+// Each output is still summed in (ic, ky, kx) order.
+typedef float v16f __attribute__((vector_size(64)));
+__attribute__((target_clones("arch=x86-64-v4", "default")))
+void conv_tile8x16(const float *xpad, int IC, int IH, int PW, const float *w, int KH, int KW,
+                   int pt, int oy, int ox0, float *y, int OH, int OW) {
+    v16f a0 = {}, a1 = {}, a2 = {}, a3 = {}, a4 = {}, a5 = {}, a6 = {}, a7 = {};
+    const size_t ws = (size_t) IC * KH * KW;  // weight stride between output channels
+    for (int ic = 0; ic < IC; ic++) {
+        for (int ky = 0; ky < KH; ky++) {
+            const int iy = oy + ky - pt;
+            if (iy < 0 || iy >= IH) continue;
+            const float *row = xpad + ((size_t) ic * IH + iy) * PW + ox0;
+            const float *wk = w + ((size_t) ic * KH + ky) * KW;
+            for (int kx = 0; kx < KW; kx++) {
+                v16f xv;
+                memcpy(&xv, row + kx, sizeof xv);
+                a0 += wk[kx] * xv;
+                a1 += wk[ws + kx] * xv;
+                a2 += wk[2 * ws + kx] * xv;
+                a3 += wk[3 * ws + kx] * xv;
+                a4 += wk[4 * ws + kx] * xv;
+                a5 += wk[5 * ws + kx] * xv;
+                a6 += wk[6 * ws + kx] * xv;
+                a7 += wk[7 * ws + kx] * xv;
+            }
+        }
+    }
+    const v16f *acc[8] = {&a0, &a1, &a2, &a3, &a4, &a5, &a6, &a7};
+    for (int o = 0; o < 8; o++) memcpy(y + ((size_t) o * OH + oy) * OW + ox0, acc[o], sizeof(v16f));
+}
+
 // y[OC][OH][OW] = corr2d(x[IC][IH][IW], w[OC][IC][KH][KW]), stride 1, top/left
 // padding pt/pl (zeros), output size given (the bottom/right padding follows).
 // Stands in for ggml_conv_2d_direct as used by src/motion_dec.cpp:597-632.
@@ -69,6 +104,20 @@ void conv2d(const float *x, int IC, int IH, int IW, const float *w, int OC, int 
             int KW, int pt, int pl, int OH, int OW, float *y) {
     const int OB = 8;
     const int nob = (OC + OB - 1) / OB;
+    // zero-padded copy of the input for the 8 x 16 tiles: columns -pl .. OW+KW
+    const int PW = OW + KW + 16;
+    std::vector<float> xpad;
+    const bool tiles = OW >= 16;
+    if (tiles) {
+        xpad.assign((size_t) IC * IH * PW, 0.0f);
+#pragma omp parallel for schedule(static)
+        for (int r = 0; r < IC * IH; r++)
+            for (int c = 0; c < IW; c++) {
+                const int pc = c + pl;
+                if (pc >= 0 && pc < PW) xpad[(size_t) r * PW + pc] = x[(size_t) r * IW + c];
+            }
+    }
+    const int ntile = tiles ? OW / 16 : 0;
 #pragma omp parallel
     {
         std::vector<float> acc((size_t) OB * OW);
@@ -76,12 +125,20 @@ void conv2d(const float *x, int IC, int IH, int IW, const float *w, int OC, int 
         for (int ob = 0; ob < nob; ob++) {
             for (int oy = 0; oy < OH; oy++) {
                 const int o0 = ob * OB, nb = std::min(OB, OC - o0);
+                if (nb == OB && ntile > 0) {
+                    for (int t = 0; t < ntile; t++)
+                        conv_tile8x16(xpad.data(), IC, IH, PW, w + (size_t) o0 * IC * KH * KW, KH, KW, pt, oy,
+                                      16 * t, y + (size_t) o0 * OH * OW, OH, OW);
+                    if (ntile * 16 == OW) continue;
+                }
+                // channel-block remainder, narrow maps and the last columns: row form
                 std::fill(acc.begin(), acc.end(), 0.0f);
                 conv_row(x, IC, IH, IW, w + (size_t) o0 * IC * KH * KW, KH, KW, pt, pl,
                          oy, OW, nb, acc.data(), OW);
+                const int c0 = (nb == OB) ? ntile * 16 : 0;
                 for (int o = 0; o < nb; o++)
-                    memcpy(y + ((size_t) (o0 + o) * OH + oy) * OW,
-                           acc.data() + (size_t) o * OW, (size_t) OW * 4);
+                    memcpy(y + ((size_t) (o0 + o) * OH + oy) * OW + c0,
+                           acc.data() + (size_t) o * OW + c0, (size_t) (OW - c0) * 4);
             }
         }
     }
