@@ -118,7 +118,9 @@ int tpmd_decode(tpmd_ctx *ctx, const float *styles, int64_t n, float *frames);
 
 /* Same with device pointers, enqueued on `stream` (a cudaStream_t; NULL =
  * the legacy default stream, as in CUDA's own APIs) without host
- * synchronisation. */
+ * synchronisation. The return code covers the enqueue only: whether the
+ * kernels' pipeline waits all completed is known once tpmd_device_status
+ * returns 0, and the frames are valid only then. */
 int tpmd_decode_device(tpmd_ctx *ctx, const float *styles_dev, int64_t n,
                        float *frames_dev, void *stream);
 
@@ -149,24 +151,44 @@ int tpmd_profile_end(tpmd_ctx *ctx, char *json, size_t cap);
 int64_t tpmd_kernel_launches(const tpmd_ctx *ctx, int64_t n);
 
 /* Decode without allocating anything. This entry point has no counterpart
- * in the reference; it exists for callers that must not allocate GPU memory
- * at decode time: code running while a CUDA graph is being captured (where
- * cudaMalloc is not allowed), real-time frame loops that cannot risk an
- * allocator stall or failure mid-stream, and hosts whose memory manager owns
- * the whole GPU and forbids other allocations. Instead of the handle's
- * workspace it uses one static device array of 48 MiB inside this library,
- * enough for one f16 frame, so it accepts n = 1 frame per call on a handle
- * created with TPMD_DTYPE_F16 and rejects anything larger with an error.
- * Every GPU that loads the library holds the array until process exit. The
- * first call on each device looks up the array's device address (make that
- * first call before any stream capture); later calls only enqueue kernels on
- * `stream` (NULL = legacy default stream), without host synchronisation. All
- * calls share the array and it keeps the last call's contents, so calls whose
- * work overlaps on the GPU (other streams, other threads, other handles on
- * the same device) race and corrupt each other's frames. Pointers are device
- * memory: styles_dev [n][512], frames_dev [n][3][512][512]. */
+ * in the reference. It is for callers that cannot call cudaMalloc while they
+ * decode: real-time frame loops that must not risk an allocator stall or an
+ * out-of-memory failure in the middle of a stream, and hosts whose own memory
+ * manager owns the GPU's memory and forbids allocations behind its back.
+ * Instead of the handle's workspace it uses one static device array of
+ * 48 MiB inside this library, enough for one f16 frame, so it accepts n = 1
+ * frame per call on a handle created with TPMD_DTYPE_F16 and rejects
+ * anything larger with an error. Every GPU that loads the library holds the
+ * array until process exit. The first call on each device does a one-time
+ * set-up (it looks up the array's device address and zeroes its error word;
+ * make that first call before any stream capture); later calls only enqueue
+ * kernels on `stream` (NULL = legacy default stream), without host
+ * synchronisation. All calls share the array and it keeps the last call's
+ * contents, so calls whose work overlaps on the GPU (other streams, other
+ * threads, other handles on the same device) race and corrupt each other's
+ * frames. The frames are valid only once tpmd_device_status returns 0: an
+ * expired pipeline wait stays recorded in the array until that call reads
+ * and clears it. Pointers are device memory: styles_dev [n][512],
+ * frames_dev [n][3][512][512]. */
 int tpmd_decode_noalloc(tpmd_ctx *ctx, const float *styles_dev, int64_t n,
                         float *frames_dev, void *stream);
+
+/* Status of the device work enqueued by tpmd_decode_device and
+ * tpmd_decode_noalloc (the reference's error convention, src/tp.cpp:70-83:
+ * an int status plus the last-error string). Synchronises `stream`, then
+ * reads and clears the handle's device error flag and this device's
+ * tpmd_decode_noalloc error word. Returns 0 when no decoder kernel reported
+ * an expired pipeline wait since the last query, else -1 with the message
+ * in tpmd_last_error(ctx) ("... timed out ... (results invalid)"). The
+ * synchronous tpmd_decode and tpmd_decode_taps make this check themselves. */
+int tpmd_device_status(tpmd_ctx *ctx, void *stream);
+
+/* Test hook: arms the next decode of this handle so that its first tcgen05
+ * conv kernel waits up to wait_ns (1 .. 2e9) on an mbarrier that nothing
+ * completes, then takes its expiry path (reports through the device flag,
+ * skips its work, frees its tensor memory). That decode's result is then an
+ * error (tpmd_decode) or a nonzero tpmd_device_status. f16 handles only. */
+int tpmd_debug_expire_wait(tpmd_ctx *ctx, long long wait_ns);
 
 /* ---- op-level kernels with the patched-op semantics ------------------ */
 

@@ -49,6 +49,7 @@ struct tc_params {
     const float *snext;
     int snext_stride;
     int *err;
+    long long stall_ns;  // test hook: wait this long on a barrier nothing completes, then abort
     // fused level tail (conv2 kernels of the levels with OC <= 256)
     const __half *feat;
     const float *fW, *fs;
@@ -258,8 +259,19 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         __syncthreads();
         tc_fence_after();
     }
+    // Test hook: thread 0 waits, with the caller's limit, on the drain barrier
+    // before anything has arrived on it. The wait expires; the CTA reports it
+    // and skips every role (no copy or MMA has been issued), then frees TMEM.
+    bool run = true;
+    if (p.stall_ns > 0) {
+        if (threadIdx.x == 0) tmem_slot[1] = mbar_wait_for(drain, 0, (uint64_t) p.stall_ns) ? 1u : 0u;
+        __syncthreads();
+        run = tmem_slot[1] != 0u;
+        if (!run && threadIdx.x == 0) atomicExch(p.err, 1);
+    }
 
-    if (warp == 0) {
+    if (!run) {
+    } else if (warp == 0) {
         if (lane == 0) {
             // ---- TMA producer: counters only, no division per k-step
             uint32_t it = 0;
@@ -782,6 +794,7 @@ cudaError_t run_tc(const conv_params &cp, const tail_params *tl, cudaStream_t st
     p.snext = cp.snext;
     p.snext_stride = cp.snext_stride;
     p.err = cp.err;
+    p.stall_ns = cp.stall_ns;
     if (TAIL) {
         // one frame per tile and the whole channel range in one tile
         if (!tl || !tl->proj || p.bb != 1 || p.tiles_n != 1 || tl->OC != BN || tl->r != cp.W)

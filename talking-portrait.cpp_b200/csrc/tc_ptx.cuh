@@ -41,15 +41,19 @@ __device__ __forceinline__ uint64_t global_ns() {
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
-// bounded phase wait: false after ~2 s without completion
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+// bounded phase wait: false after `limit_ns` of %globaltimer without completion
+__device__ __forceinline__ bool mbar_wait_for(uint32_t bar, uint32_t parity, uint64_t limit_ns) {
     if (mbar_try(bar, parity)) return true;
     const uint64_t t0 = global_ns();
     for (;;) {
         for (int i = 0; i < 64; i++)
             if (mbar_try(bar, parity)) return true;
-        if (global_ns() - t0 > 2000000000ull) return false;
+        if (global_ns() - t0 > limit_ns) return false;
     }
+}
+// the pipelines' waits: false after ~2 s without completion
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+    return mbar_wait_for(bar, parity, 2000000000ull);
 }
 
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap *tm, uint32_t bar, int c0,

@@ -69,6 +69,8 @@ struct ws_view {
     void *actA, *actB, *actC;
     float *sf[2], *sk[2];
     int *err;
+    bool timed;          // record CUDA events around each launch (live profiling)
+    long long stall_ns;  // test hook armed for this chunk's first tcgen05 conv (0: none)
 };
 
 struct graph_entry {
@@ -120,6 +122,7 @@ struct tpmd_ctx {
     int *err_flag = nullptr;                   // set by kernels whose bounded waits expired
 
     std::list<graph_entry> graphs;  // most recently used first
+    long long stall_ns = 0;          // tpmd_debug_expire_wait: armed for the next decode
 
     // live profiling: (kernel name, start event, stop event) per launch
     bool profiling = false;
@@ -710,20 +713,21 @@ namespace {
 // [nb][3][512][512]).
 ws_view ctx_ws(const tpmd_ctx *c) {
     return ws_view{c->s_all, c->inv_den, c->actA, c->actB, c->actC,
-                   {c->sf[0], c->sf[1]}, {c->sk[0], c->sk[1]}, c->err_flag};
+                   {c->sf[0], c->sf[1]}, {c->sk[0], c->sk[1]}, c->err_flag,
+                   c->profiling, 0};
 }
 
 // one kernel launch, bracketed by CUDA events while profiling
 template <typename F>
-bool launch(tpmd_ctx *c, const std::string &name, cudaStream_t st, F &&fn) {
+bool launch(tpmd_ctx *c, bool timed, const std::string &name, cudaStream_t st, F &&fn) {
     cudaEvent_t a = nullptr, b = nullptr;
-    if (c->profiling) {
+    if (timed) {
         if (!c->ck(cudaEventCreate(&a), "event") || !c->ck(cudaEventCreate(&b), "event") ||
             !c->ck(cudaEventRecord(a, st), "record"))
             return false;
     }
     if (!c->ck(fn(), name.c_str())) return false;
-    if (c->profiling) {
+    if (timed) {
         if (!c->ck(cudaEventRecord(b, st), "record")) return false;
         c->prof.push_back({name, a, b});
     }
@@ -739,17 +743,17 @@ bool enqueue_chunk(tpmd_ctx *c, const ws_view &w, const float *styles, int64_t n
                    cudaStream_t st, int last_level = N_LEVELS - 1, bool keep_conv2 = false) {
     const bool h = c->f16;
     const int B = (int) nb;
-    if (!launch(c, "style", st, [&] {
+    if (!launch(c, w.timed, "style", st, [&] {
             return launch_style(c->Wf(c->off_wmod), c->Wf(c->off_bmod), c->S_TOT, styles, B,
                                 w.s_all, st);
         }))
         return false;
-    if (!launch(c, "den", st, [&] {
+    if (!launch(c, w.timed, "den", st, [&] {
             return launch_den((const float *) c->warena, c->dtab, w.s_all, c->S_TOT, B,
                               w.inv_den, c->D_TOT, st);
         }))
         return false;
-    if (!launch(c, "conv1_input", st, [&] {
+    if (!launch(c, w.timed, "conv1_input", st, [&] {
             return launch_conv1_input(h, c->Wf(c->off_input), w.s_all + c->conv[0].s_off,
                                       c->S_TOT, B, w.actA, st);
         }))
@@ -770,6 +774,7 @@ bool enqueue_chunk(tpmd_ctx *c, const ws_view &w, const float *styles, int64_t n
         p.snext = snext;
         p.snext_stride = c->S_TOT;
         p.err = w.err;
+        p.stall_ns = k == 0 && c->use_tc ? w.stall_ns : 0;
         return p;
     };
     auto conv = [&](int k, const void *x, void *y, int Hh, const float *snext) {
@@ -777,7 +782,7 @@ bool enqueue_chunk(tpmd_ctx *c, const ws_view &w, const float *styles, int64_t n
         const conv_params p = conv_p(k, x, y, Hh, snext);
         std::string name = k == 0 ? "conv1" : (L.up ? "upconv_r" : "conv2_r") +
                                                    std::to_string(L.up ? 2 * Hh : Hh);
-        return launch(c, name, st, [&] {
+        return launch(c, w.timed, name, st, [&] {
             return c->use_tc ? launch_conv_tc(L.up, p, st) : launch_conv_simt(h, L.up, p, st);
         });
     };
@@ -818,10 +823,10 @@ bool enqueue_chunk(tpmd_ctx *c, const ws_view &w, const float *styles, int64_t n
         t.proj = c->proj + c->proj_off[j];
         if (fused) {
             const conv_params p = conv_p(2 + 2 * j, w.actC, keep_conv2 ? w.actA : nullptr, r, nullptr);
-            if (!launch(c, "conv2tail_r" + std::to_string(r), st,
+            if (!launch(c, w.timed, "conv2tail_r" + std::to_string(r), st,
                         [&] { return launch_conv_tail_tc(p, t, st); }))
                 return false;
-        } else if (!launch(c, "tail_r" + std::to_string(r), st, [&] { return launch_tail(h, t, st); })) {
+        } else if (!launch(c, w.timed, "tail_r" + std::to_string(r), st, [&] { return launch_tail(h, t, st); })) {
             return false;
         }
     }
@@ -829,6 +834,12 @@ bool enqueue_chunk(tpmd_ctx *c, const ws_view &w, const float *styles, int64_t n
 }
 
 bool run_chunk(tpmd_ctx *c, const float *styles, int64_t nb, float *out, cudaStream_t st) {
+    if (c->stall_ns) {  // the armed test hook runs once, outside any cached graph
+        ws_view w = ctx_ws(c);
+        w.stall_ns = c->stall_ns;
+        c->stall_ns = 0;
+        return enqueue_chunk(c, w, styles, nb, out, st);
+    }
     if (!c->use_graph || c->profiling) return enqueue_chunk(c, ctx_ws(c), styles, nb, out, st);
     for (auto it = c->graphs.begin(); it != c->graphs.end(); ++it) {
         if (it->nb == nb && it->styles == styles && it->out == out) {
@@ -1063,6 +1074,7 @@ bool noalloc_view(const tpmd_ctx *c, char *base, ws_view &w) {
         off = align256(off + bytes);
         return p;
     };
+    w.err = (int *) take(256);  // first: tpmd_device_status reads it at offset 0
     w.s_all = (float *) take((size_t) c->S_TOT * 4);
     w.inv_den = (float *) take((size_t) c->D_TOT * 4);
     w.actA = take(a * c->esz());
@@ -1070,7 +1082,8 @@ bool noalloc_view(const tpmd_ctx *c, char *base, ws_view &w) {
     w.actC = take(cc * c->esz());
     for (int i = 0; i < 2; i++) w.sf[i] = (float *) take(skip * 4);
     for (int i = 0; i < 2; i++) w.sk[i] = (float *) take(skip * 4);
-    w.err = (int *) take(256);
+    w.timed = false;  // CUDA events would be allocations
+    w.stall_ns = 0;
     return off <= NOALLOC_BYTES;
 }
 
@@ -1099,24 +1112,49 @@ extern "C" int tpmd_decode_noalloc(tpmd_ctx *c, const float *styles_dev, int64_t
         std::lock_guard<std::mutex> lk(g_noalloc_mu);
         if (!g_noalloc_addr[c->device]) {
             void *p = nullptr;
-            const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+            cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+            // the error word starts at zero; afterwards only tpmd_device_status clears it
+            if (e == cudaSuccess) e = cudaMemset(p, 0, 256);
             if (e != cudaSuccess)
-                return c->fail(std::string("tpmd_decode_noalloc: cudaGetSymbolAddress: ") +
-                               cudaGetErrorString(e)),
-                       -1;
+                return c->fail(std::string("tpmd_decode_noalloc: set-up: ") + cudaGetErrorString(e)), -1;
             g_noalloc_addr[c->device] = p;
         }
         base = (char *) g_noalloc_addr[c->device];
     }
     ws_view w;
     if (!noalloc_view(c, base, w)) return c->fail("tpmd_decode_noalloc: scratch layout too large"), -1;
-    cudaStream_t st = (cudaStream_t) stream;
-    // the error flag must start each call at zero; everything else is written
-    // before it is read
-    if (!c->ck(cudaMemsetAsync(w.err, 0, sizeof(int), st), "cudaMemsetAsync")) return -1;
-    const bool prof = c->profiling;
-    c->profiling = false;  // no events: they would be allocations
-    const bool ok = enqueue_chunk(c, w, styles_dev, n, frames_dev, st);
-    c->profiling = prof;
-    return ok ? 0 : -1;
+    // every scratch buffer is written before it is read; the error word keeps
+    // an expired wait until tpmd_device_status reads and clears it
+    return enqueue_chunk(c, w, styles_dev, n, frames_dev, (cudaStream_t) stream) ? 0 : -1;
+}
+
+extern "C" int tpmd_device_status(tpmd_ctx *c, void *stream) {
+    if (!c) return -1;
+    if (!c->ck(cudaSetDevice(c->device), "cudaSetDevice") ||
+        !c->ck(cudaStreamSynchronize((cudaStream_t) stream), "tpmd_device_status: stream"))
+        return -1;
+    void *na = nullptr;
+    if (c->device >= 0 && c->device < 64) {
+        std::lock_guard<std::mutex> lk(g_noalloc_mu);
+        na = g_noalloc_addr[c->device];
+    }
+    int flag = 0, nflag = 0;
+    if (!c->ck(cudaMemcpy(&flag, c->err_flag, 4, cudaMemcpyDeviceToHost), "tpmd_device_status: read") ||
+        (na && !c->ck(cudaMemcpy(&nflag, na, 4, cudaMemcpyDeviceToHost), "tpmd_device_status: read")))
+        return -1;
+    if ((flag && !c->ck(cudaMemset(c->err_flag, 0, 4), "tpmd_device_status: clear")) ||
+        (nflag && !c->ck(cudaMemset(na, 0, 4), "tpmd_device_status: clear")))
+        return -1;
+    if (flag || nflag)
+        return c->fail("a decoder kernel timed out waiting on its pipeline (results invalid)"), -1;
+    return 0;
+}
+
+extern "C" int tpmd_debug_expire_wait(tpmd_ctx *c, long long wait_ns) {
+    if (!c) return -1;
+    if (!c->use_tc) return c->fail("tpmd_debug_expire_wait: needs the tcgen05 path (TPMD_DTYPE_F16)"), -1;
+    if (wait_ns < 1 || wait_ns > 2000000000ll)
+        return c->fail("tpmd_debug_expire_wait: wait_ns must be in 1 .. 2e9"), -1;
+    c->stall_ns = wait_ns;
+    return 0;
 }

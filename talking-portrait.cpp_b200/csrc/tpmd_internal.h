@@ -37,6 +37,10 @@ struct conv_params {
     const float *snext;
     int snext_stride;
     int *err;  // device flag a kernel sets when a bounded wait expires
+    // test hook (tcgen05 convs only): when nonzero, the kernel first waits up
+    // to this many ns on an mbarrier that nothing completes, then reports the
+    // expired wait through *err and skips its work
+    long long stall_ns;
 };
 
 // The per-level tail after conv2 (ToFlow, flow head, bilinear warp of the

@@ -34,7 +34,8 @@ EXPORTS = ("tpmd_abi_version", "tpmd_create", "tpmd_create_error", "tpmd_destroy
            "tpmd_last_error", "tpmd_scale_for", "tpmd_set_tensor", "tpmd_prepare",
            "tpmd_set_feats", "tpmd_batch", "tpmd_decode", "tpmd_decode_device",
            "tpmd_arena", "tpmd_arena_adopt", "tpmd_decode_taps", "tpmd_profile_begin", "tpmd_profile_end",
-           "tpmd_kernel_launches", "tpmd_decode_noalloc", "tpmd_gguf_read", "tpmd_load_gguf",
+           "tpmd_kernel_launches", "tpmd_decode_noalloc", "tpmd_device_status", "tpmd_debug_expire_wait",
+           "tpmd_gguf_read", "tpmd_load_gguf",
            "tpmd_set_feats_device", "tpme_create", "tpme_create_error", "tpme_destroy", "tpme_last_error",
            "tpme_set_tensor", "tpme_load_gguf", "tpme_prepare", "tpme_run", "tpme_feat_device",
            "tpmd_gguf_read_kv", "tpfm_default_config", "tpfm_create", "tpfm_create_error", "tpfm_destroy",
@@ -85,6 +86,8 @@ def load_library(path: str = LIB_PATH):
     L.tpmd_profile_end.argtypes = [v, C.c_char_p, C.c_size_t]
     L.tpmd_kernel_launches.argtypes = [v, i64]
     L.tpmd_decode_noalloc.argtypes = [v, v, i64, v, v]
+    L.tpmd_device_status.argtypes = [v, v]
+    L.tpmd_debug_expire_wait.argtypes = [v, C.c_longlong]
     L.tpmd_kernel_launches.restype = i64
     L.tpmd_gguf_read.argtypes = [cp, cp, C.c_int, GGUF_TENSOR_FN, v, C.c_char_p, C.c_size_t]
     L.tpmd_load_gguf.argtypes = [v, cp]
@@ -296,6 +299,15 @@ class MotionDecoder:
         """device pointers, enqueued on `stream` (cudaStream_t as int)"""
         self._check(self._L.tpmd_decode_device(self._h, C.c_void_p(styles_ptr), n,
                                                C.c_void_p(frames_ptr), C.c_void_p(stream)))
+
+    def device_status(self, stream: int = 0):
+        """raise TpmdError if a kernel of the device entry points reported an
+        expired pipeline wait since the last query (tpmd_device_status)"""
+        self._check(self._L.tpmd_device_status(self._h, stream or None))
+
+    def debug_expire_wait(self, wait_ns: int):
+        """test hook: the next decode's first tcgen05 conv lets a wait expire"""
+        self._check(self._L.tpmd_debug_expire_wait(self._h, int(wait_ns)))
 
     def taps(self, style: np.ndarray, level: int) -> dict:
         """Parity taps of one frame at `level` (see tpmd_decode_taps)."""

@@ -1,12 +1,13 @@
 """The allocation-free decode entry point (tpmd_decode_noalloc).
 
-It serves callers that must not allocate GPU memory while decoding (a CUDA
-graph capture in progress, a real-time loop, a host memory manager that owns
-the GPU); its scratch is a static device array inside libtpmd.so. Checked
-through the C ABI against the regular device entry point, on two calls in a
-row (the second runs over the scratch the first left behind), at the same
-tolerance as the batch-composition tests: bit-identical frames. This file is
-named to be collected last."""
+It serves callers that cannot call cudaMalloc while they decode: real-time
+frame loops that must not risk an allocator stall or an out-of-memory error
+mid-stream, and hosts whose memory manager owns the GPU's memory. Its scratch
+is a static device array inside libtpmd.so. Checked through the C ABI
+against the regular device entry point, on two calls in a row (the second
+runs over the scratch the first left behind), at the same tolerance as the
+batch-composition tests: bit-identical frames, each call's device status
+read through tpmd_device_status. This file is named to be collected last."""
 from __future__ import annotations
 
 import ctypes as C
@@ -37,7 +38,9 @@ def test_noalloc_matches_decode_device(model):
         rc = L.tpmd_decode_noalloc(C.c_void_p(dec._h), C.c_void_p(st[i:i + 1].data_ptr()), 1,
                                    C.c_void_p(out.data_ptr()), None)
         assert rc == 0, L.tpmd_last_error(C.c_void_p(dec._h)).decode()
-        torch.cuda.synchronize()
+        # the frames count only once the device status is clean
+        rc = L.tpmd_device_status(C.c_void_p(dec._h), None)
+        assert rc == 0, L.tpmd_last_error(C.c_void_p(dec._h)).decode()
         got = out.cpu().numpy()[0]
         print(f"noalloc call {i}: cos {cosine(got, ref[i]):.9f} max-abs {max_abs(got, ref[i]):.3e}")
         assert np.array_equal(got, ref[i])
