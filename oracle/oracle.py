@@ -1,5 +1,6 @@
 """ctypes bindings for the CPU oracle (liboracle.so) and, when built, the
-reference's own op code (_ref/libtpref.so).
+reference's own op code (_ref/libtpref.so) and its own decoder, encoder and
+weight loader over a ggml stand-in (_ref/libtpgraph.so, see RefGraph).
 
 TEST INFRASTRUCTURE ONLY: imported by tests/, __graft_entry__.smoke() and
 bench.py's CPU-baseline / reference legs, as the checker. The product
@@ -15,10 +16,15 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "liboracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libtpref.so")
+GRAPH_SO = os.path.join(HERE, "_ref", "libtpgraph.so")
 
 # f16 emulation flags for Decoder.decode(mode=...), see tp_oracle.h
-F16_WEIGHTS, F16_FEATS, F16_ACTS, F16_OUT = 0x10, 0x20, 0x40, 0x80
-REF_F16 = F16_WEIGHTS | F16_FEATS | F16_ACTS  # the reference's f16 mode
+F16_WEIGHTS, F16_FEATS, F16_ACTS, F16_OUT, F16_FOLD = 0x10, 0x20, 0x40, 0x80, 0x100
+REF_F16 = F16_WEIGHTS | F16_FEATS | F16_ACTS  # f16 weights, feats and conv inputs
+# the reference's f16 fast graph as it runs (use with mode 1): REF_F16 plus its
+# fold-into-weights rule and f16 style GEMVs (pinned against oracle/_ref's
+# build of the reference's own graph)
+REF_F16_GRAPH = REF_F16 | F16_FOLD
 
 ST_IC = (512, 512, 512, 512, 256, 128, 64)
 ST_OC = (512, 512, 512, 256, 128, 64, 32)
@@ -411,3 +417,108 @@ def set_threads(n: int) -> None:
 
 def threads() -> int:
     return lib().orc_get_threads()
+
+
+_graph = None
+
+
+def graph_lib():
+    """oracle/_ref/libtpgraph.so (built by ref_build.py), or None if absent."""
+    global _graph
+    if _graph is None and os.path.exists(GRAPH_SO):
+        L = C.CDLL(GRAPH_SO)
+        v = C.c_void_p
+        L.rg_create.argtypes = [C.c_char_p, C.c_int, C.c_int, C.c_char_p, C.c_size_t]
+        L.rg_create.restype = v
+        L.rg_destroy.argtypes = [v]
+        L.rg_error.argtypes = [v]
+        L.rg_error.restype = C.c_char_p
+        L.rg_tensor.argtypes = [v, C.c_char_p, v, C.c_int64]
+        L.rg_tensor.restype = C.c_int64
+        L.rg_build.argtypes = [v, C.c_int, C.c_int, C.c_int]
+        L.rg_batch.argtypes = [v]
+        L.rg_set_feats.argtypes = [v, C.POINTER(v)]
+        L.rg_decode.argtypes = [v, v, v, C.c_int]
+        L.rg_decode_batch.argtypes = [v, v, v]
+        L.rg_tap.argtypes = [v, C.c_char_p, v, C.c_int64]
+        L.rg_tap.restype = C.c_int64
+        L.rg_enc_run.argtypes = [v, v, v, v, v, C.POINTER(v), C.c_int]
+        _graph = L
+    return _graph
+
+
+class RefGraph:
+    """The reference's own motion_ae path run on the CPU: weights_t::load of a
+    GGUF file (src/gguf_load.cpp) with motion_ae_scale (src/motion_enc.cpp),
+    motion_dec::prepare / build / set_feats / decode / decode_batch
+    (src/motion_dec.cpp) and motion_enc::run, compiled from the reference's
+    sources over the stand-in in oracle/refgraph/. keep_f16 is the
+    reference's f16 fast path (tp_ctx::load with ftype "f16")."""
+
+    def __init__(self, gguf_path: str, keep_f16: bool = False, gpu: bool = False):
+        L = graph_lib()
+        if L is None:
+            raise RuntimeError("oracle/_ref/libtpgraph.so not built (reference absent)")
+        self._L = L
+        err = C.create_string_buffer(512)
+        self._h = L.rg_create(gguf_path.encode(), int(keep_f16), int(gpu), err, len(err))
+        if not self._h:
+            raise RuntimeError(err.value.decode())
+
+    def _ck(self, rc):
+        if rc != 0:
+            raise RuntimeError(self._L.rg_error(self._h).decode())
+
+    def tensor(self, name: str) -> np.ndarray:
+        """a loaded weight or a prepare()-derived tensor, f32, ggml order"""
+        n = self._L.rg_tensor(self._h, name.encode(), None, 0)
+        if n < 0:
+            raise KeyError(name)
+        out = np.empty(n, np.float32)
+        self._L.rg_tensor(self._h, name.encode(), _p(out), n)
+        return out
+
+    def build(self, taps: bool = False, batch: int = 1, stages: int = 7) -> int:
+        """stages < 7: the graph ends at that stage and its image is the rgb
+        skip [3][r][r] of stage r = 8 << (stages - 1)"""
+        self._ck(self._L.rg_build(self._h, int(taps), batch, stages))
+        self.stages = stages
+        return self._L.rg_batch(self._h)
+
+    def set_feats(self, feats):
+        arrs = [np.ascontiguousarray(f, np.float32) for f in feats]
+        self._keep = arrs
+        self._ck(self._L.rg_set_feats(self._h, (C.c_void_p * 7)(*[a.ctypes.data for a in arrs])))
+
+    def decode(self, style, taps: bool = False) -> np.ndarray:
+        st = np.ascontiguousarray(style, np.float32)
+        img = np.empty((3, 512, 512), np.float32)
+        self._ck(self._L.rg_decode(self._h, _p(st), _p(img), int(taps)))
+        return img
+
+    def decode_batch(self, styles) -> np.ndarray:
+        st = np.ascontiguousarray(styles, np.float32)
+        out = np.empty((st.shape[0], 3, 512, 512), np.float32)
+        self._ck(self._L.rg_decode_batch(self._h, _p(st), _p(out)))
+        return out
+
+    def tap(self, name: str) -> np.ndarray:
+        n = self._L.rg_tap(self._h, name.encode(), None, 0)
+        if n < 0:
+            raise KeyError(name)
+        out = np.empty(n, np.float32)
+        self._L.rg_tap(self._h, name.encode(), _p(out), n)
+        return out
+
+    def encode(self, image, taps: bool = False) -> dict:
+        img = np.ascontiguousarray(image, np.float32)
+        app, lam, mot = np.empty(512, np.float32), np.empty(20, np.float32), np.empty(512, np.float32)
+        feats = [np.empty(((8 << j) ** 2, ST_OC[j]), np.float32) for j in range(7)]
+        ptrs = (C.c_void_p * 7)(*[f.ctypes.data for f in feats])
+        self._ck(self._L.rg_enc_run(self._h, _p(img), _p(app), _p(lam), _p(mot), ptrs, int(taps)))
+        return dict(appearance=app, lam=lam, motion=mot, feats=feats)
+
+    def __del__(self):
+        if getattr(self, "_h", None):
+            self._L.rg_destroy(self._h)
+            self._h = None

@@ -17,8 +17,15 @@ oracle/_ref/, which git ignores. The CUDA kernels run on the host by looping
 over every (block, thread) index. Their outputs pin the oracle's op
 restatements and generate the golden vectors under tests/golden/.
 
+It also builds oracle/_ref/libtpgraph.so, the graph-level pin: the
+reference's own src/motion_dec.cpp, src/motion_enc.cpp and src/gguf_load.cpp,
+compiled where they lie against the ggml stand-in in oracle/refgraph/, with
+the patch's op constructors (src/ggml.c part of the patch) and CPU forward
+functions extracted the same way.
+
 Usage: python oracle/ref_build.py [--reference DIR]
-Exits 0 without doing anything when the reference tree is absent.
+The reference tree is DIR, else $TP_REFERENCE, else BASELINE.json's
+"reference_path". Exits 0 without doing anything when it is absent.
 """
 from __future__ import annotations
 
@@ -29,7 +36,7 @@ import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT_DIR = os.path.join(HERE, "_ref")
-DEFAULT_REF = "/root/reference"
+GRAPH_DIR = os.path.join(HERE, "refgraph")
 
 # (file inside the patch, signature marker) for every function to extract
 CPU_FUNCS = [
@@ -42,6 +49,22 @@ CPU_FUNCS = [
     "void ggml_compute_forward_clsp_lerp(",
     "void ggml_compute_forward_flow_grid(",
 ]
+# the patch's op constructors (src/ggml.c), needed by the graph-level pin
+GRAPH_CTORS = [
+    "struct ggml_tensor * ggml_im2col_cf(",
+    "struct ggml_tensor * ggml_bilinear_gather(",
+    "struct ggml_tensor * ggml_flow_grid(",
+    "struct ggml_tensor * ggml_bilinear_gather_planar(",
+    "struct ggml_tensor * ggml_bilinear_gather_sp(",
+    "struct ggml_tensor * ggml_bias_lrelu(",
+    "struct ggml_tensor * ggml_subpix_lrelu(",
+    "struct ggml_tensor * ggml_subpix_lrelu_cl(",
+    "struct ggml_tensor * ggml_upfirdn2x(",
+    "struct ggml_tensor * ggml_clsp_mul(",
+    "struct ggml_tensor * ggml_clsp_lerp(",
+]
+# the reference's own sources compiled for the graph-level pin
+GRAPH_SOURCES = ["src/motion_dec.cpp", "src/motion_enc.cpp", "src/gguf_load.cpp"]
 CUDA_FUNCS = [
     ("src/ggml-cuda/bilinear-gather.cu", "template <typename T, bool SP>"),
     ("src/ggml-cuda/im2col.cu", "template <typename T, bool IC_POW2>"),
@@ -79,10 +102,52 @@ def extract_function(lines: list[str], marker: str) -> str:
     raise ValueError(f"unterminated function at {marker!r}")
 
 
+def reference_dir(arg: str | None) -> str | None:
+    """--reference, else $TP_REFERENCE, else BASELINE.json's reference_path"""
+    if arg:
+        return arg
+    if os.environ.get("TP_REFERENCE"):
+        return os.environ["TP_REFERENCE"]
+    bj = os.path.join(os.path.dirname(HERE), "BASELINE.json")
+    if os.path.exists(bj):
+        import json
+        return json.load(open(bj)).get("reference_path")
+    return None
+
+
+def build_graph(ref: str, added: dict[str, list[str]]) -> str:
+    """oracle/_ref/libtpgraph.so: the reference's decoder, encoder and loader
+    over the stand-in"""
+    parts = [f"// GENERATED by oracle/ref_build.py from {ref}/patches; git-ignored.\n",
+             '#include "ggml.h"\n#include <cmath>\n']
+    for marker in GRAPH_CTORS:
+        parts.append(extract_function(added["src/ggml.c"], marker))
+    for marker in CPU_FUNCS:
+        parts.append(extract_function(added["src/ggml-cpu/ops.cpp"], marker))
+    src = os.path.join(OUT_DIR, "patch_graph_ops.cpp")
+    with open(src, "w") as f:
+        f.write("\n".join(parts))
+    so = os.path.join(OUT_DIR, "libtpgraph.so")
+    srcs = [os.path.join(GRAPH_DIR, "graph.cpp"), os.path.join(GRAPH_DIR, "wrap.cpp"), src] + \
+        [os.path.join(ref, s) for s in GRAPH_SOURCES]
+    deps = srcs + [os.path.join(GRAPH_DIR, h) for h in os.listdir(GRAPH_DIR) if h.endswith(".h")]
+    if os.path.exists(so) and os.path.getmtime(so) >= max(os.path.getmtime(d) for d in deps):
+        return so
+    cmd = ["g++", "-O2", "-march=x86-64-v3", "-std=gnu++17", "-fPIC", "-shared", "-fopenmp",
+           "-I", GRAPH_DIR, "-I", os.path.join(ref, "src"), "-o", so] + srcs
+    subprocess.run(cmd, check=True)
+    return so
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=DEFAULT_REF)
+    ap.add_argument("--reference", default=None)
     args = ap.parse_args()
+    ref = reference_dir(args.reference)
+    if not ref:
+        print("ref_build: no reference tree named; using any prebuilt oracle/_ref")
+        return 0
+    args.reference = ref
     patch = os.path.join(args.reference, "patches", "ggml-tp-ops.patch")
     if not os.path.exists(patch):
         print(f"ref_build: {patch} absent; using any prebuilt oracle/_ref")
@@ -106,6 +171,7 @@ def main() -> int:
            "-o", so, src]
     subprocess.run(cmd, check=True)
     print(f"ref_build: built {so}")
+    print(f"ref_build: built {build_graph(args.reference, added)}")
     return 0
 
 

@@ -493,8 +493,11 @@ struct orc_dec {
 
     const std::vector<float> &get(const std::string &n) const { return t.at(n); }
 
-    // s = Wmod * latent + bmod (src/motion_dec.cpp:267-272)
-    std::vector<float> style_of(const std::string &base, const float *lat) const {
+    // s = Wmod * latent + bmod (src/motion_dec.cpp:267-272). f16: the
+    // reference keeps the modulation weights f16 in its f16 mode (every
+    // file-f16 tensor of >= 4096 elements, src/gguf_load.cpp:149-153), and a
+    // GEMM with f16 weights rounds its other operand to f16 too
+    std::vector<float> style_of(const std::string &base, const float *lat, bool f16 = false) const {
         const std::vector<float> &Wm = get(base + ".modulation.weight");
         const std::vector<float> &bm = get(base + ".modulation.bias");
         const int IC = (int) bm.size();
@@ -502,7 +505,8 @@ struct orc_dec {
         for (int i = 0; i < IC; i++) {
             double a = 0;
             const float *w = Wm.data() + (size_t) i * 512;
-            for (int k = 0; k < 512; k++) a += (double) w[k] * lat[k];
+            for (int k = 0; k < 512; k++)
+                a += f16 ? (double) r16(w[k]) * r16(lat[k]) : (double) w[k] * lat[k];
             s[(size_t) i] = (float) a + bm[(size_t) i];
         }
         return s;
@@ -534,11 +538,56 @@ namespace {
 
 // modulated dense 3x3 conv, map-side style (src/motion_dec.cpp:597-608):
 // lrelu(conv(x*s, W)/den + bias)
+// The reference's f16 fast graph (ORC_F16_FOLD) multiplies the style and
+// 1/den into the f16 weights when the map is larger than the weights,
+// 4|W| < 2 N (IC + OC') (src/motion_dec.cpp:322-337), and always at the
+// spatial stages (maps >= 256, src/motion_dec.cpp:452-466); the folded
+// weights are rounded to f16 and the unstyled map is rounded to f16 as the
+// GEMM's other operand. Otherwise it multiplies the map (rounded to f16 after
+// the style) and divides by den after the GEMM. conv1 (4x4) is map side.
+bool ref_folds(int64_t wsz, int64_t N, int64_t IC, int64_t OCp, int out_map) {
+    if (out_map >= 256) return true;
+    if (out_map <= 4) return false;
+    return 4 * wsz < 2 * N * (IC + OCp);
+}
+
 std::vector<float> styled_conv_exact(const orc_dec &d, const std::vector<float> &x, int IC,
                                      int Hh, const std::string &base, const float *lat,
                                      int flags) {
-    const std::vector<float> s = d.style_of(base + ".conv", lat);
+    const bool fold16 = (flags & ORC_F16_FOLD) != 0;
+    const std::vector<float> s = d.style_of(base + ".conv", lat, fold16);
     const std::vector<float> den = d.demod_den(base + ".conv.weight", s);
+    if (fold16) {
+        const std::vector<float> &W0 = d.get(base + ".conv.weight");
+        const std::vector<float> &ab = d.get(base + ".activate.bias");
+        const int OC = (int) ab.size();
+        const size_t P = (size_t) Hh * Hh;
+        const bool fold = ref_folds((int64_t) 9 * IC * OC, (int64_t) P, IC, OC, Hh);
+        std::vector<float> W(W0.size()), xs(x.size());
+        for (int o = 0; o < OC; o++)
+            for (int i = 0; i < IC; i++)
+                for (int k = 0; k < 9; k++) {
+                    const size_t q = ((size_t) o * IC + i) * 9 + k;
+                    W[q] = fold ? r16(r16(W0[q]) * s[(size_t) i] / den[(size_t) o]) : r16(W0[q]);
+                }
+        // conv1's constant input is itself stored f16; the styled map is the
+        // product of f16 operands rounded to f16 (an f16 elementwise result)
+        const bool f16_input = Hh == 4;
+        for (int i = 0; i < IC; i++)
+            for (size_t p = 0; p < P; p++) {
+                const float v = f16_input ? r16(x[i * P + p]) : x[i * P + p];
+                xs[i * P + p] = fold ? r16(v) : r16(v * s[(size_t) i]);
+            }
+        std::vector<float> y((size_t) OC * P);
+        conv2d(xs.data(), IC, Hh, Hh, W.data(), OC, 3, 3, 1, 1, Hh, Hh, y.data());
+#pragma omp parallel for schedule(static)
+        for (int o = 0; o < OC; o++)
+            for (size_t p = 0; p < P; p++) {
+                const float v = fold ? y[o * P + p] : y[o * P + p] / den[(size_t) o];
+                y[o * P + p] = lrelu(v + ab[(size_t) o], 0.2f);
+            }
+        return y;
+    }
     std::vector<float> Wr;
     if (flags & ORC_F16_WEIGHTS) {
         Wr = d.get(base + ".conv.weight");
@@ -572,7 +621,8 @@ std::vector<float> styled_conv_exact(const orc_dec &d, const std::vector<float> 
 std::vector<float> styled_conv_up(const orc_dec &d, const std::vector<float> &x, int IC,
                                   int Hh, const std::string &base, const float *lat,
                                   int mode, int flags) {
-    const std::vector<float> s = d.style_of(base + ".conv", lat);
+    const bool fold16 = mode == 1 && (flags & ORC_F16_FOLD) != 0;
+    const std::vector<float> s = d.style_of(base + ".conv", lat, fold16);
     const std::vector<float> den = d.demod_den(base + ".conv.weight", s);
     const std::vector<float> &W = d.get(base + ".conv.weight");
     const std::vector<float> &ab = d.get(base + ".activate.bias");
@@ -625,11 +675,22 @@ std::vector<float> styled_conv_up(const orc_dec &d, const std::vector<float> &x,
                     for (int kw = 0; kw < 3; kw++)
                         w4[(((size_t) q * IC + i) * 3 + kh) * 3 + kw] =
                             T[(size_t) q * R + i + (size_t) IC * (kw + 3 * kh)];
-        if (flags & ORC_F16_WEIGHTS) round16(w4);
+        // f16 fast graph: fold (style, 1/den) into the f16 composed weights
+        // or multiply the map, by the reference's rule (see ref_folds)
+        const bool fold = fold16 && ref_folds((int64_t) 9 * IC * 4 * OC, (int64_t) P, IC, 4 * OC, H2);
+        if (fold16)
+            for (int q = 0; q < 4 * OC; q++)
+                for (int i = 0; i < IC; i++)
+                    for (int k = 0; k < 9; k++) {
+                        float &v = w4[((size_t) q * IC + i) * 9 + k];
+                        v = fold ? r16(r16(v) * s[(size_t) i] / den[(size_t) (q % OC)]) : r16(v);
+                    }
+        else if (flags & ORC_F16_WEIGHTS)
+            round16(w4);
         std::vector<float> xs(x.size());
         for (int i = 0; i < IC; i++)
-            for (size_t p = 0; p < P; p++) xs[i * P + p] = x[i * P + p] * s[(size_t) i];
-        if (flags & ORC_F16_ACTS) round16(xs);
+            for (size_t p = 0; p < P; p++) xs[i * P + p] = fold ? x[i * P + p] : x[i * P + p] * s[(size_t) i];
+        if (flags & (ORC_F16_ACTS | ORC_F16_FOLD)) round16(xs);
         std::vector<float> y4((size_t) 4 * OC * P);
         conv2d(xs.data(), IC, Hh, Hh, w4.data(), 4 * OC, 3, 3, 1, 1, Hh, Hh, y4.data());
 #pragma omp parallel for schedule(static)
@@ -637,8 +698,8 @@ std::vector<float> styled_conv_up(const orc_dec &d, const std::vector<float> &x,
             for (int Y = 0; Y < H2; Y++)
                 for (int X = 0; X < H2; X++) {
                     const int k = (Y & 1) * 2 + (X & 1);
-                    const float v = y4[((size_t) (k * OC + o)) * P + (size_t) (Y >> 1) * Hh + (X >> 1)] /
-                                    den[(size_t) o];
+                    const float a = y4[((size_t) (k * OC + o)) * P + (size_t) (Y >> 1) * Hh + (X >> 1)];
+                    const float v = fold ? a : a / den[(size_t) o];
                     out[((size_t) o * H2 + Y) * H2 + X] = lrelu(v + ab[(size_t) o], 0.2f);
                 }
     }
@@ -753,7 +814,7 @@ int orc_dec_decode(orc_dec *d, const float *lat, int mode, int keep, float *img)
         d->tap(keep, R + ".conv2", out.data(), out.size());
 
         // ToFlow: 1x1 modulated conv (no demod) + bias + upsample2x(skip_flow)
-        const std::vector<float> fs = d->style_of(std::string(bf) + ".conv", lat);
+        const std::vector<float> fs = d->style_of(std::string(bf) + ".conv", lat, (flags & ORC_F16_FOLD) != 0);
         const std::vector<float> &fW = d->get(std::string(bf) + ".conv.weight");
         const std::vector<float> &fb = d->get(std::string(bf) + ".bias");
         const std::vector<float> &fup = d->get(std::string(bf) + ".upsample.kernel");
@@ -789,11 +850,11 @@ int orc_dec_decode(orc_dec *d, const float *lat, int mode, int keep, float *img)
 
         std::vector<float> samp_cl((size_t) OC * N);
         std::vector<float> f16feat;
-        if (flags & ORC_F16_FEATS) {
+        if (flags & (ORC_F16_FEATS | ORC_F16_FOLD)) {
             f16feat = d->feat[j];
             round16(f16feat);
         }
-        orc_bilinear_gather((flags & ORC_F16_FEATS) ? f16feat.data() : d->feat[j].data(), 0, OC, r,
+        orc_bilinear_gather((flags & (ORC_F16_FEATS | ORC_F16_FOLD)) ? f16feat.data() : d->feat[j].data(), 0, OC, r,
                             r, grid.data(), (int64_t) N, 0, 0, samp_cl.data());
         std::vector<float> warp((size_t) OC * N), trunk((size_t) OC * N);
 #pragma omp parallel for schedule(static)

@@ -90,6 +90,13 @@ int orc_dec_prepare(orc_dec *d);
 #define ORC_F16_FEATS 0x20
 #define ORC_F16_ACTS 0x40
 #define ORC_F16_OUT 0x80
+/* ORC_F16_FOLD (mode 1): the reference's f16 fast graph as it runs
+ * (src/motion_dec.cpp:283-337, 452-466 with keep_f16 weights): f16
+ * modulation weights and latent in the style GEMVs, f16 constant input and
+ * feats, and per conv either the style and 1/den folded into f16 weights
+ * (maps larger than the weights, and every conv at r256/r512) or the styled
+ * map rounded to f16 with /den after the GEMM. */
+#define ORC_F16_FOLD 0x100
 int orc_dec_decode(orc_dec *d, const float *style, int mode, int keep_taps,
                    float *img);
 /* copy a recorded tap (names as in src/motion_dec.cpp:805-883); returns

@@ -149,7 +149,7 @@ def test_stress_random_init(stress_model):
     g32, g16 = d32.decode(st), d16.decode(st)
     for i in range(len(st)):
         ref = od.decode(st[i], mode=0)
-        ref16 = od.decode(st[i], mode=1 | O.REF_F16)
+        ref16 = od.decode(st[i], mode=1 | O.REF_F16_GRAPH)
         c32 = cosine(g32[i], ref)
         s16, sref = ssim(g16[i], ref), ssim(ref16, ref)
         print(f"stress frame {i}: f32 cos {c32:.7f}; f16 ssim {s16:.4f} vs reference-f16 {sref:.4f}")

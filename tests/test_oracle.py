@@ -214,11 +214,11 @@ def test_decoder_rejects_bad_tensors(model):
 
 
 def test_reference_f16_arithmetic_meets_gate(model, oracle_dec, oracle_frames):
-    """the reference's f16 mode (f16 weights, feats and GEMM inputs, emulated)
-    meets SSIM >= 0.99 against fp32 on the parity configuration, so the gate
-    is one the reference itself passes"""
+    """the reference's f16 mode (its f16 fast graph, emulated and pinned in
+    test_refgraph.py) meets SSIM >= 0.99 against fp32 on the parity
+    configuration, so the gate is one the reference itself passes"""
     from metrics import ssim
-    f16 = oracle_dec.decode(model["styles"][0], mode=1 | O.REF_F16)
+    f16 = oracle_dec.decode(model["styles"][0], mode=1 | O.REF_F16_GRAPH)
     s = ssim(f16, oracle_frames[0])
     print(f"reference-f16 emulation: ssim {s:.5f} cos {cosine(f16, oracle_frames[0]):.6f}")
     assert s >= 0.99
