@@ -4,8 +4,11 @@ One step = one decode of a 50-frame chunk (f16 weights,
 per-frame styles from a seeded random walk, one shared source latent and
 feature pyramid, output [50, 3, 512, 512] f32) on every GPU. Multi-GPU runs
 (torchrun, one process per GPU) shard frames: each rank decodes its own
-50-frame chunk per step (weak scaling); the prepared weights and the feature
-pyramid are broadcast once from rank 0 over NCCL. No per-step collective.
+50-frame chunk per step (weak scaling). The decoder is a tpmd_group (C++
+behind the C ABI): each rank joins the group's NCCL clique, the prepared
+weights and the feature pyramid are broadcast once from rank 0 by the group,
+and the max over ranks is the group's NCCL all-reduce. No per-step
+collective.
 
 value   frames/s over all ranks, device-timed with CUDA events on the launch
         stream, inputs and outputs resident in HBM, max over ranks.
@@ -197,11 +200,21 @@ def cpu_baseline(tensors, feats, styles, budget_s: float = 12.0):
                       f"{dt:.1f} s wall clock, oracle sub-pixel graph"}
 
 
-def setup_inputs(rank: int, frames: int):
-    import tpmd
-    from tpmd import synth
+def load_synth():
+    """the seeded input generators (tpmd/synth.py, numpy only), loaded as a
+    plain module so the reference arm imports nothing of the product"""
+    import importlib.util
+    path = os.path.join(ROOT, "talking-portrait.cpp_b200", "tpmd", "synth.py")
+    spec = importlib.util.spec_from_file_location("tp_synth", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def setup_inputs(rank: int, frames: int, scale_for):
+    synth = load_synth()
     raw = synth.make_weights(seed=0)
-    tensors = synth.fold(raw, tpmd.scale_for)
+    tensors = synth.fold(raw, scale_for)
     feats = synth.make_feats(seed=0)
     styles = synth.styles_walk(seed=0, n=frames, clip=rank)
     return tensors, feats, styles
@@ -210,8 +223,8 @@ def setup_inputs(rank: int, frames: int):
 def run_reference(args, rank: int, world: int):
     if rank != 0:
         return
-    tensors, feats, styles = setup_inputs(0, max(8, args.warmup + args.steps))
     import oracle as O
+    tensors, feats, styles = setup_inputs(0, max(8, args.warmup + args.steps), O.scale_for)
     O.set_threads(os.cpu_count() or 1)  # all host threads (torchrun exports OMP_NUM_THREADS=1)
     dec = O.Decoder(tensors, feats)
     for i in range(args.warmup):
@@ -447,6 +460,105 @@ def run_e2e(args):
         dist.destroy_process_group()
 
 
+def run_ops(args):
+    """BASELINE config 1, the decoder's op-level sweep on cuda:0.
+
+    (b) tpk_bilinear_gather over C in {32..512} x H=W in {8..512}, grid
+        uniform in [-1.1, 1.1], f32 and f16 feats; (c) tpk_im2col_cf 3x3 pad 1
+        on the same shapes (f16 and f32 destinations). Each launch is timed
+        alone with CUDA events on its stream after a 256 MB L2 flush; GB/s are
+        compulsory bytes (gather: C*H*W*sizeof(feat) + 8N + 4CN with N = H*W;
+        im2col: 4*IC*IW*IH + 9*IC*OW*OH*sizeof(dst)) over the median launch
+        time, as a fraction of MEASURED_PEAKS.json's copy bandwidth.
+    (a) the modulated convs of every level at batch 1..64: a decode of that
+        many frames with live per-kernel CUDA-event timing
+        (tpmd_profile_begin/end); TFLOP/s per up-conv / conv2 launch against
+        the measured bf16 peak."""
+    import torch
+    import tpmd
+    from tpmd import synth
+    hbm, tf_burst, tf_sus, src = peaks()
+    dev = torch.device("cuda", 0)
+    flush = torch.empty(64 << 20, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream()
+    rng = np.random.default_rng(0)
+
+    def timed(fn, reps=5):
+        ts = []
+        for i in range(reps + 1):
+            flush.fill_(float(i))
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+            e1.synchronize()
+            if i:
+                ts.append(e0.elapsed_time(e1) / 1e3)
+        return float(np.median(ts))
+
+    chans = (32, 64, 128, 256, 512)
+    sizes = (8, 16, 32, 64, 128, 256, 512)
+    gather, im2col = [], []
+    for C in chans:
+        for H in sizes:
+            N = H * H
+            grid = torch.from_numpy(rng.uniform(-1.1, 1.1, (N, 2)).astype(np.float32)).to(dev)
+            out = torch.empty((N, C), dtype=torch.float32, device=dev)
+            for dt, es in ((torch.float32, 4), (torch.float16, 2)):
+                feat = torch.randn((N, C), device=dev).to(dt)
+                t = timed(lambda: tpmd.bilinear_gather(feat, H, H, grid, out, stream=stream.cuda_stream))
+                b = C * N * es + 8 * N + 4 * C * N
+                gather.append({"C": C, "H": H, "feat": "f16" if es == 2 else "f32", "us": t * 1e6,
+                               "GBps": b / t / 1e9, "frac": b / t / 1e9 / hbm,
+                               "tap_GBps": 4 * C * N * es / t / 1e9})
+                del feat
+            src_t = torch.randn((N, C), device=dev)
+            for dt, es in ((torch.float16, 2), (torch.float32, 4)):
+                dst = torch.empty((N, 9 * C), dtype=dt, device=dev)
+                t = timed(lambda: tpmd.im2col_cf(src_t, C, H, H, 1, dst, stream=stream.cuda_stream))
+                b = 4 * C * N + 9 * C * N * es
+                im2col.append({"C": C, "H": H, "dst": "f16" if es == 2 else "f32", "us": t * 1e6,
+                               "GBps": b / t / 1e9, "frac": b / t / 1e9 / hbm})
+                del dst
+            del src_t, out, grid
+    torch.cuda.synchronize()
+    # (a) modconv per level at batch 1..64 through live per-kernel timing
+    raw = synth.make_weights(seed=0)
+    tensors = synth.fold(raw, tpmd.scale_for)
+    feats = synth.make_feats(seed=0)
+    modconv = []
+    for B in (1, 2, 4, 8, 16, 32, 64):
+        d = tpmd.MotionDecoder(0, tpmd.DTYPE_F16, B)
+        d.set_tensors(tensors)
+        d.prepare()
+        d.set_feats(feats)
+        st = torch.from_numpy(synth.styles_walk(seed=0, n=B)).to(dev)
+        fr = torch.empty((B, 3, 512, 512), device=dev)
+        for _ in range(2):
+            d.decode_device(st.data_ptr(), B, fr.data_ptr(), stream.cuda_stream)
+        d.profile_begin()
+        for _ in range(3):
+            d.decode_device(st.data_ptr(), B, fr.data_ptr(), stream.cuda_stream)
+        prof = d.profile_end()
+        for name, (n, ms) in prof.items():
+            if name.startswith(("upconv_r", "conv2_r", "conv2tail_r")) or name == "conv1":
+                flops, _ = kernel_work(name, B, 2)
+                modconv.append({"batch": B, "kernel": name, "us": ms / n * 1e3,
+                                "TFLOPs": flops / (ms / n / 1e3) / 1e12,
+                                "frac": flops / (ms / n / 1e3) / 1e12 / tf_burst})
+        d.close()
+        del st, fr
+    g_f16 = [g for g in gather if g["feat"] == "f16"]
+    line = {"metric": "decoder op sweep (config 1)", "unit": "GB/s | TFLOP/s", "n_gpus": 1,
+            "data": "synthetic (N(0,1) maps, grid uniform in [-1.1, 1.1]; random-init decoder)",
+            "peaks": {"hbm_gbs": hbm, "bf16_tflops_burst": tf_burst, "source": src},
+            "gather_best_frac": max(g["frac"] for g in gather),
+            "gather_f16_median_frac_large": float(np.median([g["frac"] for g in g_f16 if g["H"] >= 128])),
+            "im2col_best_frac": max(g["frac"] for g in im2col),
+            "gather": gather, "im2col": im2col, "modconv": modconv}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -458,7 +570,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--clip", type=int, default=0,
                     help="config 3: decode a clip of this many frames sharded across ranks per step")
-    ap.add_argument("--path", default="decoder", choices=["decoder", "encoder", "fmt", "e2e"],
+    ap.add_argument("--path", default="decoder", choices=["decoder", "encoder", "fmt", "e2e", "ops"],
                     help="encoder: time the motion encoder (once per portrait); fmt: time the "
                          "flow-matching sampler (one 50-frame chunk per step); one GPU")
     args = ap.parse_args()
@@ -470,6 +582,9 @@ def main():
         return
     if args.path == "e2e":
         run_e2e(args)
+        return
+    if args.path == "ops":
+        run_ops(args)
         return
 
     rank = int(os.environ.get("RANK", "0"))
@@ -485,27 +600,31 @@ def main():
     from tpmd import multi, synth
 
     torch.cuda.set_device(local)
+    nccl_id = None
     if world > 1:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
+        box = [tpmd.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(box, src=0)  # the C++ group's NCCL clique id
+        nccl_id = box[0]
     nb = args.batch
-    tensors, feats, styles = setup_inputs(rank, nb)
+    tensors, feats, styles = setup_inputs(rank, nb, tpmd.scale_for)
     dtype = tpmd.DTYPE_F16 if args.dtype == "f16" else tpmd.DTYPE_F32
-    dec = tpmd.MotionDecoder(local, dtype, max_batch=nb)
-
-    # weights + feats: prepared on rank 0, broadcast once over NCCL
+    # the decoder group (tpmd_group_*, C++ behind the C ABI): this rank's GPU
+    # in a clique of `world`; weights and feats are prepared on rank 0 and
+    # broadcast once by the group's own NCCL communicator
+    group = tpmd.MotionDecoderGroup((local,), dtype, nb, rank=rank, nranks=world, nccl_id=nccl_id)
     if rank == 0:
-        dec.set_tensors(tensors)
-        dec.prepare()
-        dec.set_feats(feats)
-    if world > 1:
-        multi.share_decoder(dec, rank, torch.device("cuda", local))
+        group.set_tensors(tensors)
+    group.prepare()
+    group.set_feats(feats if rank == 0 else None)
+    dec = group.member(0)
 
     stream = torch.cuda.Stream()  # the launch stream; CUDA events are recorded on it
     if args.clip:
         # config 3: a clip of args.clip frames sharded by frame across ranks
-        lo, hi = multi.frame_range(args.clip, world, rank)
+        lo, hi = tpmd.shard_range(args.clip, world, rank)
         clip_styles = synth.styles_walk(seed=0, n=args.clip)[lo:hi]
         styles = clip_styles if hi > lo else styles[:1]
         parts = multi.sub_batches(0, len(styles), nb)
@@ -539,9 +658,7 @@ def main():
         clk.poll_until(e1)
         torch.cuda.synchronize()
     barrier()
-    ms = e0.elapsed_time(e1)
-    if world > 1:
-        ms = multi.max_over_ranks(ms, torch.device("cuda", local))
+    ms = group.max(e0.elapsed_time(e1))  # max over ranks
     frames_per_step = args.clip if args.clip else world * nb
     value = frames_per_step * args.steps / (ms / 1000.0)
 
@@ -554,10 +671,19 @@ def main():
     t0 = time.perf_counter()
     for _ in range(args.steps):
         dec.decode_ptr(s_h.data_ptr(), n_mine, f_h.data_ptr())
-    dt = time.perf_counter() - t0
-    if world > 1:
-        dt = multi.max_over_ranks(dt, torch.device("cuda", local))
+    dt = group.max(time.perf_counter() - t0)
     e2e = frames_per_step * args.steps / dt
+
+    # ---- the same with the reference's output format (RGB24 bytes, converted
+    # on the GPU: a quarter of the bytes cross to the host)
+    r_h = torch.empty((n_mine, 512, 512, 3), dtype=torch.uint8, pin_memory=True)
+    dec.decode_rgb24_ptr(s_h.data_ptr(), n_mine, r_h.data_ptr())
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        dec.decode_rgb24_ptr(s_h.data_ptr(), n_mine, r_h.data_ptr())
+    dt = group.max(time.perf_counter() - t0)
+    e2e_rgb = frames_per_step * args.steps / dt
 
     # ---- live per-kernel timing (untimed pass) for the roofline
     dec.profile_begin()
@@ -614,12 +740,16 @@ def main():
                        "conv": "tcgen05" if dec_uses_tc() else "simt"},
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": frames_per_step * 512 * 4,
                     "d2h_bytes_per_step": frames_per_step * 3 * 512 * 512 * 4},
+            "e2e_rgb24": {"value": e2e_rgb, "unit": UNIT, "h2d_bytes_per_step": frames_per_step * 512 * 4,
+                          "d2h_bytes_per_step": frames_per_step * 3 * 512 * 512,
+                          "api": "tpmd_decode_rgb24 (frames as the reference CLI's RGB24 bytes)"},
             "gpu_launches": sum(dec.kernel_launches(b - a) for a, b in parts) * args.steps * world,
             "roofline": roof, "kernels": kernels, "clocks": clk.summary(),
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
-    dec.close()
+    barrier()
+    group.close()
     if world > 1:
         dist.destroy_process_group()
 

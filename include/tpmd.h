@@ -116,6 +116,13 @@ int tpmd_batch(const tpmd_ctx *ctx);
  * src/motion_dec.cpp:1194-1220, without its fixed-batch restriction.) */
 int tpmd_decode(tpmd_ctx *ctx, const float *styles, int64_t n, float *frames);
 
+/* Same frames as tpmd_decode, delivered as the reference's output format:
+ * interleaved RGB24 bytes rgb [n][512][512][3], each channel value v mapped
+ * by clamping to [-1, 1] and (unsigned char) ((v + 1) / 2 * 255) in f32, the
+ * conversion tools/tp-cli.cpp:43-53 applies before its video encoder. The
+ * conversion runs on the GPU, so a quarter of the bytes cross to the host. */
+int tpmd_decode_rgb24(tpmd_ctx *ctx, const float *styles, int64_t n, uint8_t *rgb);
+
 /* Same with device pointers, enqueued on `stream` (a cudaStream_t; NULL =
  * the legacy default stream, as in CUDA's own APIs) without host
  * synchronisation. The return code covers the enqueue only: whether the
@@ -190,6 +197,72 @@ int tpmd_device_status(tpmd_ctx *ctx, void *stream);
  * error (tpmd_decode) or a nonzero tpmd_device_status. f16 handles only. */
 int tpmd_debug_expire_wait(tpmd_ctx *ctx, long long wait_ns);
 
+/* ---- several GPUs: frame sharding behind one handle ------------------- */
+
+/* A group is the decoder on a clique of GPUs: one tpmd_ctx and one NCCL
+ * communicator per local GPU. The reference decodes on one backend
+ * (src/pipeline.cpp:153-184); frames are independent given the weights and
+ * the portrait's feature pyramid, so a group shards a decode by frame with
+ * no collective on the data path. Global rank 0 holds the host weights and
+ * feats; tpmd_group_prepare / tpmd_group_set_feats run there and broadcast
+ * the two device arenas to every other rank (ncclBroadcast over NVLink).
+ * NCCL is loaded at run time (libnccl.so.2); communicators are created
+ * non-blocking and every wait on them is polled under a wall-clock limit
+ * (TPMD_NCCL_TIMEOUT_S, default 120 s), after which the group aborts its
+ * communicators and the call fails. Group calls that communicate
+ * (create, prepare, set_feats*, max) are collective: every rank makes them
+ * in the same order. Conventions as above: 0 / -1 and the message in
+ * tpmd_group_last_error; NULL-safe destroy; one call at a time per group. */
+typedef struct tpmd_group tpmd_group;
+
+/* All ranks in this process: devices[0..n-1] become global ranks 0..n-1
+ * (n = 1 needs no NCCL). NULL on failure, reason in
+ * tpmd_group_create_error(). */
+tpmd_group *tpmd_group_create(const int *devices, int n, int dtype, int max_batch);
+/* One process per GPU (e.g. under torchrun): global rank 0 makes an id with
+ * tpmd_group_unique_id (128 bytes), the caller hands it to every rank, and
+ * each rank creates its member for `device` with the same id. */
+int tpmd_group_unique_id(void *id, size_t len);
+tpmd_group *tpmd_group_create_rank(int device, int rank, int nranks, const void *id, size_t id_len, int dtype,
+                                   int max_batch);
+const char *tpmd_group_create_error(void);
+void tpmd_group_destroy(tpmd_group *g);
+const char *tpmd_group_last_error(const tpmd_group *g);
+/* local GPUs of this group, and its place in the clique */
+int tpmd_group_size(const tpmd_group *g);
+int tpmd_group_ranks(const tpmd_group *g, int *rank0, int *nranks);
+/* the decoder of local GPU i (for device-pointer decodes, taps, profiling) */
+tpmd_ctx *tpmd_group_member(tpmd_group *g, int i);
+
+/* Weights and feats: read on global rank 0 (other ranks' calls to
+ * set_tensor / load_gguf are accepted and ignored), then broadcast. */
+int tpmd_group_set_tensor(tpmd_group *g, const char *name, const float *data, int64_t n);
+int tpmd_group_load_gguf(tpmd_group *g, const char *path);
+int tpmd_group_prepare(tpmd_group *g);
+int tpmd_group_set_feats(tpmd_group *g, const float *const feats[TPMD_N_LEVELS]);
+/* feats_dev on global rank 0's device (e.g. tpme_feat_device output) */
+int tpmd_group_set_feats_device(tpmd_group *g, const float *const feats_dev[TPMD_N_LEVELS], void *stream);
+
+/* Frames of rank `rank` when n frames shard over nranks: the contiguous
+ * [lo, hi) = [rank*ceil(n/nranks), ...), empty for trailing ranks. */
+int tpmd_shard_range(int64_t n, int nranks, int rank, int64_t *lo, int64_t *hi);
+/* Decode n frames of host styles [n][512] into host frames
+ * [n][3][512][512] (the whole clip's buffers on every rank): each local GPU
+ * decodes its shard on its own host thread and copies it straight into its
+ * slice of `frames`; other ranks' slices are not touched. */
+int tpmd_group_decode(tpmd_group *g, const float *styles, int64_t n, float *frames);
+/* tpmd_group_decode with RGB24 frames (see tpmd_decode_rgb24):
+ * rgb [n][512][512][3] bytes. */
+int tpmd_group_decode_rgb24(tpmd_group *g, const float *styles, int64_t n, uint8_t *rgb);
+/* Maximum of `value` over all ranks (NCCL all-reduce; timing as the max
+ * over ranks). */
+int tpmd_group_max(tpmd_group *g, double value, double *out);
+/* Test hook: the communicator set-up and its failure handling against a
+ * fake NCCL, without a GPU (scenario 0 initialises, 1 never finishes and the
+ * limit expires, 2 reports an asynchronous error, 3 fails the init call);
+ * -1 and the message in err on failure, *aborted = ncclCommAbort calls. */
+int tpmd_group_selftest_nccl(int n, int scenario, double limit_s, int *aborted, char *err, size_t err_len);
+
 /* ---- op-level kernels with the patched-op semantics ------------------ */
 
 /* ggml_bilinear_gather / _planar / _sp (patches/ggml-tp-ops.patch:41-60,
@@ -210,6 +283,13 @@ int tpk_bilinear_gather(const void *feat, int feat_is_f16, int C, int W, int H,
 int tpk_im2col_cf(const float *src, int IC, int IW, int IH, int N, int KW, int KH,
                   int s0, int s1, int p0, int p1, int d0, int d1, void *dst,
                   int dst_is_f16, void *stream);
+
+/* CHW f32 frames chw [n][3][H][W] -> RGB24 bytes rgb [n][H][W][3], the
+ * conversion of tools/tp-cli.cpp:43-53 (clamp to [-1, 1], then
+ * (unsigned char) ((v + 1) / 2 * 255) in f32, truncating), bit-exact.
+ * H*W a multiple of 4, chw 16-byte and rgb 4-byte aligned; device memory,
+ * enqueued on `stream`. */
+int tpk_chw_to_rgb24(const float *chw, int64_t n, int H, int W, uint8_t *rgb, void *stream);
 
 /* Message of the last failed tpk_* call on this thread. */
 const char *tpk_last_error(void);

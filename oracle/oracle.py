@@ -103,6 +103,7 @@ def lib():
         L.orc_aud_encode.argtypes = [v, v, C.c_int64, C.c_int64, v]
         L.orc_aud_error.argtypes = [v]
         L.orc_aud_error.restype = C.c_char_p
+        L.orc_chw_to_rgb24.argtypes = [v, C.c_int64, C.c_int64, v]
         L.orc_set_threads.argtypes = [C.c_int]
         L.orc_get_threads.restype = C.c_int
         _lib = L
@@ -409,6 +410,15 @@ class Aud:
         if getattr(self, "_h", None):
             self._L.orc_aud_destroy(self._h)
             self._h = None
+
+
+def chw_to_rgb24(frames) -> np.ndarray:
+    """[n][3][H][W] f32 -> [n][H][W][3] uint8, tools/tp-cli.cpp:43-53"""
+    f = np.ascontiguousarray(frames, np.float32)
+    n, c, h, w = f.shape
+    out = np.empty((n, h, w, 3), np.uint8)
+    lib().orc_chw_to_rgb24(_p(f), n, h * w, _p(out))
+    return out
 
 
 def set_threads(n: int) -> None:

@@ -1604,3 +1604,18 @@ int orc_aud_encode(orc_aud *a, const float *audio, int64_t n_in, int64_t seq_len
 
 }  // extern "C"
 
+
+// ---------------------------------------------------------------------------
+// CHW f32 frame -> RGB24 bytes (tools/tp-cli.cpp:43-53, the frame the CLI
+// hands to its video encoder): clamp with the same comparisons, then
+// (unsigned char) ((v + 1) / 2 * 255) in f32, truncating toward zero
+// ---------------------------------------------------------------------------
+extern "C" void orc_chw_to_rgb24(const float *chw, int64_t n, int64_t hw, unsigned char *rgb) {
+    for (int64_t f = 0; f < n; f++)
+        for (int64_t i = 0; i < hw; i++)
+            for (int c = 0; c < 3; c++) {
+                float v = chw[(f * 3 + c) * hw + i];
+                v = v < -1 ? -1 : (v > 1 ? 1 : v);
+                rgb[(f * hw + i) * 3 + c] = (unsigned char) ((v + 1.0f) / 2.0f * 255.0f);
+            }
+}

@@ -103,6 +103,8 @@ int orc_dec_decode(orc_dec *d, const float *style, int mode, int keep_taps,
  * its element count or -1 */
 int64_t orc_dec_tap(const orc_dec *d, const char *name, float *out, int64_t cap);
 const char *orc_dec_error(const orc_dec *d);
+/* CHW f32 frames [n][3][hw] -> RGB24 bytes [n][hw][3] (tools/tp-cli.cpp:43-53) */
+void orc_chw_to_rgb24(const float *chw, int64_t n, int64_t hw, unsigned char *rgb);
 void orc_set_threads(int n);
 int orc_get_threads(void);
 

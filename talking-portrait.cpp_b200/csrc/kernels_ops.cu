@@ -21,14 +21,17 @@
 
 #include "../../include/tpmd.h"
 
-namespace {
-
+namespace tpmd {
 thread_local std::string g_tpk_err;
-
-int fail(const std::string &msg) {
+int tpk_fail(const std::string &msg) {
     g_tpk_err = msg;
     return -1;
 }
+}  // namespace tpmd
+
+namespace {
+
+int fail(const std::string &msg) { return tpmd::tpk_fail(msg); }
 
 constexpr int GATHER_THREADS = 256;
 constexpr int GATHER_PTS = 64;  // points staged per block iteration
@@ -239,7 +242,7 @@ cudaError_t run_im2col(const float *src, void *dst, const im2col_geom &g, cudaSt
 
 extern "C" {
 
-const char *tpk_last_error(void) { return g_tpk_err.c_str(); }
+const char *tpk_last_error(void) { return tpmd::g_tpk_err.c_str(); }
 
 int tpk_bilinear_gather(const void *feat, int feat_is_f16, int C, int W, int H,
                         const float *grid, int64_t N, int planar, int out_sp, float *dst,

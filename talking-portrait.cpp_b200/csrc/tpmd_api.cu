@@ -119,6 +119,7 @@ struct tpmd_ctx {
     void *actA = nullptr, *actB = nullptr, *actC = nullptr;
     float *sf[2] = {nullptr, nullptr}, *sk[2] = {nullptr, nullptr};
     float *frames_d[2] = {nullptr, nullptr};  // device staging for host decode
+    uint8_t *rgb_d[2] = {nullptr, nullptr};   // RGB24 staging for tpmd_decode_rgb24
     int *err_flag = nullptr;                   // set by kernels whose bounded waits expired
 
     std::list<graph_entry> graphs;  // most recently used first
@@ -314,6 +315,8 @@ bool alloc_workspace(tpmd_ctx *c) {
     take(B * skip * 4);
     take(B * frame * 4);
     take(B * frame * 4);
+    take(B * frame);  // RGB24 staging 0
+    take(B * frame);  // RGB24 staging 1
     take(256);
     if (!c->ck(cudaMalloc(&c->ws, off), "cudaMalloc(workspace)")) return false;
     c->ws_bytes = off;
@@ -332,6 +335,8 @@ bool alloc_workspace(tpmd_ctx *c) {
     c->sk[1] = (float *) (p + offs[i++]);
     c->frames_d[0] = (float *) (p + offs[i++]);
     c->frames_d[1] = (float *) (p + offs[i++]);
+    c->rgb_d[0] = (uint8_t *) (p + offs[i++]);
+    c->rgb_d[1] = (uint8_t *) (p + offs[i++]);
     c->err_flag = (int *) (p + offs[i++]);
     return c->ck(cudaMemset(c->err_flag, 0, 256), "cudaMemset");
 }
@@ -1015,12 +1020,19 @@ int tpmd_profile_end(tpmd_ctx *c, char *json, size_t cap) {
     return 0;
 }
 
-int tpmd_decode(tpmd_ctx *c, const float *styles, int64_t n, float *frames) {
+}  // extern "C"
+
+namespace {
+
+// The host decode loop: styles H2D, decode, (RGB24 conversion), frames D2H,
+// each sub-batch's copy overlapping the next sub-batch's compute.
+int host_decode(tpmd_ctx *c, const float *styles, int64_t n, void *out, bool rgb, const char *who) {
     if (!c) return -1;
-    if (!styles || !frames || n < 1) return c->fail("tpmd_decode: bad argument"), -1;
+    if (!styles || !out || n < 1) return c->fail(std::string(who) + ": bad argument"), -1;
     if (!ready(c)) return -1;
     if (!c->ck(cudaSetDevice(c->device), "cudaSetDevice")) return -1;
     const size_t fsz = (size_t) 3 * IMG * IMG;
+    const size_t osz = rgb ? fsz : fsz * 4;  // output bytes per frame
     const std::vector<int64_t> plan = sub_batch_plan(n, c->max_batch);
     int k = 0;
     int64_t f0 = 0;
@@ -1032,10 +1044,12 @@ int tpmd_decode(tpmd_ctx *c, const float *styles, int64_t n, float *frames) {
                                    (size_t) nb * STYLE_DIM * 4, cudaMemcpyHostToDevice, c->stream),
                    "styles H2D") ||
             !run_chunk(c, c->styles_d[k], nb, c->frames_d[k], c->stream) ||
+            (rgb && !c->ck(launch_chw_to_rgb24(c->frames_d[k], nb, (int64_t) IMG * IMG, c->rgb_d[k], c->stream),
+                           "rgb24")) ||
             !c->ck(cudaEventRecord(c->ev_done[k], c->stream), "record") ||
             !c->ck(cudaStreamWaitEvent(c->copy_stream, c->ev_done[k], 0), "wait") ||
-            !c->ck(cudaMemcpyAsync(frames + f0 * fsz, c->frames_d[k], (size_t) nb * fsz * 4,
-                                   cudaMemcpyDeviceToHost, c->copy_stream),
+            !c->ck(cudaMemcpyAsync((char *) out + f0 * osz, rgb ? (const void *) c->rgb_d[k] : c->frames_d[k],
+                                   (size_t) nb * osz, cudaMemcpyDeviceToHost, c->copy_stream),
                    "frames D2H") ||
             !c->ck(cudaEventRecord(c->ev_copied[k], c->copy_stream), "record"))
             return -1;
@@ -1044,6 +1058,18 @@ int tpmd_decode(tpmd_ctx *c, const float *styles, int64_t n, float *frames) {
         !c->ck(cudaStreamSynchronize(c->stream), "sync") || !device_ok(c))
         return -1;
     return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+int tpmd_decode(tpmd_ctx *c, const float *styles, int64_t n, float *frames) {
+    return host_decode(c, styles, n, frames, false, "tpmd_decode");
+}
+
+int tpmd_decode_rgb24(tpmd_ctx *c, const float *styles, int64_t n, uint8_t *rgb) {
+    return host_decode(c, styles, n, rgb, true, "tpmd_decode_rgb24");
 }
 
 }  // extern "C"

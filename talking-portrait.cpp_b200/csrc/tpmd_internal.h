@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <string>
 
 namespace tpmd {
 
@@ -116,6 +117,11 @@ cudaError_t launch_convert_feats(const float *src, int64_t n, bool f16, void *ds
 // proj[i] = (rW[0] . feat[i], rW[1] . feat[i], rW[2] . feat[i], 0) over C channels
 cudaError_t launch_project_feats(bool f16, const void *feat, int64_t npx, int C, const float *rW,
                                  float4 *proj, cudaStream_t st);
+
+// CHW f32 frames [n][3][hw] -> RGB24 bytes [n][hw][3] (tools/tp-cli.cpp:43-53)
+cudaError_t launch_chw_to_rgb24(const float *chw, int64_t n, int64_t hw, uint8_t *rgb, cudaStream_t st);
+// the last-error slot of the tpk_* entry points (sets it, returns -1)
+int tpk_fail(const std::string &msg);
 
 // tcgen05 path (f16)
 cudaError_t launch_conv_tc(bool up, const conv_params &p, cudaStream_t st);

@@ -45,7 +45,13 @@ EXPORTS = ("tpmd_abi_version", "tpmd_create", "tpmd_create_error", "tpmd_destroy
            "tppl_create", "tppl_create_error", "tppl_destroy", "tppl_last_error", "tppl_load",
            "tppl_motion_encoder", "tppl_audio_encoder", "tppl_sampler", "tppl_decoder", "tppl_prepare",
            "tppl_n_frames", "tppl_n_chunks", "tppl_generate", "tppl_generate_cb", "tppl_styles", "tppl_styles_cb",
-           "tpk_bilinear_gather", "tpk_im2col_cf", "tpk_last_error")
+           "tpk_bilinear_gather", "tpk_im2col_cf", "tpk_last_error",
+           "tpmd_group_create", "tpmd_group_unique_id", "tpmd_group_create_rank", "tpmd_group_create_error",
+           "tpmd_group_destroy", "tpmd_group_last_error", "tpmd_group_size", "tpmd_group_ranks",
+           "tpmd_group_member", "tpmd_group_set_tensor", "tpmd_group_load_gguf", "tpmd_group_prepare",
+           "tpmd_group_set_feats", "tpmd_group_set_feats_device", "tpmd_shard_range", "tpmd_group_decode",
+           "tpmd_group_max", "tpmd_group_selftest_nccl", "tpmd_decode_rgb24", "tpmd_group_decode_rgb24",
+           "tpk_chw_to_rgb24")
 
 _lib = None
 
@@ -87,6 +93,32 @@ def load_library(path: str = LIB_PATH):
     L.tpmd_kernel_launches.argtypes = [v, i64]
     L.tpmd_decode_noalloc.argtypes = [v, v, i64, v, v]
     L.tpmd_device_status.argtypes = [v, v]
+    L.tpmd_group_create.argtypes = [C.POINTER(C.c_int), C.c_int, C.c_int, C.c_int]
+    L.tpmd_group_create.restype = v
+    L.tpmd_group_unique_id.argtypes = [v, C.c_size_t]
+    L.tpmd_group_create_rank.argtypes = [C.c_int, C.c_int, C.c_int, v, C.c_size_t, C.c_int, C.c_int]
+    L.tpmd_group_create_rank.restype = v
+    L.tpmd_group_create_error.restype = cp
+    L.tpmd_group_destroy.argtypes = [v]
+    L.tpmd_group_last_error.argtypes = [v]
+    L.tpmd_group_last_error.restype = cp
+    L.tpmd_group_size.argtypes = [v]
+    L.tpmd_group_ranks.argtypes = [v, C.POINTER(C.c_int), C.POINTER(C.c_int)]
+    L.tpmd_group_member.argtypes = [v, C.c_int]
+    L.tpmd_group_member.restype = v
+    L.tpmd_group_set_tensor.argtypes = [v, cp, v, i64]
+    L.tpmd_group_load_gguf.argtypes = [v, cp]
+    L.tpmd_group_prepare.argtypes = [v]
+    L.tpmd_group_set_feats.argtypes = [v, C.POINTER(v)]
+    L.tpmd_group_set_feats_device.argtypes = [v, C.POINTER(v), v]
+    L.tpmd_shard_range.argtypes = [i64, C.c_int, C.c_int, C.POINTER(i64), C.POINTER(i64)]
+    L.tpmd_group_decode.argtypes = [v, v, i64, v]
+    L.tpmd_group_max.argtypes = [v, C.c_double, C.POINTER(C.c_double)]
+    L.tpmd_decode_rgb24.argtypes = [v, v, i64, v]
+    L.tpmd_group_decode_rgb24.argtypes = [v, v, i64, v]
+    L.tpk_chw_to_rgb24.argtypes = [v, i64, C.c_int, C.c_int, v, v]
+    L.tpmd_group_selftest_nccl.argtypes = [C.c_int, C.c_int, C.c_double, C.POINTER(C.c_int), C.c_char_p,
+                                           C.c_size_t]
     L.tpmd_debug_expire_wait.argtypes = [v, C.c_longlong]
     L.tpmd_kernel_launches.restype = i64
     L.tpmd_gguf_read.argtypes = [cp, cp, C.c_int, GGUF_TENSOR_FN, v, C.c_char_p, C.c_size_t]
@@ -291,6 +323,20 @@ class MotionDecoder:
         self._check(self._L.tpmd_decode(self._h, _np_ptr(styles), n, _np_ptr(out)))
         return out
 
+    def decode_rgb24(self, styles: np.ndarray, out: np.ndarray | None = None) -> np.ndarray:
+        """styles [n, 512] f32 (host) -> frames [n, 512, 512, 3] uint8 RGB24
+        (tpmd_decode_rgb24: converted on the GPU)"""
+        styles = np.ascontiguousarray(styles, np.float32).reshape(-1, STYLE_DIM)
+        n = styles.shape[0]
+        if out is None:
+            out = np.empty((n, IMG, IMG, 3), np.uint8)
+        assert out.flags.c_contiguous and out.dtype == np.uint8 and out.size == n * 3 * IMG * IMG
+        self._check(self._L.tpmd_decode_rgb24(self._h, _np_ptr(styles), n, _np_ptr(out)))
+        return out
+
+    def decode_rgb24_ptr(self, styles_ptr: int, n: int, rgb_ptr: int):
+        self._check(self._L.tpmd_decode_rgb24(self._h, C.c_void_p(styles_ptr), n, C.c_void_p(rgb_ptr)))
+
     def decode_ptr(self, styles_ptr: int, n: int, frames_ptr: int):
         """host pointers (e.g. pinned torch tensors' data_ptr())"""
         self._check(self._L.tpmd_decode(self._h, C.c_void_p(styles_ptr), n, C.c_void_p(frames_ptr)))
@@ -370,6 +416,13 @@ def bilinear_gather(feat, W: int, H: int, grid, out, planar=False, out_sp=False,
         C.c_void_p(grid.data_ptr()), N, int(planar), int(out_sp), C.c_void_p(out.data_ptr()),
         C.c_void_p(stream)))
     return out
+
+
+def chw_to_rgb24(chw, rgb, stream=0):
+    """torch CUDA tensors: chw [n, 3, H, W] f32 -> rgb [n, H, W, 3] uint8"""
+    n, _, h, w = chw.shape
+    _tpk_check(load_library().tpk_chw_to_rgb24(C.c_void_p(chw.data_ptr()), n, h, w,
+                                               C.c_void_p(rgb.data_ptr()), C.c_void_p(stream)))
 
 
 def im2col_cf(src, IC, IW, IH, N, out, KW=3, KH=3, s0=1, s1=1, p0=1, p1=1, d0=1, d1=1,
@@ -643,3 +696,119 @@ class Pipeline:
         except Exception:
             pass
 
+
+
+def shard_range(n: int, nranks: int, rank: int) -> tuple[int, int]:
+    """[lo, hi) of the frames global rank `rank` decodes (tpmd_shard_range)"""
+    L = load_library()
+    lo, hi = C.c_int64(), C.c_int64()
+    if L.tpmd_shard_range(n, nranks, rank, C.byref(lo), C.byref(hi)) != 0:
+        raise ValueError("bad shard arguments")
+    return lo.value, hi.value
+
+
+NCCL_ID_BYTES = 128
+
+
+def nccl_unique_id() -> bytes:
+    """a fresh NCCL clique id for tpmd_group_create_rank (made on rank 0)"""
+    L = load_library()
+    buf = C.create_string_buffer(NCCL_ID_BYTES)
+    if L.tpmd_group_unique_id(buf, NCCL_ID_BYTES) != 0:
+        raise TpmdError(L.tpmd_group_create_error().decode())
+    return buf.raw
+
+
+class MotionDecoderGroup:
+    """The decoder over several GPUs behind one handle (tpmd_group_*): all of
+    `devices` in this process, or (rank, nranks, nccl_id) for one process
+    per GPU. Weights and feats are given on global rank 0 and broadcast."""
+
+    def __init__(self, devices=(0,), dtype: int = DTYPE_F16, max_batch: int = 50, rank: int | None = None,
+                 nranks: int | None = None, nccl_id: bytes | None = None):
+        self._L = load_library()
+        if rank is None:
+            arr = (C.c_int * len(devices))(*devices)
+            self._h = self._L.tpmd_group_create(arr, len(devices), dtype, max_batch)
+        else:
+            idb = C.create_string_buffer(nccl_id or b"", NCCL_ID_BYTES)
+            self._h = self._L.tpmd_group_create_rank(devices[0], rank, nranks, idb, NCCL_ID_BYTES, dtype,
+                                                     max_batch)
+        if not self._h:
+            raise TpmdError(self._L.tpmd_group_create_error().decode())
+        r0, nr = C.c_int(), C.c_int()
+        self._L.tpmd_group_ranks(self._h, C.byref(r0), C.byref(nr))
+        self.rank0, self.nranks = r0.value, nr.value
+        self.size = self._L.tpmd_group_size(self._h)
+        self.dtype = dtype
+
+    def _check(self, rc: int):
+        if rc != 0:
+            raise TpmdError(self._L.tpmd_group_last_error(self._h).decode())
+
+    def set_tensors(self, tensors: dict):
+        for name, arr in tensors.items():
+            a = np.ascontiguousarray(arr, np.float32)
+            self._check(self._L.tpmd_group_set_tensor(self._h, name.encode(), _np_ptr(a), a.size))
+
+    def load_gguf(self, path: str):
+        self._check(self._L.tpmd_group_load_gguf(self._h, path.encode()))
+
+    def prepare(self):
+        self._check(self._L.tpmd_group_prepare(self._h))
+
+    def set_feats(self, feats=None):
+        """host feats on global rank 0 (None on the other ranks)"""
+        if feats is None:
+            feats = [np.zeros(1, np.float32)] * N_LEVELS
+        arrs = [np.ascontiguousarray(f, np.float32) for f in feats]
+        ptrs = (C.c_void_p * N_LEVELS)(*[a.ctypes.data for a in arrs])
+        self._check(self._L.tpmd_group_set_feats(self._h, ptrs))
+
+    def decode(self, styles: np.ndarray, out: np.ndarray | None = None) -> np.ndarray:
+        styles = np.ascontiguousarray(styles, np.float32).reshape(-1, STYLE_DIM)
+        n = styles.shape[0]
+        if out is None:
+            out = np.zeros((n, 3, IMG, IMG), np.float32)
+        self._check(self._L.tpmd_group_decode(self._h, _np_ptr(styles), n, _np_ptr(out)))
+        return out
+
+    def decode_ptr(self, styles_ptr: int, n: int, frames_ptr: int):
+        self._check(self._L.tpmd_group_decode(self._h, C.c_void_p(styles_ptr), n, C.c_void_p(frames_ptr)))
+
+    def decode_rgb24(self, styles: np.ndarray, out: np.ndarray | None = None) -> np.ndarray:
+        styles = np.ascontiguousarray(styles, np.float32).reshape(-1, STYLE_DIM)
+        n = styles.shape[0]
+        if out is None:
+            out = np.zeros((n, IMG, IMG, 3), np.uint8)
+        self._check(self._L.tpmd_group_decode_rgb24(self._h, _np_ptr(styles), n, _np_ptr(out)))
+        return out
+
+    def member(self, i: int = 0) -> "MotionDecoder":
+        """the decoder of local GPU i (not owned: the group frees it)"""
+        h = self._L.tpmd_group_member(self._h, i)
+        if not h:
+            raise TpmdError("no such member")
+        return MotionDecoder(_handle=h)
+
+    def max(self, value: float) -> float:
+        out = C.c_double()
+        self._check(self._L.tpmd_group_max(self._h, float(value), C.byref(out)))
+        return out.value
+
+    def close(self):
+        if getattr(self, "_h", None):
+            self._L.tpmd_group_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+
+def nccl_selftest(n: int, scenario: int, limit_s: float) -> tuple[int, int, str]:
+    """(rc, aborts, message) of the group's NCCL set-up against a fake NCCL"""
+    L = load_library()
+    ab = C.c_int()
+    err = C.create_string_buffer(256)
+    rc = L.tpmd_group_selftest_nccl(n, scenario, limit_s, C.byref(ab), err, len(err))
+    return rc, ab.value, err.value.decode()

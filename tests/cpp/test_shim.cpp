@@ -13,6 +13,38 @@
 
 #include "motion_dec_b200.h"
 
+// stand-ins for the reference's types at the decoder's call sites
+// (src/tp_internal.h backend_t, src/motion_enc.h menc_result): the shim's
+// overloads take them as the reference's motion_dec does
+namespace tp {
+struct backend_t {
+    bool gpu = true;
+};
+struct menc_result {
+    std::vector<float> appearance;
+    std::vector<std::vector<float>> feats;
+};
+}  // namespace tp
+
+// the decoder calls of the reference's decode loop (src/pipeline.cpp:153-175)
+// against the shim, with the reference's argument lists
+struct ctx_like {
+    tp::backend_t be;
+    tpmd_cpp::motion_dec_b200 mdec;
+    std::string err;
+};
+static bool decode_like_pipeline(ctx_like *c, const tp::menc_result &m, const std::vector<float> &styles,
+                                 float *dst) {
+    std::string &err = c->err;
+    if (!c->mdec.built || c->mdec.taps_in_graph) {
+        if (!c->mdec.build(c->be, false, err)) return false;
+    }
+    if (!c->mdec.set_feats(m, err)) return false;
+    const int BQ = c->mdec.batch;
+    (void) BQ;
+    return c->mdec.decode_batch(c->be, styles.data(), dst, err);
+}
+
 static const int ST_IC[7] = {512, 512, 512, 512, 256, 128, 64};
 static const int ST_OC[7] = {512, 512, 512, 256, 128, 64, 32};
 
@@ -35,6 +67,12 @@ int main(int argc, char **argv) {
     tpmd_cpp::motion_dec_b200 bad;
     assert(!bad.load(0, "f64", 2, err) && err == "ftype must be f32 or f16");
     assert(!bad.build(false, err) && err == "decoder not loaded");
+    {
+        ctx_like c;
+        tp::menc_result m;
+        std::vector<float> st(512), out(3 * 512 * 512);
+        assert(!decode_like_pipeline(&c, m, st, out.data()) && c.err == "decoder not loaded");
+    }
     if (!gpu) {
         assert(!bad.load(9999, "f16", 2, err) && !err.empty());
         printf("test_shim (no GPU) OK\n");
@@ -100,6 +138,18 @@ int main(int argc, char **argv) {
     std::vector<float> again(imgs.size());
     assert(d.decode_batch(styles.data(), again.data(), err));
     assert(memcmp(again.data(), imgs.data(), imgs.size() * 4) == 0);  // deterministic
+    // the same decode through the reference-shaped call sites
+    {
+        tp::menc_result m;
+        m.feats = feats;
+        tp::backend_t be;
+        std::vector<float> viaref(imgs.size());
+        d.built = false;
+        assert(d.build(be, false, err) && d.built);
+        assert(d.set_feats(m, err));
+        assert(d.decode_batch(be, styles.data(), viaref.data(), err));
+        assert(memcmp(viaref.data(), imgs.data(), imgs.size() * 4) == 0);
+    }
     printf("test_shim (GPU) OK mean|x| %.4f\n", s / imgs.size());
     return 0;
 }

@@ -121,38 +121,37 @@ def test_taps_f16_vs_reference_f16(model, f16_pair, level):
 
 def test_config0_white_noise():
     """BASELINE config 0 as written: white-noise N(0, 1) feats, plain random
-    init, one config-0 style, fp32. The GPU's fp32 path is compared with the
-    oracle's sub-pixel graph (mode 1, the reference fast path's formulation),
-    and the oracle's exact graph (mode 0) with the same sub-pixel graph. The
-    decoder is chaotic on this input (the warp of an uncorrelated map
-    multiplies a grid error by about r/2), so two float32 formulations of the
-    same graph drift apart level by level. The gates: levels up to r32 meet
-    cosine 0.9999 per tap; at every level and for the frame, the GPU agrees
-    with the sub-pixel graph no worse (minus 0.01) than the oracle's own exact
-    graph does."""
+    init, one config-0 style, fp32. The decoder is chaotic on this input (the
+    warp of an uncorrelated map multiplies a grid error by about r/2), so no
+    float32 evaluation is close to the exact result: the reference's own
+    exact and fast graphs (run from its sources on the CPU) and the oracle's
+    two modes all end near 1 - cosine 0.07 from a float64 evaluation
+    (tests/torch_lia.py). Gates: the GPU's fp32 frame is no further from the
+    float64 frame than twice the oracle's float32 graphs are; per-level taps
+    through r32, before the growth dominates, meet cosine 0.9999 against the
+    oracle's sub-pixel graph (the reference fast path's formulation)."""
+    from torch_lia import TorchLIA
     from tpmd import synth
     raw = synth.make_weights(seed=0)
     w = synth.fold(raw, O.scale_for)
     feats = synth.make_feats(seed=0, smooth=False)
     style = synth.styles_config0(seed=0, n=1)[0]
+    truth = TorchLIA(raw, feats).decode(style)
     od = O.Decoder(w, feats)
-    names = lambda lv: [f"r{8 << lv}.conv2", f"r{8 << lv}.rgb"]  # noqa: E731
     ref1 = od.decode(style, mode=1, keep_taps=True)
-    taps1 = {n: od.tap(n) for lv in range(7) for n in names(lv)}
-    ref0 = od.decode(style, mode=0, keep_taps=True)
-    taps0 = {n: od.tap(n) for lv in range(7) for n in names(lv)}
+    taps1 = {f"r{8 << lv}.{k}": od.tap(f"r{8 << lv}.{k}") for lv in range(3) for k in ("conv2", "rgb")}
+    ref0 = od.decode(style, mode=0)
     d = _dec(dict(w=w, feats=feats), tpmd.DTYPE_F32, 1)
     g = d.decode(style[None])[0]
-    c1, c01 = cosine(g, ref1), cosine(ref0, ref1)
-    print(f"config 0 (white-noise feats) f32 frame: GPU vs oracle sub-pixel cos {c1:.6f} "
-          f"max-abs {max_abs(g, ref1):.3e}; oracle exact vs sub-pixel cos {c01:.6f}")
-    for lv in range(7):
+    e_gpu, e0, e1 = (1.0 - cosine(x, truth) for x in (g, ref0, ref1))
+    print(f"config 0 (white-noise feats) f32 frame, 1-cos vs float64: GPU {e_gpu:.4f}, oracle exact "
+          f"{e0:.4f}, oracle sub-pixel {e1:.4f}; GPU vs oracle sub-pixel cos {cosine(g, ref1):.6f} "
+          f"max-abs {max_abs(g, ref1):.3e}")
+    for lv in range(3):
         t = d.taps(style, lv)
-        for n, k in zip(names(lv), ("conv2", "rgb")):
+        for k in ("conv2", "rgb"):
+            n = f"r{8 << lv}.{k}"
             c = cosine(t[k], taps1[n].reshape(t[k].shape))
-            cm = cosine(taps0[n], taps1[n])
-            print(f"config 0 {n}: GPU vs oracle sub-pixel cos {c:.7f}; oracle exact vs sub-pixel {cm:.7f}")
-            if lv <= 2:
-                assert c >= 0.9999, (n, c)
-            assert c >= cm - 0.01, (n, c, cm)
-    assert c1 >= c01 - 0.01, (c1, c01)
+            print(f"config 0 {n}: GPU vs oracle sub-pixel cos {c:.7f}")
+            assert c >= 0.9999, (n, c)
+    assert e_gpu <= 2.0 * max(e0, e1), (e_gpu, e0, e1)
