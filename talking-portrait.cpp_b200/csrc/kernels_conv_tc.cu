@@ -75,9 +75,16 @@ struct tc_cfg {
     // reserved per box to keep the next box 1024-byte aligned.
     static constexpr int HALO_ROWS = BM + 2;
     static constexpr int A_HALO = 136 * KC * 2;
-    // fused tail: the ToFlow and ToRGB weights [3][BN] each, shared by all
-    // epilogue groups
-    static constexpr int EXTRA = TAIL ? (3 * BN + 32) * 4 : 0;  // ToFlow weights, up kernels
+    // fused tail: the ToFlow weights [3][BN] and the two up-sampling kernels,
+    // shared by all epilogue groups, then per epilogue group two buffers
+    // (alternating by tile) of the tile's per-frame channel constants:
+    // inv_den, bias, the three ToFlow weights times the ToFlow style, and
+    // the next up-conv's style (CW floats)
+    // Staged only for tiles of at most 128 channels (r128, r256, r512): at
+    // BN = 256 (r64) the per-pixel loads of the old form measured faster
+    static constexpr bool STG = TAIL && BN <= 128;
+    static constexpr int CW = 6 * BN;
+    static constexpr int EXTRA = TAIL ? (3 * BN + 32 + (STG ? NACC * 2 * CW : 0)) * 4 : 0;
     // BRES: the whole weight matrix (9 taps x one KC chunk) stays resident in
     // shared memory for the kernel's lifetime instead of being re-loaded for
     // every pixel tile; stages then carry only A
@@ -120,7 +127,8 @@ struct tc_cfg {
     static __device__ __forceinline__ uint32_t idesc_n(int nb) {
         return (1u << 4) | ((uint32_t) ((nb * BN) >> 3) << 17) | ((uint32_t) (BM >> 4) << 24);
     }
-    static constexpr int NBARS = 2 * STAGES + 2 * NSLOT + 2;
+    // + per epilogue group one barrier for its staged constants (TAIL)
+    static constexpr int NBARS = 2 * STAGES + 2 * NSLOT + 2 + NACC;
     static constexpr int SMEM = 1024 + STAGES * A_BYTES + B_REGION + EXTRA + NBARS * 8 + 16;
     static_assert((TMEM_COLS & (TMEM_COLS - 1)) == 0 && TMEM_COLS >= 32 && TMEM_COLS <= 512, "TMEM");
     static_assert(SMEM <= 232448, "shared memory");
@@ -213,6 +221,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     auto tempty = [&](int a) { return smem_u32(&bars[2 * cfg::STAGES + cfg::NSLOT + a]); };
     const uint32_t drain = smem_u32(&bars[2 * cfg::STAGES + 2 * cfg::NSLOT]);
     const uint32_t bres_bar = smem_u32(&bars[2 * cfg::STAGES + 2 * cfg::NSLOT + 1]);
+    auto cbar = [&](int g) { return smem_u32(&bars[2 * cfg::STAGES + 2 * cfg::NSLOT + 2 + g]); };
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
@@ -226,6 +235,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         }
         mbar_init(drain, 1);
         mbar_init(bres_bar, 1);
+        for (int g = 0; g < NACC; g++) mbar_init(cbar(g), 128);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
@@ -468,6 +478,9 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         const int bx = row % p.bw, by = (row / p.bw) % p.bh, bz = row / (p.bw * p.bh);
         const uint32_t lanes = (uint32_t) (q * 32) << 16;
         const float *s_fw = sx, *s_up = sx + 3 * BN;
+        float *s_cst = sx + 3 * BN + 32 + g * 2 * cfg::CW;  // this group's two constant buffers
+        uint32_t nst = 0;  // stagings this group has made
+        int cur_b = -1;    // the frame whose constants are staged
         // one tile's epilogue: its accumulator at taddr0 is complete once
         // barrier `bar` finishes phase `par`; false if that wait timed out
         auto tile_body = [&](const tile_pos &tp, uint32_t taddr0, uint32_t bar, uint32_t par) -> bool {
@@ -512,6 +525,36 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     }
                 }
             }
+            // STG: stage the frame's channel constants when the group's frame
+            // changes: the group's 128 threads write, arrive on the group's
+            // barrier and wait (bounded) for its phase. The two buffers
+            // alternate, so a buffer is rewritten only after every thread of
+            // the group has completed the phase of the staging after the one
+            // that filled it (reached only after all tiles that read it)
+            if constexpr (cfg::STG) {
+                if (b != cur_b) {
+                float *cst = s_cst + (nst & 1) * cfg::CW;
+                const float *fden = p.inv_den + (int64_t) b * p.den_stride;
+                const float *ffs = p.fs + (int64_t) b * p.s_stride;
+                for (int c = row; c < BN; c += 128) {
+                    const float fsv = __ldg(ffs + c);
+                    cst[c] = __ldg(fden + c);
+                    cst[BN + c] = __ldg(p.bias + c);
+                    cst[2 * BN + c] = s_fw[c] * fsv;
+                    cst[3 * BN + c] = s_fw[BN + c] * fsv;
+                    cst[4 * BN + c] = s_fw[2 * BN + c] * fsv;
+                    if (p.trunk) cst[5 * BN + c] = __ldg(p.tsn + (int64_t) b * p.s_stride + c);
+                }
+                mbar_arrive(cbar(g));
+                if (!__all_sync(0xffffffffu, mbar_wait(cbar(g), nst & 1))) {
+                    if (lane == 0) atomicExch(p.err, 1);
+                    return false;
+                }
+                nst++;
+                cur_b = b;
+                }
+            }
+            const float *cst = s_cst + ((nst - 1) & 1) * cfg::CW;
             const bool ok = __all_sync(0xffffffffu, mbar_wait(bar, par));
             if (!ok) {
                 if (lane == 0) atomicExch(p.err, 1);
@@ -580,6 +623,12 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 const float *fden = p.inv_den + (int64_t) b * p.den_stride;
                 const float *ffs = p.fs + (int64_t) b * p.s_stride;
                 const float *fsn = p.trunk ? p.tsn + (int64_t) b * p.s_stride : nullptr;
+                const float4 *c_den = reinterpret_cast<const float4 *>(cst);
+                const float4 *c_bias = reinterpret_cast<const float4 *>(cst + BN);
+                const float4 *c_g0 = reinterpret_cast<const float4 *>(cst + 2 * BN);
+                const float4 *c_g1 = reinterpret_cast<const float4 *>(cst + 3 * BN);
+                const float4 *c_g2 = reinterpret_cast<const float4 *>(cst + 4 * BN);
+                const float4 *c_sn = reinterpret_cast<const float4 *>(cst + 5 * BN);
                 const int r = p.W;
                 const int64_t pix = ((int64_t) b * p.H + y) * p.W + x;
                 // the last level has no trunk: it needs neither the conv2 output
@@ -592,20 +641,46 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 for (int c0 = 0; c0 < BN; c0 += 16) {
                     uint32_t rr[16];
                     tmem_ld16(taddr0 + c0, rr);
-                    float den[16], bias[16], fsv[16], v[16];
-                    ld_f16x(fden + c0, den);
-                    ld_f16x(p.bias + c0, bias);
-                    ld_f16x(ffs + c0, fsv);
+                    float v[16];
+                    if constexpr (!cfg::STG) {
+                        float den[16], bias[16], fsv[16];
+                        ld_f16x(fden + c0, den);
+                        ld_f16x(p.bias + c0, bias);
+                        ld_f16x(ffs + c0, fsv);
 #pragma unroll
-                    for (int i = 0; i < 16; i++) {
-                        float a = fmaf(__uint_as_float(rr[i]), den[i], bias[i]);
-                        a = fmaxf(a, 0.2f * a);  // leaky relu, slope 0.2
-                        v[i] = a;
-                        rr[i] = __float_as_uint(a);
-                        const float xs = a * fsv[i];  // ToFlow input: out * style
-                        f0 = fmaf(s_fw[c0 + i], xs, f0);
-                        f1 = fmaf(s_fw[BN + c0 + i], xs, f1);
-                        f2 = fmaf(s_fw[2 * BN + c0 + i], xs, f2);
+                        for (int i = 0; i < 16; i++) {
+                            float a = fmaf(__uint_as_float(rr[i]), den[i], bias[i]);
+                            a = fmaxf(a, 0.2f * a);  // leaky relu, slope 0.2
+                            v[i] = a;
+                            rr[i] = __float_as_uint(a);
+                            const float xs = a * fsv[i];  // ToFlow input: out * style
+                            f0 = fmaf(s_fw[c0 + i], xs, f0);
+                            f1 = fmaf(s_fw[BN + c0 + i], xs, f1);
+                            f2 = fmaf(s_fw[2 * BN + c0 + i], xs, f2);
+                        }
+                    } else {
+#pragma unroll
+                    for (int i4 = 0; i4 < 4; i4++) {
+                        // four channels' constants: five broadcast 16-byte shared loads
+                        const int q4 = (c0 >> 2) + i4;
+                        const float4 dn = c_den[q4], bs = c_bias[q4], w0 = c_g0[q4], w1 = c_g1[q4],
+                                     w2 = c_g2[q4];
+                        const float dnv[4] = {dn.x, dn.y, dn.z, dn.w}, bsv[4] = {bs.x, bs.y, bs.z, bs.w};
+                        const float w0v[4] = {w0.x, w0.y, w0.z, w0.w}, w1v[4] = {w1.x, w1.y, w1.z, w1.w};
+                        const float w2v[4] = {w2.x, w2.y, w2.z, w2.w};
+#pragma unroll
+                        for (int j = 0; j < 4; j++) {
+                            const int i = 4 * i4 + j;
+                            float a = fmaf(__uint_as_float(rr[i]), dnv[j], bsv[j]);
+                            a = fmaxf(a, 0.2f * a);  // leaky relu, slope 0.2
+                            v[i] = a;
+                            rr[i] = __float_as_uint(a);
+                            // ToFlow of out * style: the style is folded into the weights
+                            f0 = fmaf(w0v[j], a, f0);
+                            f1 = fmaf(w1v[j], a, f1);
+                            f2 = fmaf(w2v[j], a, f2);
+                        }
+                    }
                     }
                     if (need_out) tmem_st16(taddr0 + c0, rr);
                     if (p.y) st_half16(p.y + pix * BN + c0, v);  // conv2 tap (debug)
@@ -666,7 +741,18 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                         for (int i = 0; i < 16; i++) smp[i] = fmaf(twt[kk], f[i], smp[i]);
                     }
                     float sn[16];
-                    ld_f16x(fsn + c0, sn);
+                    if constexpr (!cfg::STG) {
+                        ld_f16x(fsn + c0, sn);
+                    } else {
+#pragma unroll
+                        for (int i4 = 0; i4 < 4; i4++) {
+                            const float4 t = c_sn[(c0 >> 2) + i4];
+                            sn[4 * i4] = t.x;
+                            sn[4 * i4 + 1] = t.y;
+                            sn[4 * i4 + 2] = t.z;
+                            sn[4 * i4 + 3] = t.w;
+                        }
+                    }
 #pragma unroll
                     for (int i = 0; i < 16; i++) {
                         const float w = smp[i] * m;
@@ -895,7 +981,10 @@ cudaError_t launch_conv_tc(bool up, const conv_params &p, cudaStream_t st) {
 }
 
 bool conv_tail_tc_supported(int IC, int OC, int r) {
-    return IC == OC && (OC == 32 || OC == 64 || OC == 128 || OC == 256) && r >= 64;
+    // OC = 128 runs with one-row halo tiles only (maps >= 128 wide, the r128
+    // level): a 128-wide non-halo tile leaves no room for two stages next to
+    // the staged per-frame constants
+    return IC == OC && (OC == 32 || OC == 64 || OC == 128 || OC == 256) && r >= (OC == 128 ? 128 : 64);
 }
 
 cudaError_t launch_conv_tail_tc(const conv_params &p, const tail_params &t, cudaStream_t st) {
@@ -909,8 +998,7 @@ cudaError_t launch_conv_tail_tc(const conv_params &p, const tail_params &t, cuda
             return halo ? run_tc<64, 64, false, 4, true, true, true, 3>(p, &t, st)
                         : run_tc<64, 64, false, 4, true>(p, &t, st);
         case 128:
-            return halo ? run_tc<128, 64, false, 4, true, false, true>(p, &t, st)
-                        : run_tc<128, 64, false, 4, true>(p, &t, st);
+            return halo ? run_tc<128, 64, false, 4, true, false, true>(p, &t, st) : cudaErrorInvalidValue;
         default: return run_tc<256, 64, false, 2, true>(p, &t, st);
     }
 }
