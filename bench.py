@@ -498,6 +498,9 @@ def run_ops(args):
 
     chans = (32, 64, 128, 256, 512)
     sizes = (8, 16, 32, 64, 128, 256, 512)
+    if args.shape:  # one shape only (e.g. for a profiler capture), no modconv sweep
+        c1, h1 = (int(v) for v in args.shape.split(","))
+        chans, sizes = (c1,), (h1,)
     gather, im2col = [], []
     for C in chans:
         for H in sizes:
@@ -527,7 +530,7 @@ def run_ops(args):
     tensors = synth.fold(raw, tpmd.scale_for)
     feats = synth.make_feats(seed=0)
     modconv = []
-    for B in (1, 2, 4, 8, 16, 32, 64):
+    for B in (() if args.shape else (1, 2, 4, 8, 16, 32, 64)):
         d = tpmd.MotionDecoder(0, tpmd.DTYPE_F16, B)
         d.set_tensors(tensors)
         d.prepare()
@@ -553,7 +556,8 @@ def run_ops(args):
             "data": "synthetic (N(0,1) maps, grid uniform in [-1.1, 1.1]; random-init decoder)",
             "peaks": {"hbm_gbs": hbm, "bf16_tflops_burst": tf_burst, "source": src},
             "gather_best_frac": max(g["frac"] for g in gather),
-            "gather_f16_median_frac_large": float(np.median([g["frac"] for g in g_f16 if g["H"] >= 128])),
+            "gather_f16_median_frac_large": float(np.median([g["frac"] for g in g_f16 if g["H"] >= 128]))
+            if any(g["H"] >= 128 for g in g_f16) else None,
             "im2col_best_frac": max(g["frac"] for g in im2col),
             "gather": gather, "im2col": im2col, "modconv": modconv}
     print(json.dumps(line), flush=True)
@@ -568,6 +572,8 @@ def main():
     ap.add_argument("--batch", type=int, default=50)
     ap.add_argument("--dtype", default="f16", choices=["f16", "f32"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--shape", default="",
+                    help="--path ops: only this 'C,H' shape (gather and im2col), no modconv sweep")
     ap.add_argument("--clip", type=int, default=0,
                     help="config 3: decode a clip of this many frames sharded across ranks per step")
     ap.add_argument("--path", default="decoder", choices=["decoder", "encoder", "fmt", "e2e", "ops"],

@@ -64,7 +64,8 @@ struct tc_params {
     const float4 *proj;  // last level: ToRGB conv.0 applied to the feats per pixel
 };
 
-template <int BN, int KC, int NACC, bool TAIL, bool BRES, bool HALO = false, int RPS = 1, bool KHS = false>
+template <int BN, int KC, int NACC, bool TAIL, bool BRES, bool HALO = false, int RPS = 1, bool KHS = false,
+          bool DEEP = false>
 struct tc_cfg {
     static constexpr int A_TAP = BM * KC * 2;   // one tap's A tile
     static constexpr int B_TAP = BN * KC * 2;   // one tap's B tile
@@ -92,8 +93,12 @@ struct tc_cfg {
     static constexpr int BUDGET = 212992 - EXTRA - B_RES;
     // taps per pipeline stage: narrow layers put a whole kernel row (3 taps)
     // in one stage, so the per-stage barrier round trip is paid 3x less often
+    // DEEP: one tap per stage regardless of width, for layers with fewer
+    // tiles than SMs, whose CTAs each stream a long K (conv1, the r8 level):
+    // six 32 KB stages in flight hide the load latency that two 96 KB stages
+    // leave exposed
     static constexpr int TPS =
-        HALO ? 3 : BRES ? (BUDGET / (3 * A_TAP) >= 3 ? 3 : 1) : (BN <= 128 ? 3 : 1);
+        HALO ? 3 : BRES ? (BUDGET / (3 * A_TAP) >= 3 ? 3 : 1) : (BN <= 128 && !DEEP ? 3 : 1);
     // RPS: kernel rows per stage (HALO with resident weights only); a stage
     // then holds RPS halo boxes and TAPS = 3 * RPS taps, fewer commits per tile
     static constexpr int TAPS = HALO ? 3 * RPS : TPS;
@@ -202,11 +207,11 @@ __device__ __forceinline__ void unit_of(const tc_params &p, int t, int &b, int &
     b = m / p.strips;
 }
 
-template <int BN, int KC, bool UP, int NACC, bool TAIL, bool BRES, bool HALO, int RPS, bool KHS>
-__global__ void __launch_bounds__(tc_cfg<BN, KC, NACC, TAIL, BRES, HALO, RPS, KHS>::THREADS, 1)
+template <int BN, int KC, bool UP, int NACC, bool TAIL, bool BRES, bool HALO, int RPS, bool KHS, bool DEEP>
+__global__ void __launch_bounds__(tc_cfg<BN, KC, NACC, TAIL, BRES, HALO, RPS, KHS, DEEP>::THREADS, 1)
 conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const tc_params p) {
-    using cfg = tc_cfg<BN, KC, NACC, TAIL, BRES, HALO, RPS, KHS>;
+    using cfg = tc_cfg<BN, KC, NACC, TAIL, BRES, HALO, RPS, KHS, DEEP>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = (uint8_t *) (((uintptr_t) smem_raw + 1023) & ~(uintptr_t) 1023);
     uint8_t *sA = smem;
@@ -828,9 +833,9 @@ int ilog2(int v) {  // log2 of a power of two, else -1
 
 
 template <int BN, int KC, bool UP, int NACC, bool TAIL, bool BRES = false, bool HALO = false, int RPS = 1,
-          bool KHS = false>
+          bool KHS = false, bool DEEP = false>
 cudaError_t run_tc(const conv_params &cp, const tail_params *tl, cudaStream_t st) {
-    using cfg = tc_cfg<BN, KC, NACC, TAIL, BRES, HALO, RPS, KHS>;
+    using cfg = tc_cfg<BN, KC, NACC, TAIL, BRES, HALO, RPS, KHS, DEEP>;
     auto enc = encode_fn();
     if (!enc) return cudaErrorNotSupported;
     tc_params p{};
@@ -936,13 +941,13 @@ cudaError_t run_tc(const conv_params &cp, const tail_params *tl, cudaStream_t st
     int dev = 0;
     cudaGetDevice(&dev);
     if (!(attr_set >> (dev & 63) & 1)) {
-        const cudaError_t e = cudaFuncSetAttribute(conv_tc_kernel<BN, KC, UP, NACC, TAIL, BRES, HALO, RPS, KHS>,
+        const cudaError_t e = cudaFuncSetAttribute(conv_tc_kernel<BN, KC, UP, NACC, TAIL, BRES, HALO, RPS, KHS, DEEP>,
                                                    cudaFuncAttributeMaxDynamicSharedMemorySize, cfg::SMEM);
         if (e != cudaSuccess) return e;
         attr_set |= 1ull << (dev & 63);
     }
     const int grid = (int) (p.num_tiles < sm_count() ? p.num_tiles : sm_count());
-    conv_tc_kernel<BN, KC, UP, NACC, TAIL, BRES, HALO, RPS, KHS><<<grid, cfg::THREADS, cfg::SMEM, st>>>(tmA, tmB, p);
+    conv_tc_kernel<BN, KC, UP, NACC, TAIL, BRES, HALO, RPS, KHS, DEEP><<<grid, cfg::THREADS, cfg::SMEM, st>>>(tmA, tmB, p);
     return cudaGetLastError();
 }
 
@@ -964,9 +969,14 @@ cudaError_t launch_conv_tc(bool up, const conv_params &p, cudaStream_t st) {
     const int64_t m_tiles = (int64_t) ((p.B + bb - 1) / bb) * (p.H / bh) * (p.W / bw);
     // the small early levels (4x4 .. 8x8 maps) leave most SMs idle with
     // 256-wide N tiles; 128-wide ones double the tile count at the same K
-    if (N >= 256 && m_tiles * (N / 256) < sm_count())
+    if (N >= 256 && m_tiles * (N / 256) < sm_count()) {
+        // and with fewer 128-wide tiles than SMs, one tap per stage (DEEP)
+        if (m_tiles * (N / 128) < sm_count())
+            return up ? run_tc<128, 64, true, 4, false, false, false, 1, false, true>(p, nullptr, st)
+                      : run_tc<128, 64, false, 4, false, false, false, 1, false, true>(p, nullptr, st);
         return up ? run_tc<128, 64, true, 4, false>(p, nullptr, st)
                   : run_tc<128, 64, false, 4, false>(p, nullptr, st);
+    }
     if (N >= 256)
         return up ? run_tc<256, 64, true, 2, false>(p, nullptr, st)
                   : run_tc<256, 64, false, 2, false>(p, nullptr, st);

@@ -224,17 +224,65 @@ im2col_cf_kernel(const float *__restrict__ src, TD *__restrict__ dst, im2col_geo
     }
 }
 
+// 8-channel chunks, one warp per output pixel row: chunk q of the row is
+// destination element q*8 (cf rows r = ic + IC*(kw + KW*kh) make the whole
+// row of one pixel contiguous, tap-major), so lane q writes the q-th 16
+// (f16) or 32 (f32) bytes: every warp store is a contiguous run. The pixel's
+// coordinates are divided out once per row; a chunk needs only its tap and
+// channel (a shift when IC/8 is a power of two).
+template <typename TD>
+__global__ void __launch_bounds__(256)
+im2col_cf_rows_kernel(const float *__restrict__ src, TD *__restrict__ dst, im2col_geom g, int64_t npix,
+                      int lg_nchunk) {
+    const int lane = threadIdx.x & 31;
+    const int nchunk = g.IC / 8;
+    const int rowc = nchunk * g.KW * g.KH;  // chunks per output pixel
+    const int64_t R = (int64_t) g.IC * g.KW * g.KH;
+    const int64_t wstride = ((int64_t) gridDim.x * blockDim.x) >> 5;
+    for (int64_t pix = ((int64_t) blockIdx.x * blockDim.x + threadIdx.x) >> 5; pix < npix; pix += wstride) {
+        const int ow = (int) (pix % g.OW);
+        const int64_t q2 = pix / g.OW;
+        const int oh = (int) (q2 % g.OH);
+        const int64_t n = q2 / g.OH;
+        const float *sn = src + n * g.IH * g.IW * (int64_t) g.IC;
+        TD *drow = dst + pix * R;
+        for (int q = lane; q < rowc; q += 32) {
+            const int tap = lg_nchunk >= 0 ? q >> lg_nchunk : q / nchunk;
+            const int ch = q - tap * nchunk;
+            const int kh = tap / g.KW, kw = tap - kh * g.KW;
+            const int iw = ow * g.s0 + kw * g.d0 - g.p0;
+            const int ih = oh * g.s1 + kh * g.d1 - g.p1;
+            float v[8];
+            if (iw >= 0 && iw < g.IW && ih >= 0 && ih < g.IH) {
+                const float4 *s4 =
+                    reinterpret_cast<const float4 *>(sn + ((int64_t) ih * g.IW + iw) * g.IC + ch * 8);
+                const float4 a = __ldg(s4), b = __ldg(s4 + 1);
+                v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+                v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+            } else {
+#pragma unroll
+                for (int i = 0; i < 8; i++) v[i] = 0.0f;
+            }
+            st8<TD>(drow + (int64_t) q * 8, v);
+        }
+    }
+}
+
 template <typename TD>
 cudaError_t run_im2col(const float *src, void *dst, const im2col_geom &g, cudaStream_t st) {
     const bool vec = (g.IC % 8 == 0) && ((uintptr_t) src % 16 == 0) &&
                      ((uintptr_t) dst % (sizeof(TD) * 8) == 0);
-    const int64_t total =
-        (int64_t) g.N * g.OH * g.OW * g.KW * g.KH * (vec ? g.IC / 8 : g.IC);
+    if (vec) {
+        const int64_t npix = (int64_t) g.N * g.OH * g.OW;
+        const int nchunk = g.IC / 8;
+        const int lg = (nchunk & (nchunk - 1)) == 0 ? __builtin_ctz((unsigned) nchunk) : -1;
+        const int blocks = (int) std::min<int64_t>((npix * 32 + 255) / 256, 148 * 16);
+        im2col_cf_rows_kernel<TD><<<blocks, 256, 0, st>>>(src, (TD *) dst, g, npix, lg);
+        return cudaGetLastError();
+    }
+    const int64_t total = (int64_t) g.N * g.OH * g.OW * g.KW * g.KH * g.IC;
     const int blocks = (int) std::min<int64_t>((total + 255) / 256, 148 * 16);
-    if (vec)
-        im2col_cf_kernel<TD, true><<<blocks, 256, 0, st>>>(src, (TD *) dst, g, total);
-    else
-        im2col_cf_kernel<TD, false><<<blocks, 256, 0, st>>>(src, (TD *) dst, g, total);
+    im2col_cf_kernel<TD, false><<<blocks, 256, 0, st>>>(src, (TD *) dst, g, total);
     return cudaGetLastError();
 }
 
