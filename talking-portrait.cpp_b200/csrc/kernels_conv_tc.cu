@@ -85,12 +85,24 @@ struct tc_cfg {
     // BN = 256 (r64) the per-pixel loads of the old form measured faster
     static constexpr bool STG = TAIL && BN <= 128;
     static constexpr int CW = 6 * BN;
-    static constexpr int EXTRA = TAIL ? (3 * BN + 32 + (STG ? NACC * 2 * CW : 0)) * 4 : 0;
+    // XCH (levels with a trunk, BN >= 64): the trunk pass gathers the feats
+    // cooperatively, four lanes per 32-channel slice of a pixel's tap row,
+    // through a per-warp exchange area of eight pixels' activations (8 rows
+    // of 36 floats, padded against bank conflicts) and tap geometry (8 rows
+    // of 12 words). Used at 64 and 128 channels (r256, r128), where it
+    // measured faster; the 256-channel r64 tile keeps the per-pixel pass
+    static constexpr bool XCH = TAIL && (BN == 64 || BN == 128);
+    static constexpr int XW = 8 * 36 + 8 * 12;  // floats per epilogue warp
+    static constexpr int EXTRA =
+        TAIL ? (3 * BN + 32 + (STG ? NACC * 2 * CW : 0) + (XCH ? 4 * NACC * XW : 0)) * 4 : 0;
     // BRES: the whole weight matrix (9 taps x one KC chunk) stays resident in
     // shared memory for the kernel's lifetime instead of being re-loaded for
     // every pixel tile; stages then carry only A
     static constexpr int B_RES = BRES ? 9 * B_TAP : 0;
-    static constexpr int BUDGET = 212992 - EXTRA - B_RES;
+    // XCH configurations count the dynamic shared memory exactly (less the
+    // alignment pad and a bound on the barriers); the others keep the
+    // earlier cap
+    static constexpr int BUDGET = XCH ? 232448 - 1024 - 640 - EXTRA - B_RES : 212992 - EXTRA - B_RES;
     // taps per pipeline stage: narrow layers put a whole kernel row (3 taps)
     // in one stage, so the per-stage barrier round trip is paid 3x less often
     // DEEP: one tap per stage regardless of width, for layers with fewer
@@ -197,6 +209,25 @@ __device__ __forceinline__ void st_half16(__half *p, const float *v) {
     uint4 *q = reinterpret_cast<uint4 *>(p);
     q[0] = pk[0];
     q[1] = pk[1];
+}
+
+// 8 consecutive f16 values (16-byte aligned) as floats, and back
+__device__ __forceinline__ void ld_half8(const __half *p, float *v) {
+    const uint4 u = __ldg(reinterpret_cast<const uint4 *>(p));
+    const __half2 *h = reinterpret_cast<const __half2 *>(&u);
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        const float2 f = __half22float2(h[k]);
+        v[2 * k] = f.x;
+        v[2 * k + 1] = f.y;
+    }
+}
+__device__ __forceinline__ void st_half8(__half *p, const float *v) {
+    uint4 q;
+    __half2 *h2 = reinterpret_cast<__half2 *>(&q);
+#pragma unroll
+    for (int i = 0; i < 4; i++) h2[i] = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+    *reinterpret_cast<uint4 *>(p) = q;
 }
 
 // KHS work unit t: (frame, strip of p.yb output rows, 128-pixel segment)
@@ -484,6 +515,8 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         const uint32_t lanes = (uint32_t) (q * 32) << 16;
         const float *s_fw = sx, *s_up = sx + 3 * BN;
         float *s_cst = sx + 3 * BN + 32 + g * 2 * cfg::CW;  // this group's two constant buffers
+        // this warp's trunk exchange area (XCH)
+        float *s_xw = sx + 3 * BN + 32 + (cfg::STG ? NACC * 2 * cfg::CW : 0) + (warp - 2) * cfg::XW;
         uint32_t nst = 0;  // stagings this group has made
         int cur_b = -1;    // the frame whose constants are staged
         // one tile's epilogue: its accumulator at taddr0 is complete once
@@ -730,7 +763,83 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     g1 = fmaf(twt[kk], pq.y, g1);
                     g2 = fmaf(twt[kk], pq.z, g2);
                 }
-                // pass 2 (levels with a trunk): gather, blend, trunk
+                // pass 2 (levels with a trunk): gather, blend, trunk. Per 32-channel
+                // slice, four rounds of eight pixels: the eight owners publish their
+                // activations (f32, from TMEM) and tap geometry in the warp's exchange
+                // area; then four lanes per pixel each gather, blend and store eight
+                // channels, so a warp's feats loads and trunk stores cover eight
+                // 64-byte runs instead of 32 scattered 16-byte pieces
+                if constexpr (cfg::XCH) {
+                    float *xa = s_xw;                                    // [8][36]
+                    int *xm = reinterpret_cast<int *>(s_xw + 8 * 36);    // [8][12]
+                    const int pg = lane >> 2, sub = lane & 3;
+#pragma unroll 1
+                    for (int s0 = 0; s0 < BN && need_out; s0 += 32) {
+#pragma unroll 1
+                        for (int it = 0; it < 4; it++) {
+                            // the slice is re-read from TMEM each round (a warp-wide
+                            // load; only this round's owners keep it), which holds
+                            // fewer registers live than keeping it across rounds
+                            uint32_t a0[16], a1[16];
+                            tmem_ld16(taddr0 + s0, a0);
+                            tmem_ld16(taddr0 + s0 + 16, a1);
+                            if ((lane >> 3) == it) {
+                                float4 *d4 = reinterpret_cast<float4 *>(xa + (lane & 7) * 36);
+#pragma unroll
+                                for (int j = 0; j < 4; j++) {
+                                    d4[j] = make_float4(__uint_as_float(a0[4 * j]), __uint_as_float(a0[4 * j + 1]),
+                                                        __uint_as_float(a0[4 * j + 2]), __uint_as_float(a0[4 * j + 3]));
+                                    d4[4 + j] = make_float4(__uint_as_float(a1[4 * j]), __uint_as_float(a1[4 * j + 1]),
+                                                            __uint_as_float(a1[4 * j + 2]), __uint_as_float(a1[4 * j + 3]));
+                                }
+                                int4 *m4 = reinterpret_cast<int4 *>(xm + (lane & 7) * 12);
+                                m4[0] = make_int4(trow[0], trow[1], trow[2], trow[3]);
+                                m4[1] = make_int4(__float_as_int(twt[0]), __float_as_int(twt[1]),
+                                                  __float_as_int(twt[2]), __float_as_int(twt[3]));
+                                m4[2] = make_int4(__float_as_int(m), (int) (uint32_t) pix, (int) (pix >> 32), 0);
+                            }
+                            __syncwarp();
+                            const int4 *m4 = reinterpret_cast<const int4 *>(xm + pg * 12);
+                            const int4 tr = m4[0], tw = m4[1], mp = m4[2];
+                            const int trk[4] = {tr.x, tr.y, tr.z, tr.w};
+                            const float twk[4] = {__int_as_float(tw.x), __int_as_float(tw.y), __int_as_float(tw.z),
+                                                  __int_as_float(tw.w)};
+                            const float mq = __int_as_float(mp.x), omq = 1.0f - mq;
+                            const int64_t pq = (int64_t) (((uint64_t) (uint32_t) mp.z << 32) | (uint32_t) mp.y);
+                            const int cc = s0 + sub * 8;
+                            float smp[8];
+#pragma unroll
+                            for (int i = 0; i < 8; i++) smp[i] = 0.0f;
+#pragma unroll
+                            for (int kk = 0; kk < 4; kk++) {
+                                float f[8];
+                                ld_half8(p.feat + (int64_t) trk[kk] * BN + cc, f);
+#pragma unroll
+                                for (int i = 0; i < 8; i++) smp[i] = fmaf(twk[kk], f[i], smp[i]);
+                            }
+                            const float4 *ar = reinterpret_cast<const float4 *>(xa + pg * 36 + sub * 8);
+                            const float4 av0 = ar[0], av1 = ar[1];
+                            const float av[8] = {av0.x, av0.y, av0.z, av0.w, av1.x, av1.y, av1.z, av1.w};
+                            float4 sv0, sv1;
+                            if constexpr (cfg::STG) {
+                                sv0 = c_sn[cc >> 2];
+                                sv1 = c_sn[(cc >> 2) + 1];
+                            } else {
+                                sv0 = __ldg(reinterpret_cast<const float4 *>(fsn + cc));
+                                sv1 = __ldg(reinterpret_cast<const float4 *>(fsn + cc) + 1);
+                            }
+                            const float sn[8] = {sv0.x, sv0.y, sv0.z, sv0.w, sv1.x, sv1.y, sv1.z, sv1.w};
+                            float o[8];
+#pragma unroll
+                            for (int i = 0; i < 8; i++) {
+                                const float w = smp[i] * mq;
+                                o[i] = (w + av[i] * omq) * sn[i];  // trunk x next up-conv style
+                            }
+                            st_half8(p.trunk + pq * BN + cc, o);
+                            __syncwarp();
+                        }
+                    }
+                } else {
 #pragma unroll 1
                 for (int c0 = 0; c0 < BN && need_out; c0 += 16) {
                     uint32_t rr[16];
@@ -764,6 +873,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                         smp[i] = (w + __uint_as_float(rr[i]) * om) * sn[i];  // trunk x next up-conv style
                     }
                     st_half16(p.trunk + pix * BN + c0, smp);
+                }
                 }
                 const float rg[3] = {g0 * m, g1 * m, g2 * m};
 #pragma unroll
