@@ -360,6 +360,60 @@ def run_fmt(args):
     print(json.dumps(line), flush=True)
 
 
+def run_audio(args):
+    """The audio encoder of config 4 (wav2vec2-base shape: 7 conv layers, 12
+    post-norm transformer layers, d = 768) on a 30 s clip to 750 frames on
+    cuda:0, through tpae_encode (host audio in, features out), wall clock
+    around the blocking call. The CPU baseline is the oracle's restatement
+    (one clip) on the host cores."""
+    import tpmd
+    import oracle as O
+    from tpmd import synth
+    cfg = synth.AUDIO_CONFIG
+    w = synth.make_audio_weights(cfg, 0)
+    au = synth.make_audio(30.0, 0)
+    S = 750
+    e = tpmd.AudioEncoder(cfg, 0)
+    e.set_tensors(w)
+    e.prepare()
+    for _ in range(args.warmup):
+        e.encode(au, S)
+    with ClockSampler(0) as clk:
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            e.encode(au, S)
+            clk.sample()
+        ms = (time.perf_counter() - t0) / args.steps * 1e3
+    # GEMM flops: conv stack, feature projection, positional conv, layers, projection
+    T, ic, flop = au.size, 1, 0.0
+    for i in range(7):
+        T = (T - cfg["conv_kernel"][i]) // cfg["conv_stride"][i] + 1
+        flop += 2.0 * T * cfg["conv_dim"][i] * ic * cfg["conv_kernel"][i]
+        ic = cfg["conv_dim"][i]
+    H, F, L = cfg["hidden"], cfg["ffn"], cfg["n_layers"]
+    cg = H // cfg["pos_groups"]
+    flop += 2.0 * S * ic * H + 2.0 * S * H * cg * cfg["pos_kernel"]
+    flop += L * (2.0 * S * H * (4 * H + 2 * F) + 4.0 * S * S * H) + 2.0 * S * L * H * cfg["dim_w"]
+    cpu = None
+    if not args.no_cpu_baseline:
+        O.set_threads(os.cpu_count() or 1)
+        o = O.Aud(cfg, w)
+        t0 = time.perf_counter()
+        o.encode(au, S)
+        cpu = (time.perf_counter() - t0) * 1e3
+    line = {"metric": "audio encoder ms per 30 s clip (750 frames)", "value": ms, "unit": "ms",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": False,
+            "dtype": "f32", "data": "synthetic (random-init wav2vec2-base shape, band-limited speech-like audio)",
+            "config": {"workload": "config 4 audio: 30 s of 16 kHz audio -> 750 x 512 features", "global_batch": 1},
+            "achieved_tflops": flop / (ms * 1e-3) / 1e12,
+            "e2e": {"value": ms, "unit": "ms", "h2d_bytes_per_step": 4 * au.size, "d2h_bytes_per_step": 4 * S * 512},
+            "clocks": clk.summary(),
+            "cpu_baseline": None if cpu is None else {"value": cpu, "unit": "ms", "cores": O.threads(),
+                                                      "kind": "port", "sample": "1 clip"}}
+    e.close()
+    print(json.dumps(line), flush=True)
+
+
 def run_e2e(args):
     """Config 4: the end-to-end generator on a 30 s clip, real-time factor.
     Rank 0 runs the motion encoder, the audio encoder and the 15 sampler
@@ -576,15 +630,19 @@ def main():
                     help="--path ops: only this 'C,H' shape (gather and im2col), no modconv sweep")
     ap.add_argument("--clip", type=int, default=0,
                     help="config 3: decode a clip of this many frames sharded across ranks per step")
-    ap.add_argument("--path", default="decoder", choices=["decoder", "encoder", "fmt", "e2e", "ops"],
+    ap.add_argument("--path", default="decoder", choices=["decoder", "encoder", "fmt", "audio", "e2e", "ops"],
                     help="encoder: time the motion encoder (once per portrait); fmt: time the "
-                         "flow-matching sampler (one 50-frame chunk per step); one GPU")
+                         "flow-matching sampler (one 50-frame chunk per step); audio: the audio encoder "
+                         "(one 30 s clip per step); one GPU")
     args = ap.parse_args()
     if args.path == "encoder":
         run_encoder(args)
         return
     if args.path == "fmt":
         run_fmt(args)
+        return
+    if args.path == "audio":
+        run_audio(args)
         return
     if args.path == "e2e":
         run_e2e(args)

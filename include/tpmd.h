@@ -291,6 +291,21 @@ int tpk_im2col_cf(const float *src, int IC, int IW, int IH, int N, int KW, int K
  * enqueued on `stream`. */
 int tpk_chw_to_rgb24(const float *chw, int64_t n, int H, int W, uint8_t *rgb, void *stream);
 
+/* The library's tcgen05 GEMM, which the sampler and the audio encoder run
+ * their contractions on: for b < batch,
+ *   Y[b*y_batch + m*ldy + n] = act((sum_k X[m'][k'] W[n'][k'] + bias[n]) * scale)
+ * with m' = b*x_row_b + m, k' = b*x_col_b + k (X rows of stride ldx), n',
+ * k' of W likewise, m < M, n < N, k < K. dtype TPMD_DTYPE_F32: f32
+ * operands by the three-pass TF32 split (about 2^-20 relative error per
+ * product); TPMD_DTYPE_F16: f16 operands; f32 accumulation either way.
+ * act 0 none, 1 GELU (erf), 2 GELU (tanh); bias may be NULL. Strides in
+ * elements, 16-byte multiples, bases 16-byte aligned; device memory.
+ * Synchronous: returns once the GEMM finished on `stream`; -1 (message in
+ * tpk_last_error) on a bad argument or an expired pipeline wait. */
+int tpk_gemm(const void *X, int64_t ldx, const void *W, int64_t ldw, float *Y, int64_t ldy, int M, int N, int K,
+             int batch, int x_row_b, int x_col_b, int w_row_b, int w_col_b, int64_t y_batch, int dtype,
+             const float *bias, float scale, int act, void *stream);
+
 /* Message of the last failed tpk_* call on this thread. */
 const char *tpk_last_error(void);
 

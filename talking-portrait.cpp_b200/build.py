@@ -47,7 +47,7 @@ def build(verbose: bool = False) -> str:
     if not os.path.exists(SO) or os.path.getmtime(SO) < max(os.path.getmtime(o) for o in objs):
         # cuBLAS (dynamic, from the CUDA toolkit) serves the FMT sampler's plain linears
         cmd = [NVCC] + ARCH + ["-shared", "-cudart", "static", "-o", SO] + objs + \
-              ["-lcublas", "-lpthread", "-ldl", "-Xlinker", "-rpath=/usr/local/cuda/lib64"]
+              ["-lpthread", "-ldl", "-Xlinker", "-rpath=/usr/local/cuda/lib64"]
         subprocess.run(cmd, check=True)
     if verbose:
         print(f"built {SO}")

@@ -1,5 +1,5 @@
 // Kernels of the audio encoder (audio_model::encode, src/audio_enc.cpp:55-236),
-// float32, around cuBLAS GEMMs (tpae_api.cu). Activations are time-major
+// float32, around the library's tcgen05 GEMMs (tpae_api.cu). Activations are time-major
 // [T][C] (the conv stack) and token-major [S][H] (the transformer).
 #include "tpmd_internal.h"
 
@@ -13,18 +13,41 @@ __device__ __forceinline__ float silu(float v) { return v / (1.0f + expf(-v)); }
 inline int grid_for(int64_t n) { return (int) std::min<int64_t>((n + 255) / 256, 148 * 16); }
 
 // out[g][t][c*K + k] = x[t*s + k - p][c_off + g*C + c] (zero outside), the
-// column order of a torch conv1d weight row [C][K]
+// column order of a torch conv1d weight row [C][K]; rows of ldo floats
+// (the GEMM's 16-byte row stride; the padding is not written)
 __global__ void im2col1d_kernel(const float *__restrict__ x, int64_t T, int ld, int C, int K, int s, int p,
-                                int64_t OT, float *__restrict__ out) {
+                                int64_t OT, float *__restrict__ out, int ldo) {
     const int g = blockIdx.y;
-    const int64_t n = OT * C * K;
-    float *o = out + (int64_t) g * n;
+    const int CK = C * K;
+    const int64_t n = OT * CK;
+    float *o = out + (int64_t) g * OT * ldo;
     for (int64_t e = (int64_t) blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t) gridDim.x * blockDim.x) {
-        const int k = (int) (e % K);
-        const int c = (int) ((e / K) % C);
-        const int64_t t = e / ((int64_t) K * C);
+        const int ck = (int) (e % CK);
+        const int k = ck % K;
+        const int c = ck / K;
+        const int64_t t = e / CK;
         const int64_t ti = t * s + k - p;
-        o[e] = (ti >= 0 && ti < T) ? x[ti * ld + (int64_t) g * C + c] : 0.0f;
+        o[t * ldo + ck] = (ti >= 0 && ti < T) ? x[ti * ld + (int64_t) g * C + c] : 0.0f;
+    }
+}
+
+// dst[c][j] = src[j][c] for c < C, j < S (src rows of lds floats, dst rows of
+// ldd): 32 x 32 tiles through shared memory
+__global__ void transpose_kernel(const float *__restrict__ src, int64_t S, int lds, int C, float *__restrict__ dst,
+                                 int ldd) {
+    __shared__ float t[32][33];
+    const int c0 = blockIdx.x * 32;
+    const int64_t j0 = (int64_t) blockIdx.y * 32;
+    for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+        const int64_t j = j0 + r;
+        const int c = c0 + threadIdx.x;
+        t[r][threadIdx.x] = (j < S && c < C) ? src[j * lds + c] : 0.0f;
+    }
+    __syncthreads();
+    for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+        const int c = c0 + r;
+        const int64_t j = j0 + threadIdx.x;
+        if (c < C && j < S) dst[(int64_t) c * ldd + j] = t[threadIdx.x][r];
     }
 }
 
@@ -73,10 +96,6 @@ __global__ void chan_norm_gelu_kernel(float *__restrict__ x, int64_t T, int C, c
     }
 }
 
-__global__ void gelu_kernel(float *__restrict__ x, int64_t n) {
-    for (int64_t e = (int64_t) blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t) gridDim.x * blockDim.x)
-        x[e] = gelu_erf(x[e]);
-}
 
 // linear interpolation with align_corners=True from T to S rows of C
 __global__ void interp_kernel(const float *__restrict__ x, int64_t T, int C, int64_t S, float *__restrict__ y) {
@@ -138,16 +157,6 @@ __global__ void __launch_bounds__(256) layer_norm_kernel(const float *x, const f
     }
 }
 
-// y[m][n] = (y[m][n] + b[n]) * scale, act: 0 none, 1 GELU
-__global__ void bias_act_kernel(float *__restrict__ y, const float *__restrict__ b, int64_t M, int N, float scale,
-                                int act) {
-    const int64_t n = M * N;
-    for (int64_t e = (int64_t) blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t) gridDim.x * blockDim.x) {
-        float v = (y[e] + __ldg(b + e % N)) * scale;
-        if (act == 1) v = gelu_erf(v);
-        y[e] = v;
-    }
-}
 
 // e[s][i] += gelu(pos[s][i] + b[i])
 __global__ void pos_add_kernel(float *__restrict__ e, const float *__restrict__ pos, const float *__restrict__ b,
@@ -157,10 +166,11 @@ __global__ void pos_add_kernel(float *__restrict__ e, const float *__restrict__ 
         e[q] += gelu_erf(pos[q] + __ldg(b + q % H));
 }
 
-// softmax over the last dim of [rows][N] in place; one block per row
-__global__ void __launch_bounds__(256) softmax_kernel(float *__restrict__ x, int N) {
+// softmax over the first N entries of each ld-float row of x in place; one
+// block per row
+__global__ void __launch_bounds__(256) softmax_kernel(float *__restrict__ x, int N, int ld) {
     __shared__ float red[8];
-    float *r = x + (int64_t) blockIdx.x * N;
+    float *r = x + (int64_t) blockIdx.x * ld;
     float mx = -INFINITY;
     for (int i = threadIdx.x; i < N; i += blockDim.x) mx = fmaxf(mx, r[i]);
 #pragma unroll
@@ -197,19 +207,20 @@ __global__ void copy_cols_kernel(const float *__restrict__ src, int64_t S, int H
 }  // namespace
 
 cudaError_t aud_im2col(const float *x, int64_t T, int ld, int C, int K, int s, int p, int64_t OT, int groups,
-                       float *out, cudaStream_t st) {
+                       float *out, int ldo, cudaStream_t st) {
     const dim3 grid(grid_for(OT * C * K), groups);
-    im2col1d_kernel<<<grid, 256, 0, st>>>(x, T, ld, C, K, s, p, OT, out);
+    im2col1d_kernel<<<grid, 256, 0, st>>>(x, T, ld, C, K, s, p, OT, out, ldo);
+    return cudaGetLastError();
+}
+cudaError_t aud_transpose(const float *src, int64_t S, int lds, int C, float *dst, int ldd, cudaStream_t st) {
+    const dim3 grid((unsigned) ((C + 31) / 32), (unsigned) ((S + 31) / 32));
+    transpose_kernel<<<grid, dim3(32, 8), 0, st>>>(src, S, lds, C, dst, ldd);
     return cudaGetLastError();
 }
 cudaError_t aud_group_norm_gelu(float *x, int64_t T, int C, float eps, const float *w, const float *b, float *stats,
                                 cudaStream_t st) {
     chan_stats_kernel<<<C, 256, 0, st>>>(x, T, C, eps, stats, stats + C);
     chan_norm_gelu_kernel<<<grid_for(T * C), 256, 0, st>>>(x, T, C, stats, stats + C, w, b);
-    return cudaGetLastError();
-}
-cudaError_t aud_gelu(float *x, int64_t n, cudaStream_t st) {
-    gelu_kernel<<<grid_for(n), 256, 0, st>>>(x, n);
     return cudaGetLastError();
 }
 cudaError_t aud_interp(const float *x, int64_t T, int C, int64_t S, float *y, cudaStream_t st) {
@@ -221,16 +232,12 @@ cudaError_t aud_layer_norm(const float *x, const float *r, const float *rb, int6
     layer_norm_kernel<<<(unsigned) M, 256, N * sizeof(float), st>>>(x, r, rb, N, eps, w, b, silu_act ? 1 : 0, y);
     return cudaGetLastError();
 }
-cudaError_t aud_bias_act(float *y, const float *b, int64_t M, int N, float scale, bool gelu, cudaStream_t st) {
-    bias_act_kernel<<<grid_for(M * N), 256, 0, st>>>(y, b, M, N, scale, gelu ? 1 : 0);
-    return cudaGetLastError();
-}
 cudaError_t aud_pos_add(float *e, const float *pos, const float *b, int64_t S, int H, cudaStream_t st) {
     pos_add_kernel<<<grid_for(S * H), 256, 0, st>>>(e, pos, b, S, H);
     return cudaGetLastError();
 }
-cudaError_t aud_softmax(float *x, int64_t rows, int N, cudaStream_t st) {
-    softmax_kernel<<<(unsigned) rows, 256, 0, st>>>(x, N);
+cudaError_t aud_softmax(float *x, int64_t rows, int N, int ld, cudaStream_t st) {
+    softmax_kernel<<<(unsigned) rows, 256, 0, st>>>(x, N, ld);
     return cudaGetLastError();
 }
 cudaError_t aud_copy_cols(const float *src, int64_t S, int H, float *dst, int ld, int off, cudaStream_t st) {

@@ -1,10 +1,11 @@
 // Kernels of the flow-matching transformer (fmt_model::forward,
 // src/fmt.cpp:64-211) and its Euler/CFG sampler (src/pipeline.cpp:15-91),
-// around the plain linears (cuBLAS, tpfm_api.cu). Tokens are rows m = b*T + f
-// of the three CFG branches b (uncond, full, audio-only) and T frames; every
-// activation is row-major [M][width] float32 unless it feeds a GEMM, where it
-// is written in the GEMM's input type TIN (float or __half). GEMMs run
-// without bias; the kernel consuming a GEMM output adds the bias.
+// around the plain linears (the tcgen05 GEMM, tpfm_api.cu). Tokens are rows
+// m = b*T + f of the three CFG branches b (uncond, full, audio-only) and T
+// frames; every activation is row-major [M][width] float32 unless it feeds a
+// GEMM, where it is written in the GEMM's input type TIN (float or __half).
+// GEMMs other than the MLP's first (bias and GELU in its epilogue) run
+// without bias; the kernel consuming their output adds it.
 #include "tpmd_internal.h"
 
 #include <algorithm>
@@ -20,10 +21,6 @@ template <>
 __device__ __forceinline__ __half cvt<__half>(float v) { return __float2half_rn(v); }
 
 __device__ __forceinline__ float silu(float v) { return v / (1.0f + expf(-v)); }
-__device__ __forceinline__ float gelu_tanh(float v) {
-    const float c = 0.7978845608028654f;  // sqrt(2/pi)
-    return 0.5f * v * (1.0f + tanhf(c * (v + 0.044715f * v * v * v)));
-}
 
 __device__ __forceinline__ float block_sum(float v, float *red) {
 #pragma unroll
@@ -197,15 +194,6 @@ __global__ void __launch_bounds__(256) res_norm_kernel(float *__restrict__ x, co
     }
 }
 
-// y = gelu_tanh(a + b)
-template <typename TIN>
-__global__ void gelu_kernel(const float *__restrict__ a, const float *__restrict__ b, int M, int N,
-                            TIN *__restrict__ y) {
-    const int64_t n = (int64_t) M * N;
-    for (int64_t e = (int64_t) blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t) gridDim.x * blockDim.x)
-        y[e] = cvt<TIN>(gelu_tanh(a[e] + __ldg(b + e % N)));
-}
-
 // v = out + b; per current frame f: vc = (u + a_cfg (a - u)) + e_cfg (fu - a);
 // x[f] += dt * vc; the next forward's x60 rows P.. are the new x (and their
 // f16 copy, the next x_embedder GEMM's input, when x60h is given)
@@ -290,13 +278,6 @@ cudaError_t fmt_res_norm(bool f16, float *x, const float *o, const float *bo, co
     else
         res_norm_kernel<float><<<M, 256, 0, st>>>(x, o, bo, mod, bmod, mod_stride, gate_off, H, eps, mod2, bmod2,
                                                   shift_off, scale_off, (float *) h);
-    return cudaGetLastError();
-}
-cudaError_t fmt_gelu(bool f16, const float *a, const float *b, int M, int N, void *y, cudaStream_t st) {
-    if (f16)
-        gelu_kernel<__half><<<grid_for((int64_t) M * N), 256, 0, st>>>(a, b, M, N, (__half *) y);
-    else
-        gelu_kernel<float><<<grid_for((int64_t) M * N), 256, 0, st>>>(a, b, M, N, (float *) y);
     return cudaGetLastError();
 }
 cudaError_t fmt_cfg_euler(const float *vout, const float *bv, int T, int P, int D, float a_cfg, float e_cfg,

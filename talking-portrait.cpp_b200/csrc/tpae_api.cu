@@ -1,8 +1,11 @@
 // Audio encoder C ABI (include/tpae.h): audio_model::encode
-// (src/audio_enc.cpp:55-236) over cuBLAS float32 GEMMs (no TF32) and the
-// kernels of kernels_audio.cu. Convolutions are im2col + GEMM; attention is
-// two strided-batched GEMMs around a row softmax.
-#include <cublas_v2.h>
+// (src/audio_enc.cpp:55-236) over the library's tcgen05 GEMM with float32
+// operands (three-pass TF32 split, kernels_gemm_tc.cu) and the kernels of
+// kernels_audio.cu. Convolutions are im2col + GEMM (the convs' GELU and the
+// linears' biases, the q scaling and the FFN GELU in the GEMM epilogue);
+// q, k and v come from one GEMM over their stacked weights; attention is
+// two head-batched GEMMs (heads as column blocks of the qkv rows) around a
+// row softmax, the values transposed once so both operands run along j.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -17,16 +20,15 @@
 
 namespace tpmd {
 cudaError_t aud_im2col(const float *x, int64_t T, int ld, int C, int K, int s, int p, int64_t OT, int groups,
-                       float *out, cudaStream_t st);
+                       float *out, int ldo, cudaStream_t st);
+cudaError_t aud_transpose(const float *src, int64_t S, int lds, int C, float *dst, int ldd, cudaStream_t st);
 cudaError_t aud_group_norm_gelu(float *x, int64_t T, int C, float eps, const float *w, const float *b, float *stats,
                                 cudaStream_t st);
-cudaError_t aud_gelu(float *x, int64_t n, cudaStream_t st);
 cudaError_t aud_interp(const float *x, int64_t T, int C, int64_t S, float *y, cudaStream_t st);
 cudaError_t aud_layer_norm(const float *x, const float *r, const float *rb, int64_t M, int N, float eps,
                            const float *w, const float *b, bool silu_act, float *y, cudaStream_t st);
-cudaError_t aud_bias_act(float *y, const float *b, int64_t M, int N, float scale, bool gelu, cudaStream_t st);
 cudaError_t aud_pos_add(float *e, const float *pos, const float *b, int64_t S, int H, cudaStream_t st);
-cudaError_t aud_softmax(float *x, int64_t rows, int N, cudaStream_t st);
+cudaError_t aud_softmax(float *x, int64_t rows, int N, int ld, cudaStream_t st);
 cudaError_t aud_copy_cols(const float *src, int64_t S, int H, float *dst, int ld, int off, cudaStream_t st);
 }  // namespace tpmd
 
@@ -43,11 +45,11 @@ struct tpae_ctx {
     std::map<std::string, int64_t> spec;
     std::map<std::string, std::vector<float>> host;
     std::map<std::string, size_t> off;
+    std::map<std::string, int> kdim, ldk;  // conv weights: K, and rows padded to 4 floats
     float *w = nullptr;
     bool wready = false;
     cudaStream_t stream = nullptr;
-    cublasHandle_t blas = nullptr;
-    void *blas_ws = nullptr;
+    int *gerr = nullptr;  // the GEMMs' error flag
     float *ws = nullptr;
     size_t ws_floats = 0;
 
@@ -61,24 +63,42 @@ struct tpae_ctx {
         cudaGetLastError();
         return false;
     }
-    bool bk(cublasStatus_t s, const char *what) {
-        if (s == CUBLAS_STATUS_SUCCESS) return true;
-        err = std::string(what) + ": cuBLAS status " + std::to_string((int) s);
-        return false;
-    }
     const float *W(const std::string &n) const { return w + off.at(n); }
-    // Y[M][N] (ldy) = X[M][K] (ldx) W[N][K]^T, float32 without TF32
-    bool gemm(const float *X, int64_t Mr, int K, int ldx, const float *Wt, int N, float *Y, int ldy, const char *what) {
-        const float one = 1.0f, zero = 0.0f;
-        return bk(cublasGemmEx(blas, CUBLAS_OP_T, CUBLAS_OP_N, N, (int) Mr, K, &one, Wt, CUDA_R_32F, K, X,
-                               CUDA_R_32F, ldx, &zero, Y, CUDA_R_32F, ldy, CUBLAS_COMPUTE_32F_PEDANTIC,
-                               CUBLAS_GEMM_DEFAULT),
-                  what);
+    gemm_desc desc() const {
+        gemm_desc d;
+        d.f32 = true;
+        d.err = gerr;
+        return d;
+    }
+    // Y[M][N] (ldy) = act((X[M][K] (ldx) W[N][K]^T (ldw) + bias) * scale)
+    bool gemm(const float *X, int64_t Mr, int K, int ldx, const float *Wt, int ldw, int N, float *Y, int ldy,
+              const char *what, const float *bias = nullptr, float scale = 1.0f, int act = 0) {
+        gemm_desc d = desc();
+        d.X = X;
+        d.ldx = ldx;
+        d.W = Wt;
+        d.ldw = ldw;
+        d.Y = Y;
+        d.ldy = ldy;
+        d.M = (int) Mr;
+        d.N = N;
+        d.K = K;
+        d.bias = bias;
+        d.scale = scale;
+        d.act = act;
+        return ck(gemm_tc(d, stream), what);
+    }
+    // after a synchronize: a GEMM whose pipeline wait expired
+    bool gemm_status() {
+        int flag = 0;
+        if (!ck(cudaMemcpy(&flag, gerr, sizeof flag, cudaMemcpyDeviceToHost), "GEMM status")) return false;
+        if (!flag) return true;
+        cudaMemset(gerr, 0, sizeof(int));
+        return fail("a GEMM pipeline wait timed out");
     }
     ~tpae_ctx() {
         if (device >= 0) cudaSetDevice(device);
-        if (blas) cublasDestroy(blas);
-        if (blas_ws) cudaFree(blas_ws);
+        if (gerr) cudaFree(gerr);
         if (ws) cudaFree(ws);
         if (w) cudaFree(w);
         if (stream) cudaStreamDestroy(stream);
@@ -92,8 +112,10 @@ void build_spec(tpae_ctx *a) {
     const int H = c.hidden, F = c.ffn;
     int ic = 1;
     for (int i = 0; i < 7; i++) {
-        a->spec["feature_extractor.conv_layers." + std::to_string(i) + ".conv.weight"] =
-            (int64_t) c.conv_dim[i] * ic * c.conv_kernel[i];
+        const std::string n = "feature_extractor.conv_layers." + std::to_string(i) + ".conv.weight";
+        a->spec[n] = (int64_t) c.conv_dim[i] * ic * c.conv_kernel[i];
+        a->kdim[n] = ic * c.conv_kernel[i];
+        a->ldk[n] = (ic * c.conv_kernel[i] + 3) & ~3;
         ic = c.conv_dim[i];
     }
     a->spec["feature_extractor.conv_layers.0.layer_norm.weight"] = c.conv_dim[0];
@@ -186,7 +208,11 @@ tpae_ctx *tpae_create(int device, const tpae_config *cfg) {
     bool valid = cfg->n_layers > 0 && cfg->n_heads > 0 && cfg->hidden > 0 && cfg->hidden % cfg->n_heads == 0 &&
                  cfg->ffn > 0 && cfg->dim_w > 0 && cfg->pos_groups > 0 && cfg->hidden % cfg->pos_groups == 0 &&
                  cfg->pos_kernel > 0 && cfg->sample_rate > 0 && cfg->fps > 0 && cfg->dim_w <= 4096 &&
-                 cfg->hidden <= 4096 && cfg->conv_dim[6] <= 4096;
+                 cfg->hidden <= 4096 && cfg->conv_dim[6] <= 4096 &&
+                 // the GEMMs' row strides (16-byte multiples) and the attention
+                 // heads' whole 32-float k-blocks
+                 (cfg->hidden / cfg->n_heads) % 32 == 0 && cfg->ffn % 4 == 0 && cfg->dim_w % 4 == 0 &&
+                 cfg->conv_dim[6] % 4 == 0 && ((cfg->hidden / cfg->pos_groups) * cfg->pos_kernel) % 4 == 0;
     for (int i = 0; i < 7; i++)
         valid = valid && cfg->conv_dim[i] > 0 && cfg->conv_kernel[i] > 0 && cfg->conv_stride[i] > 0;
     if (!valid) {
@@ -211,10 +237,9 @@ tpae_ctx *tpae_create(int device, const tpae_config *cfg) {
     build_spec(a);
     bool ok = a->ck(cudaSetDevice(device), "cudaSetDevice") &&
               a->ck(cudaStreamCreateWithFlags(&a->stream, cudaStreamNonBlocking), "stream") &&
-              a->ck(cudaMalloc(&a->blas_ws, (size_t) 32 << 20), "cudaMalloc(cuBLAS workspace)") &&
-              a->bk(cublasCreate(&a->blas), "cublasCreate") && a->bk(cublasSetStream(a->blas, a->stream), "stream") &&
-              a->bk(cublasSetWorkspace(a->blas, a->blas_ws, (size_t) 32 << 20), "workspace") &&
-              a->bk(cublasSetMathMode(a->blas, CUBLAS_PEDANTIC_MATH), "math mode");
+              a->ck(cudaMalloc(&a->gerr, sizeof(int)), "cudaMalloc(GEMM flag)") &&
+              a->ck(cudaMemset(a->gerr, 0, sizeof(int)), "cudaMemset(GEMM flag)") &&
+              a->ck(gemm_tc_prepare(), "GEMM set-up");
     if (!ok) {
         g_create_err = a->err;
         delete a;
@@ -260,14 +285,55 @@ int tpae_prepare(tpae_ctx *a) {
     if (!a) return -1;
     for (auto &kv : a->spec)
         if (!a->host.count(kv.first)) return a->fail("tpae_prepare: missing tensor " + kv.first), -1;
+    // the arena: every tensor at a 256-byte aligned offset, conv weights with
+    // rows padded to ldk floats, and per layer q, k and v stacked into one
+    // [3H][H] weight and one [3H] bias (one GEMM computes all three)
+    const int H = a->c.hidden;
+    auto is_qkv = [](const std::string &n) {
+        return n.find(".attention.q_proj.") != std::string::npos || n.find(".attention.k_proj.") != std::string::npos ||
+               n.find(".attention.v_proj.") != std::string::npos;
+    };
+    std::vector<std::pair<std::string, size_t>> items;
+    for (auto &kv : a->spec) {
+        if (is_qkv(kv.first)) continue;
+        const auto it = a->ldk.find(kv.first);
+        items.push_back({kv.first, it == a->ldk.end() ? (size_t) kv.second
+                                                       : (size_t) (kv.second / a->kdim.at(kv.first)) * it->second});
+    }
+    for (int l = 0; l < a->c.n_layers; l++) {
+        const std::string b = "encoder.layers." + std::to_string(l) + ".attention.";
+        items.push_back({b + "qkv.weight", (size_t) 3 * H * H});
+        items.push_back({b + "qkv.bias", (size_t) 3 * H});
+    }
     size_t total = 0;
     a->off.clear();
-    for (auto &kv : a->spec) {
-        a->off[kv.first] = total;
-        total += ((size_t) kv.second + 63) & ~(size_t) 63;
+    for (auto &it : items) {
+        a->off[it.first] = total;
+        total += (it.second + 63) & ~(size_t) 63;
     }
     std::vector<float> img(total, 0.0f);
-    for (auto &kv : a->spec) memcpy(img.data() + a->off[kv.first], a->host[kv.first].data(), kv.second * 4);
+    for (auto &kv : a->spec) {
+        const std::string &n = kv.first;
+        if (is_qkv(n)) continue;
+        const auto it = a->ldk.find(n);
+        if (it == a->ldk.end()) {
+            memcpy(img.data() + a->off[n], a->host[n].data(), kv.second * 4);
+            continue;
+        }
+        const int64_t K = a->kdim.at(n);
+        for (int64_t r = 0; r < kv.second / K; r++)
+            memcpy(img.data() + a->off[n] + r * it->second, a->host[n].data() + r * K, K * 4);
+    }
+    for (int l = 0; l < a->c.n_layers; l++) {
+        const std::string b = "encoder.layers." + std::to_string(l) + ".attention.";
+        const char *pj[3] = {"q_proj", "k_proj", "v_proj"};
+        for (int j = 0; j < 3; j++) {
+            memcpy(img.data() + a->off[b + "qkv.weight"] + (size_t) j * H * H, a->host[b + pj[j] + ".weight"].data(),
+                   (size_t) H * H * 4);
+            memcpy(img.data() + a->off[b + "qkv.bias"] + (size_t) j * H, a->host[b + pj[j] + ".bias"].data(),
+                   (size_t) H * 4);
+        }
+    }
     if (!a->ck(cudaSetDevice(a->device), "cudaSetDevice")) return -1;
     if (a->w) cudaFree(a->w);
     a->w = nullptr;
@@ -303,17 +369,22 @@ int tpae_encode(tpae_ctx *a, const float *audio, int64_t n_in, int64_t seq_len, 
         T[i + 1] = (T[i] - c.conv_kernel[i]) / c.conv_stride[i] + 1;
         if (T[i] < c.conv_kernel[i] || T[i + 1] < 1) return a->fail("audio too short"), -1;
         act = std::max(act, (size_t) T[i + 1] * c.conv_dim[i]);
-        col = std::max(col, (size_t) T[i + 1] * ic * c.conv_kernel[i]);
+        col = std::max(col, (size_t) T[i + 1] * ((ic * c.conv_kernel[i] + 3) & ~3));
         ic = c.conv_dim[i];
     }
     if (T[7] < 2) return a->fail("audio too short"), -1;
     const int64_t S = seq_len;
     const int H = c.hidden, F = c.ffn, L = c.n_layers, nh = c.n_heads, hd = H / nh, C6 = c.conv_dim[6];
     const int G = c.pos_groups, cg = H / G, KP = c.pos_kernel;
+    // rows of the attention scores and of the transposed values: S floats
+    // padded to a 16-byte multiple
+    if (S > (1 << 24)) return a->fail("tpae_encode: seq_len too large"), -1;
+    const int lds = (int) ((S + 3) & ~(int64_t) 3);
     col = std::max(col, (size_t) G * S * cg * KP);
-    const size_t sizes[] = {(size_t) n, act, act, col, (size_t) 2 * c.conv_dim[0], (size_t) S * C6, (size_t) S * H,
-                            (size_t) S * H, (size_t) S * H, (size_t) S * H, (size_t) S * H, (size_t) S * H,
-                            (size_t) S * F, (size_t) nh * S * S, (size_t) S * L * H, (size_t) S * c.dim_w};
+    const size_t sizes[] = {(size_t) n,      act,           act,           col,          (size_t) 2 * c.conv_dim[0],
+                            (size_t) S * C6, (size_t) S * H, (size_t) S * 3 * H, (size_t) H * lds, (size_t) S * H,
+                            (size_t) S * H,  (size_t) S * F, (size_t) nh * S * lds, (size_t) S * L * H,
+                            (size_t) S * c.dim_w};
     const int ns = sizeof(sizes) / sizeof(sizes[0]);
     size_t offs[16], total = 0;
     for (int i = 0; i < ns; i++) {
@@ -331,51 +402,59 @@ int tpae_encode(tpae_ctx *a, const float *audio, int64_t n_in, int64_t seq_len, 
     float *bufs[16];
     for (int i = 0; i < ns; i++) bufs[i] = a->ws + offs[i];
     float *aud = bufs[0], *x0 = bufs[1], *x1 = bufs[2], *colb = bufs[3], *stats = bufs[4], *hi = bufs[5],
-          *e = bufs[6], *q = bufs[7], *k = bufs[8], *v = bufs[9], *att = bufs[10], *o = bufs[11], *f1 = bufs[12],
-          *sc = bufs[13], *stk = bufs[14], *y = bufs[15];
+          *e = bufs[6], *qkv = bufs[7], *vt = bufs[8], *att = bufs[9], *o = bufs[10], *f1 = bufs[11],
+          *sc = bufs[12], *stk = bufs[13], *y = bufs[14];
     cudaStream_t st = a->stream;
     auto K = [&](cudaError_t err, const char *w) { return a->ck(err, w); };
     if (!K(cudaMemcpyAsync(aud, audio, (size_t) n * 4, cudaMemcpyHostToDevice, st), "audio H2D")) return -1;
-    // conv stack: im2col + GEMM per layer, GroupNorm + GELU on the first
+    // conv stack: im2col + GEMM per layer; GroupNorm + GELU on the first,
+    // GELU in the GEMM epilogue on the others
     const float *x = aud;
     float *dst = x0;
     ic = 1;
     for (int i = 0; i < 7; i++) {
         const int Kk = c.conv_kernel[i], s = c.conv_stride[i], O = c.conv_dim[i];
         const std::string wn = "feature_extractor.conv_layers." + std::to_string(i) + ".conv.weight";
-        if (!K(aud_im2col(x, T[i], ic, ic, Kk, s, 0, T[i + 1], 1, colb, st), "conv im2col") ||
-            !a->gemm(colb, T[i + 1], ic * Kk, ic * Kk, a->W(wn), O, dst, O, wn.c_str()))
+        const int ldo = a->ldk.at(wn);
+        if (!K(aud_im2col(x, T[i], ic, ic, Kk, s, 0, T[i + 1], 1, colb, ldo, st), "conv im2col") ||
+            !a->gemm(colb, T[i + 1], ic * Kk, ldo, a->W(wn), ldo, O, dst, O, wn.c_str(), nullptr, 1.0f, i == 0 ? 0 : 1))
             return -1;
-        if (i == 0) {
-            if (!K(aud_group_norm_gelu(dst, T[1], O, c.ln_eps, a->W("feature_extractor.conv_layers.0.layer_norm.weight"),
-                                       a->W("feature_extractor.conv_layers.0.layer_norm.bias"), stats, st),
-                   "group norm"))
-                return -1;
-        } else if (!K(aud_gelu(dst, T[i + 1] * O, st), "gelu")) {
+        if (i == 0 &&
+            !K(aud_group_norm_gelu(dst, T[1], O, c.ln_eps, a->W("feature_extractor.conv_layers.0.layer_norm.weight"),
+                                   a->W("feature_extractor.conv_layers.0.layer_norm.bias"), stats, st),
+               "group norm"))
             return -1;
-        }
         x = dst;
         dst = dst == x0 ? x1 : x0;
         ic = O;
     }
-    // interpolation to seq_len frames, feature projection
+    // interpolation to seq_len frames, feature projection (+ bias)
     if (!K(aud_interp(x, T[7], C6, S, hi, st), "interp") ||
         !K(aud_layer_norm(hi, nullptr, nullptr, S, C6, c.ln_eps, a->W("feature_projection.layer_norm.weight"),
                           a->W("feature_projection.layer_norm.bias"), false, hi, st),
            "layer norm") ||
-        !a->gemm(hi, S, C6, C6, a->W("feature_projection.projection.weight"), H, e, H, "feature projection") ||
-        !K(aud_bias_act(e, a->W("feature_projection.projection.bias"), S, H, 1.0f, false, st), "bias"))
+        !a->gemm(hi, S, C6, C6, a->W("feature_projection.projection.weight"), C6, H, e, H, "feature projection",
+                 a->W("feature_projection.projection.bias")))
         return -1;
-    // grouped positional conv (pad K/2, first S outputs), GELU, added
+    // grouped positional conv (pad K/2, first S outputs): group g's im2col
+    // rows and weight rows are row blocks of one GEMM batch; GELU(+ bias) added
     {
-        const float one = 1.0f, zero = 0.0f;
-        if (!K(aud_im2col(e, S, H, cg, KP, 1, KP / 2, S, G, colb, st), "pos im2col") ||
-            !a->bk(cublasGemmStridedBatchedEx(a->blas, CUBLAS_OP_T, CUBLAS_OP_N, cg, (int) S, cg * KP, &one,
-                                              a->W("encoder.pos_conv_embed.conv.weight"), CUDA_R_32F, cg * KP,
-                                              (long long) cg * cg * KP, colb, CUDA_R_32F, cg * KP,
-                                              (long long) S * cg * KP, &zero, o, CUDA_R_32F, H, cg, G,
-                                              CUBLAS_COMPUTE_32F_PEDANTIC, CUBLAS_GEMM_DEFAULT),
-                   "pos conv") ||
+        gemm_desc d = a->desc();
+        d.X = colb;
+        d.ldx = cg * KP;
+        d.W = a->W("encoder.pos_conv_embed.conv.weight");
+        d.ldw = cg * KP;
+        d.Y = o;
+        d.ldy = H;
+        d.y_batch = cg;
+        d.M = (int) S;
+        d.N = cg;
+        d.K = cg * KP;
+        d.batch = G;
+        d.x_row_b = (int) S;
+        d.w_row_b = cg;
+        if (!K(aud_im2col(e, S, H, cg, KP, 1, KP / 2, S, G, colb, cg * KP, st), "pos im2col") ||
+            !K(gemm_tc(d, st), "pos conv") ||
             !K(aud_pos_add(e, o, a->W("encoder.pos_conv_embed.conv.bias"), S, H, st), "pos add") ||
             !K(aud_layer_norm(e, nullptr, nullptr, S, H, c.ln_eps, a->W("encoder.layer_norm.weight"),
                               a->W("encoder.layer_norm.bias"), false, e, st),
@@ -388,46 +467,59 @@ int tpae_encode(tpae_ctx *a, const float *audio, int64_t n_in, int64_t seq_len, 
         const std::string b = "encoder.layers." + std::to_string(l) + ".";
         auto Wn = [&](const char *s) { return a->W(b + s + ".weight"); };
         auto Bn = [&](const char *s) { return a->W(b + s + ".bias"); };
-        const float one = 1.0f, zero = 0.0f;
-        if (!a->gemm(e, S, H, H, Wn("attention.q_proj"), H, q, H, "q") ||
-            !K(aud_bias_act(q, Bn("attention.q_proj"), S, H, scaling, false, st), "bias") ||
-            !a->gemm(e, S, H, H, Wn("attention.k_proj"), H, k, H, "k") ||
-            !K(aud_bias_act(k, Bn("attention.k_proj"), S, H, 1.0f, false, st), "bias") ||
-            !a->gemm(e, S, H, H, Wn("attention.v_proj"), H, v, H, "v") ||
-            !K(aud_bias_act(v, Bn("attention.v_proj"), S, H, 1.0f, false, st), "bias") ||
-            // scores[h][i][j] = q_i . k_j (q already scaled)
-            !a->bk(cublasGemmStridedBatchedEx(a->blas, CUBLAS_OP_T, CUBLAS_OP_N, (int) S, (int) S, hd, &one, k,
-                                              CUDA_R_32F, H, hd, q, CUDA_R_32F, H, hd, &zero, sc, CUDA_R_32F, (int) S,
-                                              (long long) S * S, nh, CUBLAS_COMPUTE_32F_PEDANTIC, CUBLAS_GEMM_DEFAULT),
-                   "scores") ||
-            !K(aud_softmax(sc, (int64_t) nh * S, (int) S, st), "softmax") ||
-            // att[i][h*hd + d] = sum_j p[h][i][j] v[j][h*hd + d]
-            !a->bk(cublasGemmStridedBatchedEx(a->blas, CUBLAS_OP_N, CUBLAS_OP_N, hd, (int) S, (int) S, &one, v,
-                                              CUDA_R_32F, H, hd, sc, CUDA_R_32F, (int) S, (long long) S * S, &zero,
-                                              att, CUDA_R_32F, H, hd, nh, CUBLAS_COMPUTE_32F_PEDANTIC,
-                                              CUBLAS_GEMM_DEFAULT),
-                   "attention") ||
-            !a->gemm(att, S, H, H, Wn("attention.out_proj"), H, o, H, "out proj") ||
+        // scores[h][i][j] = scaling * q_i . k_j over head h's columns; then
+        // att[i][h*hd + d] = sum_j p[h][i][j] v[j][h*hd + d] against v^T
+        gemm_desc ds = a->desc();
+        ds.X = qkv;
+        ds.ldx = 3 * H;
+        ds.W = qkv + H;
+        ds.ldw = 3 * H;
+        ds.Y = sc;
+        ds.ldy = lds;
+        ds.y_batch = (int64_t) S * lds;
+        ds.M = ds.N = (int) S;
+        ds.K = hd;
+        ds.batch = nh;
+        ds.x_col_b = ds.w_col_b = hd;
+        ds.scale = scaling;
+        gemm_desc dv = a->desc();
+        dv.X = sc;
+        dv.ldx = lds;
+        dv.W = vt;
+        dv.ldw = lds;
+        dv.Y = att;
+        dv.ldy = H;
+        dv.y_batch = hd;
+        dv.M = (int) S;
+        dv.N = hd;
+        dv.K = (int) S;
+        dv.batch = nh;
+        dv.x_row_b = (int) S;
+        dv.w_row_b = hd;
+        if (!a->gemm(e, S, H, H, Wn("attention.qkv"), H, 3 * H, qkv, 3 * H, "qkv", Bn("attention.qkv")) ||
+            !K(gemm_tc(ds, st), "scores") || !K(aud_softmax(sc, (int64_t) nh * S, (int) S, lds, st), "softmax") ||
+            !K(aud_transpose(qkv + 2 * H, S, 3 * H, H, vt, lds, st), "values") || !K(gemm_tc(dv, st), "attention") ||
+            !a->gemm(att, S, H, H, Wn("attention.out_proj"), H, H, o, H, "out proj") ||
             !K(aud_layer_norm(e, o, Bn("attention.out_proj"), S, H, c.ln_eps, Wn("layer_norm"), Bn("layer_norm"), false,
                               e, st),
                "layer norm") ||
-            !a->gemm(e, S, H, H, Wn("feed_forward.intermediate_dense"), F, f1, F, "ffn") ||
-            !K(aud_bias_act(f1, Bn("feed_forward.intermediate_dense"), S, F, 1.0f, true, st), "gelu") ||
-            !a->gemm(f1, S, F, F, Wn("feed_forward.output_dense"), H, o, H, "ffn out") ||
+            !a->gemm(e, S, H, H, Wn("feed_forward.intermediate_dense"), H, F, f1, F, "ffn",
+                     Bn("feed_forward.intermediate_dense"), 1.0f, 1) ||
+            !a->gemm(f1, S, F, F, Wn("feed_forward.output_dense"), F, H, o, H, "ffn out") ||
             !K(aud_layer_norm(e, o, Bn("feed_forward.output_dense"), S, H, c.ln_eps, Wn("final_layer_norm"),
                               Bn("final_layer_norm"), false, e, st),
                "layer norm") ||
             !K(aud_copy_cols(e, S, H, stk, L * H, l * H, st), "stack"))
             return -1;
     }
-    // projection of all layer outputs: Linear + LayerNorm(1e-5) + SiLU
-    if (!a->gemm(stk, S, L * H, L * H, a->W("audio_projection.0.weight"), c.dim_w, y, c.dim_w, "projection") ||
-        !K(aud_bias_act(y, a->W("audio_projection.0.bias"), S, c.dim_w, 1.0f, false, st), "bias") ||
+    // projection of all layer outputs: Linear (+ bias) + LayerNorm(1e-5) + SiLU
+    if (!a->gemm(stk, S, L * H, L * H, a->W("audio_projection.0.weight"), L * H, c.dim_w, y, c.dim_w, "projection",
+                 a->W("audio_projection.0.bias")) ||
         !K(aud_layer_norm(y, nullptr, nullptr, S, c.dim_w, 1e-5f, a->W("audio_projection.1.weight"),
                           a->W("audio_projection.1.bias"), true, y, st),
            "layer norm") ||
         !K(cudaMemcpyAsync(wa, y, (size_t) S * c.dim_w * 4, cudaMemcpyDeviceToHost, st), "wa D2H") ||
-        !K(cudaStreamSynchronize(st), "audio encode"))
+        !K(cudaStreamSynchronize(st), "audio encode") || !a->gemm_status())
         return -1;
     return 0;
 }

@@ -1,12 +1,15 @@
 // Flow-matching sampler C ABI (include/tpfm.h): fmt_model::forward
 // (src/fmt.cpp:64-211) and sample_chunk_ex (src/pipeline.cpp:15-91). The
-// plain linears are cuBLAS GEMMs (row-major Y[M][N] = X[M][K] W[N][K]^T, no
-// bias). The adaLN modulations of all blocks and of the final layer depend
-// only on the conditioning, so one GEMM per forward computes them together
-// (their weights are contiguous in the arena). Norms, banded attention,
-// activations, gated residuals and the CFG/Euler update are the kernels of
-// kernels_fmt.cu. A chunk's nine forwards run as one captured CUDA graph.
-#include <cublas_v2.h>
+// plain linears run on the library's tcgen05 GEMM (kernels_gemm_tc.cu;
+// row-major Y[M][N] = X[M][K] W[N][K]^T): f16 operands in the f16 mode, the
+// three-pass TF32 split in the f32 mode. The MLP's first linear adds its
+// bias and applies GELU in the GEMM epilogue; the other GEMMs run without
+// bias and the kernel consuming their output adds it. The adaLN
+// modulations of all blocks and of the final layer depend only on the
+// conditioning, so one GEMM per forward computes them together (their
+// weights are contiguous in the arena). Norms, banded attention, gated
+// residuals and the CFG/Euler update are the kernels of kernels_fmt.cu. A
+// chunk's nine forwards run as one captured CUDA graph.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -31,7 +34,6 @@ cudaError_t fmt_norm_mod(bool f16, float *x, int M, int H, float eps, const floa
                          int T = 0);
 cudaError_t fmt_attn(bool f16, const float *qkv, const float *bqkv, int T, int H, int nh, int window, void *out,
                      cudaStream_t st);
-cudaError_t fmt_gelu(bool f16, const float *a, const float *b, int M, int N, void *y, cudaStream_t st);
 cudaError_t fmt_res_norm(bool f16, float *x, const float *o, const float *bo, const float *mod, const float *bmod,
                          int mod_stride, int gate_off, int M, int H, float eps, const float *mod2, const float *bmod2,
                          int shift_off, int scale_off, void *h, cudaStream_t st);
@@ -54,21 +56,21 @@ struct tpfm_ctx {
     int device = 0;
     bool f16 = false;
     tpfm_config c{};
-    int T = 0, M = 0, CD = 0, FF = 0, H = 0;
+    int T = 0, M = 0, CD = 0, CDp = 0, FF = 0, H = 0;  // CDp: CD padded to 8 (GEMM row strides)
     int nmod = 0;  // adaLN columns of all blocks + the final layer
     std::string err;
     std::map<std::string, int64_t> spec;
     std::map<std::string, std::vector<float>> host;
     std::map<std::string, size_t> off32, off16;
+    std::map<std::string, int> kdim, ldk;  // linear weights: K, and the row stride (K padded to 8)
     float *w32 = nullptr;
     __half *w16 = nullptr;
     bool wready = false;
     cudaStream_t stream = nullptr;
-    cublasHandle_t blas = nullptr;
-    void *blas_ws = nullptr;
     void *act = nullptr;
+    int *gerr = nullptr;  // the GEMMs' error flag
     float *x60 = nullptr, *cond = nullptr, *clin = nullptr, *te0 = nullptr, *te = nullptr, *x1 = nullptr,
-          *x = nullptr, *mod = nullptr, *qkv = nullptr, *o = nullptr, *m1raw = nullptr,
+          *x = nullptr, *mod = nullptr, *qkv = nullptr, *o = nullptr,
           *vout = nullptr, *v = nullptr, *xc = nullptr, *tf = nullptr,
           *te_all = nullptr;  // timestep embedding of every sampler step (prepare)
     void *sc = nullptr, *h = nullptr, *att = nullptr, *m1 = nullptr, *cond_in = nullptr, *x60_in = nullptr;
@@ -84,34 +86,48 @@ struct tpfm_ctx {
         cudaGetLastError();
         return false;
     }
-    bool bk(cublasStatus_t s, const char *what) {
-        if (s == CUBLAS_STATUS_SUCCESS) return true;
-        err = std::string(what) + ": cuBLAS status " + std::to_string((int) s);
-        return false;
-    }
     const float *F(const std::string &n) const { return w32 + off32.at(n); }
     const void *Wt(const std::string &n) const {
         return f16 ? (const void *) (w16 + off16.at(n)) : (const void *) F(n);
     }
-    // Y[M][N] (f32) = X[M][K] (GEMM input type) W[N][K]^T
-    bool gemm_w(const void *X, int Mr, int K, const void *W, int N, float *Y, const char *what) {
-        const float one = 1.0f, zero = 0.0f;
-        const cudaDataType_t t = f16 ? CUDA_R_16F : CUDA_R_32F;
-        return bk(cublasGemmEx(blas, CUBLAS_OP_T, CUBLAS_OP_N, N, Mr, K, &one, W, t, K, X, t, K, &zero, Y,
-                               CUDA_R_32F, N, f16 ? CUBLAS_COMPUTE_32F : CUBLAS_COMPUTE_32F_PEDANTIC,
-                               CUBLAS_GEMM_DEFAULT),
-                  what);
+    // Y[M][N] (f32, or f16 into Yh) = epi(X[M][K] (GEMM input type) W[N][K]^T)
+    // with row strides ldx, ldw; epi adds bias and applies act (gemm_desc)
+    bool gemm_w(const void *X, int Mr, int K, int ldx, const void *W, int ldw, int N, float *Y, const char *what,
+                const float *bias = nullptr, int act = 0, __half *Yh = nullptr) {
+        gemm_desc d;
+        d.f32 = !f16;
+        d.X = X;
+        d.ldx = ldx;
+        d.W = W;
+        d.ldw = ldw;
+        d.Y = Yh ? nullptr : Y;
+        d.Yh = Yh;
+        d.ldy = N;
+        d.M = Mr;
+        d.N = N;
+        d.K = K;
+        d.bias = bias;
+        d.act = act;
+        d.err = gerr;
+        return ck(gemm_tc(d, stream), what);
     }
     bool gemm(const void *X, int Mr, int K, const std::string &wname, int N, float *Y) {
-        return gemm_w(X, Mr, K, Wt(wname), N, Y, wname.c_str());
+        return gemm_w(X, Mr, K, K, Wt(wname), ldk.at(wname), N, Y, wname.c_str());
+    }
+    // after a synchronize: a GEMM whose pipeline wait expired
+    bool gemm_status() {
+        int flag = 0;
+        if (!ck(cudaMemcpy(&flag, gerr, sizeof flag, cudaMemcpyDeviceToHost), "GEMM status")) return false;
+        if (!flag) return true;
+        cudaMemset(gerr, 0, sizeof(int));
+        return fail("a GEMM pipeline wait timed out");
     }
     // the first adaLN weight: all depth + 1 of them are contiguous from here
     const void *adaln_w() const { return Wt("blocks.0.adaLN_modulation.1.weight"); }
     ~tpfm_ctx() {
         if (device >= 0) cudaSetDevice(device);
         if (graph) cudaGraphExecDestroy(graph);
-        if (blas) cublasDestroy(blas);
-        if (blas_ws) cudaFree(blas_ws);
+        if (gerr) cudaFree(gerr);
         if (act) cudaFree(act);
         if (w32) cudaFree(w32);
         if (w16) cudaFree(w16);
@@ -126,6 +142,8 @@ void build_spec(tpfm_ctx *c) {
     auto lin = [&](const std::string &n, int64_t out, int64_t in) {
         c->spec[n + ".weight"] = out * in;
         c->spec[n + ".bias"] = out;
+        c->kdim[n + ".weight"] = (int) in;
+        c->ldk[n + ".weight"] = (int) ((in + 7) & ~(int64_t) 7);
     };
     lin("t_embedder.mlp.0", H, c->c.t_freq_dim);
     lin("t_embedder.mlp.2", H, H);
@@ -144,7 +162,7 @@ void build_spec(tpfm_ctx *c) {
     lin("decoder.linear", c->c.dim_w, H);
 }
 
-// the weights that go through cuBLAS (kept f16 in f16 mode)
+// the weights that go through the GEMM (kept f16 in f16 mode)
 bool is_gemm_weight(const std::string &n) {
     const size_t k = n.size();
     return k > 7 && n.compare(k - 7, 7, ".weight") == 0 && n.rfind("t_embedder.", 0) != 0;
@@ -184,7 +202,7 @@ bool forward_device(tpfm_ctx *c, int s, bool in_chunk = false) {
     }
     const int NM = c->nmod;
     if (!c->gemm(x60_in, T, c->c.dim_w, "x_embedder.proj.weight", H, c->x1) ||
-        !c->gemm_w(c->sc, M, H, c->adaln_w(), NM, c->mod, "adaLN modulation"))
+        !c->gemm_w(c->sc, M, H, H, c->adaln_w(), H, NM, c->mod, "adaLN modulation"))
         return false;
     // each gated residual runs fused with the layer norm after it; the first
     // block's attention norm forms the embedded rows (x1 + bias + pos, three
@@ -210,8 +228,10 @@ bool forward_device(tpfm_ctx *c, int s, bool in_chunk = false) {
             !K(fmt_res_norm(h16, c->x, c->o, c->F(b + "attn.proj.bias"), md, bmod, NM, 2 * H, M, H, eps, md, bmod,
                             3 * H, 4 * H, c->h, st),
                "residual + norm") ||
-            !c->gemm(c->h, M, H, b + "mlp.fc1.weight", FF, c->m1raw) ||
-            !K(fmt_gelu(h16, c->m1raw, c->F(b + "mlp.fc1.bias"), M, FF, c->m1, st), "gelu") ||
+            // m1 = gelu_tanh(h fc1^T + bias), in the GEMM input type
+            !c->gemm_w(c->h, M, H, H, c->Wt(b + "mlp.fc1.weight"), c->ldk.at(b + "mlp.fc1.weight"), FF,
+                       h16 ? nullptr : (float *) c->m1, "mlp.fc1", c->F(b + "mlp.fc1.bias"), 2,
+                       h16 ? (__half *) c->m1 : nullptr) ||
             !c->gemm(c->m1, M, FF, b + "mlp.fc2.weight", H, c->o) ||
             !K(fmt_res_norm(h16, c->x, c->o, c->F(b + "mlp.fc2.bias"), md, bmod, NM, 5 * H, M, H, eps, md2, bmod2, 0,
                             H, c->h, st),
@@ -225,11 +245,12 @@ bool forward_device(tpfm_ctx *c, int s, bool in_chunk = false) {
 bool embed_cond(tpfm_ctx *c) {
     const void *in = c->cond;
     if (c->f16) {
-        if (!c->ck(fmt_to_half(c->cond, (int64_t) c->M * c->CD, (__half *) c->cond_in, c->stream), "cond f16"))
+        if (!c->ck(fmt_to_half(c->cond, (int64_t) c->M * c->CDp, (__half *) c->cond_in, c->stream), "cond f16"))
             return false;
         in = c->cond_in;
     }
-    return c->gemm(in, c->M, c->CD, "c_embedder.weight", c->H, c->clin);
+    return c->gemm_w(in, c->M, c->CD, c->CDp, c->Wt("c_embedder.weight"), c->ldk.at("c_embedder.weight"), c->H,
+                     c->clin, "c_embedder");
 }
 
 bool ready(tpfm_ctx *c) {
@@ -255,7 +276,7 @@ tpfm_ctx *tpfm_create(int device, int dtype, const tpfm_config *cfg) {
     if (cfg->dim_h <= 0 || cfg->n_heads <= 0 || cfg->dim_h % cfg->n_heads || cfg->depth <= 0 || cfg->nfe < 2 ||
         cfg->chunk_frames <= 0 || cfg->prev_frames < 0 || cfg->attn_window < 0 || 2 * cfg->attn_window + 1 > 16 ||
         cfg->t_freq_dim < 2 || cfg->t_freq_dim % 2 || cfg->dim_w <= 0 || cfg->dim_a < 0 || cfg->dim_e < 0 ||
-        cfg->mlp_ratio <= 0.0f) {
+        cfg->mlp_ratio <= 0.0f || cfg->dim_h % 8 || cfg->dim_w % 8 || (int) (cfg->dim_h * cfg->mlp_ratio) % 8) {
         g_create_err = "tpfm_create: invalid config";
         return nullptr;
     }
@@ -278,14 +299,15 @@ tpfm_ctx *tpfm_create(int device, int dtype, const tpfm_config *cfg) {
     c->T = cfg->chunk_frames + cfg->prev_frames;
     c->M = 3 * c->T;
     c->CD = cfg->dim_w + cfg->dim_a + cfg->dim_e;
+    c->CDp = (c->CD + 7) & ~7;
     c->FF = (int) (cfg->dim_h * cfg->mlp_ratio);
     c->nmod = cfg->depth * 6 * cfg->dim_h + 2 * cfg->dim_h;
     build_spec(c);
     // activations
-    const size_t H = c->H, T = c->T, M = c->M, D = cfg->dim_w, FF = c->FF, CD = c->CD;
+    const size_t H = c->H, T = c->T, M = c->M, D = cfg->dim_w, FF = c->FF, CD = c->CDp;
     const size_t es = c->f16 ? 2 : 4;
     size_t sizes[] = {T * D * 4, M * CD * 4, M * H * 4, H * 4, H * 4, T * H * 4, M * H * 4, M * (size_t) c->nmod * 4,
-                      M * 3 * H * 4, M * H * 4, M * FF * 4, M * D * 4, M * D * 4,
+                      M * 3 * H * 4, M * H * 4, M * D * 4, M * D * 4,
                       (size_t) cfg->chunk_frames * D * 4, (size_t) (cfg->nfe) * cfg->t_freq_dim * 4,
                       (size_t) cfg->nfe * H * 4,
                       M * H * es, M * H * es, M * H * es, M * FF * es, M * CD * es, T * D * es};
@@ -298,10 +320,10 @@ tpfm_ctx *tpfm_create(int device, int dtype, const tpfm_config *cfg) {
     bool ok = c->ck(cudaSetDevice(device), "cudaSetDevice") &&
               c->ck(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking), "stream") &&
               c->ck(cudaMalloc(&c->act, total), "cudaMalloc(fmt activations)") &&
-              c->ck(cudaMalloc(&c->blas_ws, (size_t) 32 << 20), "cudaMalloc(cuBLAS workspace)") &&
-              c->bk(cublasCreate(&c->blas), "cublasCreate") && c->bk(cublasSetStream(c->blas, c->stream), "stream") &&
-              c->bk(cublasSetWorkspace(c->blas, c->blas_ws, (size_t) 32 << 20), "workspace") &&
-              c->bk(cublasSetMathMode(c->blas, c->f16 ? CUBLAS_DEFAULT_MATH : CUBLAS_PEDANTIC_MATH), "math mode");
+              c->ck(cudaMemset(c->act, 0, total), "cudaMemset(fmt activations)") &&
+              c->ck(cudaMalloc(&c->gerr, sizeof(int)), "cudaMalloc(GEMM flag)") &&
+              c->ck(cudaMemset(c->gerr, 0, sizeof(int)), "cudaMemset(GEMM flag)") &&
+              c->ck(gemm_tc_prepare(), "GEMM set-up");
     if (!ok) {
         g_create_err = c->err;
         delete c;
@@ -310,7 +332,7 @@ tpfm_ctx *tpfm_create(int device, int dtype, const tpfm_config *cfg) {
     char *b = (char *) c->act;
     int i = 0;
     float **fl[] = {&c->x60, &c->cond, &c->clin, &c->te0, &c->te, &c->x1, &c->x, &c->mod, &c->qkv, &c->o,
-                    &c->m1raw, &c->vout, &c->v, &c->xc, &c->tf, &c->te_all};
+                    &c->vout, &c->v, &c->xc, &c->tf, &c->te_all};
     for (float **p : fl) *p = (float *) (b + offs[i++]);
     void **vp[] = {&c->sc, &c->h, &c->att, &c->m1, &c->cond_in, &c->x60_in};
     for (void **p : vp) *p = b + offs[i++];
@@ -418,9 +440,14 @@ int tpfm_prepare(tpfm_ctx *c) {
     for (auto &kv : c->spec)
         if (std::find(order.begin(), order.end(), kv.first) == order.end()) order.push_back(kv.first);
     const size_t n_adaln = (size_t) c->c.depth + 1;
+    // GEMM weights are stored with rows padded to ldk (16-byte row strides)
+    auto padded = [&](const std::string &n) { return is_gemm_weight(n) && c->ldk.at(n) != c->kdim.at(n); };
+    auto stored = [&](const std::string &n) {
+        return padded(n) ? (size_t) (c->spec.at(n) / c->kdim.at(n)) * c->ldk.at(n) : (size_t) c->spec.at(n);
+    };
     for (size_t i = 0; i < order.size(); i++) {
         const std::string &n = order[i];
-        const size_t sz = (size_t) c->spec.at(n);
+        const size_t sz = stored(n);
         c->off32[n] = n32;
         n32 += sz;
         if (c->f16 && is_gemm_weight(n)) {
@@ -433,7 +460,16 @@ int tpfm_prepare(tpfm_ctx *c) {
         }
     }
     std::vector<float> img(n32, 0.0f);
-    for (auto &kv : c->spec) memcpy(img.data() + c->off32[kv.first], c->host[kv.first].data(), kv.second * 4);
+    for (auto &kv : c->spec) {
+        const std::string &n = kv.first;
+        if (!padded(n)) {
+            memcpy(img.data() + c->off32[n], c->host[n].data(), kv.second * 4);
+            continue;
+        }
+        const int64_t K = c->kdim.at(n), ld = c->ldk.at(n);
+        for (int64_t r = 0; r < kv.second / K; r++)
+            memcpy(img.data() + c->off32[n] + r * ld, c->host[n].data() + r * K, K * 4);
+    }
     if (!c->ck(cudaSetDevice(c->device), "cudaSetDevice")) return -1;
     if (c->w32) cudaFree(c->w32);
     if (c->w16) cudaFree(c->w16);
@@ -449,7 +485,8 @@ int tpfm_prepare(tpfm_ctx *c) {
     if (c->f16) {
         if (!c->ck(cudaMalloc(&c->w16, n16 * 2), "cudaMalloc(fmt f16 weights)")) return -1;
         for (auto &kv : c->off16)
-            if (!c->ck(fmt_to_half(c->w32 + c->off32[kv.first], c->spec[kv.first], c->w16 + kv.second, c->stream),
+            if (!c->ck(fmt_to_half(c->w32 + c->off32[kv.first], (int64_t) stored(kv.first), c->w16 + kv.second,
+                                   c->stream),
                        "f16 weights"))
                 return -1;
         if (!c->ck(cudaStreamSynchronize(c->stream), "f16 weights")) return -1;
@@ -480,11 +517,13 @@ int tpfm_forward(tpfm_ctx *c, const float *x60, const float *cond, float t, floa
     const size_t D = c->c.dim_w;
     if (!c->ck(cudaMemcpyAsync(row, tf.data(), tf.size() * 4, cudaMemcpyHostToDevice, st), "t freq") ||
         !c->ck(cudaMemcpyAsync(c->x60, x60, (size_t) c->T * D * 4, cudaMemcpyHostToDevice, st), "x60") ||
-        !c->ck(cudaMemcpyAsync(c->cond, cond, (size_t) c->M * c->CD * 4, cudaMemcpyHostToDevice, st), "cond") ||
+        !c->ck(cudaMemcpy2DAsync(c->cond, (size_t) c->CDp * 4, cond, (size_t) c->CD * 4, (size_t) c->CD * 4,
+                                 (size_t) c->M, cudaMemcpyHostToDevice, st),
+               "cond") ||
         !embed_cond(c) || !forward_device(c, c->c.nfe - 1) ||
         !c->ck(fmt_add_bias(c->vout, c->F("decoder.linear.bias"), c->M, (int) D, c->v, st), "bias") ||
         !c->ck(cudaMemcpyAsync(v, c->v, (size_t) c->M * D * 4, cudaMemcpyDeviceToHost, st), "v D2H") ||
-        !c->ck(cudaStreamSynchronize(st), "forward"))
+        !c->ck(cudaStreamSynchronize(st), "forward") || !c->gemm_status())
         return -1;
     return 0;
 }
@@ -495,7 +534,8 @@ int tpfm_sample_chunk(tpfm_ctx *c, const float *wr, const float *prev_wa, const 
     if (!wr || !cond_audio || !x0 || !motion || (c->c.prev_frames > 0 && (!prev_wa || !prev_x)))
         return c->fail("tpfm_sample_chunk: null argument"), -1;
     if (!ready(c)) return -1;
-    const int T = c->T, P = c->c.prev_frames, CF = c->c.chunk_frames, D = c->c.dim_w, CD = c->CD;
+    // rows of CDp floats (the GEMM's padded row stride), padding zero
+    const int T = c->T, P = c->c.prev_frames, CF = c->c.chunk_frames, D = c->c.dim_w, CD = c->CDp;
     // condition rows [wr | wa | we] per branch: uncond nulls the current
     // frames' wa and we, audio-only nulls we; prev_wa rows stay in all
     std::vector<float> cond((size_t) 3 * T * CD, 0.0f);
@@ -539,7 +579,7 @@ int tpfm_sample_chunk(tpfm_ctx *c, const float *wr, const float *prev_wa, const 
     }
     if (!c->ck(cudaGraphLaunch(c->graph, st), "graph launch") ||
         !c->ck(cudaMemcpyAsync(motion, c->xc, (size_t) CF * D * 4, cudaMemcpyDeviceToHost, st), "motion D2H") ||
-        !c->ck(cudaStreamSynchronize(st), "sample chunk"))
+        !c->ck(cudaStreamSynchronize(st), "sample chunk") || !c->gemm_status())
         return -1;
     return 0;
 }

@@ -123,6 +123,34 @@ cudaError_t launch_chw_to_rgb24(const float *chw, int64_t n, int64_t hw, uint8_t
 // the last-error slot of the tpk_* entry points (sets it, returns -1)
 int tpk_fail(const std::string &msg);
 
+// The tcgen05 GEMM of the sampler and the audio encoder (kernels_gemm_tc.cu):
+//   Y[m][n] = act((sum_k X[m][k] W[n][k] + bias[n]) * scale), m < M, n < N
+// X and W K-major with row strides ldx, ldw (elements, 16-byte multiples);
+// f32 operands by the three-pass TF32 split, else f16. Batch b (grid z)
+// reads X at row b*x_row_b, column b*x_col_b (W likewise) and writes Y (or
+// Yh, f16) at b*y_batch. Grids with fewer tiles than SMs split K over a
+// thread-block cluster per tile.
+struct gemm_desc {
+    bool f32 = true;
+    const void *X = nullptr;
+    int64_t ldx = 0;
+    const void *W = nullptr;
+    int64_t ldw = 0;
+    float *Y = nullptr;
+    __half *Yh = nullptr;
+    int64_t ldy = 0, y_batch = 0;
+    int M = 0, N = 0, K = 0, batch = 1;
+    int x_row_b = 0, x_col_b = 0, w_row_b = 0, w_col_b = 0;
+    const float *bias = nullptr;
+    float scale = 1.0f;
+    int act = 0;  // 0 none, 1 GELU (erf), 2 GELU (tanh)
+    int *err = nullptr;  // set when a bounded wait expires
+};
+cudaError_t gemm_tc(const gemm_desc &d, cudaStream_t st);
+// the GEMM kernels' shared-memory attribute on the current device (before a
+// stream capture that launches them)
+cudaError_t gemm_tc_prepare();
+
 // tcgen05 path (f16)
 cudaError_t launch_conv_tc(bool up, const conv_params &p, cudaStream_t st);
 bool conv_tc_supported(bool up, int IC, int OC);

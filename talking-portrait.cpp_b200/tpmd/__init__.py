@@ -51,7 +51,7 @@ EXPORTS = ("tpmd_abi_version", "tpmd_create", "tpmd_create_error", "tpmd_destroy
            "tpmd_group_member", "tpmd_group_set_tensor", "tpmd_group_load_gguf", "tpmd_group_prepare",
            "tpmd_group_set_feats", "tpmd_group_set_feats_device", "tpmd_shard_range", "tpmd_group_decode",
            "tpmd_group_max", "tpmd_group_selftest_nccl", "tpmd_decode_rgb24", "tpmd_group_decode_rgb24",
-           "tpk_chw_to_rgb24")
+           "tpk_chw_to_rgb24", "tpk_gemm")
 
 _lib = None
 
@@ -117,6 +117,8 @@ def load_library(path: str = LIB_PATH):
     L.tpmd_decode_rgb24.argtypes = [v, v, i64, v]
     L.tpmd_group_decode_rgb24.argtypes = [v, v, i64, v]
     L.tpk_chw_to_rgb24.argtypes = [v, i64, C.c_int, C.c_int, v, v]
+    L.tpk_gemm.argtypes = [v, i64, v, i64, v, i64, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                           C.c_int, C.c_int, i64, C.c_int, v, C.c_float, C.c_int, v]
     L.tpmd_group_selftest_nccl.argtypes = [C.c_int, C.c_int, C.c_double, C.POINTER(C.c_int), C.c_char_p,
                                            C.c_size_t]
     L.tpmd_debug_expire_wait.argtypes = [v, C.c_longlong]
@@ -423,6 +425,20 @@ def chw_to_rgb24(chw, rgb, stream=0):
     n, _, h, w = chw.shape
     _tpk_check(load_library().tpk_chw_to_rgb24(C.c_void_p(chw.data_ptr()), n, h, w,
                                                C.c_void_p(rgb.data_ptr()), C.c_void_p(stream)))
+
+
+def gemm(X, W, Y, M, N, K, ldx=None, ldw=None, ldy=None, batch=1, x_row_b=0, x_col_b=0, w_row_b=0, w_col_b=0,
+         y_batch=0, bias=None, scale=1.0, act=0, stream=0):
+    """The library's tcgen05 GEMM on torch CUDA tensors (see tpk_gemm in
+    include/tpmd.h): Y = act((X . W^T + bias) * scale), f32 operands by the
+    three-pass TF32 split, f16 operands on f16 tensors"""
+    import torch
+    dt = DTYPE_F16 if X.dtype == torch.float16 else DTYPE_F32
+    _tpk_check(load_library().tpk_gemm(
+        C.c_void_p(X.data_ptr()), ldx or X.shape[-1], C.c_void_p(W.data_ptr()), ldw or W.shape[-1],
+        C.c_void_p(Y.data_ptr()), ldy or Y.shape[-1], M, N, K, batch, x_row_b, x_col_b, w_row_b, w_col_b, y_batch,
+        dt, C.c_void_p(bias.data_ptr() if bias is not None else None), scale, act, C.c_void_p(stream)))
+    return Y
 
 
 def im2col_cf(src, IC, IW, IH, N, out, KW=3, KH=3, s0=1, s1=1, p0=1, p1=1, d0=1, d1=1,
