@@ -45,7 +45,6 @@ def build(verbose: bool = False) -> str:
     with cf.ThreadPoolExecutor(max_workers=os.cpu_count() or 4) as ex:
         objs = list(ex.map(_compile, srcs))
     if not os.path.exists(SO) or os.path.getmtime(SO) < max(os.path.getmtime(o) for o in objs):
-        # cuBLAS (dynamic, from the CUDA toolkit) serves the FMT sampler's plain linears
         cmd = [NVCC] + ARCH + ["-shared", "-cudart", "static", "-o", SO] + objs + \
               ["-lpthread", "-ldl", "-Xlinker", "-rpath=/usr/local/cuda/lib64"]
         subprocess.run(cmd, check=True)

@@ -10,6 +10,7 @@ namespace {
 
 __device__ __forceinline__ float gelu_erf(float v) { return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f)); }
 __device__ __forceinline__ float silu(float v) { return v / (1.0f + expf(-v)); }
+constexpr int AUD_STAT_BLOCKS = 256;
 inline int grid_for(int64_t n) { return (int) std::min<int64_t>((n + 255) / 256, 148 * 16); }
 
 // out[g][t][c*K + k] = x[t*s + k - p][c_off + g*C + c] (zero outside), the
@@ -51,48 +52,58 @@ __global__ void transpose_kernel(const float *__restrict__ src, int64_t S, int l
     }
 }
 
-// per channel of x [T][C]: mean and 1/sqrt(var + eps) over time (double
-// accumulation); one block per channel
-__global__ void __launch_bounds__(256) chan_stats_kernel(const float *__restrict__ x, int64_t T, int C, float eps,
-                                                         float *__restrict__ mean, float *__restrict__ inv) {
-    __shared__ double red[8];
-    const int c = blockIdx.x;
-    double s = 0.0;
-    for (int64_t t = threadIdx.x; t < T; t += blockDim.x) s += x[t * C + c];
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
-    __syncthreads();
-    double m = 0.0;
-    for (int i = 0; i < 8; i++) m += red[i];
-    m /= (double) T;
-    __syncthreads();
-    double q = 0.0;
-    for (int64_t t = threadIdx.x; t < T; t += blockDim.x) {
-        const double d = x[t * C + c] - m;
-        q += d * d;
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = q;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        double v = 0.0;
-        for (int i = 0; i < 8; i++) v += red[i];
-        v /= (double) T;
-        mean[c] = (float) m;
-        inv[c] = (float) (1.0 / sqrt(v + (double) eps));
+// per channel of x [T][C], over the rows of block b's chunk: (sum, sum of
+// squares) in double into part[b][c]; threads along C (coalesced rows)
+__global__ void __launch_bounds__(256) chan_partial_kernel(const float *__restrict__ x, int64_t T, int C,
+                                                           int64_t rows_per, double2 *__restrict__ part) {
+    const int64_t t0 = (int64_t) blockIdx.x * rows_per, t1 = min(T, t0 + rows_per);
+    for (int c = threadIdx.x; c < C; c += blockDim.x) {
+        double s = 0.0, q = 0.0;
+#pragma unroll 4
+        for (int64_t t = t0; t < t1; t++) {
+            const double v = x[t * C + c];
+            s += v;
+            q = fma(v, v, q);
+        }
+        part[(int64_t) blockIdx.x * C + c] = make_double2(s, q);
     }
 }
 
+// per channel: the partials added in block order -> mean and
+// 1/sqrt(var + eps), var = E[x^2] - mean^2 (double)
+__global__ void chan_finalize_kernel(const double2 *__restrict__ part, int nb, int64_t T, int C, float eps,
+                                     float *__restrict__ mean, float *__restrict__ inv) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= C) return;
+    double s = 0.0, q = 0.0;
+    for (int i = 0; i < nb; i++) {
+        const double2 p = part[(int64_t) i * C + c];
+        s += p.x;
+        q += p.y;
+    }
+    const double m = s / (double) T;
+    const double v = fmax(q / (double) T - m * m, 0.0);
+    mean[c] = (float) m;
+    inv[c] = (float) (1.0 / sqrt(v + (double) eps));
+}
+
 // x = gelu((x - mean[c]) * inv[c] * w[c] + b[c])  (GroupNorm, one group per channel)
+// (C a multiple of 4: rows of float4, blocks over rows)
 __global__ void chan_norm_gelu_kernel(float *__restrict__ x, int64_t T, int C, const float *__restrict__ mean,
                                       const float *__restrict__ inv, const float *__restrict__ w,
                                       const float *__restrict__ b) {
-    const int64_t n = T * C;
-    for (int64_t e = (int64_t) blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t) gridDim.x * blockDim.x) {
-        const int c = (int) (e % C);
-        x[e] = gelu_erf((x[e] - mean[c]) * inv[c] * __ldg(w + c) + __ldg(b + c));
+    const int C4 = C >> 2;
+    for (int64_t t = blockIdx.x; t < T; t += gridDim.x) {
+        float4 *r = (float4 *) (x + t * C);
+        for (int c4 = threadIdx.x; c4 < C4; c4 += blockDim.x) {
+            float4 v = r[c4];
+            const int c = 4 * c4;
+            v.x = gelu_erf((v.x - mean[c]) * inv[c] * __ldg(w + c) + __ldg(b + c));
+            v.y = gelu_erf((v.y - mean[c + 1]) * inv[c + 1] * __ldg(w + c + 1) + __ldg(b + c + 1));
+            v.z = gelu_erf((v.z - mean[c + 2]) * inv[c + 2] * __ldg(w + c + 2) + __ldg(b + c + 2));
+            v.w = gelu_erf((v.w - mean[c + 3]) * inv[c + 3] * __ldg(w + c + 3) + __ldg(b + c + 3));
+            r[c4] = v;
+        }
     }
 }
 
@@ -219,8 +230,14 @@ cudaError_t aud_transpose(const float *src, int64_t S, int lds, int C, float *ds
 }
 cudaError_t aud_group_norm_gelu(float *x, int64_t T, int C, float eps, const float *w, const float *b, float *stats,
                                 cudaStream_t st) {
-    chan_stats_kernel<<<C, 256, 0, st>>>(x, T, C, eps, stats, stats + C);
-    chan_norm_gelu_kernel<<<grid_for(T * C), 256, 0, st>>>(x, T, C, stats, stats + C, w, b);
+    // stats: mean [C], inv [C], then AUD_STAT_BLOCKS x C partials (double2)
+    if (C % 4) return cudaErrorInvalidValue;
+    double2 *part = (double2 *) (stats + 2 * (int64_t) ((C + 1) & ~1));
+    const int64_t rows_per = (T + AUD_STAT_BLOCKS - 1) / AUD_STAT_BLOCKS;
+    const int nb = (int) ((T + rows_per - 1) / rows_per);
+    chan_partial_kernel<<<nb, 256, 0, st>>>(x, T, C, rows_per, part);
+    chan_finalize_kernel<<<(C + 127) / 128, 128, 0, st>>>(part, nb, T, C, eps, stats, stats + C);
+    chan_norm_gelu_kernel<<<(unsigned) std::min<int64_t>(T, 148 * 16), 128, 0, st>>>(x, T, C, stats, stats + C, w, b);
     return cudaGetLastError();
 }
 cudaError_t aud_interp(const float *x, int64_t T, int C, int64_t S, float *y, cudaStream_t st) {

@@ -38,6 +38,8 @@ __device__ __forceinline__ float block_sum(float v, float *red) {
 __global__ void __launch_bounds__(256) gemv_kernel(const float *__restrict__ W, const float *__restrict__ x,
                                                    const float *__restrict__ b, int N, int K, int act_silu,
                                                    float *__restrict__ y) {
+    pdl_wait();
+    pdl_trigger();
     const int lane = threadIdx.x & 31, n = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     if (n >= N) return;
     float a = 0.0f;
@@ -54,6 +56,8 @@ __global__ void __launch_bounds__(256) gemv_kernel(const float *__restrict__ W, 
 template <typename TIN>
 __global__ void cond_silu_kernel(const float *__restrict__ clin, const float *__restrict__ bc,
                                  const float *__restrict__ te, int M, int H, TIN *__restrict__ sc) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t n = (int64_t) M * H;
     for (int64_t e = (int64_t) blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t) gridDim.x * blockDim.x) {
         const int i = (int) (e % H);
@@ -72,6 +76,8 @@ __global__ void __launch_bounds__(256) norm_mod_kernel(float *__restrict__ x, in
                                                        int shift_off, int scale_off, TIN *__restrict__ h,
                                                        const float *__restrict__ x1, const float *__restrict__ bx,
                                                        const float *__restrict__ pos, int T) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ float red[32];
     const int m = blockIdx.x;
     float *r = x + (int64_t) m * H;
@@ -102,39 +108,62 @@ __global__ void __launch_bounds__(256) norm_mod_kernel(float *__restrict__ x, in
 // banded self-attention per (branch, head, query row i): keys j with
 // |i - j| <= window (the additive -inf mask elsewhere contributes nothing),
 // scores q.k / sqrt(hd), softmax, weighted sum of v. One warp per query;
-// qkv = GEMM output + bias, row m = [q | k | v] of width 3H.
-template <typename TIN>
+// qkv = GEMM output + bias, row m = [q | k | v] of width 3H. Every q, k and
+// v element the warp needs is loaded up front (EPL per lane and row, MAXJ
+// keys at most), so the band costs one memory round trip.
+template <typename TIN, int EPL, int MAXJ>
 __global__ void __launch_bounds__(256) attn_kernel(const float *__restrict__ qkv, const float *__restrict__ bqkv,
                                                    int T, int H, int nh, int window, TIN *__restrict__ out) {
+    pdl_wait();
+    pdl_trigger();
     const int lane = threadIdx.x & 31;
     const int g = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int hd = H / nh;
     if (g >= 3 * nh * T) return;
     const int i = g % T, head = (g / T) % nh, b = g / (T * nh);
-    const int j0 = max(0, i - window), j1 = min(T, i + window + 1);
+    const int j0 = max(0, i - window), j1 = min(T, i + window + 1), nj = j1 - j0;
     const float scale = 1.0f / sqrtf((float) hd);
-    const float *qrow = qkv + ((int64_t) b * T + i) * 3 * H + head * hd;
-    float sc[16];
+    const float *base = qkv + (int64_t) b * T * 3 * H + head * hd;
+    float q[EPL], k[MAXJ][EPL], v[MAXJ][EPL];
+#pragma unroll
+    for (int e = 0; e < EPL; e++) {
+        const int d = lane + 32 * e;
+        q[e] = d < hd ? base[(int64_t) i * 3 * H + d] + __ldg(bqkv + head * hd + d) : 0.0f;
+    }
+#pragma unroll
+    for (int jj = 0; jj < MAXJ; jj++)
+#pragma unroll
+        for (int e = 0; e < EPL; e++) {
+            const int d = lane + 32 * e;
+            const bool in = jj < nj && d < hd;
+            const float *row = base + (int64_t) (j0 + jj) * 3 * H;
+            k[jj][e] = in ? row[H + d] + __ldg(bqkv + H + head * hd + d) : 0.0f;
+            v[jj][e] = in ? row[2 * H + d] + __ldg(bqkv + 2 * H + head * hd + d) : 0.0f;
+        }
+    float sc[MAXJ];
     float mx = -INFINITY;
-    for (int j = j0; j < j1; j++) {
-        const float *krow = qkv + ((int64_t) b * T + j) * 3 * H + H + head * hd;
+#pragma unroll
+    for (int jj = 0; jj < MAXJ; jj++) {
         float a = 0.0f;
-        for (int d = lane; d < hd; d += 32)
-            a = fmaf(qrow[d] + __ldg(bqkv + head * hd + d), krow[d] + __ldg(bqkv + H + head * hd + d), a);
+#pragma unroll
+        for (int e = 0; e < EPL; e++) a = fmaf(q[e], k[jj][e], a);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-        sc[j - j0] = a * scale;
-        mx = fmaxf(mx, sc[j - j0]);
+        sc[jj] = a * scale;
+        if (jj < nj) mx = fmaxf(mx, sc[jj]);
     }
     float sum = 0.0f;
-    for (int j = j0; j < j1; j++) sum += (sc[j - j0] = expf(sc[j - j0] - mx));
-    for (int d = lane; d < hd; d += 32) {
+#pragma unroll
+    for (int jj = 0; jj < MAXJ; jj++)
+        if (jj < nj) sum += (sc[jj] = expf(sc[jj] - mx));
+#pragma unroll
+    for (int e = 0; e < EPL; e++) {
+        const int d = lane + 32 * e;
         float a = 0.0f;
-        for (int j = j0; j < j1; j++)
-            a = fmaf(sc[j - j0] / sum, qkv[((int64_t) b * T + j) * 3 * H + 2 * H + head * hd + d] +
-                                           __ldg(bqkv + 2 * H + head * hd + d),
-                     a);
-        out[((int64_t) b * T + i) * H + head * hd + d] = cvt<TIN>(a);
+#pragma unroll
+        for (int jj = 0; jj < MAXJ; jj++)
+            if (jj < nj) a = fmaf(sc[jj] / sum, v[jj][e], a);
+        if (d < hd) out[((int64_t) b * T + i) * H + head * hd + d] = cvt<TIN>(a);
     }
 }
 
@@ -151,17 +180,24 @@ __global__ void __launch_bounds__(256) res_norm_kernel(float *__restrict__ x, co
                                                        int H, float eps, const float *__restrict__ mod2,
                                                        const float *__restrict__ bmod2, int shift_off, int scale_off,
                                                        TIN *__restrict__ h) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ float red[32];
     const int m = blockIdx.x;
     float *r = x + (int64_t) m * H;
     const float *orow = o + (int64_t) m * H;
     const float *md = mod + (int64_t) m * mod_stride;
-    float xv[RN_PER_THREAD];
+    const float *md2 = mod2 + (int64_t) m * mod_stride;
+    float xv[RN_PER_THREAD], scv[RN_PER_THREAD], shv[RN_PER_THREAD];
     float s = 0.0f;
+    // every load up front (the next norm's modulation included): one
+    // memory round trip per row
 #pragma unroll
     for (int k = 0; k < RN_PER_THREAD; k++) {
         const int i = threadIdx.x + k * blockDim.x;
         if (i < H) {
+            scv[k] = md2[scale_off + i] + __ldg(bmod2 + scale_off + i);
+            shv[k] = md2[shift_off + i] + __ldg(bmod2 + shift_off + i);
             const float g = md[gate_off + i] + __ldg(bmod + gate_off + i);
             const float v = r[i] + g * (orow[i] + __ldg(bo + i));
             r[i] = v;
@@ -181,15 +217,12 @@ __global__ void __launch_bounds__(256) res_norm_kernel(float *__restrict__ x, co
     }
     const float var = block_sum(q, red) / (float) H;
     const float inv = 1.0f / sqrtf(var + eps);
-    const float *md2 = mod2 + (int64_t) m * mod_stride;
 #pragma unroll
     for (int k = 0; k < RN_PER_THREAD; k++) {
         const int i = threadIdx.x + k * blockDim.x;
         if (i < H) {
             const float v = (xv[k] - mean) * inv;
-            const float sc = md2[scale_off + i] + __ldg(bmod2 + scale_off + i);
-            const float sh = md2[shift_off + i] + __ldg(bmod2 + shift_off + i);
-            h[(int64_t) m * H + i] = cvt<TIN>(v * sc + v + sh);
+            h[(int64_t) m * H + i] = cvt<TIN>(v * scv[k] + v + shv[k]);
         }
     }
 }
@@ -200,6 +233,8 @@ __global__ void __launch_bounds__(256) res_norm_kernel(float *__restrict__ x, co
 __global__ void cfg_euler_kernel(const float *__restrict__ vout, const float *__restrict__ bv, int T, int P,
                                  int D, float a_cfg, float e_cfg, float dt, float *__restrict__ x,
                                  float *__restrict__ x60, __half *__restrict__ x60h) {
+    pdl_wait();
+    pdl_trigger();
     const int CF = T - P;
     const int64_t n = (int64_t) CF * D;
     const int64_t br = (int64_t) T * D;
@@ -219,12 +254,16 @@ __global__ void cfg_euler_kernel(const float *__restrict__ vout, const float *__
 // v_out = out + b (the plain forward's output)
 __global__ void add_bias_kernel(const float *__restrict__ a, const float *__restrict__ b, int M, int N,
                                 float *__restrict__ y) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t n = (int64_t) M * N;
     for (int64_t e = (int64_t) blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t) gridDim.x * blockDim.x)
         y[e] = a[e] + __ldg(b + e % N);
 }
 
 __global__ void to_half_kernel(const float *__restrict__ a, int64_t n, __half *__restrict__ y) {
+    pdl_wait();
+    pdl_trigger();
     for (int64_t e = (int64_t) blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t) gridDim.x * blockDim.x)
         y[e] = __float2half_rn(a[e]);
 }
@@ -235,64 +274,59 @@ inline int grid_for(int64_t n) { return (int) std::min<int64_t>((n + 255) / 256,
 
 cudaError_t fmt_gemv(const float *W, const float *x, const float *b, int N, int K, bool silu_act, float *y,
                      cudaStream_t st) {
-    gemv_kernel<<<(N * 32 + 255) / 256, 256, 0, st>>>(W, x, b, N, K, silu_act ? 1 : 0, y);
-    return cudaGetLastError();
+    return launch_pdl(gemv_kernel, dim3((N * 32 + 255) / 256), dim3(256), 0, st, W, x, b, N, K, silu_act ? 1 : 0, y);
 }
 cudaError_t fmt_cond_silu(bool f16, const float *clin, const float *bc, const float *te, int M, int H, void *sc,
                           cudaStream_t st) {
-    if (f16)
-        cond_silu_kernel<__half><<<grid_for((int64_t) M * H), 256, 0, st>>>(clin, bc, te, M, H, (__half *) sc);
-    else
-        cond_silu_kernel<float><<<grid_for((int64_t) M * H), 256, 0, st>>>(clin, bc, te, M, H, (float *) sc);
-    return cudaGetLastError();
+    const dim3 g(grid_for((int64_t) M * H));
+    if (f16) return launch_pdl(cond_silu_kernel<__half>, g, dim3(256), 0, st, clin, bc, te, M, H, (__half *) sc);
+    return launch_pdl(cond_silu_kernel<float>, g, dim3(256), 0, st, clin, bc, te, M, H, (float *) sc);
 }
 cudaError_t fmt_norm_mod(bool f16, float *x, int M, int H, float eps, const float *mod, const float *bmod,
                          int mod_stride, int shift_off, int scale_off, void *h, cudaStream_t st, const float *x1,
                          const float *bx, const float *pos, int T) {
     if (x1 && (!bx || !pos || T <= 0)) return cudaErrorInvalidValue;
     if (f16)
-        norm_mod_kernel<__half><<<M, 256, 0, st>>>(x, H, eps, mod, bmod, mod_stride, shift_off, scale_off,
-                                                   (__half *) h, x1, bx, pos, T);
-    else
-        norm_mod_kernel<float><<<M, 256, 0, st>>>(x, H, eps, mod, bmod, mod_stride, shift_off, scale_off,
-                                                  (float *) h, x1, bx, pos, T);
-    return cudaGetLastError();
+        return launch_pdl(norm_mod_kernel<__half>, dim3(M), dim3(256), 0, st, x, H, eps, mod, bmod, mod_stride,
+                          shift_off, scale_off, (__half *) h, x1, bx, pos, T);
+    return launch_pdl(norm_mod_kernel<float>, dim3(M), dim3(256), 0, st, x, H, eps, mod, bmod, mod_stride, shift_off,
+                      scale_off, (float *) h, x1, bx, pos, T);
 }
 cudaError_t fmt_attn(bool f16, const float *qkv, const float *bqkv, int T, int H, int nh, int window, void *out,
                      cudaStream_t st) {
     if (2 * window + 1 > 16 || H % nh) return cudaErrorInvalidValue;
-    const int warps = 3 * nh * T;
+    const dim3 g((3 * nh * T * 32 + 255) / 256);
+    const int hd = H / nh;
+    if (hd > 128) return cudaErrorInvalidValue;
+    if (hd <= 64 && window <= 2) {  // the sampler's band of five keys
+        if (f16)
+            return launch_pdl(attn_kernel<__half, 2, 5>, g, dim3(256), 0, st, qkv, bqkv, T, H, nh, window, (__half *) out);
+        return launch_pdl(attn_kernel<float, 2, 5>, g, dim3(256), 0, st, qkv, bqkv, T, H, nh, window, (float *) out);
+    }
     if (f16)
-        attn_kernel<__half><<<(warps * 32 + 255) / 256, 256, 0, st>>>(qkv, bqkv, T, H, nh, window, (__half *) out);
-    else
-        attn_kernel<float><<<(warps * 32 + 255) / 256, 256, 0, st>>>(qkv, bqkv, T, H, nh, window, (float *) out);
-    return cudaGetLastError();
+        return launch_pdl(attn_kernel<__half, 4, 16>, g, dim3(256), 0, st, qkv, bqkv, T, H, nh, window, (__half *) out);
+    return launch_pdl(attn_kernel<float, 4, 16>, g, dim3(256), 0, st, qkv, bqkv, T, H, nh, window, (float *) out);
 }
 cudaError_t fmt_res_norm(bool f16, float *x, const float *o, const float *bo, const float *mod, const float *bmod,
                          int mod_stride, int gate_off, int M, int H, float eps, const float *mod2, const float *bmod2,
                          int shift_off, int scale_off, void *h, cudaStream_t st) {
     if (H > RN_PER_THREAD * 256) return cudaErrorInvalidValue;
     if (f16)
-        res_norm_kernel<__half><<<M, 256, 0, st>>>(x, o, bo, mod, bmod, mod_stride, gate_off, H, eps, mod2, bmod2,
-                                                   shift_off, scale_off, (__half *) h);
-    else
-        res_norm_kernel<float><<<M, 256, 0, st>>>(x, o, bo, mod, bmod, mod_stride, gate_off, H, eps, mod2, bmod2,
-                                                  shift_off, scale_off, (float *) h);
-    return cudaGetLastError();
+        return launch_pdl(res_norm_kernel<__half>, dim3(M), dim3(256), 0, st, x, o, bo, mod, bmod, mod_stride,
+                          gate_off, H, eps, mod2, bmod2, shift_off, scale_off, (__half *) h);
+    return launch_pdl(res_norm_kernel<float>, dim3(M), dim3(256), 0, st, x, o, bo, mod, bmod, mod_stride, gate_off, H,
+                      eps, mod2, bmod2, shift_off, scale_off, (float *) h);
 }
 cudaError_t fmt_cfg_euler(const float *vout, const float *bv, int T, int P, int D, float a_cfg, float e_cfg,
                           float dt, float *x, float *x60, __half *x60h, cudaStream_t st) {
-    cfg_euler_kernel<<<grid_for((int64_t) (T - P) * D), 256, 0, st>>>(vout, bv, T, P, D, a_cfg, e_cfg, dt, x, x60,
-                                                                     x60h);
-    return cudaGetLastError();
+    return launch_pdl(cfg_euler_kernel, dim3(grid_for((int64_t) (T - P) * D)), dim3(256), 0, st, vout, bv, T, P, D,
+                      a_cfg, e_cfg, dt, x, x60, x60h);
 }
 cudaError_t fmt_add_bias(const float *a, const float *b, int M, int N, float *y, cudaStream_t st) {
-    add_bias_kernel<<<grid_for((int64_t) M * N), 256, 0, st>>>(a, b, M, N, y);
-    return cudaGetLastError();
+    return launch_pdl(add_bias_kernel, dim3(grid_for((int64_t) M * N)), dim3(256), 0, st, a, b, M, N, y);
 }
 cudaError_t fmt_to_half(const float *a, int64_t n, __half *y, cudaStream_t st) {
-    to_half_kernel<<<grid_for(n), 256, 0, st>>>(a, n, y);
-    return cudaGetLastError();
+    return launch_pdl(to_half_kernel, dim3(grid_for(n)), dim3(256), 0, st, a, n, y);
 }
 
 }  // namespace tpmd

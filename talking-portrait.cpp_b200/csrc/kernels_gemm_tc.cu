@@ -7,8 +7,7 @@
 // both operands K-major (rows of X and of W run along k), f32 accumulation
 // in tensor memory. A CTA owns a 128 x BN output tile: the 128 rows of W
 // are the MMA's M side, BN rows of X its N side, so the accumulator lane is
-// the output column n and each epilogue warp stores 32 consecutive n of a
-// row m with one 128-byte transaction.
+// the output column n.
 //
 // Two arithmetic kinds:
 //  * f16: f16 operands (kind::f16), as the reference's f16 mode runs its
@@ -19,27 +18,30 @@
 //    (the "3xTF32" decomposition of Ootomo and Yokota, "Recovering single
 //    precision accuracy from Tensor Cores while surpassing the FP32
 //    theoretical peak", 2022). The split happens in shared memory: TMA lands
-//    the raw f32 tile, the four epilogue warps (idle in the main loop)
+//    the raw f32 tile, the eight epilogue warps (idle in the main loop)
 //    overwrite it with hi and write lo beside it, and the MMA warp issues the
 //    three products. Relative error per product is about 2^-20.
 //
 // Batches (grid z) address their operands by row and column offsets into
 // one 2-D view of each buffer (attention heads are column blocks of the
-// q/k/v rows, grouped-conv groups are row blocks). Split-K, for grids with
-// fewer tiles than SMs: the S <= 8 CTAs of a tile's K splits form one
-// thread-block cluster (grid y). After every CTA of the cluster finished its
-// main loop, CTA s sends its partial accumulator, column slice by column
-// slice, into the shared memory of the CTA that owns the slice (distributed
-// shared memory, the stage buffers reused); after a second cluster barrier
-// each CTA adds the S partials of its slice in split order and stores them,
-// so results do not depend on scheduling. Every pipeline wait is bounded;
-// an expired wait sets *err and the CTA skips the rest of its work (it
-// still takes part in both cluster barriers).
+// q/k/v rows, grouped-conv groups are row blocks). Eight epilogue warps
+// (two per TMEM lane quarter, each half of the columns) apply the epilogue
+// into a shared-memory tile that one TMA store writes out (clipped to M and
+// N per batch by the tensor map); outputs whose strides TMA cannot address
+// take plain stores. Split-K, for grids with fewer tiles than SMs: the
+// S <= 8 CTAs of a tile's K splits form one thread-block cluster (grid y);
+// each leaves its partial accumulator in its own shared memory, and after a
+// cluster barrier each CTA reads its column slice from all S CTAs
+// (distributed shared memory), adds the partials in split order and stores
+// it, so results do not depend on scheduling. Every pipeline wait is
+// bounded; an expired wait sets *err and the CTA skips the rest of its work
+// (it still takes part in the cluster barriers).
 #include "tc_ptx.cuh"
 #include "tpmd_internal.h"
 #include "../../include/tpmd.h"
 
 #include <algorithm>
+#include <cstring>
 #include <mutex>
 
 namespace tpmd {
@@ -82,11 +84,13 @@ struct gemm_cfg {
     // both; N >> 3 at bit 17; M >> 4 at bit 24
     static constexpr uint32_t IDESC = (1u << 4) | ((X3 ? 2u : 0u) << 7) | ((X3 ? 2u : 0u) << 10) |
                                       ((uint32_t) (BN >> 3) << 17) | ((uint32_t) (128 >> 4) << 24);
-    // split-K receive area, for up to 8 splits: slot s holds split s's
-    // partial of this CTA's column slice [128 rows][<= ceil(BN/S) columns]
+    // the output tile [BN][128] (f32 at most) staged for the TMA store, or
+    // the split-K partial, in the stage buffers once the main loop is done
     static constexpr int MAX_SPLITS = 8;
-    static constexpr int RECV_BYTES = (BN + MAX_SPLITS) * 128 * 4;
-    static constexpr int DATA_BYTES = STAGES * STAGE_BYTES > RECV_BYTES ? STAGES * STAGE_BYTES : RECV_BYTES;
+    static constexpr int OUT_BYTES = BN * 128 * 4;
+    static constexpr int DATA_BYTES = STAGES * STAGE_BYTES > OUT_BYTES ? STAGES * STAGE_BYTES : OUT_BYTES;
+    static constexpr int NEPI = 8;  // epilogue (and TF32 split) warps: 256 threads (named barrier 1)
+    static constexpr int THREADS = 64 + 32 * NEPI;
     static constexpr int NBARS = 3 * STAGES + 1;
     static constexpr int SMEM = 1024 + DATA_BYTES + NBARS * 8 + 16;
     static_assert(BN % 16 == 0 && BN >= 64 && BN <= 256, "N tile");
@@ -103,6 +107,9 @@ struct gemm_kparams {
     const float *bias;
     float scale;
     int act;  // 0 none, 1 GELU (erf), 2 GELU (tanh)
+    int y_tma;  // 0: plain stores; 2 / 3: the output tensor map's rank
+    int y_vec;  // the output takes 4-element vector stores (aligned base and strides)
+    int w_pre;  // W tiles loaded before the programmatic-dependence wait
     int *err;
 };
 
@@ -114,8 +121,39 @@ __device__ __forceinline__ uint32_t map_to_rank(uint32_t saddr, uint32_t rank) {
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
     return r;
 }
-__device__ __forceinline__ void st_cluster_f32(uint32_t addr, uint32_t v) {
-    asm volatile("st.shared::cluster.b32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+__device__ __forceinline__ float4 ld_cluster_f32x4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(addr)
+                 : "memory");
+    return v;
+}
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *tm, uint32_t src, int c0, int c1) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                     (uint64_t) tm),
+                 "r"(src), "r"(c0), "r"(c1)
+                 : "memory");
+}
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap *tm, uint32_t src, int c0, int c1, int c2) {
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                     (uint64_t) tm),
+                 "r"(src), "r"(c0), "r"(c1), "r"(c2)
+                 : "memory");
+}
+
+// AND of v over the 256 epilogue threads (named barrier 1)
+__device__ __forceinline__ bool epi_all(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.and.pred q, 1, 256, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t) v)
+        : "memory");
+    return r != 0;
 }
 
 __device__ __forceinline__ float epi(float v, float bn, float scale, int act) {
@@ -144,9 +182,10 @@ __device__ __forceinline__ void split_tf32(float4 *x, float4 *lo, int n4, int t,
 }
 
 template <int KIND, int BN>
-__global__ void __launch_bounds__(192) gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW,
-                                                      const __grid_constant__ CUtensorMap tmX,
-                                                      const gemm_kparams p) {
+__global__ void __launch_bounds__(gemm_cfg<KIND, BN>::THREADS, 2) gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW,
+                                                                             const __grid_constant__ CUtensorMap tmX,
+                                                                             const __grid_constant__ CUtensorMap tmY,
+                                                                             const gemm_kparams p) {
     using cfg = gemm_cfg<KIND, BN>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = (uint8_t *) (((uintptr_t) smem_raw + 1023) & ~(uintptr_t) 1023);
@@ -171,7 +210,7 @@ __global__ void __launch_bounds__(192) gemm_tc_kernel(const __grid_constant__ CU
         for (int s = 0; s < cfg::STAGES; s++) {
             mbar_init(full(s), 1);
             mbar_init(empty(s), 1);
-            mbar_init(split_done(s), 4);
+            mbar_init(split_done(s), cfg::NEPI);
         }
         mbar_init(tfull, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -191,6 +230,15 @@ __global__ void __launch_bounds__(192) gemm_tc_kernel(const __grid_constant__ CU
 
     if (warp == 0) {
         if (lane == 0) {  // TMA producer
+            // constant W: the first stages' W tiles before the wait on the
+            // kernel before this one (which may still be running)
+            const int pre = p.w_pre ? min(nk, cfg::STAGES) : 0;
+            for (int i = 0; i < pre; i++) {
+                mbar_expect_tx(full(i), cfg::STAGE_TX);
+                tma_load_2d(smem_u32(A(i)), &tmW, full(i), (kb0 + i) * cfg::KB + b * p.w_col_b, n0 + b * p.w_row_b);
+            }
+            pdl_wait();
+            pdl_trigger();
             int issued = 0;
             for (int i = 0; i < nk; i++) {
                 const int s = i % cfg::STAGES;
@@ -199,11 +247,15 @@ __global__ void __launch_bounds__(192) gemm_tc_kernel(const __grid_constant__ CU
                     break;
                 }
                 const int kc = (kb0 + i) * cfg::KB;
-                mbar_expect_tx(full(s), cfg::STAGE_TX);
-                tma_load_2d(smem_u32(A(s)), &tmW, full(s), kc + b * p.w_col_b, n0 + b * p.w_row_b);
+                if (i >= pre) {
+                    mbar_expect_tx(full(s), cfg::STAGE_TX);
+                    tma_load_2d(smem_u32(A(s)), &tmW, full(s), kc + b * p.w_col_b, n0 + b * p.w_row_b);
+                }
                 tma_load_2d(smem_u32(B(s)), &tmX, full(s), kc + b * p.x_col_b, m0 + b * p.x_row_b);
                 issued++;
             }
+            // W tiles issued before an early exit still land
+            if (issued < pre) issued = pre;
             // the copies in flight land before the CTA goes on
             for (int j = issued > cfg::STAGES ? issued - cfg::STAGES : 0; j < issued; j++)
                 if (!mbar_wait(full(j % cfg::STAGES), (j / cfg::STAGES) & 1)) ok = false;
@@ -239,7 +291,7 @@ __global__ void __launch_bounds__(192) gemm_tc_kernel(const __grid_constant__ CU
             else atomicExch(p.err, 1);
         }
     } else {
-        // warps 2..5: the TF32 split of each stage, then the epilogue
+        // warps 2..9: the TF32 split of each stage, then the epilogue
         const int et = threadIdx.x - 64;
         if constexpr (cfg::X3) {
             for (int i = 0; i < nk; i++) {
@@ -248,8 +300,8 @@ __global__ void __launch_bounds__(192) gemm_tc_kernel(const __grid_constant__ CU
                     ok = false;
                     break;
                 }
-                split_tf32((float4 *) A(s), (float4 *) Alo(s), cfg::A_BYTES / 16, et, 128);
-                split_tf32((float4 *) B(s), (float4 *) Blo(s), cfg::B_BYTES / 16, et, 128);
+                split_tf32((float4 *) A(s), (float4 *) Alo(s), cfg::A_BYTES / 16, et, 32 * cfg::NEPI);
+                split_tf32((float4 *) B(s), (float4 *) Blo(s), cfg::B_BYTES / 16, et, 32 * cfg::NEPI);
                 // generic-proxy writes before the tensor core's async-proxy reads
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 __syncwarp();
@@ -257,79 +309,151 @@ __global__ void __launch_bounds__(192) gemm_tc_kernel(const __grid_constant__ CU
             }
         }
         if (ok && !mbar_wait(tfull, 0)) ok = false;
-        ok = __all_sync(0xffffffffu, ok);  // warp-uniform: tcgen05.ld is warp-collective
+        // uniform over the epilogue warps: tcgen05.ld is warp-collective and
+        // the TMA store waits on the epilogue's named barrier
+        ok = epi_all(ok);
+        pdl_wait();  // (returned long ago in the producer) before any global write
         if (!ok) {
             if (et == 0) atomicExch(p.err, 1);
-        } else if (p.splits == 1) {
+        } else {
             tc_fence_after();
-            const int q = warp & 3;  // the TMEM lane quarter this warp may read
-            const int row = q * 32 + lane;
-            const int n = n0 + row;
-            const float bn = (p.bias && n < p.N) ? __ldg(p.bias + n) : 0.0f;
-            const int64_t ybase = (int64_t) b * p.y_batch;
+            // lane quarter q of TMEM (row n0 + row), columns [c_lo, c_lo + BN/2)
+            const int q = warp & 3, row = q * 32 + lane, n = n0 + row;
+            const int c_lo = ((warp - 2) >> 2) * (BN / 2);
+            const uint32_t taddr = tmem + ((uint32_t) (q * 32) << 16);
+            float *sf = (float *) smem;  // [BN][128]: the output tile for the TMA store
+            __half *sh = (__half *) smem;
+            const float bn = (p.splits == 1 && p.bias && n < p.N) ? __ldg(p.bias + n) : 0.0f;
+            const bool plain = p.splits == 1 && !p.y_tma;
+            float *yp = nullptr;
+            __half *yhp = nullptr;
+            if (plain) {
+                const int64_t o = (int64_t) b * p.y_batch + (int64_t) (m0 + c_lo) * p.ldy + n;
+                if (p.Yh) yhp = p.Yh + o;
+                else yp = p.Y + o;
+            }
+            const int mlim = p.M - m0;
 #pragma unroll 1
-            for (int c = 0; c < BN && m0 + c < p.M; c += 16) {
+            for (int c = c_lo; p.splits == 1 && c < c_lo + BN / 2 && c < mlim; c += 16) {
                 uint32_t r[16];
-                tmem_ld16(tmem + ((uint32_t) (q * 32) << 16) + c, r);
-                if (n < p.N) {
+                tmem_ld16(taddr + c, r);
+                if (!plain) {
+                    if (p.Yh) {
+#pragma unroll
+                        for (int j = 0; j < 16; j++)
+                            sh[(c + j) * 128 + row] = __float2half_rn(epi(__uint_as_float(r[j]), bn, p.scale, p.act));
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 16; j++)
+                            sf[(c + j) * 128 + row] = epi(__uint_as_float(r[j]), bn, p.scale, p.act);
+                    }
+                } else if (n < p.N) {
 #pragma unroll
                     for (int j = 0; j < 16; j++) {
-                        const int m = m0 + c + j;
-                        if (m < p.M) {
+                        if (c + j < mlim) {
                             const float v = epi(__uint_as_float(r[j]), bn, p.scale, p.act);
-                            if (p.Yh) p.Yh[ybase + (int64_t) m * p.ldy + n] = __float2half_rn(v);
-                            else p.Y[ybase + (int64_t) m * p.ldy + n] = v;
+                            if (yhp) yhp[(int64_t) (c - c_lo + j) * p.ldy] = __float2half_rn(v);
+                            else yp[(int64_t) (c - c_lo + j) * p.ldy] = v;
                         }
                     }
+                }
+            }
+            if (p.splits == 1 && p.y_tma) {
+                // the tile to global memory by one TMA store (clipped to M, N)
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                asm volatile("bar.sync 1, 256;" ::: "memory");
+                if (et == 0) {
+                    if (p.y_tma == 3) tma_store_3d(&tmY, smem_u32(smem), n0, m0, b);
+                    else tma_store_2d(&tmY, smem_u32(smem), n0, m0);
+                    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+                    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
                 }
             }
         }
     }
     if (p.splits > 1) {
-        // split-K over the cluster: every CTA finished its main loop (stage
-        // memory is free everywhere), then each sends its partial columns to
-        // their owners' receive areas, then each owner adds its slice
-        const int S = p.splits, W = (BN + S - 1) / S;  // slice q: columns [q W, min(BN, (q + 1) W))
-        float *recv = (float *) smem;
+        // split-K over the cluster: every CTA leaves its partial [BN][128]
+        // in its own shared memory; after a cluster barrier CTA `split` adds
+        // columns [c0, c1) of all S partials in split order (distributed
+        // shared memory reads, four rows per 16-byte load; thread: rows
+        // 4 rq .. 4 rq + 3, columns c0 + cl + 8 i, two columns per round)
+        const int S = p.splits, W = (BN + S - 1) / S;
+        if (warp >= 2 && ok) {
+            const int q = warp & 3, row = q * 32 + lane;
+            const int c_lo = ((warp - 2) >> 2) * (BN / 2);
+            const uint32_t taddr = tmem + ((uint32_t) (q * 32) << 16);
+            float *part = (float *) smem;
+#pragma unroll 1
+            for (int c = c_lo; c < c_lo + BN / 2; c += 16) {
+                uint32_t r[16];
+                tmem_ld16(taddr + c, r);
+#pragma unroll
+                for (int j = 0; j < 16; j++) part[(c + j) * 128 + row] = __uint_as_float(r[j]);
+            }
+        }
         __syncwarp();
         cluster_sync_all();
         if (warp >= 2 && ok) {
-            tc_fence_after();
-            const int q = warp & 3, row = q * 32 + lane;
-            const uint32_t base = smem_u32(recv) + (uint32_t) (split * W * 128 + row) * 4u;
-            int own = 0, col = 0;  // owner CTA of column c and the column's place in its slice
-            uint32_t dst = map_to_rank(base, 0);
-#pragma unroll 1
-            for (int c = 0; c < BN; c += 16) {
-                uint32_t r[16];
-                tmem_ld16(tmem + ((uint32_t) (q * 32) << 16) + c, r);
+            const int et = threadIdx.x - 64;
+            const int rq = et & 31, cl = et >> 5;
+            const int nq = n0 + 4 * rq;
+            const int c0 = split * W, c1 = min(min(BN, c0 + W), p.M - m0);
+            uint32_t src[cfg::MAX_SPLITS];
+            const uint32_t mine = smem_u32(smem) + (uint32_t) rq * 16u;
 #pragma unroll
-                for (int j = 0; j < 16; j++) {
-                    st_cluster_f32(dst + (uint32_t) col * 512u, r[j]);
-                    if (++col == W) {
-                        col = 0;
-                        if (++own < S) dst = map_to_rank(base, (uint32_t) own);
+            for (int s2 = 0; s2 < cfg::MAX_SPLITS; s2++) src[s2] = s2 < S ? map_to_rank(mine, (uint32_t) s2) : 0u;
+            float bq[4];
+#pragma unroll
+            for (int e = 0; e < 4; e++) bq[e] = (p.bias && nq + e < p.N) ? __ldg(p.bias + nq + e) : 0.0f;
+            const int64_t ybase = (int64_t) b * p.y_batch;
+            const bool full4 = nq + 3 < p.N;
+            for (int cb = c0 + cl; cb < c1; cb += 16) {
+                // columns cb and cb + 8: all their loads in flight together
+                float4 pv[2][cfg::MAX_SPLITS];
+#pragma unroll
+                for (int u = 0; u < 2; u++)
+#pragma unroll
+                    for (int s2 = 0; s2 < cfg::MAX_SPLITS; s2++)
+                        if (s2 < S && cb + 8 * u < c1) pv[u][s2] = ld_cluster_f32x4(src[s2] + (uint32_t) (cb + 8 * u) * 512u);
+#pragma unroll
+                for (int u = 0; u < 2; u++) {
+                    const int c = cb + 8 * u;
+                    if (c >= c1) break;
+                    float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+                    for (int s2 = 0; s2 < cfg::MAX_SPLITS; s2++)
+                        if (s2 < S) {
+                            v[0] += pv[u][s2].x;
+                            v[1] += pv[u][s2].y;
+                            v[2] += pv[u][s2].z;
+                            v[3] += pv[u][s2].w;
+                        }
+#pragma unroll
+                    for (int e = 0; e < 4; e++) v[e] = epi(v[e], bq[e], p.scale, p.act);
+                    const int64_t o = ybase + (int64_t) (m0 + c) * p.ldy + nq;
+                    if (p.y_vec && full4) {
+                        if (p.Yh) {
+                            __half2 h01 = __floats2half2_rn(v[0], v[1]), h23 = __floats2half2_rn(v[2], v[3]);
+                            uint2 w2;
+                            w2.x = *(uint32_t *) &h01;
+                            w2.y = *(uint32_t *) &h23;
+                            *(uint2 *) (p.Yh + o) = w2;
+                        } else {
+                            *(float4 *) (p.Y + o) = make_float4(v[0], v[1], v[2], v[3]);
+                        }
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 4; e++)
+                            if (nq + e < p.N) {
+                                if (p.Yh) p.Yh[o + e] = __float2half_rn(v[e]);
+                                else p.Y[o + e] = v[e];
+                            }
                     }
                 }
             }
         }
         __syncwarp();
-        cluster_sync_all();
-        if (warp >= 2 && ok) {
-            const int q = warp & 3, row = q * 32 + lane, n = n0 + row;
-            const int c0 = split * W, c1 = min(min(BN, c0 + W), p.M - m0);
-            if (n < p.N) {
-                const float bn = p.bias ? __ldg(p.bias + n) : 0.0f;
-                const int64_t ybase = (int64_t) b * p.y_batch;
-                for (int c = c0; c < c1; c++) {
-                    float v = 0.0f;
-                    for (int s2 = 0; s2 < S; s2++) v += recv[(s2 * W + (c - c0)) * 128 + row];
-                    v = epi(v, bn, p.scale, p.act);
-                    if (p.Yh) p.Yh[ybase + (int64_t) (m0 + c) * p.ldy + n] = __float2half_rn(v);
-                    else p.Y[ybase + (int64_t) (m0 + c) * p.ldy + n] = v;
-                }
-            }
-        }
+        cluster_sync_all();  // no CTA leaves while others read its partial
     }
     tc_fence_before();
     __syncthreads();
@@ -403,7 +527,33 @@ cudaError_t run_gemm(const gemm_desc &d, cudaStream_t st) {
     p.scale = d.scale;
     p.act = d.act;
     p.err = d.err;
-    CUtensorMap tmW, tmX;
+    p.w_pre = d.pdl && d.w_const;
+    CUtensorMap tmW, tmX, tmY;
+    memset(&tmY, 0, sizeof tmY);
+    {
+        const int eo = d.Yh ? 2 : 4;
+        const uintptr_t yb = d.Yh ? (uintptr_t) d.Yh : (uintptr_t) d.Y;
+        p.y_vec = !(yb & (uintptr_t) (4 * eo - 1)) && d.ldy % 4 == 0 && (d.batch == 1 || d.y_batch % 4 == 0);
+    }
+    p.y_tma = 0;
+    if (splits == 1) {
+        // the output by TMA where its strides allow: [batch][M][N], clipped
+        const int eo = d.Yh ? 2 : 4;
+        const void *yb = d.Yh ? (const void *) d.Yh : (const void *) d.Y;
+        auto enc = encode_fn();
+        if (enc && !((uintptr_t) yb & 15) && (d.ldy * eo) % 16 == 0 && (d.batch == 1 || (d.y_batch * eo) % 16 == 0)) {
+            const CUtensorMapDataType ty = d.Yh ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+            const cuuint64_t dims[3] = {(cuuint64_t) d.N, (cuuint64_t) d.M, (cuuint64_t) d.batch};
+            const cuuint64_t strides[2] = {(cuuint64_t) (d.ldy * eo), (cuuint64_t) (d.y_batch * eo)};
+            const cuuint32_t box[3] = {128, (cuuint32_t) BN, 1};
+            const cuuint32_t estr[3] = {1, 1, 1};
+            const int rank = d.batch == 1 ? 2 : 3;
+            if (enc(&tmY, ty, rank, (void *) yb, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS)
+                p.y_tma = rank;
+        }
+    }
     const bool f32 = cfg::X3;
     const int64_t xrows = (int64_t) (d.batch - 1) * d.x_row_b + d.M, xcols = (int64_t) (d.batch - 1) * d.x_col_b + d.K;
     const int64_t wrows = (int64_t) (d.batch - 1) * d.w_row_b + d.N, wcols = (int64_t) (d.batch - 1) * d.w_col_b + d.K;
@@ -414,17 +564,26 @@ cudaError_t run_gemm(const gemm_desc &d, cudaStream_t st) {
     if (ae != cudaSuccess) return ae;
     cudaLaunchConfig_t lc = {};
     lc.gridDim = dim3((unsigned) tiles, (unsigned) p.splits, (unsigned) d.batch);
-    lc.blockDim = dim3(192, 1, 1);
+    lc.blockDim = dim3(cfg::THREADS, 1, 1);
     lc.dynamicSmemBytes = cfg::SMEM;
     lc.stream = st;
-    cudaLaunchAttribute at[1];
-    at[0].id = cudaLaunchAttributeClusterDimension;
-    at[0].val.clusterDim.x = 1;
-    at[0].val.clusterDim.y = (unsigned) p.splits;
-    at[0].val.clusterDim.z = 1;
+    cudaLaunchAttribute at[2];
+    int na = 0;
+    if (p.splits > 1) {
+        at[na].id = cudaLaunchAttributeClusterDimension;
+        at[na].val.clusterDim.x = 1;
+        at[na].val.clusterDim.y = (unsigned) p.splits;
+        at[na].val.clusterDim.z = 1;
+        na++;
+    }
+    if (d.pdl) {
+        at[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[na].val.programmaticStreamSerializationAllowed = 1;
+        na++;
+    }
     lc.attrs = at;
-    lc.numAttrs = p.splits > 1 ? 1 : 0;
-    const cudaError_t le = cudaLaunchKernelEx(&lc, gemm_tc_kernel<KIND, BN>, tmW, tmX, p);
+    lc.numAttrs = na;
+    const cudaError_t le = cudaLaunchKernelEx(&lc, gemm_tc_kernel<KIND, BN>, tmW, tmX, tmY, p);
     return le != cudaSuccess ? le : cudaGetLastError();
 }
 
@@ -437,6 +596,10 @@ cudaError_t run_kind(const gemm_desc &d, cudaStream_t st) {
     else if (d.M <= 192) bn = 192;
     else if (d.M <= 256) bn = 256;
     else bn = ((d.M + 255) / 256) * 256 - d.M <= ((d.M + 191) / 192) * 192 - d.M ? 256 : 192;
+    // grids too small for the SMs split K over a cluster; 64-wide N tiles
+    // there give more CTAs, fewer splits and smaller partials to add
+    const int64_t tiles = (int64_t) ((d.N + 127) / 128) * ((d.M + bn - 1) / bn) * d.batch;
+    if (bn > 64 && tiles < sm_count()) bn = 64;
     switch (bn) {
         case 64: return run_gemm<KIND, 64>(d, st);
         case 128: return run_gemm<KIND, 128>(d, st);

@@ -212,7 +212,8 @@ tpae_ctx *tpae_create(int device, const tpae_config *cfg) {
                  // the GEMMs' row strides (16-byte multiples) and the attention
                  // heads' whole 32-float k-blocks
                  (cfg->hidden / cfg->n_heads) % 32 == 0 && cfg->ffn % 4 == 0 && cfg->dim_w % 4 == 0 &&
-                 cfg->conv_dim[6] % 4 == 0 && ((cfg->hidden / cfg->pos_groups) * cfg->pos_kernel) % 4 == 0;
+                 cfg->conv_dim[0] % 4 == 0 && cfg->conv_dim[6] % 4 == 0 &&
+                 ((cfg->hidden / cfg->pos_groups) * cfg->pos_kernel) % 4 == 0;
     for (int i = 0; i < 7; i++)
         valid = valid && cfg->conv_dim[i] > 0 && cfg->conv_kernel[i] > 0 && cfg->conv_stride[i] > 0;
     if (!valid) {
@@ -381,7 +382,9 @@ int tpae_encode(tpae_ctx *a, const float *audio, int64_t n_in, int64_t seq_len, 
     if (S > (1 << 24)) return a->fail("tpae_encode: seq_len too large"), -1;
     const int lds = (int) ((S + 3) & ~(int64_t) 3);
     col = std::max(col, (size_t) G * S * cg * KP);
-    const size_t sizes[] = {(size_t) n,      act,           act,           col,          (size_t) 2 * c.conv_dim[0],
+    // stats: mean and 1/std per channel, then 256 x C partial (sum, sum of squares) doubles
+    const size_t stat_floats = (size_t) 2 * ((c.conv_dim[0] + 1) & ~1) + (size_t) 256 * c.conv_dim[0] * 4;
+    const size_t sizes[] = {(size_t) n,      act,           act,           col,          stat_floats,
                             (size_t) S * C6, (size_t) S * H, (size_t) S * 3 * H, (size_t) H * lds, (size_t) S * H,
                             (size_t) S * H,  (size_t) S * F, (size_t) nh * S * lds, (size_t) S * L * H,
                             (size_t) S * c.dim_w};

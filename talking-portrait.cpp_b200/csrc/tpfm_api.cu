@@ -109,6 +109,7 @@ struct tpfm_ctx {
         d.bias = bias;
         d.act = act;
         d.err = gerr;
+        d.pdl = d.w_const = true;  // W: weights; the forward's kernels are programmatic dependents
         return ck(gemm_tc(d, stream), what);
     }
     bool gemm(const void *X, int Mr, int K, const std::string &wname, int N, float *Y) {

@@ -7,8 +7,35 @@
 
 #include <cstdint>
 #include <string>
+#include <utility>
 
 namespace tpmd {
+
+// Programmatic dependent launch: a kernel launched by launch_pdl may start
+// while the kernel before it in the stream is still running. It calls
+// pdl_wait() before touching anything that kernel writes or reads (the
+// wait returns once that grid has completed and its writes are visible),
+// and pdl_trigger() after its own pdl_wait(), so that when a kernel starts,
+// every kernel before its predecessor has completed.
+#ifdef __CUDACC__
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       Args &&...args) {
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = grid;
+    lc.blockDim = block;
+    lc.dynamicSmemBytes = smem;
+    lc.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    lc.attrs = at;
+    lc.numAttrs = 1;
+    return cudaLaunchKernelEx(&lc, kernel, std::forward<Args>(args)...);
+}
+#endif
 
 constexpr int N_LEVELS = 7;
 constexpr int STYLE_DIM = 512;
@@ -145,6 +172,10 @@ struct gemm_desc {
     float scale = 1.0f;
     int act = 0;  // 0 none, 1 GELU (erf), 2 GELU (tanh)
     int *err = nullptr;  // set when a bounded wait expires
+    // launched as a programmatic dependent (launch_pdl rules); with w_const
+    // W is not written by the kernels before it, so its first tiles load
+    // before the wait
+    bool pdl = false, w_const = false;
 };
 cudaError_t gemm_tc(const gemm_desc &d, cudaStream_t st);
 // the GEMM kernels' shared-memory attribute on the current device (before a
