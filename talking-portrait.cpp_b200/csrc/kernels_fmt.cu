@@ -112,7 +112,7 @@ __global__ void __launch_bounds__(256) norm_mod_kernel(float *__restrict__ x, in
 // v element the warp needs is loaded up front (EPL per lane and row, MAXJ
 // keys at most), so the band costs one memory round trip.
 template <typename TIN, int EPL, int MAXJ>
-__global__ void __launch_bounds__(256) attn_kernel(const float *__restrict__ qkv, const float *__restrict__ bqkv,
+__global__ void __launch_bounds__(128) attn_kernel(const float *__restrict__ qkv, const float *__restrict__ bqkv,
                                                    int T, int H, int nh, int window, TIN *__restrict__ out) {
     pdl_wait();
     pdl_trigger();
@@ -295,17 +295,18 @@ cudaError_t fmt_norm_mod(bool f16, float *x, int M, int H, float eps, const floa
 cudaError_t fmt_attn(bool f16, const float *qkv, const float *bqkv, int T, int H, int nh, int window, void *out,
                      cudaStream_t st) {
     if (2 * window + 1 > 16 || H % nh) return cudaErrorInvalidValue;
-    const dim3 g((3 * nh * T * 32 + 255) / 256);
+    // 128-thread blocks: the 3 nh T warps fit the SMs in one wave
+    const dim3 g((3 * nh * T * 32 + 127) / 128);
     const int hd = H / nh;
     if (hd > 128) return cudaErrorInvalidValue;
     if (hd <= 64 && window <= 2) {  // the sampler's band of five keys
         if (f16)
-            return launch_pdl(attn_kernel<__half, 2, 5>, g, dim3(256), 0, st, qkv, bqkv, T, H, nh, window, (__half *) out);
-        return launch_pdl(attn_kernel<float, 2, 5>, g, dim3(256), 0, st, qkv, bqkv, T, H, nh, window, (float *) out);
+            return launch_pdl(attn_kernel<__half, 2, 5>, g, dim3(128), 0, st, qkv, bqkv, T, H, nh, window, (__half *) out);
+        return launch_pdl(attn_kernel<float, 2, 5>, g, dim3(128), 0, st, qkv, bqkv, T, H, nh, window, (float *) out);
     }
     if (f16)
-        return launch_pdl(attn_kernel<__half, 4, 16>, g, dim3(256), 0, st, qkv, bqkv, T, H, nh, window, (__half *) out);
-    return launch_pdl(attn_kernel<float, 4, 16>, g, dim3(256), 0, st, qkv, bqkv, T, H, nh, window, (float *) out);
+        return launch_pdl(attn_kernel<__half, 4, 16>, g, dim3(128), 0, st, qkv, bqkv, T, H, nh, window, (__half *) out);
+    return launch_pdl(attn_kernel<float, 4, 16>, g, dim3(128), 0, st, qkv, bqkv, T, H, nh, window, (float *) out);
 }
 cudaError_t fmt_res_norm(bool f16, float *x, const float *o, const float *bo, const float *mod, const float *bmod,
                          int mod_stride, int gate_off, int M, int H, float eps, const float *mod2, const float *bmod2,

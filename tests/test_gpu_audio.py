@@ -1,6 +1,7 @@
 """The B200 audio encoder (tpae_*) against the oracle's restatement of
-audio_model::encode (src/audio_enc.cpp:55-236), float32 both sides (cuBLAS
-without TF32); exact, padded and cropped inputs; the GGUF path."""
+audio_model::encode (src/audio_enc.cpp:55-236), float32 both sides (the GPU's
+tcgen05 GEMMs by the three-pass TF32 split); exact, padded and cropped
+inputs; the GGUF path."""
 import numpy as np
 import pytest
 

@@ -1,7 +1,7 @@
 """The B200 flow-matching sampler (tpfm_*) against the oracle's restatement
 (src/fmt.cpp:9-211, src/pipeline.cpp:15-91): one CFG-batched forward and a
-whole 9-step chunk, float32 (cuBLAS without TF32) and f16-weight modes; the
-GGUF path with its hyper-parameter check."""
+whole 9-step chunk, float32 (tcgen05 GEMMs by the three-pass TF32 split) and
+f16-weight modes; the GGUF path with its hyper-parameter check."""
 import numpy as np
 import pytest
 
