@@ -298,7 +298,8 @@ int tpk_chw_to_rgb24(const float *chw, int64_t n, int H, int W, uint8_t *rgb, vo
  * k' of W likewise, m < M, n < N, k < K. dtype TPMD_DTYPE_F32: f32
  * operands by the three-pass TF32 split (about 2^-20 relative error per
  * product); TPMD_DTYPE_F16: f16 operands; f32 accumulation either way.
- * act 0 none, 1 GELU (erf), 2 GELU (tanh); bias may be NULL. Strides in
+ * act 0 none, 1 GELU (erf), 2 GELU (tanh), 3 leaky ReLU (slope 0.2); bias
+ * may be NULL. Strides in
  * elements, 16-byte multiples, bases 16-byte aligned; device memory.
  * Synchronous: returns once the GEMM finished on `stream`; -1 (message in
  * tpk_last_error) on a bad argument or an expired pipeline wait. */

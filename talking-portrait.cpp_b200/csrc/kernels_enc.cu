@@ -8,20 +8,17 @@
 //          EqualConv2d with its scale folded (src/ops_common.h:12-26)
 //  blur:   upfirdn2d(up 1, pad (p0, p1)) with a 4x4 FIR, depthwise
 //          correlation (src/ops_common.h:39-43)
-//  head:   five plain EqualLinears and motion = Q lambda, one block
+//  head:   five plain EqualLinears (a warp per output) and motion = Q lambda
 //
-// The conv is an FFMA implicit GEMM: 128 output pixels x 64 output channels
-// x 16 k per step, 256 threads, 8x4 outputs per thread; per (tap, 16-channel
-// slice) the block loads the strided, shifted input rows straight from
-// memory (zeros outside the map), so no im2col buffer exists.
+// The conv is im2col (rows of K*K*IC floats, zeros outside the map) and the
+// library's tcgen05 GEMM with f32 operands by the three-pass TF32 split
+// (kernels_gemm_tc.cu), bias, leaky ReLU and the residual in its epilogue.
 #include "tpmd_internal.h"
 
 #include <algorithm>
 
 namespace tpmd {
 namespace {
-
-constexpr int EBM = 128, EBN = 64, EBK = 16;
 
 __global__ void __launch_bounds__(256) enc_stem_kernel(const float *__restrict__ img, int P,
                                                        const float *__restrict__ w,
@@ -47,118 +44,28 @@ __global__ void __launch_bounds__(256) enc_stem_kernel(const float *__restrict__
     }
 }
 
-// blockIdx.z = split: the block sums the k-steps (tap, 16-channel chunk)
-// [z * per, (z + 1) * per) of K; with several splits the raw sums go to
-// p.part[z][m][n] and enc_split_reduce_kernel applies the epilogue
-__global__ void __launch_bounds__(256) enc_conv_kernel(enc_conv_params p, int per) {
-    __shared__ __align__(16) float As[EBK][EBM + 4];
-    __shared__ __align__(16) float Bs[EBK][EBN + 4];
-    const int M = p.OH * p.OW, N = p.OC, KT = p.K * p.K, Kall = KT * p.IC;
-    const int m0 = blockIdx.x * EBM, n0 = blockIdx.y * EBN;
-    const int tid = threadIdx.x;
-
-    // A loads: output pixel tid%128, channels (tid/128)*8 .. +8 of the slice
-    const int a_row = tid & (EBM - 1), a_c = (tid >> 7) * 8;
-    const int am = m0 + a_row;
-    const bool a_valid = am < M;
-    const int ox = a_valid ? am % p.OW : 0, oy = a_valid ? am / p.OW : 0;
-    // B loads: column tid/4, k (tid%4)*4 .. +4 of the slice
-    const int b_n = tid >> 2, b_k = (tid & 3) * 4;
-    const bool b_valid = n0 + b_n < N;
-    const float *wrow = p.w + (int64_t) (b_valid ? n0 + b_n : 0) * Kall;
-    const int tn = tid & 15, tm = tid >> 4;
-
-    float acc[8][4];
-#pragma unroll
-    for (int i = 0; i < 8; i++)
-#pragma unroll
-        for (int j = 0; j < 4; j++) acc[i][j] = 0.0f;
-
-    const int CK = p.IC / EBK;  // 16-channel chunks per tap
-    const int ks0 = blockIdx.z * per, ks1 = min(KT * CK, ks0 + per);
-    for (int tap = ks0 / CK; tap < KT && tap * CK < ks1; tap++) {
-        const int iy = oy * p.stride + tap / p.K - p.pad, ix = ox * p.stride + tap % p.K - p.pad;
-        const bool in_b = a_valid && iy >= 0 && iy < p.IH && ix >= 0 && ix < p.IW;
-        const float *xp = p.x + ((int64_t) iy * p.IW + ix) * p.IC + a_c;
-        const float *wp = wrow + (int64_t) tap * p.IC + b_k;
-        const int cb = max(ks0 - tap * CK, 0) * EBK, ce = min(ks1 - tap * CK, CK) * EBK;
-        for (int c0 = cb; c0 < ce; c0 += EBK) {
-            float av[8], bv[4];
-            if (in_b) {
-                const float4 u = __ldg(reinterpret_cast<const float4 *>(xp + c0));
-                const float4 v = __ldg(reinterpret_cast<const float4 *>(xp + c0) + 1);
-                av[0] = u.x; av[1] = u.y; av[2] = u.z; av[3] = u.w;
-                av[4] = v.x; av[5] = v.y; av[6] = v.z; av[7] = v.w;
-            } else {
-#pragma unroll
-                for (int i = 0; i < 8; i++) av[i] = 0.0f;
-            }
-            if (b_valid) {
-                const float4 u = __ldg(reinterpret_cast<const float4 *>(wp + c0));
-                bv[0] = u.x; bv[1] = u.y; bv[2] = u.z; bv[3] = u.w;
-            } else {
-#pragma unroll
-                for (int i = 0; i < 4; i++) bv[i] = 0.0f;
-            }
-#pragma unroll
-            for (int i = 0; i < 8; i++) As[a_c + i][a_row] = av[i];
-#pragma unroll
-            for (int i = 0; i < 4; i++) Bs[b_k + i][b_n] = bv[i];
-            __syncthreads();
-#pragma unroll
-            for (int kk = 0; kk < EBK; kk++) {
-                const float4 a0 = *reinterpret_cast<const float4 *>(&As[kk][tm * 8]);
-                const float4 a1 = *reinterpret_cast<const float4 *>(&As[kk][tm * 8 + 4]);
-                const float4 bq = *reinterpret_cast<const float4 *>(&Bs[kk][tn * 4]);
-                const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-                const float bb[4] = {bq.x, bq.y, bq.z, bq.w};
-#pragma unroll
-                for (int i = 0; i < 8; i++)
-#pragma unroll
-                    for (int j = 0; j < 4; j++) acc[i][j] = fmaf(a[i], bb[j], acc[i][j]);
-            }
-            __syncthreads();
-        }
-    }
-
-#pragma unroll
-    for (int i = 0; i < 8; i++) {
-        const int m = m0 + tm * 8 + i;
-        if (m >= M) continue;
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-            const int n = n0 + tn * 4 + j;
-            if (n >= N) continue;
-            float v = acc[i][j];
-            if (gridDim.z > 1) {
-                p.part[((int64_t) blockIdx.z * M + m) * N + n] = v;
-                continue;
-            }
-            if (p.bias) v += __ldg(p.bias + n);
-            if (p.lrelu) v = fmaxf(v, 0.2f * v);
-            const int64_t dst = (int64_t) m * N + n;
-            if (p.res) v += p.res[dst];
-            p.y[dst] = v;
+// col[m][k] = x[oy*s - p + kh][ox*s - p + kw][ic] (zero outside), m = oy*OW +
+// ox, k = (kh*K + kw)*IC + ic; a block per output pixel (grid-stride), four
+// channels per thread (IC % 4 == 0)
+__global__ void __launch_bounds__(128) enc_im2col_kernel(const float *__restrict__ x, int IH, int IW, int IC, int K,
+                                                         int stride, int pad, int OH, int OW,
+                                                         float *__restrict__ col) {
+    const int IC4 = IC >> 2, row4 = K * K * IC4;
+    const int64_t M = (int64_t) OH * OW;
+    for (int64_t m = blockIdx.x; m < M; m += gridDim.x) {
+        const int oy = (int) (m / OW), ox = (int) (m - (int64_t) oy * OW);
+        float4 *dst = reinterpret_cast<float4 *>(col) + m * row4;
+        for (int r = threadIdx.x; r < row4; r += blockDim.x) {
+            const int t = r / IC4, c4 = r - t * IC4;
+            const int iy = oy * stride - pad + t / K, ix = ox * stride - pad + t % K;
+            float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (iy >= 0 && iy < IH && ix >= 0 && ix < IW)
+                v = __ldg(reinterpret_cast<const float4 *>(x + ((int64_t) iy * IW + ix) * IC) + c4);
+            dst[r] = v;
         }
     }
 }
 
-// the split-K sums in split order (deterministic), then the conv epilogue
-__global__ void __launch_bounds__(256) enc_split_reduce_kernel(enc_conv_params p, int S) {
-    const int64_t MN = (int64_t) p.OH * p.OW * p.OC;
-    for (int64_t e = (int64_t) blockIdx.x * blockDim.x + threadIdx.x; e < MN; e += (int64_t) gridDim.x * blockDim.x) {
-        float v = p.part[e];
-        for (int z = 1; z < S; z++) v += p.part[z * MN + e];
-        const int n = (int) (e % p.OC);
-        if (p.bias) v += __ldg(p.bias + n);
-        if (p.lrelu) v = fmaxf(v, 0.2f * v);
-        if (p.res) v += p.res[e];
-        p.y[e] = v;
-    }
-}
-
-// y[Y][X][c] = sum_{a,b} k[a][b] x[Y+a-p0][X+b-p0][c], zero outside x;
-// y is (IH+p0+p1-3) x (IW+p0+p1-3); four channels per thread
 __global__ void __launch_bounds__(256) enc_blur_kernel(const float *__restrict__ x, int IH, int IW, int C,
                                                        const float *__restrict__ k4, int p0, int OH, int OW,
                                                        float *__restrict__ y) {
@@ -195,31 +102,36 @@ __global__ void __launch_bounds__(256) enc_blur_kernel(const float *__restrict__
 // appearance [512] -> five EqualLinears (512 -> 512 x4 -> 20) -> lambda [20];
 // motion = Q lambda with Q [512][20]. One block of 512 threads, a warp per
 // output row with coalesced weight reads, layers separated by barriers.
-__global__ void __launch_bounds__(512) enc_head_kernel(const float *__restrict__ app, enc_head_params h,
-                                                       float *__restrict__ lam, float *__restrict__ motion) {
-    __shared__ float v[2][512];
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    v[0][tid] = app[tid];
-    __syncthreads();
-    int cur = 0;
-    for (int l = 0; l < 5; l++) {
-        const int out = l == 4 ? 20 : 512;
-        for (int o = warp; o < out; o += 16) {
-            const float *w = h.W[l] + (int64_t) o * 512;
-            float a = 0.0f;
-            for (int k = lane; k < 512; k += 32) a = fmaf(__ldg(w + k), v[cur][k], a);
+// one EqualLinear of the head: out[o] = W[o] . in + b[o] over 512 inputs,
+// one warp per output (16-byte weight loads, four per lane)
+__global__ void __launch_bounds__(256) enc_fc_kernel(const float *__restrict__ in, const float *__restrict__ W,
+                                                     const float *__restrict__ b, int N, float *__restrict__ out) {
+    const int lane = threadIdx.x & 31, o = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (o >= N) return;
+    const float4 *w4 = reinterpret_cast<const float4 *>(W + (int64_t) o * 512);
+    const float4 *x4 = reinterpret_cast<const float4 *>(in);
+    float a = 0.0f;
 #pragma unroll
-            for (int s = 16; s > 0; s >>= 1) a += __shfl_xor_sync(0xffffffffu, a, s);
-            if (lane == 0) v[cur ^ 1][o] = a + __ldg(h.b[l] + o);
-        }
-        __syncthreads();
-        cur ^= 1;
+    for (int k = 0; k < 4; k++) {
+        const float4 w = __ldg(w4 + lane + 32 * k), x = __ldg(x4 + lane + 32 * k);
+        a = fmaf(w.x, x.x, a);
+        a = fmaf(w.y, x.y, a);
+        a = fmaf(w.z, x.z, a);
+        a = fmaf(w.w, x.w, a);
     }
-    if (tid < 20) lam[tid] = v[cur][tid];
+#pragma unroll
+    for (int s = 16; s > 0; s >>= 1) a += __shfl_xor_sync(0xffffffffu, a, s);
+    if (lane == 0) out[o] = a + __ldg(b + o);
+}
+
+// motion = Q lambda (Q [512][20])
+__global__ void __launch_bounds__(512) enc_motion_kernel(const float *__restrict__ lam, const float *__restrict__ Q,
+                                                         float *__restrict__ motion) {
+    const int t = threadIdx.x;
     float m = 0.0f;
 #pragma unroll
-    for (int k = 0; k < 20; k++) m = fmaf(__ldg(h.Q + tid * 20 + k), v[cur][k], m);
-    motion[tid] = m;
+    for (int k = 0; k < 20; k++) m = fmaf(__ldg(Q + t * 20 + k), __ldg(lam + k), m);
+    motion[t] = m;
 }
 
 __global__ void convert_feats_kernel(const float *__restrict__ src, int64_t n, __half *__restrict__ dst) {
@@ -243,28 +155,29 @@ cudaError_t launch_enc_stem(const float *img, const float *w, const float *b, fl
 }
 
 cudaError_t launch_enc_conv(const enc_conv_params &p, cudaStream_t st) {
-    if (p.IC % EBK || p.OH <= 0 || p.OW <= 0) return cudaErrorInvalidValue;
-    const int64_t M = (int64_t) p.OH * p.OW;
-    const int gx = (int) ((M + EBM - 1) / EBM), gy = (p.OC + EBN - 1) / EBN;
-    const int ksteps = p.K * p.K * (p.IC / EBK);
-    // the deep low-resolution convs launch a few blocks with long K loops:
-    // split K so that about two blocks per SM work on them
-    int S = 1;
-    if (p.part && gx * gy < 148) {
-        S = (2 * 148 + gx * gy - 1) / (gx * gy);
-        S = std::min(S, 16);
-        S = std::min(S, ksteps / 4);  // at least four k-steps per split
-        while (S > 1 && (int64_t) S * M * p.OC > p.part_floats) S--;
-        if (S < 1) S = 1;
-    }
-    const int per = (ksteps + S - 1) / S;
-    S = (ksteps + per - 1) / per;  // no empty split
-    enc_conv_kernel<<<dim3((unsigned) gx, (unsigned) gy, (unsigned) S), 256, 0, st>>>(p, per);
-    if (S > 1) {
-        const int64_t n = M * p.OC;
-        enc_split_reduce_kernel<<<(int) std::min<int64_t>((n + 255) / 256, 148 * 8), 256, 0, st>>>(p, S);
-    }
-    return cudaGetLastError();
+    if (p.IC % 4 || p.OC % 4 || p.OH <= 0 || p.OW <= 0 || !p.err) return cudaErrorInvalidValue;
+    const int64_t M = (int64_t) p.OH * p.OW, Kall = (int64_t) p.K * p.K * p.IC;
+    if (M * Kall > p.col_floats || M >= (1ll << 31) || Kall >= (1ll << 31)) return cudaErrorInvalidValue;
+    enc_im2col_kernel<<<(unsigned) std::min<int64_t>(M, 148 * 32), 128, 0, st>>>(p.x, p.IH, p.IW, p.IC, p.K, p.stride,
+                                                                               p.pad, p.OH, p.OW, p.col);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    gemm_desc d;
+    d.f32 = true;
+    d.X = p.col;
+    d.ldx = Kall;
+    d.W = p.w;
+    d.ldw = Kall;
+    d.Y = p.y;
+    d.ldy = p.OC;
+    d.M = (int) M;
+    d.N = p.OC;
+    d.K = (int) Kall;
+    d.bias = p.bias;
+    d.act = p.lrelu ? 3 : 0;
+    d.res = p.res;
+    d.err = p.err;
+    return gemm_tc(d, st);
 }
 
 cudaError_t launch_enc_blur(const float *x, int IH, int IW, int C, const float *k4, int p0, int p1, float *y,
@@ -277,9 +190,18 @@ cudaError_t launch_enc_blur(const float *x, int IH, int IW, int C, const float *
     return cudaGetLastError();
 }
 
-cudaError_t launch_enc_head(const float *app, const enc_head_params &h, float *lam, float *motion,
+cudaError_t launch_enc_head(const float *app, const enc_head_params &h, float *lam, float *motion, float *scratch,
                             cudaStream_t st) {
-    enc_head_kernel<<<1, 512, 0, st>>>(app, h, lam, motion);
+    // fc 0..3 (512 -> 512) alternate between the two scratch rows, fc 4 (512 -> 20) into lam
+    float *t0 = scratch, *t1 = scratch + 512;
+    const float *in = app;
+    for (int l = 0; l < 4; l++) {
+        float *o = (l & 1) ? t1 : t0;
+        enc_fc_kernel<<<512 * 32 / 256, 256, 0, st>>>(in, h.W[l], h.b[l], 512, o);
+        in = o;
+    }
+    enc_fc_kernel<<<(20 * 32 + 255) / 256, 256, 0, st>>>(in, h.W[4], h.b[4], 20, lam);
+    enc_motion_kernel<<<1, 512, 0, st>>>(lam, h.Q, motion);
     return cudaGetLastError();
 }
 

@@ -2,7 +2,7 @@
 // linears (src/fmt.cpp:64-211) and the audio encoder's convolutions, linears
 // and attention products (src/audio_enc.cpp:55-236):
 //
-//   Y[m][n] = epi( sum_k X[m][k] * W[n][k] ),  epi(v) = act((v + bias[n]) * scale)
+//   Y[m][n] = epi( sum_k X[m][k] * W[n][k] ),  epi(v) = act((v + bias[n]) * scale) (+ res[m][n])
 //
 // both operands K-major (rows of X and of W run along k), f32 accumulation
 // in tensor memory. A CTA owns a 128 x BN output tile: the 128 rows of W
@@ -106,7 +106,8 @@ struct gemm_kparams {
     int64_t ldy, y_batch;
     const float *bias;
     float scale;
-    int act;  // 0 none, 1 GELU (erf), 2 GELU (tanh)
+    int act;  // 0 none, 1 GELU (erf), 2 GELU (tanh), 3 leaky ReLU (0.2)
+    const float *res;  // added after act, laid out as Y (may be Y itself)
     int y_tma;  // 0: plain stores; 2 / 3: the output tensor map's rank
     int y_vec;  // the output takes 4-element vector stores (aligned base and strides)
     int w_pre;  // W tiles loaded before the programmatic-dependence wait
@@ -160,6 +161,7 @@ __device__ __forceinline__ float epi(float v, float bn, float scale, int act) {
     v = (v + bn) * scale;
     if (act == 1) v = gelu_erf_g(v);
     else if (act == 2) v = gelu_tanh_g(v);
+    else if (act == 3) v = fmaxf(v, 0.2f * v);
     return v;
 }
 
@@ -342,6 +344,13 @@ __global__ void __launch_bounds__(gemm_cfg<KIND, BN>::THREADS, 2) gemm_tc_kernel
 #pragma unroll
                         for (int j = 0; j < 16; j++)
                             sh[(c + j) * 128 + row] = __float2half_rn(epi(__uint_as_float(r[j]), bn, p.scale, p.act));
+                    } else if (p.res) {
+                        // the residual of rows inside the output only (the rest is clipped)
+                        const float *rp = p.res + (int64_t) b * p.y_batch + (int64_t) (m0 + c) * p.ldy + n;
+#pragma unroll
+                        for (int j = 0; j < 16; j++)
+                            sf[(c + j) * 128 + row] = epi(__uint_as_float(r[j]), bn, p.scale, p.act) +
+                                                      ((n < p.N && c + j < mlim) ? rp[(int64_t) j * p.ldy] : 0.0f);
                     } else {
 #pragma unroll
                         for (int j = 0; j < 16; j++)
@@ -351,9 +360,14 @@ __global__ void __launch_bounds__(gemm_cfg<KIND, BN>::THREADS, 2) gemm_tc_kernel
 #pragma unroll
                     for (int j = 0; j < 16; j++) {
                         if (c + j < mlim) {
-                            const float v = epi(__uint_as_float(r[j]), bn, p.scale, p.act);
-                            if (yhp) yhp[(int64_t) (c - c_lo + j) * p.ldy] = __float2half_rn(v);
-                            else yp[(int64_t) (c - c_lo + j) * p.ldy] = v;
+                            const int64_t o = (int64_t) (c - c_lo + j) * p.ldy;
+                            float v = epi(__uint_as_float(r[j]), bn, p.scale, p.act);
+                            if (yhp) {
+                                yhp[o] = __float2half_rn(v);
+                            } else {
+                                if (p.res) v += p.res[(yp - p.Y) + o];
+                                yp[o] = v;
+                            }
                         }
                     }
                 }
@@ -431,6 +445,11 @@ __global__ void __launch_bounds__(gemm_cfg<KIND, BN>::THREADS, 2) gemm_tc_kernel
 #pragma unroll
                     for (int e = 0; e < 4; e++) v[e] = epi(v[e], bq[e], p.scale, p.act);
                     const int64_t o = ybase + (int64_t) (m0 + c) * p.ldy + nq;
+                    if (p.res && !p.Yh) {
+#pragma unroll
+                        for (int e = 0; e < 4; e++)
+                            if (nq + e < p.N) v[e] += p.res[o + e];
+                    }
                     if (p.y_vec && full4) {
                         if (p.Yh) {
                             __half2 h01 = __floats2half2_rn(v[0], v[1]), h23 = __floats2half2_rn(v[2], v[3]);
@@ -526,6 +545,7 @@ cudaError_t run_gemm(const gemm_desc &d, cudaStream_t st) {
     p.bias = d.bias;
     p.scale = d.scale;
     p.act = d.act;
+    p.res = d.res;
     p.err = d.err;
     p.w_pre = d.pdl && d.w_const;
     CUtensorMap tmW, tmX, tmY;
@@ -626,7 +646,7 @@ cudaError_t gemm_tc(const gemm_desc &d, cudaStream_t st) {
         return cudaErrorInvalidValue;
     // TMA: 16-byte aligned bases and row strides
     if (((uintptr_t) d.X | (uintptr_t) d.W) & 15 || (d.ldx * es) % 16 || (d.ldw * es) % 16 || d.ldx < d.K ||
-        d.ldw < d.K || d.ldy < d.N)
+        d.ldw < d.K || d.ldy < d.N || d.act < 0 || d.act > 3 || (d.res && d.Yh))
         return cudaErrorInvalidValue;
     if (d.batch > 1 && (d.x_row_b < 0 || d.x_col_b < 0 || d.w_row_b < 0 || d.w_col_b < 0 || d.y_batch < 0))
         return cudaErrorInvalidValue;
@@ -646,7 +666,7 @@ extern "C" int tpk_gemm(const void *X, int64_t ldx, const void *W, int64_t ldw, 
                         int dtype, const float *bias, float scale, int act, void *stream) {
     using namespace tpmd;
     if (dtype != TPMD_DTYPE_F32 && dtype != TPMD_DTYPE_F16) return tpk_fail("tpk_gemm: dtype");
-    if (act < 0 || act > 2) return tpk_fail("tpk_gemm: act");
+    if (act < 0 || act > 3) return tpk_fail("tpk_gemm: act");
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return tpk_fail("tpk_gemm: no device");
     int *flag_d = nullptr;

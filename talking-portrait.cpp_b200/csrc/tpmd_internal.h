@@ -125,8 +125,9 @@ struct enc_conv_params {
     int lrelu;             // leaky relu 0.2 after the bias
     const float *res;      // [OH][OW][OC] added last, or nullptr (may alias y)
     float *y;              // [OH][OW][OC]
-    float *part;           // split-K partial sums (nullptr: no split)
-    int64_t part_floats;   // its capacity
+    float *col;            // im2col workspace [OH*OW][K*K*IC]
+    int64_t col_floats;    // its capacity
+    int *err;              // the GEMM's expired-wait flag
 };
 struct enc_head_params {
     const float *W[5], *b[5];  // EqualLinears, [out][512]
@@ -136,7 +137,8 @@ cudaError_t launch_enc_stem(const float *img, const float *w, const float *b, fl
 cudaError_t launch_enc_conv(const enc_conv_params &p, cudaStream_t st);
 cudaError_t launch_enc_blur(const float *x, int IH, int IW, int C, const float *k4, int p0, int p1, float *y,
                             cudaStream_t st);
-cudaError_t launch_enc_head(const float *app, const enc_head_params &h, float *lam, float *motion,
+// scratch: 1024 floats (the fc chain's intermediate rows)
+cudaError_t launch_enc_head(const float *app, const enc_head_params &h, float *lam, float *motion, float *scratch,
                             cudaStream_t st);
 // f32 channel-last feats -> the decoder's feats storage (f16 or f32)
 cudaError_t launch_convert_feats(const float *src, int64_t n, bool f16, void *dst, cudaStream_t st);
@@ -151,7 +153,7 @@ cudaError_t launch_chw_to_rgb24(const float *chw, int64_t n, int64_t hw, uint8_t
 int tpk_fail(const std::string &msg);
 
 // The tcgen05 GEMM of the sampler and the audio encoder (kernels_gemm_tc.cu):
-//   Y[m][n] = act((sum_k X[m][k] W[n][k] + bias[n]) * scale), m < M, n < N
+//   Y[m][n] = act((sum_k X[m][k] W[n][k] + bias[n]) * scale) (+ res[m][n]), m < M, n < N
 // X and W K-major with row strides ldx, ldw (elements, 16-byte multiples);
 // f32 operands by the three-pass TF32 split, else f16. Batch b (grid z)
 // reads X at row b*x_row_b, column b*x_col_b (W likewise) and writes Y (or
@@ -170,7 +172,8 @@ struct gemm_desc {
     int x_row_b = 0, x_col_b = 0, w_row_b = 0, w_col_b = 0;
     const float *bias = nullptr;
     float scale = 1.0f;
-    int act = 0;  // 0 none, 1 GELU (erf), 2 GELU (tanh)
+    int act = 0;  // 0 none, 1 GELU (erf), 2 GELU (tanh), 3 leaky ReLU (0.2)
+    const float *res = nullptr;  // f32 output only: added after act, laid out as Y (may alias Y)
     int *err = nullptr;  // set when a bounded wait expires
     // launched as a programmatic dependent (launch_pdl rules); with w_const
     // W is not written by the kernels before it, so its first tiles load

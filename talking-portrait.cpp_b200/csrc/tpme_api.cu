@@ -1,8 +1,9 @@
 // Motion encoder C ABI (include/tpme.h): the host orchestration of
 // motion_enc::run (src/motion_enc.cpp:46-184) over the kernels in
-// kernels_enc.cu. One stream; a fixed device workspace sized for the
-// 512x512 input; the pyramid stays on the device after a run so the decoder
-// can take it directly (tpmd_set_feats_device).
+// kernels_enc.cu (its convs: im2col + the library's tcgen05 GEMM, f32
+// operands by the three-pass TF32 split). One stream; a fixed device
+// workspace sized for the 512x512 input; the pyramid stays on the device
+// after a run so the decoder can take it directly (tpmd_set_feats_device).
 #include <cuda_runtime.h>
 
 #include <cstdio>
@@ -64,7 +65,8 @@ void to_tap_major(const float *w, int OC, int IC, int K, float *out) {
 
 }  // namespace
 
-constexpr size_t PART_FLOATS = (size_t) 4 << 20;  // 16 MB
+// the largest im2col: block 1's first conv, 512 x 512 pixels x 9 taps x 32 channels
+constexpr size_t COL_FLOATS = (size_t) 512 * 512 * 9 * 32;
 
 struct tpme_ctx {
     int device = 0;
@@ -79,7 +81,8 @@ struct tpme_ctx {
     void *ws = nullptr;
     float *img = nullptr, *pyr[8] = {nullptr}, *x1 = nullptr, *xb = nullptr, *sb = nullptr;
     float *app = nullptr, *lam = nullptr, *mot = nullptr;
-    float *part = nullptr;  // split-K partial sums (PART_FLOATS)
+    float *col = nullptr;  // im2col rows of the current conv (COL_FLOATS)
+    int *gerr = nullptr;   // the GEMMs' expired-wait flag
 
     bool fail(const std::string &m) {
         err = m;
@@ -95,6 +98,7 @@ struct tpme_ctx {
     ~tpme_ctx() {
         if (device >= 0) cudaSetDevice(device);
         if (ws) cudaFree(ws);
+        if (gerr) cudaFree(gerr);
         if (warena) cudaFree(warena);
         if (stream) cudaStreamDestroy(stream);
     }
@@ -129,7 +133,7 @@ tpme_ctx *tpme_create(int device) {
     sizes[k++] = 512;
     sizes[k++] = 32;
     sizes[k++] = 512;
-    sizes[k++] = PART_FLOATS;  // split-K partial sums of the deep convs
+    sizes[k++] = COL_FLOATS;  // im2col rows
     size_t offs[16];
     for (int i = 0; i < k; i++) {
         offs[i] = total;
@@ -137,7 +141,9 @@ tpme_ctx *tpme_create(int device) {
     }
     bool ok = c->ck(cudaSetDevice(device), "cudaSetDevice") &&
               c->ck(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking), "stream") &&
-              c->ck(cudaMalloc(&c->ws, total * 4), "cudaMalloc(encoder workspace)");
+              c->ck(cudaMalloc(&c->ws, total * 4), "cudaMalloc(encoder workspace)") &&
+              c->ck(cudaMalloc(&c->gerr, sizeof(int)), "cudaMalloc(GEMM flag)") &&
+              c->ck(cudaMemset(c->gerr, 0, sizeof(int)), "cudaMemset(GEMM flag)") && c->ck(gemm_tc_prepare(), "GEMM set-up");
     if (!ok) {
         g_create_err = c->err;
         delete c;
@@ -153,7 +159,7 @@ tpme_ctx *tpme_create(int device) {
     c->app = b + offs[i++];
     c->lam = b + offs[i++];
     c->mot = b + offs[i++];
-    c->part = b + offs[i++];
+    c->col = b + offs[i++];
     return c;
 }
 
@@ -265,7 +271,7 @@ int tpme_run(tpme_ctx *c, const float *image, float *appearance, float *lambda, 
             return c->W(nm);
         };
         enc_conv_params p{};
-        p.part = c->part, p.part_floats = PART_FLOATS;
+        p.col = c->col, p.col_floats = COL_FLOATS, p.err = c->gerr;
         // conv1: 3x3 pad 1 + FusedLeakyReLU -> x1
         p.x = c->pyr[i - 1], p.IH = H, p.IW = H, p.IC = C;
         p.w = T("conv1.0.weight"), p.OC = C, p.K = 3, p.stride = 1, p.pad = 1, p.OH = H, p.OW = H;
@@ -288,7 +294,7 @@ int tpme_run(tpme_ctx *c, const float *image, float *appearance, float *lambda, 
     }
     // 4x4 valid conv -> appearance; fc chain and motion
     enc_conv_params p{};
-    p.part = c->part, p.part_floats = PART_FLOATS;
+    p.col = c->col, p.col_floats = COL_FLOATS, p.err = c->gerr;
     p.x = c->pyr[7], p.IH = 4, p.IW = 4, p.IC = 512;
     p.w = c->W("enc.net_app.convs.8.weight"), p.OC = 512, p.K = 4, p.stride = 1, p.pad = 0, p.OH = 1, p.OW = 1;
     p.y = c->app;
@@ -301,7 +307,7 @@ int tpme_run(tpme_ctx *c, const float *image, float *appearance, float *lambda, 
         hp.b[l] = c->W(nm);
     }
     hp.Q = c->W("dec.direction.Q");
-    if (!K(launch_enc_head(c->app, hp, c->lam, c->mot, st), "encoder head")) return -1;
+    if (!K(launch_enc_head(c->app, hp, c->lam, c->mot, c->col, st), "encoder head")) return -1;
     if ((appearance && !K(cudaMemcpyAsync(appearance, c->app, 512 * 4, cudaMemcpyDeviceToHost, st), "D2H")) ||
         (lambda && !K(cudaMemcpyAsync(lambda, c->lam, 20 * 4, cudaMemcpyDeviceToHost, st), "D2H")) ||
         (motion && !K(cudaMemcpyAsync(motion, c->mot, 512 * 4, cudaMemcpyDeviceToHost, st), "D2H")))
@@ -314,6 +320,12 @@ int tpme_run(tpme_ctx *c, const float *image, float *appearance, float *lambda, 
             return -1;
     }
     if (!K(cudaStreamSynchronize(st), "encoder run")) return -1;
+    int flag = 0;
+    if (!K(cudaMemcpy(&flag, c->gerr, sizeof flag, cudaMemcpyDeviceToHost), "GEMM status")) return -1;
+    if (flag) {
+        cudaMemset(c->gerr, 0, sizeof(int));
+        return c->fail("encoder: a GEMM pipeline wait timed out"), -1;
+    }
     c->ran = true;
     return 0;
 }
