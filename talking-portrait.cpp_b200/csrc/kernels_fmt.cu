@@ -227,6 +227,86 @@ __global__ void __launch_bounds__(256) res_norm_kernel(float *__restrict__ x, co
     }
 }
 
+// res_norm_kernel with one warp per row for H = 128 NV: each lane holds NV
+// float4 groups (columns 4 lane + 128 j); every load of the row (x, o and
+// its bias, both modulations) goes out before the first use, the sums are
+// warp shuffles in a fixed order, no block barrier
+template <typename TIN, int NV>
+__global__ void __launch_bounds__(256) res_norm_warp_kernel(float *__restrict__ x, const float *__restrict__ o,
+                                                            const float *__restrict__ bo,
+                                                            const float *__restrict__ mod,
+                                                            const float *__restrict__ bmod, int mod_stride,
+                                                            int gate_off, int M, float eps,
+                                                            const float *__restrict__ mod2,
+                                                            const float *__restrict__ bmod2, int shift_off,
+                                                            int scale_off, TIN *__restrict__ h) {
+    pdl_wait();
+    pdl_trigger();
+    constexpr int H = 128 * NV;
+    const int lane = threadIdx.x & 31, m = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (m >= M) return;
+    float4 *r4 = reinterpret_cast<float4 *>(x + (int64_t) m * H);
+    const float4 *o4 = reinterpret_cast<const float4 *>(o + (int64_t) m * H);
+    const float4 *g4 = reinterpret_cast<const float4 *>(mod + (int64_t) m * mod_stride + gate_off);
+    const float4 *s4 = reinterpret_cast<const float4 *>(mod2 + (int64_t) m * mod_stride + scale_off);
+    const float4 *t4 = reinterpret_cast<const float4 *>(mod2 + (int64_t) m * mod_stride + shift_off);
+    const float4 *bo4 = reinterpret_cast<const float4 *>(bo);
+    const float4 *bg4 = reinterpret_cast<const float4 *>(bmod + gate_off);
+    const float4 *bs4 = reinterpret_cast<const float4 *>(bmod2 + scale_off);
+    const float4 *bt4 = reinterpret_cast<const float4 *>(bmod2 + shift_off);
+    float4 xv[NV], ov[NV], gv[NV], sv[NV], tv[NV];
+#pragma unroll
+    for (int j = 0; j < NV; j++) {
+        const int q = lane + 32 * j;
+        xv[j] = r4[q];
+        ov[j] = o4[q];
+        gv[j] = g4[q];
+        sv[j] = s4[q];
+        tv[j] = t4[q];
+    }
+    float s = 0.0f;
+#pragma unroll
+    for (int j = 0; j < NV; j++) {
+        const int q = lane + 32 * j;
+        const float4 b = __ldg(bo4 + q), bg = __ldg(bg4 + q);
+        xv[j].x += (gv[j].x + bg.x) * (ov[j].x + b.x);
+        xv[j].y += (gv[j].y + bg.y) * (ov[j].y + b.y);
+        xv[j].z += (gv[j].z + bg.z) * (ov[j].z + b.z);
+        xv[j].w += (gv[j].w + bg.w) * (ov[j].w + b.w);
+        r4[q] = xv[j];
+        s += xv[j].x + xv[j].y + xv[j].z + xv[j].w;
+    }
+#pragma unroll
+    for (int w = 16; w > 0; w >>= 1) s += __shfl_xor_sync(0xffffffffu, s, w);
+    const float mean = s / (float) H;
+    float qs = 0.0f;
+#pragma unroll
+    for (int j = 0; j < NV; j++) {
+        const float a = xv[j].x - mean, b = xv[j].y - mean, c = xv[j].z - mean, d = xv[j].w - mean;
+        qs = fmaf(a, a, qs);
+        qs = fmaf(b, b, qs);
+        qs = fmaf(c, c, qs);
+        qs = fmaf(d, d, qs);
+    }
+#pragma unroll
+    for (int w = 16; w > 0; w >>= 1) qs += __shfl_xor_sync(0xffffffffu, qs, w);
+    const float inv = 1.0f / sqrtf(qs / (float) H + eps);
+#pragma unroll
+    for (int j = 0; j < NV; j++) {
+        const int q = lane + 32 * j;
+        const float4 bs = __ldg(bs4 + q), bt = __ldg(bt4 + q);
+        float v[4] = {(xv[j].x - mean) * inv, (xv[j].y - mean) * inv, (xv[j].z - mean) * inv,
+                      (xv[j].w - mean) * inv};
+        const float sc[4] = {sv[j].x + bs.x, sv[j].y + bs.y, sv[j].z + bs.z, sv[j].w + bs.w};
+        const float sh[4] = {tv[j].x + bt.x, tv[j].y + bt.y, tv[j].z + bt.z, tv[j].w + bt.w};
+#pragma unroll
+        for (int e = 0; e < 4; e++) v[e] = v[e] * sc[e] + v[e] + sh[e];
+        TIN *hp = h + (int64_t) m * H + 4 * q;
+#pragma unroll
+        for (int e = 0; e < 4; e++) hp[e] = cvt<TIN>(v[e]);
+    }
+}
+
 // v = out + b; per current frame f: vc = (u + a_cfg (a - u)) + e_cfg (fu - a);
 // x[f] += dt * vc; the next forward's x60 rows P.. are the new x (and their
 // f16 copy, the next x_embedder GEMM's input, when x60h is given)
@@ -312,6 +392,17 @@ cudaError_t fmt_res_norm(bool f16, float *x, const float *o, const float *bo, co
                          int mod_stride, int gate_off, int M, int H, float eps, const float *mod2, const float *bmod2,
                          int shift_off, int scale_off, void *h, cudaStream_t st) {
     if (H > RN_PER_THREAD * 256) return cudaErrorInvalidValue;
+    const bool al = !(((uintptr_t) x | (uintptr_t) o | (uintptr_t) bo | (uintptr_t) mod | (uintptr_t) bmod |
+                       (uintptr_t) mod2 | (uintptr_t) bmod2) & 15) &&
+                    mod_stride % 4 == 0 && gate_off % 4 == 0 && shift_off % 4 == 0 && scale_off % 4 == 0;
+    if (H == 1024 && al) {  // the sampler's width: a warp per row
+        const dim3 g((M * 32 + 255) / 256);
+        if (f16)
+            return launch_pdl(res_norm_warp_kernel<__half, 8>, g, dim3(256), 0, st, x, o, bo, mod, bmod, mod_stride,
+                              gate_off, M, eps, mod2, bmod2, shift_off, scale_off, (__half *) h);
+        return launch_pdl(res_norm_warp_kernel<float, 8>, g, dim3(256), 0, st, x, o, bo, mod, bmod, mod_stride, gate_off,
+                          M, eps, mod2, bmod2, shift_off, scale_off, (float *) h);
+    }
     if (f16)
         return launch_pdl(res_norm_kernel<__half>, dim3(M), dim3(256), 0, st, x, o, bo, mod, bmod, mod_stride,
                           gate_off, H, eps, mod2, bmod2, shift_off, scale_off, (__half *) h);
