@@ -4,8 +4,8 @@
 // m = b*T + f of the three CFG branches b (uncond, full, audio-only) and T
 // frames; every activation is row-major [M][width] float32 unless it feeds a
 // GEMM, where it is written in the GEMM's input type TIN (float or __half).
-// GEMMs other than the MLP's first (bias and GELU in its epilogue) run
-// without bias; the kernel consuming their output adds it.
+// The block linears add their bias in the GEMM epilogue (fc1 also GELU);
+// the kernel consuming the other GEMMs' output adds their bias.
 #include "tpmd_internal.h"
 
 #include <algorithm>
@@ -108,12 +108,13 @@ __global__ void __launch_bounds__(256) norm_mod_kernel(float *__restrict__ x, in
 // banded self-attention per (branch, head, query row i): keys j with
 // |i - j| <= window (the additive -inf mask elsewhere contributes nothing),
 // scores q.k / sqrt(hd), softmax, weighted sum of v. One warp per query;
-// qkv = GEMM output + bias, row m = [q | k | v] of width 3H. Every q, k and
+// qkv = the GEMM output (bias added in its epilogue), row m = [q | k | v] of
+// width 3H. Every q, k and
 // v element the warp needs is loaded up front (EPL per lane and row, MAXJ
 // keys at most), so the band costs one memory round trip.
 template <typename TIN, int EPL, int MAXJ>
-__global__ void __launch_bounds__(128) attn_kernel(const float *__restrict__ qkv, const float *__restrict__ bqkv,
-                                                   int T, int H, int nh, int window, TIN *__restrict__ out) {
+__global__ void __launch_bounds__(128) attn_kernel(const float *__restrict__ qkv, int T, int H, int nh, int window,
+                                                   TIN *__restrict__ out) {
     pdl_wait();
     pdl_trigger();
     const int lane = threadIdx.x & 31;
@@ -128,7 +129,7 @@ __global__ void __launch_bounds__(128) attn_kernel(const float *__restrict__ qkv
 #pragma unroll
     for (int e = 0; e < EPL; e++) {
         const int d = lane + 32 * e;
-        q[e] = d < hd ? base[(int64_t) i * 3 * H + d] + __ldg(bqkv + head * hd + d) : 0.0f;
+        q[e] = d < hd ? base[(int64_t) i * 3 * H + d] : 0.0f;
     }
 #pragma unroll
     for (int jj = 0; jj < MAXJ; jj++)
@@ -137,8 +138,8 @@ __global__ void __launch_bounds__(128) attn_kernel(const float *__restrict__ qkv
             const int d = lane + 32 * e;
             const bool in = jj < nj && d < hd;
             const float *row = base + (int64_t) (j0 + jj) * 3 * H;
-            k[jj][e] = in ? row[H + d] + __ldg(bqkv + H + head * hd + d) : 0.0f;
-            v[jj][e] = in ? row[2 * H + d] + __ldg(bqkv + 2 * H + head * hd + d) : 0.0f;
+            k[jj][e] = in ? row[H + d] : 0.0f;
+            v[jj][e] = in ? row[2 * H + d] : 0.0f;
         }
     float sc[MAXJ];
     float mx = -INFINITY;
@@ -168,14 +169,15 @@ __global__ void __launch_bounds__(128) attn_kernel(const float *__restrict__ qkv
 }
 
 // the gated residual of one sub-block followed by the next layer norm, per
-// row: x += (mod[gate] + bmod[gate]) * (o + bo), then h = LN(x) * (1 + scale)
+// row: x += (mod[gate] + bmod[gate]) * o (o: the GEMM output, its bias added
+// in the GEMM epilogue), then h = LN(x) * (1 + scale)
 // + shift with the next norm's modulation (mod2, bmod2). Each element and
 // each sum is formed in the same order as a separate residual update then
 // norm_mod_kernel would form them.
 constexpr int RN_PER_THREAD = 16;  // H <= 16 x blockDim
 template <typename TIN>
 __global__ void __launch_bounds__(256) res_norm_kernel(float *__restrict__ x, const float *__restrict__ o,
-                                                       const float *__restrict__ bo, const float *__restrict__ mod,
+                                                       const float *__restrict__ mod,
                                                        const float *__restrict__ bmod, int mod_stride, int gate_off,
                                                        int H, float eps, const float *__restrict__ mod2,
                                                        const float *__restrict__ bmod2, int shift_off, int scale_off,
@@ -199,7 +201,7 @@ __global__ void __launch_bounds__(256) res_norm_kernel(float *__restrict__ x, co
             scv[k] = md2[scale_off + i] + __ldg(bmod2 + scale_off + i);
             shv[k] = md2[shift_off + i] + __ldg(bmod2 + shift_off + i);
             const float g = md[gate_off + i] + __ldg(bmod + gate_off + i);
-            const float v = r[i] + g * (orow[i] + __ldg(bo + i));
+            const float v = r[i] + g * orow[i];
             r[i] = v;
             xv[k] = v;
             s += v;
@@ -228,12 +230,11 @@ __global__ void __launch_bounds__(256) res_norm_kernel(float *__restrict__ x, co
 }
 
 // res_norm_kernel with one warp per row for H = 128 NV: each lane holds NV
-// float4 groups (columns 4 lane + 128 j); every load of the row (x, o and
-// its bias, both modulations) goes out before the first use, the sums are
-// warp shuffles in a fixed order, no block barrier
+// float4 groups (columns 4 lane + 128 j); every load of the row (x, o, both
+// modulations) goes out before the first use, the sums are warp shuffles in
+// a fixed order, no block barrier
 template <typename TIN, int NV>
 __global__ void __launch_bounds__(256) res_norm_warp_kernel(float *__restrict__ x, const float *__restrict__ o,
-                                                            const float *__restrict__ bo,
                                                             const float *__restrict__ mod,
                                                             const float *__restrict__ bmod, int mod_stride,
                                                             int gate_off, int M, float eps,
@@ -250,7 +251,6 @@ __global__ void __launch_bounds__(256) res_norm_warp_kernel(float *__restrict__ 
     const float4 *g4 = reinterpret_cast<const float4 *>(mod + (int64_t) m * mod_stride + gate_off);
     const float4 *s4 = reinterpret_cast<const float4 *>(mod2 + (int64_t) m * mod_stride + scale_off);
     const float4 *t4 = reinterpret_cast<const float4 *>(mod2 + (int64_t) m * mod_stride + shift_off);
-    const float4 *bo4 = reinterpret_cast<const float4 *>(bo);
     const float4 *bg4 = reinterpret_cast<const float4 *>(bmod + gate_off);
     const float4 *bs4 = reinterpret_cast<const float4 *>(bmod2 + scale_off);
     const float4 *bt4 = reinterpret_cast<const float4 *>(bmod2 + shift_off);
@@ -268,11 +268,11 @@ __global__ void __launch_bounds__(256) res_norm_warp_kernel(float *__restrict__ 
 #pragma unroll
     for (int j = 0; j < NV; j++) {
         const int q = lane + 32 * j;
-        const float4 b = __ldg(bo4 + q), bg = __ldg(bg4 + q);
-        xv[j].x += (gv[j].x + bg.x) * (ov[j].x + b.x);
-        xv[j].y += (gv[j].y + bg.y) * (ov[j].y + b.y);
-        xv[j].z += (gv[j].z + bg.z) * (ov[j].z + b.z);
-        xv[j].w += (gv[j].w + bg.w) * (ov[j].w + b.w);
+        const float4 bg = __ldg(bg4 + q);
+        xv[j].x += (gv[j].x + bg.x) * ov[j].x;
+        xv[j].y += (gv[j].y + bg.y) * ov[j].y;
+        xv[j].z += (gv[j].z + bg.z) * ov[j].z;
+        xv[j].w += (gv[j].w + bg.w) * ov[j].w;
         r4[q] = xv[j];
         s += xv[j].x + xv[j].y + xv[j].z + xv[j].w;
     }
@@ -372,8 +372,7 @@ cudaError_t fmt_norm_mod(bool f16, float *x, int M, int H, float eps, const floa
     return launch_pdl(norm_mod_kernel<float>, dim3(M), dim3(256), 0, st, x, H, eps, mod, bmod, mod_stride, shift_off,
                       scale_off, (float *) h, x1, bx, pos, T);
 }
-cudaError_t fmt_attn(bool f16, const float *qkv, const float *bqkv, int T, int H, int nh, int window, void *out,
-                     cudaStream_t st) {
+cudaError_t fmt_attn(bool f16, const float *qkv, int T, int H, int nh, int window, void *out, cudaStream_t st) {
     if (2 * window + 1 > 16 || H % nh) return cudaErrorInvalidValue;
     // 128-thread blocks: the 3 nh T warps fit the SMs in one wave
     const dim3 g((3 * nh * T * 32 + 127) / 128);
@@ -381,32 +380,32 @@ cudaError_t fmt_attn(bool f16, const float *qkv, const float *bqkv, int T, int H
     if (hd > 128) return cudaErrorInvalidValue;
     if (hd <= 64 && window <= 2) {  // the sampler's band of five keys
         if (f16)
-            return launch_pdl(attn_kernel<__half, 2, 5>, g, dim3(128), 0, st, qkv, bqkv, T, H, nh, window, (__half *) out);
-        return launch_pdl(attn_kernel<float, 2, 5>, g, dim3(128), 0, st, qkv, bqkv, T, H, nh, window, (float *) out);
+            return launch_pdl(attn_kernel<__half, 2, 5>, g, dim3(128), 0, st, qkv, T, H, nh, window, (__half *) out);
+        return launch_pdl(attn_kernel<float, 2, 5>, g, dim3(128), 0, st, qkv, T, H, nh, window, (float *) out);
     }
     if (f16)
-        return launch_pdl(attn_kernel<__half, 4, 16>, g, dim3(128), 0, st, qkv, bqkv, T, H, nh, window, (__half *) out);
-    return launch_pdl(attn_kernel<float, 4, 16>, g, dim3(128), 0, st, qkv, bqkv, T, H, nh, window, (float *) out);
+        return launch_pdl(attn_kernel<__half, 4, 16>, g, dim3(128), 0, st, qkv, T, H, nh, window, (__half *) out);
+    return launch_pdl(attn_kernel<float, 4, 16>, g, dim3(128), 0, st, qkv, T, H, nh, window, (float *) out);
 }
-cudaError_t fmt_res_norm(bool f16, float *x, const float *o, const float *bo, const float *mod, const float *bmod,
+cudaError_t fmt_res_norm(bool f16, float *x, const float *o, const float *mod, const float *bmod,
                          int mod_stride, int gate_off, int M, int H, float eps, const float *mod2, const float *bmod2,
                          int shift_off, int scale_off, void *h, cudaStream_t st) {
     if (H > RN_PER_THREAD * 256) return cudaErrorInvalidValue;
-    const bool al = !(((uintptr_t) x | (uintptr_t) o | (uintptr_t) bo | (uintptr_t) mod | (uintptr_t) bmod |
+    const bool al = !(((uintptr_t) x | (uintptr_t) o | (uintptr_t) mod | (uintptr_t) bmod |
                        (uintptr_t) mod2 | (uintptr_t) bmod2) & 15) &&
                     mod_stride % 4 == 0 && gate_off % 4 == 0 && shift_off % 4 == 0 && scale_off % 4 == 0;
     if (H == 1024 && al) {  // the sampler's width: a warp per row
         const dim3 g((M * 32 + 255) / 256);
         if (f16)
-            return launch_pdl(res_norm_warp_kernel<__half, 8>, g, dim3(256), 0, st, x, o, bo, mod, bmod, mod_stride,
+            return launch_pdl(res_norm_warp_kernel<__half, 8>, g, dim3(256), 0, st, x, o, mod, bmod, mod_stride,
                               gate_off, M, eps, mod2, bmod2, shift_off, scale_off, (__half *) h);
-        return launch_pdl(res_norm_warp_kernel<float, 8>, g, dim3(256), 0, st, x, o, bo, mod, bmod, mod_stride, gate_off,
+        return launch_pdl(res_norm_warp_kernel<float, 8>, g, dim3(256), 0, st, x, o, mod, bmod, mod_stride, gate_off,
                           M, eps, mod2, bmod2, shift_off, scale_off, (float *) h);
     }
     if (f16)
-        return launch_pdl(res_norm_kernel<__half>, dim3(M), dim3(256), 0, st, x, o, bo, mod, bmod, mod_stride,
+        return launch_pdl(res_norm_kernel<__half>, dim3(M), dim3(256), 0, st, x, o, mod, bmod, mod_stride,
                           gate_off, H, eps, mod2, bmod2, shift_off, scale_off, (__half *) h);
-    return launch_pdl(res_norm_kernel<float>, dim3(M), dim3(256), 0, st, x, o, bo, mod, bmod, mod_stride, gate_off, H,
+    return launch_pdl(res_norm_kernel<float>, dim3(M), dim3(256), 0, st, x, o, mod, bmod, mod_stride, gate_off, H,
                       eps, mod2, bmod2, shift_off, scale_off, (float *) h);
 }
 cudaError_t fmt_cfg_euler(const float *vout, const float *bv, int T, int P, int D, float a_cfg, float e_cfg,

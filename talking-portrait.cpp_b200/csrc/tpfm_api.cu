@@ -2,12 +2,12 @@
 // (src/fmt.cpp:64-211) and sample_chunk_ex (src/pipeline.cpp:15-91). The
 // plain linears run on the library's tcgen05 GEMM (kernels_gemm_tc.cu;
 // row-major Y[M][N] = X[M][K] W[N][K]^T): f16 operands in the f16 mode, the
-// three-pass TF32 split in the f32 mode. The MLP's first linear adds its
-// bias and applies GELU in the GEMM epilogue; the other GEMMs run without
-// bias and the kernel consuming their output adds it. The adaLN
-// modulations of all blocks and of the final layer depend only on the
-// conditioning, so one GEMM per forward computes them together (their
-// weights are contiguous in the arena). Norms, banded attention, gated
+// three-pass TF32 split in the f32 mode. The block linears add their bias
+// in the GEMM epilogue (fc1 also applies GELU); the embedding, adaLN and
+// output linears run without bias and the kernel consuming their output
+// adds it. The adaLN modulations of all blocks and of the final layer depend
+// only on the conditioning, so one GEMM per forward computes them together
+// (their weights are contiguous in the arena). Norms, banded attention, gated
 // residuals and the CFG/Euler update are the kernels of kernels_fmt.cu. A
 // chunk's nine forwards run as one captured CUDA graph.
 #include <cuda_runtime.h>
@@ -32,9 +32,8 @@ cudaError_t fmt_norm_mod(bool f16, float *x, int M, int H, float eps, const floa
                          int mod_stride, int shift_off, int scale_off, void *h, cudaStream_t st,
                          const float *x1 = nullptr, const float *bx = nullptr, const float *pos = nullptr,
                          int T = 0);
-cudaError_t fmt_attn(bool f16, const float *qkv, const float *bqkv, int T, int H, int nh, int window, void *out,
-                     cudaStream_t st);
-cudaError_t fmt_res_norm(bool f16, float *x, const float *o, const float *bo, const float *mod, const float *bmod,
+cudaError_t fmt_attn(bool f16, const float *qkv, int T, int H, int nh, int window, void *out, cudaStream_t st);
+cudaError_t fmt_res_norm(bool f16, float *x, const float *o, const float *mod, const float *bmod,
                          int mod_stride, int gate_off, int M, int H, float eps, const float *mod2, const float *bmod2,
                          int shift_off, int scale_off, void *h, cudaStream_t st);
 cudaError_t fmt_cfg_euler(const float *vout, const float *bv, int T, int P, int D, float a_cfg, float e_cfg,
@@ -112,8 +111,8 @@ struct tpfm_ctx {
         d.pdl = d.w_const = true;  // W: weights; the forward's kernels are programmatic dependents
         return ck(gemm_tc(d, stream), what);
     }
-    bool gemm(const void *X, int Mr, int K, const std::string &wname, int N, float *Y) {
-        return gemm_w(X, Mr, K, K, Wt(wname), ldk.at(wname), N, Y, wname.c_str());
+    bool gemm(const void *X, int Mr, int K, const std::string &wname, int N, float *Y, const float *bias = nullptr) {
+        return gemm_w(X, Mr, K, K, Wt(wname), ldk.at(wname), N, Y, wname.c_str(), bias);
     }
     // after a synchronize: a GEMM whose pipeline wait expired
     bool gemm_status() {
@@ -222,19 +221,18 @@ bool forward_device(tpfm_ctx *c, int s, bool in_chunk = false) {
         const float *md2 = c->mod + (size_t) (l + 1) * 6 * H;
         const float *bmod2 = last ? c->F("decoder.adaLN_modulation.1.bias")
                                   : c->F("blocks." + std::to_string(l + 1) + ".adaLN_modulation.1.bias");
-        if (!c->gemm(c->h, M, H, b + "attn.qkv.weight", 3 * H, c->qkv) ||
-            !K(fmt_attn(h16, c->qkv, c->F(b + "attn.qkv.bias"), T, H, c->c.n_heads, c->c.attn_window, c->att, st),
-               "attention") ||
-            !c->gemm(c->att, M, H, b + "attn.proj.weight", H, c->o) ||
-            !K(fmt_res_norm(h16, c->x, c->o, c->F(b + "attn.proj.bias"), md, bmod, NM, 2 * H, M, H, eps, md, bmod,
+        if (!c->gemm(c->h, M, H, b + "attn.qkv.weight", 3 * H, c->qkv, c->F(b + "attn.qkv.bias")) ||
+            !K(fmt_attn(h16, c->qkv, T, H, c->c.n_heads, c->c.attn_window, c->att, st), "attention") ||
+            !c->gemm(c->att, M, H, b + "attn.proj.weight", H, c->o, c->F(b + "attn.proj.bias")) ||
+            !K(fmt_res_norm(h16, c->x, c->o, md, bmod, NM, 2 * H, M, H, eps, md, bmod,
                             3 * H, 4 * H, c->h, st),
                "residual + norm") ||
             // m1 = gelu_tanh(h fc1^T + bias), in the GEMM input type
             !c->gemm_w(c->h, M, H, H, c->Wt(b + "mlp.fc1.weight"), c->ldk.at(b + "mlp.fc1.weight"), FF,
                        h16 ? nullptr : (float *) c->m1, "mlp.fc1", c->F(b + "mlp.fc1.bias"), 2,
                        h16 ? (__half *) c->m1 : nullptr) ||
-            !c->gemm(c->m1, M, FF, b + "mlp.fc2.weight", H, c->o) ||
-            !K(fmt_res_norm(h16, c->x, c->o, c->F(b + "mlp.fc2.bias"), md, bmod, NM, 5 * H, M, H, eps, md2, bmod2, 0,
+            !c->gemm(c->m1, M, FF, b + "mlp.fc2.weight", H, c->o, c->F(b + "mlp.fc2.bias")) ||
+            !K(fmt_res_norm(h16, c->x, c->o, md, bmod, NM, 5 * H, M, H, eps, md2, bmod2, 0,
                             H, c->h, st),
                "residual + norm"))
             return false;
