@@ -77,8 +77,21 @@ struct graph_entry {
     int64_t nb;
     const void *styles;
     void *out;
+    int last;           // last level enqueued
+    const void *split;  // split_in::trunk of a tail-levels chunk, else null
     cudaGraphExec_t exec;
 };
+
+// The inputs of a chunk that runs only the last two levels (r256, r512) of
+// frames whose earlier levels ran in an earlier chunk: that chunk's r128
+// trunk and skip planes of the first frame of this one. The r256 trunk then
+// goes to the conv2 buffer (unused by the fused levels), so the earlier
+// chunk's trunk and skips stay intact for the chunks that follow.
+struct split_in {
+    const void *trunk;
+    const float *sf, *sk;
+};
+constexpr int SPLIT_LEVEL = N_LEVELS - 2;  // the first level of a tail-levels chunk
 
 }  // namespace
 
@@ -414,7 +427,8 @@ void derive_conv(tpmd_ctx *c, const conv_layout &L, std::vector<char> &img) {
         memcpy(img.data() + L.wg, g.data(), g.size() * 4);
 }
 
-bool run_chunk(tpmd_ctx *c, const float *styles, int64_t nb, float *out, cudaStream_t st);
+bool run_chunk(tpmd_ctx *c, const float *styles, int64_t nb, float *out, cudaStream_t st,
+               int last_level = N_LEVELS - 1, const split_in *in = nullptr, int64_t row0 = 0);
 
 }  // namespace
 
@@ -745,20 +759,27 @@ bool fused_level(const tpmd_ctx *c, int j) {
 }
 
 bool enqueue_chunk(tpmd_ctx *c, const ws_view &w, const float *styles, int64_t nb, float *out,
-                   cudaStream_t st, int last_level = N_LEVELS - 1, bool keep_conv2 = false) {
+                   cudaStream_t st, int last_level = N_LEVELS - 1, bool keep_conv2 = false,
+                   const split_in *in = nullptr) {
     const bool h = c->f16;
     const int B = (int) nb;
-    if (!launch(c, w.timed, "style", st, [&] {
+    // a tail-levels chunk: styles, denominators and levels up to r128 came from
+    // an earlier chunk (w.s_all / w.inv_den point at this chunk's first frame)
+    const int first = in ? SPLIT_LEVEL : 0;
+    if (in && (keep_conv2 || last_level != N_LEVELS - 1 || !fused_level(c, SPLIT_LEVEL) ||
+               !fused_level(c, N_LEVELS - 1)))
+        return c->fail("tail-levels chunk: needs the fused tcgen05 levels"), false;
+    if (!in && !launch(c, w.timed, "style", st, [&] {
             return launch_style(c->Wf(c->off_wmod), c->Wf(c->off_bmod), c->S_TOT, styles, B,
                                 w.s_all, st);
         }))
         return false;
-    if (!launch(c, w.timed, "den", st, [&] {
+    if (!in && !launch(c, w.timed, "den", st, [&] {
             return launch_den((const float *) c->warena, c->dtab, w.s_all, c->S_TOT, B,
                               w.inv_den, c->D_TOT, st);
         }))
         return false;
-    if (!launch(c, w.timed, "conv1_input", st, [&] {
+    if (!in && !launch(c, w.timed, "conv1_input", st, [&] {
             return launch_conv1_input(h, c->Wf(c->off_input), w.s_all + c->conv[0].s_off,
                                       c->S_TOT, B, w.actA, st);
         }))
@@ -792,12 +813,16 @@ bool enqueue_chunk(tpmd_ctx *c, const ws_view &w, const float *styles, int64_t n
         });
     };
     // conv1: 4x4 map, output x style of convs.0 -> trunk buffer
-    if (!conv(0, w.actA, w.actB, 4, w.s_all + c->conv[1].s_off)) return false;
-    for (int j = 0; j <= last_level; j++) {
+    if (!in && !conv(0, w.actA, w.actB, 4, w.s_all + c->conv[1].s_off)) return false;
+    // trunk ping-pong: the tail writes its trunk where the up-conv read it
+    // from (a tail-levels chunk: into the conv2 buffer)
+    void *trunk = in ? w.actA : w.actB;
+    for (int j = first; j <= last_level; j++) {
         const int r = 8 << j;
         const conv_layout &Lu = c->conv[1 + 2 * j], &Ld = c->conv[2 + 2 * j];
+        const bool split_first = in && j == first;
         // up-conv: trunk (x its style) -> c1 (x conv2's style)
-        if (!conv(1 + 2 * j, w.actB, w.actC, r / 2, w.s_all + Ld.s_off)) return false;
+        if (!conv(1 + 2 * j, split_first ? in->trunk : trunk, w.actC, r / 2, w.s_all + Ld.s_off)) return false;
         (void) Lu;
         const bool fused = fused_level(c, j);
         // conv2: c1 -> out (unscaled, read by the tail)
@@ -814,16 +839,16 @@ bool enqueue_chunk(tpmd_ctx *c, const ws_view &w, const float *styles, int64_t n
         t.s_stride = c->S_TOT;
         t.fb = c->Wf(S.fb);
         t.fup = c->Wf(S.fup);
-        t.skipf_prev = j == 0 ? nullptr : w.sf[(j - 1) & 1];
+        t.skipf_prev = split_first ? in->sf : j == 0 ? nullptr : w.sf[(j - 1) & 1];
         t.skipf_out = j == N_LEVELS - 1 ? nullptr : w.sf[j & 1];
         t.rW = c->Wf(S.rW);
         t.rlb = c->Wf(S.rlb);
         t.rb = c->Wf(S.rb);
         t.rup = c->Wf(S.rup);
-        t.skip_prev = j == 0 ? nullptr : w.sk[(j - 1) & 1];
+        t.skip_prev = split_first ? in->sk : j == 0 ? nullptr : w.sk[(j - 1) & 1];
         t.skip_out = j == N_LEVELS - 1 ? out : w.sk[j & 1];
         t.lin = c->Wf(S.lin);
-        t.trunk = j == N_LEVELS - 1 ? nullptr : w.actB;
+        t.trunk = j == N_LEVELS - 1 ? nullptr : trunk;
         t.snext = j == N_LEVELS - 1 ? nullptr : w.s_all + c->conv[3 + 2 * j].s_off;
         t.proj = c->proj + c->proj_off[j];
         if (fused) {
@@ -838,16 +863,26 @@ bool enqueue_chunk(tpmd_ctx *c, const ws_view &w, const float *styles, int64_t n
     return true;
 }
 
-bool run_chunk(tpmd_ctx *c, const float *styles, int64_t nb, float *out, cudaStream_t st) {
-    if (c->stall_ns) {  // the armed test hook runs once, outside any cached graph
-        ws_view w = ctx_ws(c);
+// One chunk: the whole decode of nb frames, or (last_level < the last) its
+// levels up to last_level, or (in != null) the tail levels of the frames
+// whose per-frame styles and denominators start at row row0 of the
+// workspace. Launched from a cached CUDA graph where possible.
+bool run_chunk(tpmd_ctx *c, const float *styles, int64_t nb, float *out, cudaStream_t st,
+               int last_level, const split_in *in, int64_t row0) {
+    ws_view w0 = ctx_ws(c);
+    w0.s_all += row0 * c->S_TOT;
+    w0.inv_den += row0 * c->D_TOT;
+    if (c->stall_ns && !in) {  // the armed test hook runs once, outside any cached graph
+        ws_view w = w0;
         w.stall_ns = c->stall_ns;
         c->stall_ns = 0;
-        return enqueue_chunk(c, w, styles, nb, out, st);
+        return enqueue_chunk(c, w, styles, nb, out, st, last_level);
     }
-    if (!c->use_graph || c->profiling) return enqueue_chunk(c, ctx_ws(c), styles, nb, out, st);
+    if (!c->use_graph || c->profiling) return enqueue_chunk(c, w0, styles, nb, out, st, last_level, false, in);
+    const void *split = in ? in->trunk : nullptr;
     for (auto it = c->graphs.begin(); it != c->graphs.end(); ++it) {
-        if (it->nb == nb && it->styles == styles && it->out == out) {
+        if (it->nb == nb && it->styles == styles && it->out == out && it->last == last_level &&
+            it->split == split) {
             c->graphs.splice(c->graphs.begin(), c->graphs, it);
             return c->ck(cudaGraphLaunch(c->graphs.front().exec, st), "cudaGraphLaunch");
         }
@@ -856,7 +891,7 @@ bool run_chunk(tpmd_ctx *c, const float *styles, int64_t nb, float *out, cudaStr
     if (!c->ck(cudaStreamBeginCapture(c->cap_stream, cudaStreamCaptureModeThreadLocal),
                "begin capture"))
         return false;
-    const bool ok = enqueue_chunk(c, ctx_ws(c), styles, nb, out, c->cap_stream);
+    const bool ok = enqueue_chunk(c, w0, styles, nb, out, c->cap_stream, last_level, false, in);
     const cudaError_t e = cudaStreamEndCapture(c->cap_stream, &g);
     if (!ok) {
         if (g) cudaGraphDestroy(g);
@@ -867,8 +902,8 @@ bool run_chunk(tpmd_ctx *c, const float *styles, int64_t nb, float *out, cudaStr
     const cudaError_t ie = cudaGraphInstantiate(&exec, g, 0);
     cudaGraphDestroy(g);
     if (!c->ck(ie, "cudaGraphInstantiate")) return false;
-    c->graphs.push_front({nb, styles, out, exec});
-    while (c->graphs.size() > 16) {
+    c->graphs.push_front({nb, styles, out, last_level, split, exec});
+    while (c->graphs.size() > 32) {
         cudaGraphExecDestroy(c->graphs.back().exec);
         c->graphs.pop_back();
     }
@@ -886,7 +921,9 @@ bool device_ok(tpmd_ctx *c) {
     return true;
 }
 
-// Sub-batches of a host decode. The frame copy (D2H) of one sub-batch
+// Sub-batches of a host decode on a handle without the split schedule below
+// (the FFMA path, fewer than four frames, or TPMD_SUBBATCH / TPMD_NO_SPLIT
+// set). The frame copy (D2H) of one sub-batch
 // overlaps the compute of the next, so only the last copy is exposed: whole
 // max_batch chunks first, then the last chunk split into shrinking parts
 // (ratio about 0.62, the copy/compute time ratio per frame with margin) so
@@ -910,6 +947,52 @@ std::vector<int64_t> sub_batch_plan(int64_t n, int64_t max_batch) {
         k = std::min<int64_t>(k, left - (parts - 1 - i));  // leave at least one frame per later part
         plan.push_back(k);
         left -= k;
+    }
+    return plan;
+}
+
+// The schedule of a host decode on a tcgen05 handle. A group's frames first
+// run the levels up to r128 together; the r256 and r512 levels then run in
+// parts, and each part's frames go to the host (second stream) while the
+// next part, or the next group, computes. Splitting only the last two
+// levels keeps the small, latency-bound early levels at the group's full
+// batch. Measured on one B200 (50-frame chunk): the levels up to r128 cost
+// about 0.30 ms + 36 us per frame, the r256 and r512 levels 43 us per frame
+// and the copy of an f32 frame 58 us, so the copies, not the compute, set
+// the pace of the tail levels. A chunk's last group therefore holds about a
+// quarter of its frames in parts of about three: its copies start while
+// the group computes and little is left to copy when the compute ends. The
+// other group starts with a small part so that copying starts early.
+struct group_plan {
+    int64_t f0, n;               // the group's frames within the call
+    std::vector<int64_t> parts;  // its tail-level parts, in order
+};
+
+std::vector<int64_t> equal_parts(int64_t total, int64_t k) {
+    k = std::max<int64_t>(1, std::min(k, total));
+    std::vector<int64_t> v;
+    for (int64_t i = 0; i < k; i++) v.push_back(total / k + (i < total % k ? 1 : 0));
+    return v;
+}
+
+std::vector<group_plan> split_plan(int64_t n, int64_t max_batch) {
+    std::vector<group_plan> plan;
+    auto lead = [](int64_t g, double first, int64_t k) {  // a small first part, then k equal ones
+        const int64_t f = std::min<int64_t>(g, std::max<int64_t>(1, std::llround(first * g)));
+        std::vector<int64_t> v{f};
+        if (g > f)
+            for (int64_t x : equal_parts(g - f, k)) v.push_back(x);
+        return v;
+    };
+    int64_t f0 = 0;
+    for (; n - f0 > max_batch; f0 += max_batch) plan.push_back({f0, max_batch, lead(max_batch, 0.21, 3)});
+    const int64_t m = n - f0;
+    if (m < 16) {
+        plan.push_back({f0, m, lead(m, 0.3, 2)});
+    } else {
+        const int64_t g2 = std::max<int64_t>(2, std::llround(0.24 * (double) m)), g1 = m - g2;
+        plan.push_back({f0, g1, lead(g1, 0.21, 3)});
+        plan.push_back({f0 + g1, g2, equal_parts(g2, std::max<int64_t>(1, std::llround((double) g2 / 3.0)))});
     }
     return plan;
 }
@@ -1033,6 +1116,44 @@ int host_decode(tpmd_ctx *c, const float *styles, int64_t n, void *out, bool rgb
     if (!c->ck(cudaSetDevice(c->device), "cudaSetDevice")) return -1;
     const size_t fsz = (size_t) 3 * IMG * IMG;
     const size_t osz = rgb ? fsz : fsz * 4;  // output bytes per frame
+    if (c->use_tc && n >= 4 && !getenv("TPMD_SUBBATCH") && !getenv("TPMD_NO_SPLIT")) {
+        // levels up to r128 per group, then the last two levels in parts
+        constexpr int rs = 8 << (SPLIT_LEVEL - 1);
+        const size_t tsz = (size_t) rs * rs * ST_OC[SPLIT_LEVEL - 1] * c->esz();  // r128 trunk bytes per frame
+        const size_t ssz = (size_t) 3 * rs * rs;                                   // skip floats per frame
+        const float *sf_in = c->sf[(SPLIT_LEVEL - 1) & 1], *sk_in = c->sk[(SPLIT_LEVEL - 1) & 1];
+        int k = 0;
+        for (const group_plan &g : split_plan(n, c->max_batch)) {
+            if (!c->ck(cudaMemcpyAsync(c->styles_d[k], styles + g.f0 * STYLE_DIM,
+                                       (size_t) g.n * STYLE_DIM * 4, cudaMemcpyHostToDevice, c->stream),
+                       "styles H2D") ||
+                !run_chunk(c, c->styles_d[k], g.n, nullptr, c->stream, SPLIT_LEVEL - 1) ||
+                // staging buffer k is free once its previous frame copy finished
+                !c->ck(cudaStreamWaitEvent(c->stream, c->ev_copied[k], 0), "wait"))
+                return -1;
+            int64_t p0 = 0;
+            for (const int64_t np : g.parts) {
+                const split_in in{(const char *) c->actB + p0 * tsz, sf_in + p0 * ssz, sk_in + p0 * ssz};
+                float *fr = c->frames_d[k] + p0 * fsz;
+                uint8_t *rg = c->rgb_d[k] + p0 * fsz;
+                if (!run_chunk(c, nullptr, np, fr, c->stream, N_LEVELS - 1, &in, p0) ||
+                    (rgb && !c->ck(launch_chw_to_rgb24(fr, np, (int64_t) IMG * IMG, rg, c->stream), "rgb24")) ||
+                    !c->ck(cudaEventRecord(c->ev_done[k], c->stream), "record") ||
+                    !c->ck(cudaStreamWaitEvent(c->copy_stream, c->ev_done[k], 0), "wait") ||
+                    !c->ck(cudaMemcpyAsync((char *) out + (g.f0 + p0) * osz, rgb ? (const void *) rg : fr,
+                                           (size_t) np * osz, cudaMemcpyDeviceToHost, c->copy_stream),
+                           "frames D2H"))
+                    return -1;
+                p0 += np;
+            }
+            if (!c->ck(cudaEventRecord(c->ev_copied[k], c->copy_stream), "record")) return -1;
+            k ^= 1;
+        }
+        if (!c->ck(cudaStreamSynchronize(c->copy_stream), "sync") ||
+            !c->ck(cudaStreamSynchronize(c->stream), "sync") || !device_ok(c))
+            return -1;
+        return 0;
+    }
     const std::vector<int64_t> plan = sub_batch_plan(n, c->max_batch);
     int k = 0;
     int64_t f0 = 0;
