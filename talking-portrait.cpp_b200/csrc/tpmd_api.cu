@@ -963,6 +963,10 @@ std::vector<int64_t> sub_batch_plan(int64_t n, int64_t max_batch) {
 // quarter of its frames in parts of about three: its copies start while
 // the group computes and little is left to copy when the compute ends. The
 // other group starts with a small part so that copying starts early.
+// RGB24 frames copy in 14 us each, a third of their tail-level compute, so
+// there the compute sets the pace: one group per chunk, most of its frames
+// in the first part and three short parts after it, whose copies leave
+// little to copy at the end.
 struct group_plan {
     int64_t f0, n;               // the group's frames within the call
     std::vector<int64_t> parts;  // its tail-level parts, in order
@@ -975,7 +979,7 @@ std::vector<int64_t> equal_parts(int64_t total, int64_t k) {
     return v;
 }
 
-std::vector<group_plan> split_plan(int64_t n, int64_t max_batch) {
+std::vector<group_plan> split_plan(int64_t n, int64_t max_batch, bool rgb) {
     std::vector<group_plan> plan;
     auto lead = [](int64_t g, double first, int64_t k) {  // a small first part, then k equal ones
         const int64_t f = std::min<int64_t>(g, std::max<int64_t>(1, std::llround(first * g)));
@@ -985,6 +989,13 @@ std::vector<group_plan> split_plan(int64_t n, int64_t max_batch) {
         return v;
     };
     int64_t f0 = 0;
+    if (rgb) {
+        for (; f0 < n; f0 += max_batch) {
+            const int64_t g = std::min(max_batch, n - f0);
+            plan.push_back({f0, g, lead(g, 0.58, 3)});
+        }
+        return plan;
+    }
     for (; n - f0 > max_batch; f0 += max_batch) plan.push_back({f0, max_batch, lead(max_batch, 0.21, 3)});
     const int64_t m = n - f0;
     if (m < 16) {
@@ -1123,7 +1134,7 @@ int host_decode(tpmd_ctx *c, const float *styles, int64_t n, void *out, bool rgb
         const size_t ssz = (size_t) 3 * rs * rs;                                   // skip floats per frame
         const float *sf_in = c->sf[(SPLIT_LEVEL - 1) & 1], *sk_in = c->sk[(SPLIT_LEVEL - 1) & 1];
         int k = 0;
-        for (const group_plan &g : split_plan(n, c->max_batch)) {
+        for (const group_plan &g : split_plan(n, c->max_batch, rgb)) {
             if (!c->ck(cudaMemcpyAsync(c->styles_d[k], styles + g.f0 * STYLE_DIM,
                                        (size_t) g.n * STYLE_DIM * 4, cudaMemcpyHostToDevice, c->stream),
                        "styles H2D") ||
