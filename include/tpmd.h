@@ -112,7 +112,10 @@ int tpmd_batch(const tpmd_ctx *ctx);
 
 /* styles (host) -> frames (host), n >= 1 frames; blocks until the frames
  * are in `frames`. Page-locked `frames` memory lets the device-to-host copy
- * overlap the next batch's compute. (motion_dec::decode_batch,
+ * overlap compute: on an f16 handle (n >= 4) the levels up to r128 run once
+ * per group of frames and the r256 and r512 levels in parts, each part's
+ * frames copied while the next part computes; the frames are the same bits
+ * as tpmd_decode_device's. (motion_dec::decode_batch,
  * src/motion_dec.cpp:1194-1220, without its fixed-batch restriction.) */
 int tpmd_decode(tpmd_ctx *ctx, const float *styles, int64_t n, float *frames);
 
