@@ -11,8 +11,10 @@
 //
 // Both reductions are small f32 GEMMs (rows x frames x K <= 512). One
 // register-tiled kernel serves both: a block owns 64 rows x 64 frames, K is
-// staged through shared memory 32 at a time, and each thread accumulates a
-// 4 x 4 outer product (rows o0 + tx + 16 i, frames b0 + 4 ty + j) in K order.
+// staged through shared memory 64 at a time (fewer barrier round trips per
+// block: the grid is about one block per SM, so each block's latency is the
+// kernel's), and each thread accumulates a 4 x 4 outer product (rows
+// o0 + tx + 16 i, frames b0 + 4 ty + j) in K order.
 // Shared reads are conflict-free or broadcast; stores are coalesced along
 // rows.
 #include "tpmd_internal.h"
@@ -20,7 +22,7 @@
 namespace tpmd {
 namespace {
 
-constexpr int PT = 64, PK = 32;  // tile rows and frames, K per stage
+constexpr int PT = 64, PK = 64;  // tile rows and frames, K per stage
 
 // DEN = false: s_all[b][o] = W[o] . lat[b] + bmod[o] (W [rows][512]).
 // DEN = true:  per conv (a tile never spans two), inv_den[b][d_off + o] =
@@ -64,26 +66,34 @@ prologue_gemm_kernel(const float *__restrict__ w, const float *__restrict__ bmod
     for (int i = 0; i < 4; i++)
 #pragma unroll
         for (int j = 0; j < 4; j++) acc[i][j] = 0.0f;
-    const int lk = threadIdx.x & 31, lr = threadIdx.x >> 5;  // loader: column lk, rows lr + 8 m
+    // loader: columns lk and lk + 32, rows lr + 8 m (columns past K load zeros,
+    // which add +0 to every sum)
+    const int lk = threadIdx.x & 31, lr = threadIdx.x >> 5;
     // the next K chunk is fetched into registers while this one is multiplied
-    float wn[PT / 8], an[PT / 8];
+    float wn[PK / 32][PT / 8], an[PK / 32][PT / 8];
     auto fetch = [&](int k0) {
-        const bool kin = k0 + lk < K;
 #pragma unroll
-        for (int m = 0; m < PT / 8; m++) {
-            const int r = lr + 8 * m, b = b0 + r;
-            wn[m] = (kin && r < nrow) ? __ldg(W + (int64_t) (o0 + r) * ldw + k0 + lk) : 0.0f;
-            an[m] = (kin && b < B) ? __ldg(a + (int64_t) b * a_stride + a_off + k0 + lk) : 0.0f;
+        for (int hh = 0; hh < PK / 32; hh++) {
+            const int kc = k0 + lk + 32 * hh;
+            const bool kin = kc < K;
+#pragma unroll
+            for (int m = 0; m < PT / 8; m++) {
+                const int r = lr + 8 * m, b = b0 + r;
+                wn[hh][m] = (kin && r < nrow) ? __ldg(W + (int64_t) (o0 + r) * ldw + kc) : 0.0f;
+                an[hh][m] = (kin && b < B) ? __ldg(a + (int64_t) b * a_stride + a_off + kc) : 0.0f;
+            }
         }
     };
     fetch(0);
     for (int k0 = 0; k0 < K; k0 += PK) {
 #pragma unroll
-        for (int m = 0; m < PT / 8; m++) {
-            const int r = lr + 8 * m;
-            Ws[r][lk] = wn[m];
-            As[r][lk] = DEN ? an[m] * an[m] : an[m];
-        }
+        for (int hh = 0; hh < PK / 32; hh++)
+#pragma unroll
+            for (int m = 0; m < PT / 8; m++) {
+                const int r = lr + 8 * m;
+                Ws[r][lk + 32 * hh] = wn[hh][m];
+                As[r][lk + 32 * hh] = DEN ? an[hh][m] * an[hh][m] : an[hh][m];
+            }
         __syncthreads();
         if (k0 + PK < K) fetch(k0 + PK);
 #pragma unroll 8

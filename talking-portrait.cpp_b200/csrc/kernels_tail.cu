@@ -144,6 +144,25 @@ __global__ void __launch_bounds__(256) tail_kernel(tail_params p) {
         float o[CPL], fs[CPL];
         chans<T, CPL>::load(outp + pix * OC + c0, o);
         chans<float, CPL>::load(p.fs + b * p.s_stride + c0, fs);
+        // the up-sampled skips depend on the pixel only, so their loads are
+        // issued here, in flight with the channel loads above. Groups of 8 or
+        // more lanes split them: lanes 0-2 form the flow skip's three
+        // channels, lanes 3-5 the rgb skip's, each with the four taps in
+        // order (shuffled to the group later); narrower groups form all six
+        float skv = 0.0f, skf[3] = {0.0f, 0.0f, 0.0f}, skr[3] = {0.0f, 0.0f, 0.0f};
+        if constexpr (G >= 8) {
+            if (gl < 6) {
+                const int k = gl < 3 ? gl : gl - 3;
+                const float *plane = gl < 3 ? p.skipf_prev : p.skip_prev;
+                if (plane) skv = up2x(plane + (b * 3 + k) * (int64_t) h * h, gl < 3 ? p.fup : p.rup, ut);
+            }
+        } else {
+#pragma unroll
+            for (int k = 0; k < 3; k++) {
+                if (p.skipf_prev) skf[k] = up2x(p.skipf_prev + (b * 3 + k) * (int64_t) h * h, p.fup, ut);
+                if (p.skip_prev) skr[k] = up2x(p.skip_prev + (b * 3 + k) * (int64_t) h * h, p.rup, ut);
+            }
+        }
         float f0 = 0.0f, f1 = 0.0f, f2 = 0.0f;
 #pragma unroll
         for (int c = 0; c < CPL; c++) {
@@ -153,11 +172,18 @@ __global__ void __launch_bounds__(256) tail_kernel(tail_params p) {
             f2 = fmaf(s_fw[(2 * CPL + c) * G + gl], xs, f2);
         }
         float fl[3] = {group_sum<G>(f0), group_sum<G>(f1), group_sum<G>(f2)};
+        const int lead = lane - gl;  // lane 0 of this pixel's group
+        if constexpr (G >= 8) {
+#pragma unroll
+            for (int k = 0; k < 3; k++) {
+                skf[k] = __shfl_sync(0xffffffffu, skv, lead + k);
+                skr[k] = __shfl_sync(0xffffffffu, skv, lead + 3 + k);
+            }
+        }
 #pragma unroll
         for (int k = 0; k < 3; k++) {
             fl[k] += __ldg(p.fb + k);
-            if (p.skipf_prev)
-                fl[k] += up2x(p.skipf_prev + (b * 3 + k) * (int64_t) h * h, p.fup, ut);
+            if (p.skipf_prev) fl[k] += skf[k];
         }
         if (p.skipf_out && gl == 0) {
 #pragma unroll
@@ -177,15 +203,24 @@ __global__ void __launch_bounds__(256) tail_kernel(tail_params p) {
         float smp[CPL];
 #pragma unroll
         for (int c = 0; c < CPL; c++) smp[c] = 0.0f;
+        // the four taps without branches, so their loads are in flight
+        // together: a tap outside the map (zeros padding) reads pixel 0 with
+        // weight 0, which adds +0 to every channel
+        int trow[4];
+        float twt[4];
 #pragma unroll
         for (int k = 0; k < 4; k++) {
             const int cx = x0 + (k & 1), cy = y0 + (k >> 1);
-            if (!sane || cx < 0 || cx >= r || cy < 0 || cy >= r) continue;
-            const float wgt = ((k & 1) ? wx : 1.0f - wx) * ((k >> 1) ? wy : 1.0f - wy);
-            float f[CPL];
-            chans<T, CPL>::load(featp + ((int64_t) cy * r + cx) * OC + c0, f);
+            const bool in = sane && cx >= 0 && cx < r && cy >= 0 && cy < r;
+            trow[k] = in ? cy * r + cx : 0;
+            twt[k] = in ? ((k & 1) ? wx : 1.0f - wx) * ((k >> 1) ? wy : 1.0f - wy) : 0.0f;
+        }
 #pragma unroll
-            for (int c = 0; c < CPL; c++) smp[c] = fmaf(wgt, f[c], smp[c]);
+        for (int k = 0; k < 4; k++) {
+            float f[CPL];
+            chans<T, CPL>::load(featp + (int64_t) trow[k] * OC + c0, f);
+#pragma unroll
+            for (int c = 0; c < CPL; c++) smp[c] = fmaf(twt[k], f[c], smp[c]);
         }
 
         const float om = 1.0f - m;
@@ -204,7 +239,7 @@ __global__ void __launch_bounds__(256) tail_kernel(tail_params p) {
             for (int k = 0; k < 3; k++) {
                 float v = rg[k] + __ldg(p.rlb + k);
                 v = (v > 0.0f ? v : 0.2f * v) + __ldg(p.rb + k);
-                if (p.skip_prev) v += up2x(p.skip_prev + (b * 3 + k) * (int64_t) h * h, p.rup, ut);
+                if (p.skip_prev) v += skr[k];
                 p.skip_out[(b * 3 + k) * rr + pr] = v;
             }
         }
