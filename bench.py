@@ -520,6 +520,72 @@ def run_e2e(args):
         dist.destroy_process_group()
 
 
+def run_schedule(args):
+    """The host decode's schedule on cuda:0 (tpmd_decode / tpmd_decode_rgb24
+    with pinned host buffers), config 2's decoder and inputs.
+
+    Prints one JSON line: the device time of one decode of nb frames
+    (tpmd_decode_device, CUDA events, median of 5 after 2 warm-ups) for
+    several nb, which gives the fixed and per-frame parts of a decode; the
+    device-to-host copy time of nb f32 frames into pinned memory; and the
+    host-buffer throughput of a 50-frame call (10 calls after 1 warm-up) with
+    the split schedule and with TPMD_NO_SPLIT (whole-decode sub-batches), for
+    f32 and RGB24 frames, alternating so both see the same box state."""
+    import torch
+    import tpmd
+    tensors, feats, styles = setup_inputs(0, args.batch, tpmd.scale_for)
+    nb_max = args.batch
+    dec = tpmd.MotionDecoder(0, tpmd.DTYPE_F16, max_batch=nb_max)
+    dec.set_tensors(tensors)
+    dec.prepare()
+    dec.set_feats(feats)
+    st = torch.cuda.Stream()
+    s_d = torch.from_numpy(np.ascontiguousarray(styles)).cuda()
+    f_d = torch.empty((nb_max, 3, 512, 512), device="cuda")
+    out = {"path": "schedule", "config": f"config 2 decoder, {nb_max}-frame calls, f16", "decode_ms": {},
+           "d2h_ms": {}, "host_fps": {}}
+    for nb in sorted({1, 2, 4, 8, 16, 25, 32, nb_max}):
+        if nb > nb_max:
+            continue
+        ts = []
+        for _ in range(7):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            dec.decode_device(s_d.data_ptr(), nb, f_d.data_ptr(), st.cuda_stream)
+            e1.record(st)
+            e1.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        out["decode_ms"][nb] = float(np.median(ts[2:]))
+    f_h = torch.empty((nb_max, 3, 512, 512), pin_memory=True)
+    r_h = torch.empty((nb_max, 512, 512, 3), dtype=torch.uint8, pin_memory=True)
+    for nb in sorted({1, 10, nb_max}):
+        ts = []
+        for _ in range(5):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            with torch.cuda.stream(st):
+                f_h[:nb].copy_(f_d[:nb], non_blocking=True)
+            e1.record(st)
+            e1.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        out["d2h_ms"][nb] = float(np.median(ts[1:]))
+    s_h = torch.from_numpy(np.ascontiguousarray(styles)).pin_memory()
+    for rep in range(2):
+        for fmt in ("f32", "rgb24"):
+            for plan in ("split", "no_split"):
+                if plan == "no_split":
+                    os.environ["TPMD_NO_SPLIT"] = "1"
+                call = (lambda: dec.decode_ptr(s_h.data_ptr(), nb_max, f_h.data_ptr())) if fmt == "f32" else \
+                       (lambda: dec.decode_rgb24_ptr(s_h.data_ptr(), nb_max, r_h.data_ptr()))
+                call()
+                t0 = time.perf_counter()
+                for _ in range(10):
+                    call()
+                out["host_fps"].setdefault(f"{fmt}_{plan}", []).append(10 * nb_max / (time.perf_counter() - t0))
+                os.environ.pop("TPMD_NO_SPLIT", None)
+    print(json.dumps(out), flush=True)
+
+
 def run_ops(args):
     """BASELINE config 1, the decoder's op-level sweep on cuda:0.
 
@@ -636,10 +702,13 @@ def main():
                     help="--path ops: only this 'C,H' shape (gather and im2col), no modconv sweep")
     ap.add_argument("--clip", type=int, default=0,
                     help="config 3: decode a clip of this many frames sharded across ranks per step")
-    ap.add_argument("--path", default="decoder", choices=["decoder", "encoder", "fmt", "audio", "e2e", "ops"],
+    ap.add_argument("--path", default="decoder",
+                    choices=["decoder", "encoder", "fmt", "audio", "e2e", "ops", "schedule"],
                     help="encoder: time the motion encoder (once per portrait); fmt: time the "
                          "flow-matching sampler (one 50-frame chunk per step); audio: the audio encoder "
-                         "(one 30 s clip per step); one GPU")
+                         "(one 30 s clip per step); schedule: the host decode's schedule (decode time "
+                         "by batch, frame copy time, host-buffer throughput with and without the split "
+                         "schedule); one GPU")
     args = ap.parse_args()
     if args.path == "encoder":
         run_encoder(args)
@@ -655,6 +724,9 @@ def main():
         return
     if args.path == "ops":
         run_ops(args)
+        return
+    if args.path == "schedule":
+        run_schedule(args)
         return
 
     rank = int(os.environ.get("RANK", "0"))
@@ -781,9 +853,11 @@ def main():
     tp = os.path.join(ROOT, "profiles", "ncu_traffic.json")
     if os.path.exists(tp):
         # ncu DRAM bytes of this kernel from a batch-8 capture, scaled to this
-        # launch: the feats are read once per launch, the rest per frame
+        # launch: the feats are read once per launch, the rest per frame. Used
+        # only while the kernel's sources are the ones captured (their hash)
         tj = json.load(open(tp))
-        if tj.get("kernel") == name and tj.get("conv") == ("tc" if dec_uses_tc() else "simt"):
+        if tj.get("kernel") == name and tj.get("conv") == ("tc" if dec_uses_tc() else "simt") and \
+                tj.get("source_sha256") == conv_source_hash():
             traffic = tj["fixed_bytes"] + tj["bytes_per_frame"] * nb
     roof["traffic"] = traffic
     roof["algorithmic_bytes"] = byts
@@ -822,6 +896,17 @@ def main():
     group.close()
     if world > 1:
         dist.destroy_process_group()
+
+
+def conv_source_hash() -> str:
+    """sha256 over the tcgen05 conv kernel's sources (kernels_conv_tc.cu,
+    tc_ptx.cuh): the key of the recorded ncu traffic figure"""
+    import hashlib
+    h = hashlib.sha256()
+    for f in ("kernels_conv_tc.cu", "tc_ptx.cuh"):
+        with open(os.path.join(ROOT, "talking-portrait.cpp_b200", "csrc", f), "rb") as fh:
+            h.update(fh.read())
+    return h.hexdigest()
 
 
 def dec_uses_tc() -> bool:
