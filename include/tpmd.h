@@ -119,6 +119,17 @@ int tpmd_batch(const tpmd_ctx *ctx);
  * src/motion_dec.cpp:1194-1220, without its fixed-batch restriction.) */
 int tpmd_decode(tpmd_ctx *ctx, const float *styles, int64_t n, float *frames);
 
+/* The schedule tpmd_decode (rgb = 0) or tpmd_decode_rgb24 (rgb = 1) runs for
+ * n >= 4 frames on an f16 handle created with max_batch: per group of frames
+ * the levels up to r128 run once, then the r256 and r512 levels in parts,
+ * each part's frames copied to the host while the next part computes. Writes
+ * per group {first frame, frames, number of parts k, k part sizes} into
+ * out (capacity cap entries) and returns the entries written, or -1 for bad
+ * arguments, n < 4 (decoded as whole-decode sub-batches instead) or too
+ * small a cap. Host-only; no counterpart in the reference (its decode_batch
+ * copies each batch after computing it, src/motion_dec.cpp:1194-1220). */
+int64_t tpmd_decode_schedule(int64_t n, int64_t max_batch, int rgb, int64_t *out, int64_t cap);
+
 /* Same frames as tpmd_decode, delivered as the reference's output format:
  * interleaved RGB24 bytes rgb [n][512][512][3], each channel value v mapped
  * by clamping to [-1, 1] and (unsigned char) ((v + 1) / 2 * 255) in f32, the

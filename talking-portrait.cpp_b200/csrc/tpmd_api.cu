@@ -1200,6 +1200,19 @@ int tpmd_decode(tpmd_ctx *c, const float *styles, int64_t n, float *frames) {
     return host_decode(c, styles, n, frames, false, "tpmd_decode");
 }
 
+int64_t tpmd_decode_schedule(int64_t n, int64_t max_batch, int rgb, int64_t *out, int64_t cap) {
+    if (n < 4 || max_batch < 1 || !out || cap < 0) return -1;
+    int64_t w = 0;
+    for (const group_plan &g : split_plan(n, max_batch, rgb != 0)) {
+        if (w + 3 + (int64_t) g.parts.size() > cap) return -1;
+        out[w++] = g.f0;
+        out[w++] = g.n;
+        out[w++] = (int64_t) g.parts.size();
+        for (const int64_t p : g.parts) out[w++] = p;
+    }
+    return w;
+}
+
 int tpmd_decode_rgb24(tpmd_ctx *c, const float *styles, int64_t n, uint8_t *rgb) {
     return host_decode(c, styles, n, rgb, true, "tpmd_decode_rgb24");
 }

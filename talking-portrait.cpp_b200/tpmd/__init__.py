@@ -51,7 +51,7 @@ EXPORTS = ("tpmd_abi_version", "tpmd_create", "tpmd_create_error", "tpmd_destroy
            "tpmd_group_member", "tpmd_group_set_tensor", "tpmd_group_load_gguf", "tpmd_group_prepare",
            "tpmd_group_set_feats", "tpmd_group_set_feats_device", "tpmd_shard_range", "tpmd_group_decode",
            "tpmd_group_max", "tpmd_group_selftest_nccl", "tpmd_decode_rgb24", "tpmd_group_decode_rgb24",
-           "tpk_chw_to_rgb24", "tpk_gemm")
+           "tpk_chw_to_rgb24", "tpk_gemm", "tpmd_decode_schedule")
 
 _lib = None
 
@@ -112,6 +112,8 @@ def load_library(path: str = LIB_PATH):
     L.tpmd_group_set_feats.argtypes = [v, C.POINTER(v)]
     L.tpmd_group_set_feats_device.argtypes = [v, C.POINTER(v), v]
     L.tpmd_shard_range.argtypes = [i64, C.c_int, C.c_int, C.POINTER(i64), C.POINTER(i64)]
+    L.tpmd_decode_schedule.argtypes = [i64, i64, C.c_int, C.POINTER(i64), i64]
+    L.tpmd_decode_schedule.restype = i64
     L.tpmd_group_decode.argtypes = [v, v, i64, v]
     L.tpmd_group_max.argtypes = [v, C.c_double, C.POINTER(C.c_double)]
     L.tpmd_decode_rgb24.argtypes = [v, v, i64, v]
@@ -712,6 +714,23 @@ class Pipeline:
         except Exception:
             pass
 
+
+
+def decode_schedule(n: int, max_batch: int, rgb: bool = False) -> list[tuple[int, int, list[int]]]:
+    """The host decode's groups (first frame, frames, tail-level part sizes)
+    for n >= 4 frames on an f16 handle (tpmd_decode_schedule)"""
+    L = load_library()
+    cap = 4 * n + 64
+    buf = (C.c_int64 * cap)()
+    w = L.tpmd_decode_schedule(n, max_batch, 1 if rgb else 0, buf, cap)
+    if w < 0:
+        raise ValueError("no split schedule for these arguments")
+    out, i = [], 0
+    while i < w:
+        f0, g, k = buf[i], buf[i + 1], buf[i + 2]
+        out.append((f0, g, list(buf[i + 3:i + 3 + k])))
+        i += 3 + k
+    return out
 
 
 def shard_range(n: int, nranks: int, rank: int) -> tuple[int, int]:
