@@ -35,9 +35,14 @@ def test_noalloc_matches_decode_device(model):
     ref = ref.cpu().numpy()
     for i in range(2):  # two calls in a row through the shared static scratch
         out = torch.full((1, 3, 512, 512), float("nan"), device="cuda")
+        torch.cuda.synchronize()
+        free0 = torch.cuda.mem_get_info()[0]
         rc = L.tpmd_decode_noalloc(C.c_void_p(dec._h), C.c_void_p(st[i:i + 1].data_ptr()), 1,
                                    C.c_void_p(out.data_ptr()), None)
         assert rc == 0, L.tpmd_last_error(C.c_void_p(dec._h)).decode()
+        torch.cuda.synchronize()
+        if i == 1:  # past the first call's one-time set-up, the device's free memory is untouched
+            assert torch.cuda.mem_get_info()[0] == free0
         # the frames count only once the device status is clean
         rc = L.tpmd_device_status(C.c_void_p(dec._h), None)
         assert rc == 0, L.tpmd_last_error(C.c_void_p(dec._h)).decode()
