@@ -1119,7 +1119,8 @@ int tpmd_profile_end(tpmd_ctx *c, char *json, size_t cap) {
 namespace {
 
 // The host decode loop: styles H2D, decode, (RGB24 conversion), frames D2H,
-// each sub-batch's copy overlapping the next sub-batch's compute.
+// each part's frame copy overlapping the next part's compute (split_plan on
+// tcgen05 handles, else whole-decode sub-batches by sub_batch_plan).
 int host_decode(tpmd_ctx *c, const float *styles, int64_t n, void *out, bool rgb, const char *who) {
     if (!c) return -1;
     if (!styles || !out || n < 1) return c->fail(std::string(who) + ": bad argument"), -1;
@@ -1127,6 +1128,14 @@ int host_decode(tpmd_ctx *c, const float *styles, int64_t n, void *out, bool rgb
     if (!c->ck(cudaSetDevice(c->device), "cudaSetDevice")) return -1;
     const size_t fsz = (size_t) 3 * IMG * IMG;
     const size_t osz = rgb ? fsz : fsz * 4;  // output bytes per frame
+    // once anything is enqueued, a failure waits for both streams before
+    // returning: no copy may still read the caller's styles or write its
+    // frames after the call (the error message is the first failure's)
+    auto bail = [&]() {
+        cudaStreamSynchronize(c->copy_stream);
+        cudaStreamSynchronize(c->stream);
+        return -1;
+    };
     if (c->use_tc && n >= 4 && !getenv("TPMD_SUBBATCH") && !getenv("TPMD_NO_SPLIT")) {
         // levels up to r128 per group, then the last two levels in parts
         constexpr int rs = 8 << (SPLIT_LEVEL - 1);
@@ -1141,7 +1150,7 @@ int host_decode(tpmd_ctx *c, const float *styles, int64_t n, void *out, bool rgb
                 !run_chunk(c, c->styles_d[k], g.n, nullptr, c->stream, SPLIT_LEVEL - 1) ||
                 // staging buffer k is free once its previous frame copy finished
                 !c->ck(cudaStreamWaitEvent(c->stream, c->ev_copied[k], 0), "wait"))
-                return -1;
+                return bail();
             int64_t p0 = 0;
             for (const int64_t np : g.parts) {
                 const split_in in{(const char *) c->actB + p0 * tsz, sf_in + p0 * ssz, sk_in + p0 * ssz};
@@ -1154,16 +1163,16 @@ int host_decode(tpmd_ctx *c, const float *styles, int64_t n, void *out, bool rgb
                     !c->ck(cudaMemcpyAsync((char *) out + (g.f0 + p0) * osz, rgb ? (const void *) rg : fr,
                                            (size_t) np * osz, cudaMemcpyDeviceToHost, c->copy_stream),
                            "frames D2H"))
-                    return -1;
+                    return bail();
                 p0 += np;
             }
-            if (!c->ck(cudaEventRecord(c->ev_copied[k], c->copy_stream), "record")) return -1;
+            if (!c->ck(cudaEventRecord(c->ev_copied[k], c->copy_stream), "record")) return bail();
             k ^= 1;
         }
         if (!c->ck(cudaStreamSynchronize(c->copy_stream), "sync") ||
-            !c->ck(cudaStreamSynchronize(c->stream), "sync") || !device_ok(c))
-            return -1;
-        return 0;
+            !c->ck(cudaStreamSynchronize(c->stream), "sync"))
+            return bail();
+        return device_ok(c) ? 0 : -1;
     }
     const std::vector<int64_t> plan = sub_batch_plan(n, c->max_batch);
     int k = 0;
@@ -1184,12 +1193,12 @@ int host_decode(tpmd_ctx *c, const float *styles, int64_t n, void *out, bool rgb
                                    (size_t) nb * osz, cudaMemcpyDeviceToHost, c->copy_stream),
                    "frames D2H") ||
             !c->ck(cudaEventRecord(c->ev_copied[k], c->copy_stream), "record"))
-            return -1;
+            return bail();
     }
     if (!c->ck(cudaStreamSynchronize(c->copy_stream), "sync") ||
-        !c->ck(cudaStreamSynchronize(c->stream), "sync") || !device_ok(c))
-        return -1;
-    return 0;
+        !c->ck(cudaStreamSynchronize(c->stream), "sync"))
+        return bail();
+    return device_ok(c) ? 0 : -1;
 }
 
 }  // namespace
