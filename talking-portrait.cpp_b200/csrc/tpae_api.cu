@@ -345,7 +345,7 @@ int tpae_prepare(tpae_ctx *a) {
     return 0;
 }
 
-int tpae_encode(tpae_ctx *a, const float *audio, int64_t n_in, int64_t seq_len, float *wa) {
+static int tpae_encode_enqueue(tpae_ctx *a, const float *audio, int64_t n_in, int64_t seq_len, float *wa) {
     if (!a) return -1;
     if (!audio || !wa || n_in < 1 || seq_len < 1) return a->fail("tpae_encode: bad argument"), -1;
     if (!a->wready) return a->fail("weights not prepared (tpae_prepare)"), -1;
@@ -525,6 +525,14 @@ int tpae_encode(tpae_ctx *a, const float *audio, int64_t n_in, int64_t seq_len, 
         !K(cudaStreamSynchronize(st), "audio encode") || !a->gemm_status())
         return -1;
     return 0;
+}
+
+// On a failure after work was enqueued, the stream is drained before the
+// call returns, so no copy reads or writes the caller's buffers after it.
+int tpae_encode(tpae_ctx *a, const float *audio, int64_t n_in, int64_t seq_len, float *wa) {
+    const int rc = tpae_encode_enqueue(a, audio, n_in, seq_len, wa);
+    if (rc != 0 && a && a->stream) cudaStreamSynchronize(a->stream);
+    return rc;
 }
 
 }  // extern "C"

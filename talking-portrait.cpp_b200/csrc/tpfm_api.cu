@@ -498,7 +498,7 @@ int tpfm_prepare(tpfm_ctx *c) {
     return 0;
 }
 
-int tpfm_forward(tpfm_ctx *c, const float *x60, const float *cond, float t, float *v) {
+static int tpfm_forward_enqueue(tpfm_ctx *c, const float *x60, const float *cond, float t, float *v) {
     if (!c) return -1;
     if (!x60 || !cond || !v) return c->fail("tpfm_forward: null argument"), -1;
     if (!ready(c)) return -1;
@@ -527,8 +527,16 @@ int tpfm_forward(tpfm_ctx *c, const float *x60, const float *cond, float t, floa
     return 0;
 }
 
-int tpfm_sample_chunk(tpfm_ctx *c, const float *wr, const float *prev_wa, const float *cond_audio,
-                      const float *prev_x, const float *x0, int emotion, float *motion) {
+// On a failure after work was enqueued, the stream is drained before the
+// call returns, so no copy reads or writes the caller's buffers after it.
+int tpfm_forward(tpfm_ctx *c, const float *x60, const float *cond, float t, float *v) {
+    const int rc = tpfm_forward_enqueue(c, x60, cond, t, v);
+    if (rc != 0 && c && c->stream) cudaStreamSynchronize(c->stream);
+    return rc;
+}
+
+static int tpfm_sample_chunk_enqueue(tpfm_ctx *c, const float *wr, const float *prev_wa, const float *cond_audio,
+                                     const float *prev_x, const float *x0, int emotion, float *motion) {
     if (!c) return -1;
     if (!wr || !cond_audio || !x0 || !motion || (c->c.prev_frames > 0 && (!prev_wa || !prev_x)))
         return c->fail("tpfm_sample_chunk: null argument"), -1;
@@ -581,6 +589,15 @@ int tpfm_sample_chunk(tpfm_ctx *c, const float *wr, const float *prev_wa, const 
         !c->ck(cudaStreamSynchronize(st), "sample chunk") || !c->gemm_status())
         return -1;
     return 0;
+}
+
+// On a failure after work was enqueued, the stream is drained before the
+// call returns, so no copy reads or writes the caller's buffers after it.
+int tpfm_sample_chunk(tpfm_ctx *c, const float *wr, const float *prev_wa, const float *cond_audio,
+                      const float *prev_x, const float *x0, int emotion, float *motion) {
+    const int rc = tpfm_sample_chunk_enqueue(c, wr, prev_wa, cond_audio, prev_x, x0, emotion, motion);
+    if (rc != 0 && c && c->stream) cudaStreamSynchronize(c->stream);
+    return rc;
 }
 
 }  // extern "C"

@@ -249,7 +249,7 @@ int tpme_prepare(tpme_ctx *c) {
     return 0;
 }
 
-int tpme_run(tpme_ctx *c, const float *image, float *appearance, float *lambda, float *motion,
+static int tpme_run_enqueue(tpme_ctx *c, const float *image, float *appearance, float *lambda, float *motion,
              float *const feats[TPMD_N_LEVELS]) {
     if (!c) return -1;
     if (!image) return c->fail("tpme_run: null image"), -1;
@@ -328,6 +328,15 @@ int tpme_run(tpme_ctx *c, const float *image, float *appearance, float *lambda, 
     }
     c->ran = true;
     return 0;
+}
+
+// On a failure after work was enqueued, the stream is drained before the
+// call returns, so no copy reads or writes the caller's buffers after it.
+int tpme_run(tpme_ctx *c, const float *image, float *appearance, float *lambda, float *motion,
+             float *const feats[TPMD_N_LEVELS]) {
+    const int rc = tpme_run_enqueue(c, image, appearance, lambda, motion, feats);
+    if (rc != 0 && c && c->stream) cudaStreamSynchronize(c->stream);
+    return rc;
 }
 
 int tpme_feat_device(tpme_ctx *c, int j, const float **dev_ptr, int64_t *count) {
