@@ -64,13 +64,22 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, mode, q):
+def _init_gloo(rank, world, port, collective_s):
+    """gloo process group whose rendezvous waits up to 120 s for ranks that
+    start late (spawned processes importing torch on a loaded host), while
+    its collectives time out after collective_s"""
     import datetime
+    import torch.distributed as dist
+    store = dist.TCPStore("127.0.0.1", port, world, rank == 0, timeout=datetime.timedelta(seconds=120))
+    dist.init_process_group("gloo", store=store, rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=collective_s))
+
+
+def _worker(rank, world, port, mode, q):
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     try:
-        dist.init_process_group("gloo", rank=rank, world_size=world,
-                                timeout=datetime.timedelta(seconds=10))
+        _init_gloo(rank, world, port, 10)
         if mode == "fail" and rank == 1:
             raise RuntimeError("injected failure on rank 1 before the broadcast")
         arena = torch.arange(4096, dtype=torch.uint8) if rank == 0 else torch.zeros(4096, dtype=torch.uint8)
@@ -135,11 +144,10 @@ class _FakePipeline:
 
 
 def _pipe_worker(rank, world, port, n, chunk, q):
-    import datetime
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     try:
-        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=20))
+        _init_gloo(rank, world, port, 30)
         multi.arena_tensor = lambda dec, which, device: dec.feats
         multi.FRAME_BYTES = 16  # a 4-float frame keeps the buffers small
         dec = _FakeDecoder(rank)
