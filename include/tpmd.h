@@ -141,7 +141,10 @@ int tpmd_decode_rgb24(tpmd_ctx *ctx, const float *styles, int64_t n, uint8_t *rg
  * the legacy default stream, as in CUDA's own APIs) without host
  * synchronisation. The return code covers the enqueue only: whether the
  * kernels' pipeline waits all completed is known once tpmd_device_status
- * returns 0, and the frames are valid only then. */
+ * returns 0, and the frames are valid only then. The handle's later calls
+ * (on any stream, and the synchronous ones) start on the GPU after this
+ * decode's work, outside a stream capture; inside one, the caller orders
+ * the captured work against the handle's other calls. */
 int tpmd_decode_device(tpmd_ctx *ctx, const float *styles_dev, int64_t n,
                        float *frames_dev, void *stream);
 

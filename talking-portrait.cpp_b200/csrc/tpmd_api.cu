@@ -102,6 +102,10 @@ struct tpmd_ctx {
     bool use_graph = true;
     cudaStream_t stream = nullptr, copy_stream = nullptr, cap_stream = nullptr;
     cudaEvent_t ev_done[2] = {nullptr, nullptr}, ev_copied[2] = {nullptr, nullptr};
+    // the end of the handle's last asynchronous decode (tpmd_decode_device),
+    // on the caller's stream: the handle's later calls wait for it, so calls
+    // on one handle use its workspace in call order on the GPU
+    cudaEvent_t ev_order = nullptr;
     std::string err;
 
     std::map<std::string, int64_t> spec;
@@ -440,6 +444,7 @@ tpmd_ctx::~tpmd_ctx() {
         if (ev_done[i]) cudaEventDestroy(ev_done[i]);
         if (ev_copied[i]) cudaEventDestroy(ev_copied[i]);
     }
+    if (ev_order) cudaEventDestroy(ev_order);
     for (auto &r : prof) {
         cudaEventDestroy(r.a);
         cudaEventDestroy(r.b);
@@ -524,6 +529,7 @@ tpmd_ctx *tpmd_create(int device, int dtype, int max_batch) {
     for (int i = 0; ok && i < 2; i++)
         ok = c->ck(cudaEventCreateWithFlags(&c->ev_done[i], cudaEventDisableTiming), "event") &&
              c->ck(cudaEventCreateWithFlags(&c->ev_copied[i], cudaEventDisableTiming), "event");
+    ok = ok && c->ck(cudaEventCreateWithFlags(&c->ev_order, cudaEventDisableTiming), "event");
     if (!ok) {
         g_create_err = c->err;
         delete c;
@@ -1027,10 +1033,18 @@ int tpmd_decode_device(tpmd_ctx *c, const float *styles_dev, int64_t n, float *f
     if (!c->ck(cudaSetDevice(c->device), "cudaSetDevice")) return -1;
     cudaStream_t st = (cudaStream_t) stream;  // NULL: the legacy default stream
     const size_t fsz = (size_t) 3 * IMG * IMG;
+    // after the handle's previous asynchronous decode, which may have run on
+    // another stream (skipped inside a stream capture, which may not wait on
+    // an event recorded outside it)
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (!c->ck(cudaStreamIsCapturing(st, &cs), "capture status") ||
+        (cs == cudaStreamCaptureStatusNone && !c->ck(cudaStreamWaitEvent(st, c->ev_order, 0), "order wait")))
+        return -1;
     for (int64_t f0 = 0; f0 < n; f0 += c->max_batch) {
         const int64_t nb = std::min<int64_t>(c->max_batch, n - f0);
         if (!run_chunk(c, styles_dev + f0 * STYLE_DIM, nb, frames_dev + f0 * fsz, st)) return -1;
     }
+    if (cs == cudaStreamCaptureStatusNone && !c->ck(cudaEventRecord(c->ev_order, st), "order record")) return -1;
     return 0;
 }
 
@@ -1042,6 +1056,7 @@ int tpmd_decode_taps(tpmd_ctx *c, const float *style, int level, float *conv1, f
     if (!style || level < 0 || level >= N_LEVELS) return c->fail("tpmd_decode_taps: bad argument"), -1;
     if (!ready(c)) return -1;
     if (!c->ck(cudaSetDevice(c->device), "cudaSetDevice") ||
+        !c->ck(cudaStreamWaitEvent(c->stream, c->ev_order, 0), "order wait") ||
         !c->ck(cudaMemcpyAsync(c->styles_d[0], style, STYLE_DIM * 4, cudaMemcpyHostToDevice,
                                c->stream),
                "style H2D") ||
@@ -1136,6 +1151,8 @@ int host_decode(tpmd_ctx *c, const float *styles, int64_t n, void *out, bool rgb
         cudaStreamSynchronize(c->stream);
         return -1;
     };
+    // after the handle's previous asynchronous decode (tpmd_decode_device)
+    if (!c->ck(cudaStreamWaitEvent(c->stream, c->ev_order, 0), "order wait")) return -1;
     if (c->use_tc && n >= 4 && !getenv("TPMD_SUBBATCH") && !getenv("TPMD_NO_SPLIT")) {
         // levels up to r128 per group, then the last two levels in parts
         constexpr int rs = 8 << (SPLIT_LEVEL - 1);
