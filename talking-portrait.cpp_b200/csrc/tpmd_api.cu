@@ -875,6 +875,8 @@ bool enqueue_chunk(tpmd_ctx *c, const ws_view &w, const float *styles, int64_t n
 // workspace. Launched from a cached CUDA graph where possible.
 bool run_chunk(tpmd_ctx *c, const float *styles, int64_t nb, float *out, cudaStream_t st,
                int last_level, const split_in *in, int64_t row0) {
+    nvtx_range range(in ? "tpmd chunk: r256-r512 part" : last_level < N_LEVELS - 1 ? "tpmd chunk: levels to r128"
+                                                                                  : "tpmd chunk: all levels");
     ws_view w0 = ctx_ws(c);
     w0.s_all += row0 * c->S_TOT;
     w0.inv_den += row0 * c->D_TOT;
@@ -1027,6 +1029,7 @@ extern "C" {
 
 int tpmd_decode_device(tpmd_ctx *c, const float *styles_dev, int64_t n, float *frames_dev,
                        void *stream) {
+    nvtx_range range("tpmd_decode_device");
     if (!c) return -1;
     if (!styles_dev || !frames_dev || n < 1) return c->fail("tpmd_decode_device: bad argument"), -1;
     if (!ready(c)) return -1;
@@ -1137,6 +1140,7 @@ namespace {
 // each part's frame copy overlapping the next part's compute (split_plan on
 // tcgen05 handles, else whole-decode sub-batches by sub_batch_plan).
 int host_decode(tpmd_ctx *c, const float *styles, int64_t n, void *out, bool rgb, const char *who) {
+    nvtx_range range(who);
     if (!c) return -1;
     if (!styles || !out || n < 1) return c->fail(std::string(who) + ": bad argument"), -1;
     if (!ready(c)) return -1;

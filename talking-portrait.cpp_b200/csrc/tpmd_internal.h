@@ -9,7 +9,19 @@
 #include <string>
 #include <utility>
 
+#include <nvtx3/nvToolsExt.h>
+
 namespace tpmd {
+
+// A named NVTX range over a host scope (decode calls, their phases): shows
+// the host side of a decode on a profiler's timeline. NVTX v3 is header-only
+// and its calls do nothing unless a profiling tool is attached.
+struct nvtx_range {
+    explicit nvtx_range(const char *name) { nvtxRangePushA(name); }
+    ~nvtx_range() { nvtxRangePop(); }
+    nvtx_range(const nvtx_range &) = delete;
+    nvtx_range &operator=(const nvtx_range &) = delete;
+};
 
 // Programmatic dependent launch: a kernel launched by launch_pdl may start
 // while the kernel before it in the stream is still running. It calls
