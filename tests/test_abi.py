@@ -31,6 +31,18 @@ def test_exports_every_declared_symbol():
     assert set(names) == set(tpmd.EXPORTS)
 
 
+def test_library_links_no_vendor_math_library():
+    """every contraction on the path is the library's own tcgen05 code: the
+    shared object depends on the C/C++ runtime only (CUDA runtime linked
+    statically, NCCL opened at run time by the multi-GPU group), not on
+    cuBLAS, cuBLASLt, cuDNN or a CUDA runtime of the host process"""
+    import subprocess
+    so = tpmd.LIB_PATH
+    deps = subprocess.run(["ldd", so], capture_output=True, text=True, check=True).stdout
+    for lib in ("cublas", "cudnn", "cudart", "nccl", "torch"):
+        assert lib not in deps, (lib, deps)
+
+
 def test_abi_version():
     assert tpmd.load_library().tpmd_abi_version() == 1
 
